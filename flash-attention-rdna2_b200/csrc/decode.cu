@@ -1,0 +1,395 @@
+// decode.cu — paged-KV decode: append, split-K partial attention, split merge; plus the
+// standalone LSE-merge kernel behind flash_attn_combine.
+//
+// Cache layout is flash-attn's: Kc/Vc [num_blocks, page, NKV, HD], block_table [batch,
+// max_blocks].  Position pos of sequence b lives in page block_table[b][pos / page], slot
+// pos % page.  The decode is HBM-bound: one CTA streams the K/V rows of one (sequence, kv head,
+// split) exactly once for all the query heads of its group (up to 8 per CTA; larger groups
+// use several CTAs), so K/V bytes are read once per group.
+//
+// Work layout inside a CTA: a "row group" of HD/8 lanes owns one cache position at a time,
+// each lane 8 contiguous dims (one 16-byte load for 2-byte types).  Every row group keeps its
+// own online-softmax state (m, l, acc[g][8]) over the positions it visits, so the streaming
+// loop has no block-wide synchronisation; the row groups are merged once at the end.  Scores
+// are kept in the log2 domain; the scratch holds (m, l, acc[HD]) per (token, head, split)
+// with m in log2 units.
+#include "fa_common.cuh"
+#include "fa_launch.h"
+
+namespace {
+
+constexpr int DEC_THREADS = 256;
+
+template <typename T> struct Vec8;   // 8 elements of T, loaded as one (or two) 16-byte words
+template <> struct Vec8<__half> {
+  static __device__ __forceinline__ void load(const __half* p, float* f) {
+    const uint4 r = __ldg(reinterpret_cast<const uint4*>(p));
+    const __half2* h = reinterpret_cast<const __half2*>(&r);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) { const float2 v = __half22float2(h[i]); f[2 * i] = v.x; f[2 * i + 1] = v.y; }
+  }
+};
+template <> struct Vec8<__nv_bfloat16> {
+  static __device__ __forceinline__ void load(const __nv_bfloat16* p, float* f) {
+    const uint4 r = __ldg(reinterpret_cast<const uint4*>(p));
+    const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) { f[2 * i] = __uint_as_float(w[i] << 16); f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u); }
+  }
+};
+template <> struct Vec8<float> {
+  static __device__ __forceinline__ void load(const float* p, float* f) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(p)), b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  }
+};
+
+__device__ __forceinline__ void rotate_row(float* v, int rdim, int mode, const float* c, const float* s) {
+  const int half = rdim / 2;
+  for (int d = 0; d < half; ++d) {
+    if (mode == 1) {
+      const float x = v[d], y = v[d + half];
+      v[d] = x * c[d] - y * s[d];
+      v[d + half] = y * c[d] + x * s[d];
+    } else {
+      const float x = v[2 * d], y = v[2 * d + 1];
+      v[2 * d] = x * c[d] - y * s[d];
+      v[2 * d + 1] = y * c[d] + x * s[d];
+    }
+  }
+}
+
+// Page lookup with a bounds check; an invalid page index marks the position invisible and
+// raises the caller's error flag (the cache is never read out of bounds).
+__device__ __forceinline__ long long page_of(const FaDecParams& p, int b, int pos, int shift, bool& ok) {
+  const int blk = p.block_table[(long long)b * p.max_blocks + (pos >> shift)];
+  ok = blk >= 0 && (p.num_blocks <= 0 || blk < p.num_blocks);
+  if (!ok && p.err_flag) atomicExch(p.err_flag, 1);
+  return ok ? (long long)blk : 0;
+}
+
+// ---------------------------------------------------------------- append (new k/v -> cache)
+template <typename T>
+__global__ void dec_append_kernel(const FaDecParams p, const void* new_k, const void* new_v) {
+  extern __shared__ float ks[];
+  const int bx = blockIdx.x, kvh = blockIdx.y, t = threadIdx.x;
+  const int b = bx / p.nq, tk = bx % p.nq, NKV = p.NH / p.gqa, HD = p.HD;
+  const int pos = p.ctx_len[b] + tk;
+  const int shift = __ffs(p.page) - 1;
+  bool ok;
+  const long long blk = page_of(p, b, pos, shift, ok);
+  if (!ok) return;
+  const long long src = ((long long)(b * p.nq + tk) * NKV + kvh) * HD;
+  const long long dst = ((blk * p.page + (pos & (p.page - 1))) * NKV + kvh) * HD;
+  const T* nk = (const T*)new_k + src;
+  const T* nv = (const T*)new_v + src;
+  for (int d = t; d < HD; d += blockDim.x) ks[d] = Elem<T>::to_f(nk[d]);
+  __syncthreads();
+  if (p.rotary && t == 0) {
+    const int rdim = p.rotary_dim > 0 ? p.rotary_dim : HD;
+    const int rp = (p.rotary_pos ? p.rotary_pos[b] : p.ctx_len[b]) + tk;
+    rotate_row(ks, rdim, p.rotary, p.cos + (long long)rp * (rdim / 2), p.sin + (long long)rp * (rdim / 2));
+  }
+  __syncthreads();
+  T* kc = (T*)p.Kc + dst;
+  T* vc = (T*)p.Vc + dst;
+  for (int d = t; d < HD; d += blockDim.x) {
+    kc[d] = Elem<T>::from_f(ks[d]);
+    vc[d] = nv[d];
+  }
+}
+
+// ---------------------------------------------------------------- split-K partial attention
+// grid (batch*nq, NKV*groups, nsplit); G = query heads handled per CTA
+template <typename T, int HD, int G>
+__global__ void __launch_bounds__(DEC_THREADS) dec_partial_kernel(const FaDecParams p, int groups) {
+  // lanes per row group: HD/8 rounded up to a power of two (lanes past HD/8 stay idle)
+  constexpr int LPR = (HD / 8 <= 2) ? 2 : (HD / 8 <= 4) ? 4 : (HD / 8 <= 8) ? 8 : (HD / 8 <= 16) ? 16 : 32;
+  constexpr int RPW = 32 / LPR;               // row groups per warp
+  constexpr int NRG = (DEC_THREADS / 32) * RPW;
+  constexpr int U = 4;                        // positions in flight per row group
+  __shared__ float qs[G][HD];
+  __shared__ float ms[NRG][G], ls[NRG][G];
+  __shared__ float red[NRG][8 * LPR];         // one head's accumulators of every row group
+
+  const int bx = blockIdx.x, kvh = blockIdx.y / groups, grp = blockIdx.y % groups, sp = blockIdx.z;
+  const int b = bx / p.nq, tk = bx % p.nq;
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int rg = warp * RPW + lane / LPR, li = lane % LPR, d0 = li * 8;
+  const bool dlive = d0 < HD;                 // this lane owns real dims
+  const int NKV = p.NH / p.gqa;
+  const int hbase = kvh * p.gqa + grp * G;
+  const int nh = min(G, p.gqa - grp * G);     // heads of this CTA that exist
+
+  const int ctx0 = p.ctx_len[b];
+  const int qpos = ctx0 + tk;
+  const int ctx = ctx0 + (p.append ? tk + 1 : 0);
+  int lo = p.leftpad ? p.leftpad[b] : 0;
+  if (p.window >= 0) lo = max(lo, qpos - p.window + 1);
+  lo = max(lo, 0);
+  const int n = max(ctx - lo, 0);
+  const int chunk = (n + p.nsplit - 1) / p.nsplit;
+  const int start = lo + sp * chunk, end = min(start + chunk, ctx);
+
+  // q (+ rotary) into shared memory, fp32
+  const T* qg = (const T*)p.q + ((long long)(b * p.nq + tk) * p.NH + hbase) * HD;
+  for (int e = t; e < G * HD; e += DEC_THREADS) {
+    const int g = e / HD, d = e % HD;
+    qs[g][d] = (g < nh) ? Elem<T>::to_f(qg[(long long)g * HD + d]) : 0.f;
+  }
+  __syncthreads();
+  if (p.rotary && t < G && t < nh) {
+    const int rdim = p.rotary_dim > 0 ? p.rotary_dim : HD;
+    const int rp = (p.rotary_pos ? p.rotary_pos[b] : ctx0) + tk;
+    rotate_row(qs[t], rdim, p.rotary, p.cos + (long long)rp * (rdim / 2), p.sin + (long long)rp * (rdim / 2));
+  }
+  __syncthreads();
+
+  const float scale2 = p.scale * FA_LOG2E;
+  float qr[G][8];
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) qr[g][i] = dlive ? qs[g][d0 + i] : 0.f;
+  float slope[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) slope[g] = (p.alibi && g < nh) ? p.alibi[hbase + g] : 0.f;
+
+  float m[G], l[G], acc[G][8];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    m[g] = -INFINITY; l[g] = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[g][i] = 0.f;
+  }
+
+  const int shift = __ffs(p.page) - 1, pmask = p.page - 1;
+  const T* Kc = (const T*)p.Kc;
+  const T* Vc = (const T*)p.Vc;
+  for (int base = start + rg; base < end; base += NRG * U) {
+    float kf[U][8], vf[U][8];
+    bool vis[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int pos = base + u * NRG;
+      vis[u] = pos < end;
+      if (vis[u]) {
+        bool ok;
+        const long long blk = page_of(p, b, pos, shift, ok);
+        vis[u] = ok;
+        const long long off = ((blk * p.page + (pos & pmask)) * NKV + kvh) * HD + d0;
+        if (ok && dlive) {
+          Vec8<T>::load(Kc + off, kf[u]);
+          Vec8<T>::load(Vc + off, vf[u]);
+        }
+      }
+      if (!vis[u] || !dlive) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) { kf[u][i] = 0.f; vf[u][i] = 0.f; }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int pos = base + u * NRG;
+      float s[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float a = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) a = fmaf(qr[g][i], kf[u][i], a);
+#pragma unroll
+        for (int o = LPR / 2; o >= 1; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+        s[g] = a;
+      }
+      if (!vis[u]) continue;   // uniform across the row group
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float v;
+        if (p.softcap > 0.f) v = p.softcap * tanhf(s[g] * p.scale / p.softcap) * FA_LOG2E;
+        else v = s[g] * scale2;
+        v += slope[g] * (float)(pos - qpos) * FA_LOG2E;
+        const float mn = fmaxf(m[g], v);
+        const float corr = exp2f(m[g] - mn);
+        const float pw = exp2f(v - mn);
+        l[g] = l[g] * corr + pw;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[g][i] = fmaf(pw, vf[u][i], acc[g][i] * corr);
+        m[g] = mn;
+      }
+    }
+  }
+
+  // merge the row groups: max, rescaled sums, then accumulators one head at a time
+  if (li == 0) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) { ms[rg][g] = m[g]; ls[rg][g] = l[g]; }
+  }
+  __syncthreads();
+  float M[G], L[G], w[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float mx = -INFINITY;
+    for (int r = 0; r < NRG; ++r) mx = fmaxf(mx, ms[r][g]);
+    M[g] = mx;
+    float sum = 0.f;
+    if (mx != -INFINITY)
+      for (int r = 0; r < NRG; ++r) sum += ls[r][g] * exp2f(ms[r][g] - mx);
+    L[g] = sum;
+    w[g] = (mx != -INFINITY) ? exp2f(m[g] - mx) : 0.f;
+  }
+  float* out_base = p.scratch + ((long long)(b * p.nq + tk) * p.NH) * (long long)p.nsplit * (HD + 2);
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 8; ++i) red[rg][d0 + i] = acc[g][i] * w[g];
+    __syncthreads();
+    if (g < nh) {
+      float* out = out_base + ((long long)(hbase + g) * p.nsplit + sp) * (HD + 2);
+      if (t == 0) { out[0] = M[g]; out[1] = L[g]; }
+      for (int d = t; d < HD; d += DEC_THREADS) {
+        float a = 0.f;
+        for (int r = 0; r < NRG; ++r) a += red[r][d];
+        out[2 + d] = a;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------- split merge -> O, LSE
+template <typename T>
+__global__ void dec_merge_kernel(const FaDecParams p) {
+  const int row = blockIdx.x, h = blockIdx.y, HD = p.HD;
+  const float* base = p.scratch + ((long long)row * p.NH + h) * (long long)p.nsplit * (HD + 2);
+  float M = -INFINITY;
+  for (int s = 0; s < p.nsplit; ++s) M = fmaxf(M, base[(long long)s * (HD + 2)]);
+  float L = 0.f;
+  if (M != -INFINITY)
+    for (int s = 0; s < p.nsplit; ++s) {
+      const float ms = base[(long long)s * (HD + 2)];
+      if (ms != -INFINITY) L += base[(long long)s * (HD + 2) + 1] * exp2f(ms - M);
+    }
+  const float invL = L > 0.f ? 1.f / L : 0.f;
+  T* o = (T*)p.o + ((long long)row * p.NH + h) * HD;
+  for (int d = threadIdx.x; d < HD; d += blockDim.x) {
+    float a = 0.f;
+    if (M != -INFINITY)
+      for (int s = 0; s < p.nsplit; ++s) {
+        const float ms = base[(long long)s * (HD + 2)];
+        if (ms != -INFINITY) a += base[(long long)s * (HD + 2) + 2 + d] * exp2f(ms - M);
+      }
+    o[d] = Elem<T>::from_f(a * invL);
+  }
+  if (p.lse_out && threadIdx.x == 0)
+    p.lse_out[(long long)row * p.NH + h] = L > 0.f ? M * FA_LN2 + logf(L) : -INFINITY;
+}
+
+template <typename T, int HD>
+int launch_partial(const FaDecParams& p, cudaStream_t st) {
+  const int NKV = p.NH / p.gqa;
+  const int gq = p.gqa;
+  dim3 grid(p.batch * p.nq, 1, p.nsplit);
+#define FA_DEC_G(GG)                                                                  \
+  {                                                                                   \
+    const int groups = (gq + GG - 1) / GG;                                            \
+    grid.y = NKV * groups;                                                            \
+    dec_partial_kernel<T, HD, GG><<<grid, DEC_THREADS, 0, st>>>(p, groups);           \
+  }
+  if (gq <= 1) FA_DEC_G(1)
+  else if (gq <= 2) FA_DEC_G(2)
+  else if (gq <= 4) FA_DEC_G(4)
+  else FA_DEC_G(8)
+#undef FA_DEC_G
+  fa::count_launch();
+  return fa::cuda_status(cudaGetLastError(), "decode partial launch");
+}
+
+template <typename T>
+int launch_t(const FaDecParams& p, cudaStream_t st, const void* nk, const void* nv) {
+  if (nk) {
+    const int NKV = p.NH / p.gqa;
+    const int thr = p.HD < 32 ? 32 : p.HD;
+    dec_append_kernel<T><<<dim3(p.batch * p.nq, NKV), thr, p.HD * sizeof(float), st>>>(p, nk, nv);
+    fa::count_launch();
+    if (int rc = fa::cuda_status(cudaGetLastError(), "decode append launch")) return rc;
+  }
+  int rc;
+  switch (p.HD) {
+    case 16: rc = launch_partial<T, 16>(p, st); break;
+    case 32: rc = launch_partial<T, 32>(p, st); break;
+    case 48: rc = launch_partial<T, 48>(p, st); break;
+    case 64: rc = launch_partial<T, 64>(p, st); break;
+    case 80: rc = launch_partial<T, 80>(p, st); break;
+    case 96: rc = launch_partial<T, 96>(p, st); break;
+    case 112: rc = launch_partial<T, 112>(p, st); break;
+    case 128: rc = launch_partial<T, 128>(p, st); break;
+    case 160: rc = launch_partial<T, 160>(p, st); break;
+    case 192: rc = launch_partial<T, 192>(p, st); break;
+    case 224: rc = launch_partial<T, 224>(p, st); break;
+    case 256: rc = launch_partial<T, 256>(p, st); break;
+    default:
+      fa::set_error("decode: head_dim=%d not instantiated", p.HD);
+      return FA_ERR_UNSUPPORTED;
+  }
+  if (rc) return rc;
+  const int thr = p.HD < 32 ? 32 : p.HD;
+  dec_merge_kernel<T><<<dim3(p.batch * p.nq, p.NH), thr, 0, st>>>(p);
+  fa::count_launch();
+  return fa::cuda_status(cudaGetLastError(), "decode merge launch");
+}
+
+// ---------------------------------------------------------------- flash_attn_combine
+template <typename TI, typename TO>
+__global__ void combine_kernel(const FaCombineParams p) {
+  // one CTA per (b, s, h) row; threads over D
+  const long long row = blockIdx.x;   // ((b*S)+s)*H + h
+  const int h = (int)(row % p.H);
+  const long long bs = row / p.H;
+  const int s = (int)(bs % p.S);
+  const int b = (int)(bs / p.S);
+  const long long rows = (long long)p.B * p.S * p.H;
+  float M = -INFINITY;
+  for (int k = 0; k < p.nsplit; ++k)
+    M = fmaxf(M, p.lse_partial[(((long long)k * p.B + b) * p.H + h) * p.S + s]);
+  float W = 0.f;
+  if (M != -INFINITY)
+    for (int k = 0; k < p.nsplit; ++k) W += expf(p.lse_partial[(((long long)k * p.B + b) * p.H + h) * p.S + s] - M);
+  const float invW = W > 0.f ? 1.f / W : 0.f;
+  for (int d = threadIdx.x; d < p.D; d += blockDim.x) {
+    float a = 0.f;
+    if (M != -INFINITY)
+      for (int k = 0; k < p.nsplit; ++k) {
+        const float w = expf(p.lse_partial[(((long long)k * p.B + b) * p.H + h) * p.S + s] - M);
+        a += w * Elem<TI>::to_f(((const TI*)p.out_partial)[((long long)k * rows + row) * p.D + d]);
+      }
+    ((TO*)p.out)[row * p.D + d] = Elem<TO>::from_f(a * invW);
+  }
+  if (p.lse_out && threadIdx.x == 0)
+    p.lse_out[((long long)b * p.H + h) * p.S + s] = W > 0.f ? M + logf(W) : -INFINITY;
+}
+
+template <typename TI>
+int combine_out(const FaCombineParams& p, cudaStream_t st) {
+  const long long rows = (long long)p.B * p.S * p.H;
+  const int thr = p.D < 32 ? 32 : (p.D > 256 ? 256 : p.D);
+  if (p.out_dtype == FA_DTYPE_F16) combine_kernel<TI, __half><<<(unsigned)rows, thr, 0, st>>>(p);
+  else if (p.out_dtype == FA_DTYPE_BF16) combine_kernel<TI, __nv_bfloat16><<<(unsigned)rows, thr, 0, st>>>(p);
+  else combine_kernel<TI, float><<<(unsigned)rows, thr, 0, st>>>(p);
+  fa::count_launch();
+  return fa::cuda_status(cudaGetLastError(), "combine launch");
+}
+
+}  // namespace
+
+namespace fa {
+int dec_run(const FaDecParams& p, int dtype, cudaStream_t st, const void* nk, const void* nv) {
+  if (dtype == FA_DTYPE_F16) return launch_t<__half>(p, st, nk, nv);
+  if (dtype == FA_DTYPE_BF16) return launch_t<__nv_bfloat16>(p, st, nk, nv);
+  return launch_t<float>(p, st, nk, nv);
+}
+int combine_run(const FaCombineParams& p, cudaStream_t st) {
+  if (p.in_dtype == FA_DTYPE_F16) return combine_out<__half>(p, st);
+  if (p.in_dtype == FA_DTYPE_BF16) return combine_out<__nv_bfloat16>(p, st);
+  return combine_out<float>(p, st);
+}
+}  // namespace fa

@@ -1,0 +1,280 @@
+// dispatch.cpp — torch extension fable_attn._C: turns tensors into the C-ABI parameter blocks of
+// include/fable_attn.h and enqueues the launch on torch's current stream for the tensor's device.
+// Same function names and argument order as the reference's extension
+// (package/csrc/dispatch.cpp:239-267): fwd, bwd, fwd_varlen, dec; plus bwd_varlen (native varlen
+// backward), combine (flash_attn_combine on the GPU) and kernel_launch_count.
+// Outputs and workspaces (out, lse, dq/dk/dv, dsum, decode scratch) are allocated here by torch,
+// as in the reference; kernels own nothing.  No host synchronisation anywhere.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cmath>
+#include "fable_attn.h"
+
+namespace {
+
+int dt_of(const torch::Tensor& t) {
+  if (t.scalar_type() == torch::kHalf) return FA_DTYPE_F16;
+  if (t.scalar_type() == torch::kBFloat16) return FA_DTYPE_BF16;
+  if (t.scalar_type() == torch::kFloat32) return FA_DTYPE_F32;
+  TORCH_CHECK_VALUE(false, "fable_attn: dtype ", t.scalar_type(), " not supported; need fp16/bf16/fp32");
+  return -1;
+}
+
+void* cur_stream(const torch::Tensor& t) {
+  return (void*)at::cuda::getCurrentCUDAStream(t.device().index()).stream();
+}
+
+void check(int rc, const char* what) {
+  if (rc == FA_OK) return;
+  const std::string msg = std::string("fable_attn ") + what + ": " + fa_last_error();
+  if (rc == FA_ERR_UNSUPPORTED) TORCH_CHECK_NOT_IMPLEMENTED(false, msg);
+  if (rc == FA_ERR_INVALID || rc == FA_ERR_SIZE) TORCH_CHECK_VALUE(false, msg);
+  TORCH_CHECK(false, msg);
+}
+
+FaStrides S4(const torch::Tensor& x) { return FaStrides{x.stride(0), x.stride(1), x.stride(2)}; }
+// (total, H, D) varlen tensors: token stride = stride(0), head stride = stride(1)
+FaStrides S3(const torch::Tensor& x) { return FaStrides{0, x.stride(1), x.stride(0)}; }
+
+void need_cuda_lastdim(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK_VALUE(t.is_cuda(), "fable_attn: ", name, " must be a CUDA tensor");
+  TORCH_CHECK_VALUE(t.stride(-1) == 1, "fable_attn: ", name, " must have a contiguous last dimension");
+}
+
+const float* opt_f32(const c10::optional<torch::Tensor>& t) {
+  if (!t.has_value() || !t->defined()) return nullptr;
+  TORCH_CHECK_VALUE(t->scalar_type() == torch::kFloat32 && t->is_contiguous(), "fable_attn: expected contiguous fp32");
+  return t->data_ptr<float>();
+}
+const int* opt_i32(const c10::optional<torch::Tensor>& t) {
+  if (!t.has_value() || !t->defined()) return nullptr;
+  TORCH_CHECK_VALUE(t->scalar_type() == torch::kInt32 && t->is_contiguous(), "fable_attn: expected contiguous int32");
+  return t->data_ptr<int>();
+}
+
+// ------------------------------------------------------------------ forward (dense)
+std::vector<torch::Tensor> fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, double scale, bool causal,
+                               int64_t win_left, int64_t win_right, double softcap,
+                               c10::optional<torch::Tensor> alibi, double dropout_p, int64_t seed,
+                               int64_t attn_chunk, c10::optional<torch::Tensor> out_opt) {
+  need_cuda_lastdim(q, "q"); need_cuda_lastdim(k, "k"); need_cuda_lastdim(v, "v");
+  TORCH_CHECK_VALUE(q.dim() == 4 && k.dim() == 4 && v.dim() == 4, "fable_attn: fwd expects [B,H,S,D]");
+  const c10::cuda::CUDAGuard guard(q.device());
+  const int B = q.size(0), Hq = q.size(1), SQ = q.size(2), D = q.size(3), Hk = k.size(1), SK = k.size(2);
+  TORCH_CHECK_VALUE(Hq % Hk == 0, "fable_attn: Hq must be a multiple of Hk (GQA)");
+  TORCH_CHECK_VALUE(k.scalar_type() == q.scalar_type() && v.scalar_type() == q.scalar_type(), "fable_attn: q/k/v dtypes differ");
+  torch::Tensor out = out_opt.has_value() ? *out_opt : torch::empty_like(q);
+  if (out_opt.has_value()) {
+    TORCH_CHECK_VALUE(out.sizes() == q.sizes() && out.scalar_type() == q.scalar_type() && out.stride(3) == 1,
+                      "fable_attn: out must match q's shape/dtype with a contiguous last dim");
+  }
+  auto lse = torch::empty({B, Hq, SQ}, q.options().dtype(torch::kFloat32));
+  FaFwdParams p{};
+  p.struct_size = sizeof(FaFwdParams);
+  p.Q = q.data_ptr(); p.K = k.data_ptr(); p.V = v.data_ptr(); p.O = out.data_ptr(); p.LSE = lse.data_ptr<float>();
+  p.sQ = S4(q); p.sK = S4(k); p.sV = S4(v); p.sO = S4(out);
+  p.batch = B; p.SQ = SQ; p.SK = SK; p.HD = D; p.NH = Hq; p.gqa = Hq / Hk;
+  p.scale = (float)scale; p.softcap = (float)softcap;
+  p.causal = causal ? 1 : 0; p.win_left = (int)win_left; p.win_right = (int)win_right;
+  p.attn_chunk = (int)attn_chunk; p.alibi_slopes = opt_f32(alibi);
+  p.dropout_p = (float)dropout_p; p.philox_seed = (unsigned long long)seed;
+  check(fa_forward_launch(&p, dt_of(q), cur_stream(q)), "forward");
+  return {out, lse};
+}
+
+// ------------------------------------------------------------------ forward (varlen)
+py::object fwd_varlen(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor cu_q, torch::Tensor cu_k,
+                      int64_t max_sq, int64_t max_sk, double scale, bool causal, int64_t win_left,
+                      int64_t win_right, double softcap, c10::optional<torch::Tensor> alibi, double dropout_p,
+                      int64_t seed, int64_t attn_chunk, c10::optional<torch::Tensor> seqused_q,
+                      c10::optional<torch::Tensor> seqused_k, bool return_lse) {
+  need_cuda_lastdim(q, "q"); need_cuda_lastdim(k, "k"); need_cuda_lastdim(v, "v");
+  TORCH_CHECK_VALUE(q.dim() == 3 && k.dim() == 3 && v.dim() == 3, "fable_attn: varlen expects (total, H, D)");
+  const c10::cuda::CUDAGuard guard(q.device());
+  const int Hq = q.size(1), D = q.size(2), Hk = k.size(1);
+  TORCH_CHECK_VALUE(Hq % Hk == 0, "fable_attn: Hq must be a multiple of Hk (GQA)");
+  const int batch = (int)cu_q.numel() - 1;
+  // rows past seqused_q are not written by the kernel: zero them so nothing uninitialised leaks
+  auto out = seqused_q.has_value() ? torch::zeros_like(q) : torch::empty_like(q);
+  torch::Tensor lse;
+  if (return_lse) lse = torch::full({Hq, q.size(0)}, -INFINITY, q.options().dtype(torch::kFloat32));
+  FaFwdParams p{};
+  p.struct_size = sizeof(FaFwdParams);
+  p.Q = q.data_ptr(); p.K = k.data_ptr(); p.V = v.data_ptr(); p.O = out.data_ptr();
+  p.LSE = return_lse ? lse.data_ptr<float>() : nullptr;
+  p.sQ = S3(q); p.sK = S3(k); p.sV = S3(v); p.sO = S3(out);
+  p.batch = batch; p.SQ = (int)max_sq; p.SK = (int)max_sk; p.HD = D; p.NH = Hq; p.gqa = Hq / Hk;
+  p.scale = (float)scale; p.softcap = (float)softcap;
+  p.causal = causal ? 1 : 0; p.win_left = (int)win_left; p.win_right = (int)win_right;
+  p.attn_chunk = (int)attn_chunk; p.alibi_slopes = opt_f32(alibi);
+  p.dropout_p = (float)dropout_p; p.philox_seed = (unsigned long long)seed;
+  p.cu_q = opt_i32(cu_q); p.cu_k = opt_i32(cu_k);
+  p.seqused_q = opt_i32(seqused_q); p.seqused_k = opt_i32(seqused_k);
+  p.lse_total_q = q.size(0);
+  check(fa_forward_launch(&p, dt_of(q), cur_stream(q)), "forward (varlen)");
+  if (return_lse) return py::make_tuple(out, lse);
+  return py::cast(out);
+}
+
+// ------------------------------------------------------------------ backward
+FaBwdParams bwd_common(torch::Tensor& dout, torch::Tensor& q, torch::Tensor& k, torch::Tensor& v,
+                       torch::Tensor& out, torch::Tensor& lse, double scale, bool causal, int64_t win_left,
+                       int64_t win_right, double softcap, const c10::optional<torch::Tensor>& alibi,
+                       double dropout_p, int64_t seed) {
+  FaBwdParams p{};
+  p.struct_size = sizeof(FaBwdParams);
+  p.Q = q.data_ptr(); p.K = k.data_ptr(); p.V = v.data_ptr(); p.O = out.data_ptr(); p.dO = dout.data_ptr();
+  p.lse = lse.data_ptr<float>();
+  p.scale = (float)scale; p.softcap = (float)softcap; p.alibi = opt_f32(alibi);
+  p.causal = causal ? 1 : 0; p.win_left = (int)win_left; p.win_right = (int)win_right;
+  p.dropout = dropout_p > 0 ? 1 : 0; p.drop_seed = (unsigned long long)seed; p.dropout_p = (float)dropout_p;
+  p.keep_scale = dropout_p > 0 ? (float)(1.0 / (1.0 - dropout_p)) : 1.f;
+  return p;
+}
+
+std::vector<torch::Tensor> bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
+                               torch::Tensor out, torch::Tensor lse, double scale, bool causal, int64_t win_left,
+                               int64_t win_right, double softcap, c10::optional<torch::Tensor> alibi,
+                               double dropout_p, int64_t seed) {
+  for (auto* t : {&dout, &q, &k, &v, &out}) need_cuda_lastdim(*t, "backward input");
+  TORCH_CHECK_VALUE(lse.is_contiguous() && lse.scalar_type() == torch::kFloat32, "fable_attn: lse must be contiguous fp32");
+  const c10::cuda::CUDAGuard guard(q.device());
+  const int B = q.size(0), Hq = q.size(1), SQ = q.size(2), D = q.size(3), Hk = k.size(1), SK = k.size(2);
+  auto dq = torch::empty_like(q), dk = torch::empty_like(k), dv = torch::empty_like(v);
+  auto dsum = torch::empty({B, Hq, SQ}, q.options().dtype(torch::kFloat32));
+  FaBwdParams p = bwd_common(dout, q, k, v, out, lse, scale, causal, win_left, win_right, softcap, alibi, dropout_p, seed);
+  p.dQ = dq.data_ptr(); p.dK = dk.data_ptr(); p.dV = dv.data_ptr(); p.dsum = dsum.data_ptr<float>();
+  p.qs = S4(q); p.ks = S4(k); p.vs = S4(v); p.os = S4(out); p.dos = S4(dout);
+  p.dqs = S4(dq); p.dks = S4(dk); p.dvs = S4(dv);
+  p.B = B; p.Hq = Hq; p.Hk = Hk; p.SQ = SQ; p.SK = SK; p.D = D; p.gqa = Hq / Hk;
+  check(fable_attn_backward_launch(&p, dt_of(q), cur_stream(q)), "backward");
+  return {dq, dk, dv};
+}
+
+std::vector<torch::Tensor> bwd_varlen(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
+                                      torch::Tensor out, torch::Tensor lse, torch::Tensor cu_q, torch::Tensor cu_k,
+                                      int64_t max_sq, int64_t max_sk, double scale, bool causal, int64_t win_left,
+                                      int64_t win_right, double softcap, c10::optional<torch::Tensor> alibi,
+                                      double dropout_p, int64_t seed, c10::optional<torch::Tensor> seqused_q,
+                                      c10::optional<torch::Tensor> seqused_k) {
+  for (auto* t : {&dout, &q, &k, &v, &out}) need_cuda_lastdim(*t, "backward input");
+  TORCH_CHECK_VALUE(lse.is_contiguous() && lse.scalar_type() == torch::kFloat32, "fable_attn: lse must be contiguous fp32");
+  const c10::cuda::CUDAGuard guard(q.device());
+  const int Hq = q.size(1), D = q.size(2), Hk = k.size(1);
+  auto dq = torch::zeros_like(q), dk = torch::zeros_like(k), dv = torch::zeros_like(v);
+  auto dsum = torch::empty({Hq, q.size(0)}, q.options().dtype(torch::kFloat32));
+  FaBwdParams p = bwd_common(dout, q, k, v, out, lse, scale, causal, win_left, win_right, softcap, alibi, dropout_p, seed);
+  p.dQ = dq.data_ptr(); p.dK = dk.data_ptr(); p.dV = dv.data_ptr(); p.dsum = dsum.data_ptr<float>();
+  p.qs = S3(q); p.ks = S3(k); p.vs = S3(v); p.os = S3(out); p.dos = S3(dout);
+  p.dqs = S3(dq); p.dks = S3(dk); p.dvs = S3(dv);
+  p.B = (int)cu_q.numel() - 1; p.Hq = Hq; p.Hk = Hk; p.SQ = (int)max_sq; p.SK = (int)max_sk; p.D = D;
+  p.gqa = Hq / Hk;
+  p.cu_q = opt_i32(cu_q); p.cu_k = opt_i32(cu_k);
+  p.seqused_q = opt_i32(seqused_q); p.seqused_k = opt_i32(seqused_k);
+  p.lse_total_q = q.size(0);
+  check(fable_attn_backward_launch(&p, dt_of(q), cur_stream(q)), "backward (varlen)");
+  return {dq, dk, dv};
+}
+
+// ------------------------------------------------------------------ decode
+std::vector<torch::Tensor> dec(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_table,
+                               torch::Tensor cache_seqlens, c10::optional<torch::Tensor> new_k,
+                               c10::optional<torch::Tensor> new_v, c10::optional<torch::Tensor> rotary_cos,
+                               c10::optional<torch::Tensor> rotary_sin, bool rotary_interleaved, double scale,
+                               int64_t window, int64_t num_splits, c10::optional<torch::Tensor> cache_leftpad,
+                               bool return_lse, double softcap, c10::optional<torch::Tensor> alibi,
+                               int64_t rotary_dim, c10::optional<torch::Tensor> rotary_pos) {
+  TORCH_CHECK_VALUE(q.is_cuda() && k_cache.is_cuda() && v_cache.is_cuda(), "fable_attn: decode needs CUDA tensors");
+  TORCH_CHECK_VALUE(q.dim() == 4 && q.is_contiguous(), "fable_attn: decode q must be contiguous [B,nq,Hq,D]");
+  TORCH_CHECK_VALUE(k_cache.dim() == 4 && k_cache.is_contiguous() && v_cache.is_contiguous(),
+                    "fable_attn: k_cache/v_cache must be contiguous [num_blocks, page, Hk, D]");
+  const c10::cuda::CUDAGuard guard(q.device());
+  const int B = q.size(0), NQ = q.size(1), Hq = q.size(2), D = q.size(3);
+  const int page = k_cache.size(1), Hk = k_cache.size(2);
+  TORCH_CHECK_VALUE(Hq % Hk == 0, "fable_attn: Hq must be a multiple of nheads_k (GQA)");
+  TORCH_CHECK_VALUE((page & (page - 1)) == 0, "fable_attn: page size must be a power of two");
+  // split count from shapes only (no .item(): no host sync)
+  const long long ctx_bound = (long long)block_table.size(1) * page;
+  const int nsplit = fa_decode_num_splits(B, NQ, Hk, ctx_bound, (int)num_splits);
+  auto out = torch::empty({B, NQ, Hq, D}, q.options());
+  auto scratch = torch::empty({fa_decode_scratch_floats(B, NQ, Hq, D, nsplit)}, q.options().dtype(torch::kFloat32));
+  auto lse = return_lse ? torch::empty({B, NQ, Hq}, q.options().dtype(torch::kFloat32))
+                        : torch::empty({0}, q.options().dtype(torch::kFloat32));
+  FaDecParams p{};
+  p.struct_size = sizeof(FaDecParams);
+  p.q = q.data_ptr(); p.Kc = k_cache.data_ptr(); p.Vc = v_cache.data_ptr();
+  p.block_table = opt_i32(block_table); p.o = out.data_ptr(); p.scratch = scratch.data_ptr<float>();
+  p.ctx_len = opt_i32(cache_seqlens);
+  p.cos = opt_f32(rotary_cos); p.sin = opt_f32(rotary_sin);
+  p.batch = B; p.NH = Hq; p.gqa = Hq / Hk; p.HD = D; p.page = page; p.max_blocks = (int)block_table.size(1);
+  p.nsplit = nsplit; p.window = (int)window;
+  p.rotary = rotary_cos.has_value() ? (rotary_interleaved ? 2 : 1) : 0;
+  p.scale = (float)scale; p.leftpad = opt_i32(cache_leftpad);
+  p.lse_out = return_lse ? lse.data_ptr<float>() : nullptr;
+  p.softcap = (float)softcap; p.alibi = opt_f32(alibi); p.nq = NQ;
+  p.rotary_dim = (int)rotary_dim; p.rotary_pos = opt_i32(rotary_pos);
+  p.num_blocks = k_cache.size(0);
+  const void* nk = nullptr; const void* nv = nullptr;
+  if (new_k.has_value()) {
+    TORCH_CHECK_VALUE(new_v.has_value() && new_k->is_contiguous() && new_v->is_contiguous(),
+                      "fable_attn: new k/v must be contiguous and given together");
+    nk = new_k->data_ptr(); nv = new_v->data_ptr();
+  }
+  check(fa_decode_launch(&p, dt_of(q), cur_stream(q), nk, nv), "decode");
+  return {out, lse};
+}
+
+// ------------------------------------------------------------------ combine
+std::vector<torch::Tensor> combine(torch::Tensor out_partial, torch::Tensor lse_partial, c10::ScalarType out_dtype,
+                                   bool return_lse) {
+  TORCH_CHECK_VALUE(out_partial.is_cuda() && out_partial.dim() == 5 && out_partial.is_contiguous(),
+                    "fable_attn: out_partial must be contiguous CUDA (nsplit, B, S, H, D)");
+  TORCH_CHECK_VALUE(lse_partial.dim() == 4 && lse_partial.is_contiguous() && lse_partial.scalar_type() == torch::kFloat32,
+                    "fable_attn: lse_partial must be contiguous fp32 (nsplit, B, H, S)");
+  const c10::cuda::CUDAGuard guard(out_partial.device());
+  const int ns = out_partial.size(0), B = out_partial.size(1), S = out_partial.size(2), H = out_partial.size(3),
+            D = out_partial.size(4);
+  auto out = torch::empty({B, S, H, D}, out_partial.options().dtype(out_dtype));
+  auto lse = return_lse ? torch::empty({B, H, S}, lse_partial.options()) : torch::empty({0}, lse_partial.options());
+  FaCombineParams p{};
+  p.struct_size = sizeof(FaCombineParams);
+  p.out_partial = out_partial.data_ptr(); p.in_dtype = dt_of(out_partial);
+  p.lse_partial = lse_partial.data_ptr<float>(); p.out = out.data_ptr(); p.out_dtype = dt_of(out);
+  p.lse_out = return_lse ? lse.data_ptr<float>() : nullptr;
+  p.nsplit = ns; p.B = B; p.S = S; p.H = H; p.D = D;
+  check(fa_combine_launch(&p, cur_stream(out_partial)), "combine");
+  return {out, lse};
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "fable_attn sm_100a attention kernels (binds the C ABI of include/fable_attn.h)";
+  m.def("fwd", &fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("scale"), py::arg("causal"),
+        py::arg("win_left"), py::arg("win_right"), py::arg("softcap"), py::arg("alibi"), py::arg("dropout_p"),
+        py::arg("seed"), py::arg("attn_chunk") = 0, py::arg("out") = c10::optional<torch::Tensor>());
+  m.def("bwd", &bwd, py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"), py::arg("out"), py::arg("lse"),
+        py::arg("scale"), py::arg("causal"), py::arg("win_left"), py::arg("win_right"), py::arg("softcap"),
+        py::arg("alibi"), py::arg("dropout_p"), py::arg("seed"));
+  m.def("fwd_varlen", &fwd_varlen, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("cu_q"), py::arg("cu_k"),
+        py::arg("max_sq"), py::arg("max_sk"), py::arg("scale"), py::arg("causal"), py::arg("win_left"),
+        py::arg("win_right"), py::arg("softcap"), py::arg("alibi"), py::arg("dropout_p"), py::arg("seed"),
+        py::arg("attn_chunk") = 0, py::arg("seqused_q") = c10::optional<torch::Tensor>(),
+        py::arg("seqused_k") = c10::optional<torch::Tensor>(), py::arg("return_lse") = false);
+  m.def("bwd_varlen", &bwd_varlen, py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"), py::arg("out"),
+        py::arg("lse"), py::arg("cu_q"), py::arg("cu_k"), py::arg("max_sq"), py::arg("max_sk"), py::arg("scale"),
+        py::arg("causal"), py::arg("win_left"), py::arg("win_right"), py::arg("softcap"), py::arg("alibi"),
+        py::arg("dropout_p"), py::arg("seed"), py::arg("seqused_q") = c10::optional<torch::Tensor>(),
+        py::arg("seqused_k") = c10::optional<torch::Tensor>());
+  m.def("dec", &dec, py::arg("q"), py::arg("k_cache"), py::arg("v_cache"), py::arg("block_table"),
+        py::arg("cache_seqlens"), py::arg("new_k"), py::arg("new_v"), py::arg("rotary_cos"), py::arg("rotary_sin"),
+        py::arg("rotary_interleaved"), py::arg("scale"), py::arg("window"), py::arg("num_splits"),
+        py::arg("cache_leftpad") = c10::optional<torch::Tensor>(), py::arg("return_lse") = false,
+        py::arg("softcap") = 0.0, py::arg("alibi") = c10::optional<torch::Tensor>(), py::arg("rotary_dim") = 0,
+        py::arg("rotary_pos") = c10::optional<torch::Tensor>());
+  m.def("combine", &combine, py::arg("out_partial"), py::arg("lse_partial"), py::arg("out_dtype"),
+        py::arg("return_lse") = false);
+  m.def("kernel_launch_count", []() { return fa_kernel_launch_count(); });
+  m.def("abi_version", []() { return fa_abi_version(); });
+}

@@ -1,0 +1,131 @@
+// fa_common.cuh — shared device helpers of the sm_100a attention engine: element conversions,
+// the Philox4x32-10 dropout generator, per-sequence geometry (dense / varlen) and the
+// host-side launch bookkeeping used by every kernel file.
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+#include <math.h>
+#include "fable_attn.h"
+
+#define FA_LOG2E 1.4426950408889634f
+#define FA_LN2 0.6931471805599453f
+
+// ---------------------------------------------------------------- element conversions
+template <typename T> struct Elem;
+template <> struct Elem<float> {
+  static __device__ __forceinline__ float to_f(float x) { return x; }
+  static __device__ __forceinline__ float from_f(float x) { return x; }
+};
+template <> struct Elem<__half> {
+  static __device__ __forceinline__ float to_f(__half x) { return __half2float(x); }
+  static __device__ __forceinline__ __half from_f(float x) { return __float2half_rn(x); }
+};
+template <> struct Elem<__nv_bfloat16> {
+  static __device__ __forceinline__ float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+  static __device__ __forceinline__ __nv_bfloat16 from_f(float x) { return __float2bfloat16_rn(x); }
+};
+
+// ---------------------------------------------------------------- Philox4x32-10 dropout
+// Counter-based generator keyed by the 64-bit seed, counter = (idx lo, idx hi, 0, 0); round
+// multipliers 0xD2511F53 / 0xCD9E8D57, key increments 0x9E3779B9 / 0xBB67AE85 (the published
+// Philox4x32 constants, Salmon et al. 2011).  Only the first output word decides the keep bit,
+// exactly as kernels/fa_common.hpp:71-88 of the reference:  u = (r0 >> 8) / 2^24,
+// keep iff u >= p.
+__host__ __device__ __forceinline__ uint32_t fa_philox_r0(uint64_t seed, uint64_t idx) {
+  uint32_t k0 = (uint32_t)seed, k1 = (uint32_t)(seed >> 32);
+  uint32_t c0 = (uint32_t)idx, c1 = (uint32_t)(idx >> 32), c2 = 0u, c3 = 0u;
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+#ifdef __CUDA_ARCH__
+    const uint32_t hi0 = __umulhi(0xD2511F53u, c0), hi1 = __umulhi(0xCD9E8D57u, c2);
+#else
+    const uint32_t hi0 = (uint32_t)(((uint64_t)0xD2511F53u * c0) >> 32);
+    const uint32_t hi1 = (uint32_t)(((uint64_t)0xCD9E8D57u * c2) >> 32);
+#endif
+    const uint32_t lo0 = 0xD2511F53u * c0, lo1 = 0xCD9E8D57u * c2;
+    const uint32_t n0 = hi1 ^ c1 ^ k0, n2 = hi0 ^ c3 ^ k1;
+    c0 = n0; c1 = lo1; c2 = n2; c3 = lo0;
+    k0 += 0x9E3779B9u; k1 += 0xBB67AE85u;
+  }
+  return c0;
+}
+// multiplier applied to a kept probability: inv_keep if kept, 0 if dropped
+__host__ __device__ __forceinline__ float fa_dropout_mul(uint64_t seed, uint64_t idx, float p,
+                                                         float inv_keep) {
+  const float u = (float)(fa_philox_r0(seed, idx) >> 8) * (1.0f / 16777216.0f);
+  return (u >= p) ? inv_keep : 0.0f;
+}
+
+// ---------------------------------------------------------------- sequence geometry
+// Resolves, for batch index / sequence z, the lengths and the element offsets of row 0 of the
+// q / k / o tensors.  Dense: offsets from the batch stride.  Varlen: token offsets from
+// cu_seqlens (the batch stride is ignored) and lengths clipped by seqused.
+struct SeqGeom {
+  int SQ, SK;
+  long long q0, k0, v0, o0;   // element offsets of row 0 (head 0)
+  long long tok_q;            // first token index of this sequence in the packed q (varlen), else 0
+};
+
+__device__ __forceinline__ SeqGeom fa_seq_geom(int z, int SQd, int SKd, const int* cu_q, const int* cu_k,
+                                               const int* su_q, const int* su_k, const FaStrides& sq,
+                                               const FaStrides& sk, const FaStrides& sv,
+                                               const FaStrides& so) {
+  SeqGeom g;
+  if (cu_q) {
+    const int qs = cu_q[z], ks = cu_k[z];
+    g.SQ = cu_q[z + 1] - qs;
+    g.SK = cu_k[z + 1] - ks;
+    if (su_q) { const int u = su_q[z]; if (u < g.SQ) g.SQ = u; }
+    if (su_k) { const int u = su_k[z]; if (u < g.SK) g.SK = u; }
+    if (g.SQ < 0) g.SQ = 0;
+    if (g.SK < 0) g.SK = 0;
+    g.q0 = (long long)qs * sq.s; g.k0 = (long long)ks * sk.s; g.v0 = (long long)ks * sv.s;
+    g.o0 = (long long)qs * so.s; g.tok_q = qs;
+  } else {
+    g.SQ = SQd; g.SK = SKd;
+    g.q0 = (long long)z * sq.b; g.k0 = (long long)z * sk.b; g.v0 = (long long)z * sv.b;
+    g.o0 = (long long)z * so.b; g.tok_q = 0;
+  }
+  return g;
+}
+
+// LSE / dsum row address: dense [batch, NH, SQ]; varlen [NH, total_q]
+__device__ __forceinline__ long long fa_lse_index(bool varlen, int z, int h, int NH, int SQd,
+                                                  long long tok_q, long long total_q, int q) {
+  return varlen ? (long long)h * total_q + tok_q + q : ((long long)z * NH + h) * SQd + q;
+}
+
+// Key range [lo, hi] that query row q may see (bottom-right aligned masks).  Returns lo > hi
+// when the row sees nothing.  Chunk handling follows kernels/fa_forward.hip:227-234.
+__host__ __device__ __forceinline__ void fa_key_range(int q, int SQ, int SK, int causal, int wl,
+                                                      int wr, int chunk, int& lo, int& hi) {
+  const int diag = q + SK - SQ;
+  lo = 0; hi = SK - 1;
+  if (causal && diag < hi) hi = diag;
+  if (wl >= 0 && diag - wl > lo) lo = diag - wl;
+  if (wr >= 0 && diag + wr < hi) hi = diag + wr;
+  if (chunk > 0) {
+    int pp = diag < 0 ? 0 : diag;
+    const int cs = (pp / chunk) * chunk;
+    if (cs > lo) lo = cs;
+    if (cs + chunk - 1 < hi) hi = cs + chunk - 1;
+  }
+}
+
+// ---------------------------------------------------------------- host bookkeeping
+namespace fa {
+void set_error(const char* fmt, ...);
+int cuda_status(cudaError_t e, const char* what);
+void count_launch(unsigned n = 1);
+int num_sms();
+}  // namespace fa
+
+#define FA_CHECK_ARG(cond, ...)             \
+  do {                                      \
+    if (!(cond)) {                          \
+      fa::set_error(__VA_ARGS__);           \
+      return FA_ERR_INVALID;                \
+    }                                       \
+  } while (0)

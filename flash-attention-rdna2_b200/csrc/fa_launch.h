@@ -1,0 +1,17 @@
+// fa_launch.h — host-side declarations shared by the kernel files and the C-ABI layer (api.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include "fable_attn.h"
+
+namespace fa {
+// kernel families (each returns FA_OK or an FA_ERR_* code; never aborts)
+int fwd_simt(const FaFwdParams& p, int dtype, cudaStream_t st);
+int fwd_sm100(const FaFwdParams& p, int dtype, cudaStream_t st, bool* taken);
+int bwd_simt(const FaBwdParams& p, int dtype, cudaStream_t st);
+int dec_run(const FaDecParams& p, int dtype, cudaStream_t st, const void* new_k, const void* new_v);
+int combine_run(const FaCombineParams& p, cudaStream_t st);
+
+int current_device();
+// Raise the dynamic shared-memory limit of `func` to `bytes` once per device.
+int ensure_smem(const void* func, int bytes, unsigned long long* done_mask);
+}  // namespace fa

@@ -1,0 +1,202 @@
+// fwd_simt.cu — exact attention forward on the CUDA cores, fp32 arithmetic.
+//
+// Serves the fp32 dtype (the reference's fp32 path, kernels/fa_forward.hip:317-400) and every
+// fp16/bf16 configuration the tensor-core kernel (fwd_sm100.cu) does not take.  One CTA owns
+// a 32-row query tile of one head of one sequence and streams 32-key tiles of K/V through
+// shared memory with an online softmax (log2 domain).  Every mask, softcap, alibi, Philox
+// dropout, varlen/seqused and LSE output follows the FaFwdParams contract in fable_attn.h.
+#include "fa_common.cuh"
+#include "fa_launch.h"
+
+namespace {
+
+constexpr int BR = 32, BC = 32;
+
+template <typename T, int HD>
+__global__ void __launch_bounds__(256) fwd_simt_kernel(const FaFwdParams p) {
+  constexpr int DPT = HD / 16, LDQ = HD + 1;
+  extern __shared__ float smem[];
+  float* Qs = smem;                 // [BR][HD+1]
+  float* Ks = Qs + BR * LDQ;        // [BC][HD+1]
+  float* Vs = Ks + BC * LDQ;        // [BC][HD]
+  float* Ps = Vs + BC * HD;         // [BR][BC+1]
+
+  const int t = threadIdx.x, tx = t & 15, ty = t >> 4;
+  const int z = blockIdx.z, h = blockIdx.y, kvh = h / p.gqa;
+  const bool varlen = p.cu_q != nullptr;
+  const SeqGeom g = fa_seq_geom(z, p.SQ, p.SK, p.cu_q, p.cu_k, p.seqused_q, p.seqused_k, p.sQ, p.sK,
+                                p.sV, p.sO);
+  const int qb = blockIdx.x * BR;
+  if (qb >= g.SQ) return;
+  const int SQ = g.SQ, SK = g.SK;
+
+  const T* Qg = (const T*)p.Q + g.q0 + (long long)h * p.sQ.h;
+  const T* Kg = (const T*)p.K + g.k0 + (long long)kvh * p.sK.h;
+  const T* Vg = (const T*)p.V + g.v0 + (long long)kvh * p.sV.h;
+
+  for (int e = t; e < BR * HD; e += 256) {
+    const int r = e / HD, d = e % HD, q = qb + r;
+    Qs[r * LDQ + d] = (q < SQ) ? Elem<T>::to_f(Qg[(long long)q * p.sQ.s + d]) : 0.f;
+  }
+
+  // per-row key windows; the tile loop covers their union
+  int rlo[2], rhi[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+    fa_key_range(qb + ty * 2 + i, SQ, SK, p.causal, p.win_left, p.win_right, p.attn_chunk, rlo[i],
+                 rhi[i]);
+  int klo, khi, dummy;
+  fa_key_range(qb, SQ, SK, p.causal, p.win_left, p.win_right, p.attn_chunk, klo, dummy);
+  fa_key_range(min(qb + BR, SQ) - 1, SQ, SK, p.causal, p.win_left, p.win_right, p.attn_chunk, dummy,
+               khi);
+  if (klo < 0) klo = 0;
+  if (khi > SK - 1) khi = SK - 1;
+
+  const float slope = p.alibi_slopes ? p.alibi_slopes[h] : 0.f;
+  const float scale2 = p.scale * FA_LOG2E;
+  const bool drop = p.dropout_p > 0.f;
+  const float inv_keep = drop ? 1.0f / (1.0f - p.dropout_p) : 1.f;
+
+  float acc[2][DPT], m[2], l[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    m[i] = -INFINITY; l[i] = 0.f;
+#pragma unroll
+    for (int e = 0; e < DPT; ++e) acc[i][e] = 0.f;
+  }
+
+  for (int kb = (klo / BC) * BC; kb <= khi; kb += BC) {
+    __syncthreads();
+    for (int e = t; e < BC * HD; e += 256) {
+      const int r = e / HD, d = e % HD, k = kb + r;
+      const bool ok = k < SK;
+      Ks[r * LDQ + d] = ok ? Elem<T>::to_f(Kg[(long long)k * p.sK.s + d]) : 0.f;
+      Vs[r * HD + d] = ok ? Elem<T>::to_f(Vg[(long long)k * p.sV.s + d]) : 0.f;
+    }
+    __syncthreads();
+
+    float s[2][2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) s[i][j] = 0.f;
+#pragma unroll 4
+    for (int d = 0; d < HD; ++d) {
+      const float q0 = Qs[(ty * 2) * LDQ + d], q1 = Qs[(ty * 2 + 1) * LDQ + d];
+      const float k0 = Ks[tx * LDQ + d], k1 = Ks[(tx + 16) * LDQ + d];
+      s[0][0] = fmaf(q0, k0, s[0][0]); s[0][1] = fmaf(q0, k1, s[0][1]);
+      s[1][0] = fmaf(q1, k0, s[1][0]); s[1][1] = fmaf(q1, k1, s[1][1]);
+    }
+
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int q = qb + ty * 2 + i;
+      float sv[2], tmax = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int key = kb + tx + 16 * j;
+        float v;
+        if (p.softcap > 0.f) v = p.softcap * tanhf(s[i][j] * p.scale / p.softcap) * FA_LOG2E;
+        else v = s[i][j] * scale2;
+        if (p.alibi_slopes) v += slope * (float)(key - q) * FA_LOG2E;
+        if (q >= SQ || key < rlo[i] || key > rhi[i]) v = -INFINITY;
+        sv[j] = v;
+        tmax = fmaxf(tmax, v);
+      }
+#pragma unroll
+      for (int o = 8; o >= 1; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
+      const float mnew = fmaxf(m[i], tmax);
+      // a row that has seen no visible key yet keeps m = -inf and contributes nothing
+      const float muse = (mnew == -INFINITY) ? 0.f : mnew;
+      float pj[2], ls = 0.f;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) { pj[j] = exp2f(sv[j] - muse); ls += pj[j]; }
+#pragma unroll
+      for (int o = 8; o >= 1; o >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
+      if (mnew != -INFINITY) {
+        const float corr = exp2f(m[i] - mnew);
+        l[i] = l[i] * corr + ls;
+#pragma unroll
+        for (int e = 0; e < DPT; ++e) acc[i][e] *= corr;
+        m[i] = mnew;
+        if (drop) {
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int key = kb + tx + 16 * j;
+            const unsigned long long idx = ((unsigned long long)h * SQ + q) * SK + key;
+            pj[j] *= fa_dropout_mul(p.philox_seed, idx, p.dropout_p, inv_keep);
+          }
+        }
+      }
+      Ps[(ty * 2 + i) * (BC + 1) + tx] = pj[0];
+      Ps[(ty * 2 + i) * (BC + 1) + tx + 16] = pj[1];
+    }
+    __syncthreads();
+#pragma unroll 4
+    for (int c = 0; c < BC; ++c) {
+      const float p0 = Ps[(ty * 2) * (BC + 1) + c], p1 = Ps[(ty * 2 + 1) * (BC + 1) + c];
+#pragma unroll
+      for (int e = 0; e < DPT; ++e) {
+        const float v = Vs[c * HD + tx + 16 * e];
+        acc[0][e] = fmaf(p0, v, acc[0][e]);
+        acc[1][e] = fmaf(p1, v, acc[1][e]);
+      }
+    }
+  }
+
+  T* Og = (T*)p.O + g.o0 + (long long)h * p.sO.h;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int q = qb + ty * 2 + i;
+    if (q >= SQ) continue;
+    const float inv = l[i] > 0.f ? 1.f / l[i] : 0.f;
+#pragma unroll
+    for (int e = 0; e < DPT; ++e) Og[(long long)q * p.sO.s + tx + 16 * e] = Elem<T>::from_f(acc[i][e] * inv);
+    if (p.LSE && tx == 0) {
+      const long long li = fa_lse_index(varlen, z, h, p.NH, p.SQ, g.tok_q, p.lse_total_q, q);
+      p.LSE[li] = l[i] > 0.f ? m[i] * FA_LN2 + logf(l[i]) : -INFINITY;
+    }
+  }
+}
+
+template <typename T, int HD>
+int launch_hd(const FaFwdParams& p, cudaStream_t st) {
+  const size_t smem = sizeof(float) * (size_t)(BR * (HD + 1) + BC * (HD + 1) + BC * HD + BR * (BC + 1));
+  static unsigned long long done = 0;
+  if (int rc = fa::ensure_smem((const void*)fwd_simt_kernel<T, HD>, (int)smem, &done)) return rc;
+  dim3 grid((p.SQ + BR - 1) / BR, p.NH, p.batch);
+  fwd_simt_kernel<T, HD><<<grid, 256, smem, st>>>(p);
+  fa::count_launch();
+  return fa::cuda_status(cudaGetLastError(), "fwd_simt launch");
+}
+
+template <typename T>
+int launch_t(const FaFwdParams& p, cudaStream_t st) {
+  switch (p.HD) {
+    case 16: return launch_hd<T, 16>(p, st);
+    case 32: return launch_hd<T, 32>(p, st);
+    case 48: return launch_hd<T, 48>(p, st);
+    case 64: return launch_hd<T, 64>(p, st);
+    case 80: return launch_hd<T, 80>(p, st);
+    case 96: return launch_hd<T, 96>(p, st);
+    case 112: return launch_hd<T, 112>(p, st);
+    case 128: return launch_hd<T, 128>(p, st);
+    case 160: return launch_hd<T, 160>(p, st);
+    case 192: return launch_hd<T, 192>(p, st);
+    case 224: return launch_hd<T, 224>(p, st);
+    case 256: return launch_hd<T, 256>(p, st);
+  }
+  fa::set_error("forward: head_dim=%d not instantiated (valid: multiples of 16 up to 256 "
+                "from the list 16,32,48,64,80,96,112,128,160,192,224,256)", p.HD);
+  return FA_ERR_UNSUPPORTED;
+}
+
+}  // namespace
+
+namespace fa {
+int fwd_simt(const FaFwdParams& p, int dtype, cudaStream_t st) {
+  if (dtype == FA_DTYPE_F16) return launch_t<__half>(p, st);
+  if (dtype == FA_DTYPE_BF16) return launch_t<__nv_bfloat16>(p, st);
+  return launch_t<float>(p, st);
+}
+}  // namespace fa

@@ -1,0 +1,207 @@
+/*
+ * fable_attn.h — C ABI of the B200 (sm_100a) exact-attention engine.
+ *
+ * This is the boundary the Python layer (fable_attn._C) binds, and the one any other host
+ * (ctypes, cgo, JNI, N-API) can bind directly: plain C structs of device pointers, element
+ * strides and scalars, no torch types.  Every entry point enqueues work on the caller's CUDA
+ * stream and returns without synchronising; the return value is FA_OK (0) or an FA_ERR_* code,
+ * with a human-readable message available from fa_last_error().  Nothing here aborts the
+ * process.
+ *
+ * Each parameter block starts with `struct_size`, which the caller sets to sizeof(the struct)
+ * it was compiled against; a mismatch is rejected with FA_ERR_ABI instead of reading a
+ * differently laid-out block.
+ *
+ * Counterparts in the reference (MatafakaRespect/flash-attention-rdna2):
+ *   fa_forward_launch           <- package/csrc/fa_iface.h:65   (FwdParams, fa_iface.h:10-24)
+ *   fable_attn_backward_launch  <- package/csrc/fa_iface.h:66   (BwdParams, fa_iface.h:28-38)
+ *   fa_decode_launch            <- package/csrc/fa_iface.h:67-68 (DecParams, fa_iface.h:42-63)
+ *   fa_decode_num_splits        <- package/csrc/dispatch.cpp:182-200 (nsplit heuristic)
+ *   fa_combine_launch           <- package/fable_attn/flash_attn_interface.py:567-580
+ *                                  (flash_attn_combine, torch arithmetic in the reference)
+ * The reference passes its structs by value and returns void (aborting on bad input); here they
+ * are passed by pointer and the functions return a status code.
+ */
+#ifndef FABLE_ATTN_H
+#define FABLE_ATTN_H
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FA_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define FA_API __attribute__((visibility("default")))
+#else
+#define FA_API
+#endif
+
+/* dtype codes — same numbering as the reference (kernels/fa_forward.hip:403) */
+enum { FA_DTYPE_F16 = 0, FA_DTYPE_BF16 = 1, FA_DTYPE_F32 = 2 };
+
+/* status codes */
+enum {
+  FA_OK = 0,
+  FA_ERR_ABI = 1,          /* struct_size mismatch */
+  FA_ERR_INVALID = 2,      /* null pointer, bad shape, bad stride */
+  FA_ERR_UNSUPPORTED = 3,  /* valid request the engine does not implement (e.g. head_dim) */
+  FA_ERR_CUDA = 4,         /* a CUDA runtime/driver call failed */
+  FA_ERR_SIZE = 5          /* request exceeds a stated size limit */
+};
+
+/* Element strides of a [batch, head, seq, dim] view; the dim stride must be 1. */
+typedef struct FaStrides { long long b, h, s; } FaStrides;
+
+/* ------------------------------------------------------------------------------------------
+ * Forward (dense and varlen).  Replaces FwdParams / fa_forward_launch.
+ *   dense : Q [batch, NH, SQ, HD], K/V [batch, NKV, SK, HD] through the strides (any order of
+ *           b/h/s, dim contiguous).  LSE (optional) is written as [batch, NH, SQ] fp32,
+ *           natural log.  The reference launches once per batch element
+ *           (package/csrc/dispatch.cpp:62-78); here batch is a grid dimension.
+ *   varlen: cu_q/cu_k non-null, `batch` = number of sequences, SQ/SK = max_seqlen_q/k (used
+ *           only to size the grid), strides.b ignored (token offsets come from cu_*),
+ *           seqused_q/k optionally clip each sequence.  LSE (optional) is [NH, lse_total_q].
+ * Semantics follow kernels/fa_forward.hip:52-313: s = scale*q.k, softcap c>0 -> c*tanh(s/c),
+ * alibi adds slope[h]*(key - q) (signed, no diagonal offset), masks are bottom-right aligned
+ * (delta = SK - SQ): causal key > q+delta; window key < q+delta-win_left or
+ * key > q+delta+win_right (negative = unbounded); attn_chunk c>0 keeps keys in
+ * [floor(max(q+delta,0)/c)*c, +c).  Fully masked rows give O = 0 and LSE = -inf.
+ * Dropout: Philox4x32-10 keyed by philox_seed, counter = (h*SQ + q)*SK + key with h the global
+ * query head and no batch term (kernels/fa_forward.hip:258); keep iff (r0>>8)/2^24 >= p, kept
+ * values scaled by 1/(1-p); the row sum is taken before dropout.
+ * -------------------------------------------------------------------------------------------*/
+typedef struct FaFwdParams {
+  unsigned int struct_size;
+  const void* Q; const void* K; const void* V;
+  void* O;
+  float* LSE;                          /* optional */
+  FaStrides sQ, sK, sV, sO;
+  int batch;
+  int SQ, SK, HD, NH, gqa;             /* gqa = NH / (number of kv heads) */
+  float scale, softcap;                /* softcap <= 0 disables */
+  int causal, win_left, win_right;     /* window bounds < 0 = unbounded */
+  int attn_chunk;                      /* 0 disables */
+  const float* alibi_slopes;           /* [NH] or null */
+  float dropout_p;
+  unsigned long long philox_seed;
+  const int* cu_q; const int* cu_k;    /* varlen: [batch+1] int32, or null */
+  const int* seqused_q; const int* seqused_k;   /* varlen: [batch] int32, or null */
+  long long lse_total_q;               /* varlen LSE row length (total tokens of q) */
+} FaFwdParams;
+
+FA_API int fa_forward_launch(const FaFwdParams* p, int dtype, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Backward.  Replaces BwdParams / fable_attn_backward_launch.  Computes dQ, dK, dV with no
+ * atomics (bit-reproducible): a preprocessing kernel writes dsum = rowsum(O*dO), a dK/dV kernel
+ * per key tile sums over every query tile and every query head of the kv group, and a dQ kernel
+ * per query tile sums over key tiles (kernels/backward.hip:86-387).  dsum is caller-provided
+ * workspace of [B, Hq, SQ] fp32 (varlen: [Hq, lse_total_q]).  Dense or varlen (cu_q/cu_k),
+ * same geometry rules as the forward.  The mask is the forward's without attn_chunk
+ * (kernels/backward.hip:76-83); dropout recomputes the forward's Philox mask bit-identically.
+ * -------------------------------------------------------------------------------------------*/
+typedef struct FaBwdParams {
+  unsigned int struct_size;
+  const void *Q, *K, *V, *O, *dO;
+  void *dQ, *dK, *dV;
+  const float* lse;                    /* forward LSE, same layout as FaFwdParams.LSE */
+  float* dsum;                         /* workspace, same layout as lse */
+  FaStrides qs, ks, vs, os, dos, dqs, dks, dvs;
+  int B, Hq, Hk, SQ, SK, D, gqa;
+  float scale, softcap;
+  const float* alibi;
+  int causal, win_left, win_right;
+  int dropout;
+  unsigned long long drop_seed;
+  float dropout_p, keep_scale;
+  const int* cu_q; const int* cu_k;
+  const int* seqused_q; const int* seqused_k;
+  long long lse_total_q;
+} FaBwdParams;
+
+FA_API int fable_attn_backward_launch(const FaBwdParams* p, int dtype, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Paged-KV decode (one or several new tokens per sequence).  Replaces DecParams /
+ * fa_decode_launch (kernels/fa_decode.hip:343-362).
+ *   q         [batch, nq, NH, HD] contiguous (nq new tokens per sequence)
+ *   Kc, Vc    paged cache [num_blocks, page, NH/gqa, HD] contiguous; page a power of two
+ *   block_table [batch, max_blocks] int32 (row stride max_blocks)
+ *   ctx_len   [batch] int32: cache length BEFORE this call's append (flash-attn cache_seqlens)
+ *   o         [batch, nq, NH, HD]
+ *   scratch   fp32 workspace of fa_decode_scratch_floats(...) floats (split-K partials)
+ *   lse_out   optional [batch, nq, NH] fp32, natural log
+ * New token tk sits at position ctx_len+tk; it sees keys [lo, ctx_len) plus, when new_k/new_v
+ * are given (appended at ctx_len.. before attention, rotary applied to k), the new keys up to
+ * and including its own.  lo = max(leftpad, pos - window + 1) (window < 0 = unbounded).
+ * Rotary (1 = NeoX halves, 2 = interleaved pairs) rotates q (and appended k) by the table row
+ * cos/sin[rotary_pos ? rotary_pos[b]+tk : ctx_len[b]+tk], rotary_dim dims (0 = all).
+ * softcap/alibi as in the forward with query position ctx_len+tk.  Any gqa is supported
+ * (the reference's kernel covers only gqa in {1,2,4,8}, kernels/fa_decode.hip:326-331).
+ * nsplit: number of KV splits per sequence (fa_decode_num_splits gives the default).
+ * -------------------------------------------------------------------------------------------*/
+typedef struct FaDecParams {
+  unsigned int struct_size;
+  const void* q;
+  void* Kc; void* Vc;
+  const int* block_table;
+  void* o;
+  float* scratch;
+  const int* ctx_len;
+  const float* cos; const float* sin;
+  int batch, NH, gqa, HD, page, max_blocks, nsplit, window;
+  int rotary;                          /* 0 none, 1 neox, 2 interleaved */
+  float scale;
+  const int* leftpad;                  /* [batch] or null */
+  float* lse_out;                      /* [batch, nq, NH] or null */
+  float softcap;
+  const float* alibi;                  /* [NH] or null */
+  int nq;
+  int append;                          /* set by fa_decode_launch: new_k/new_v given */
+  int rotary_dim;                      /* 0 = HD */
+  const int* rotary_pos;               /* [batch] or null */
+  long long num_blocks;                /* pages in the cache (block_table entries are checked
+                                          against it on the device; out-of-range pages read as
+                                          empty and set the error flag) */
+  int* err_flag;                       /* optional device int set non-zero on a bad page index */
+} FaDecParams;
+
+FA_API int fa_decode_launch(const FaDecParams* p, int dtype, void* stream,
+                     const void* new_k, const void* new_v);
+
+/* Default split count: enough CTAs to fill the GPU, each split at least 256 positions, at most
+ * 512 splits; num_splits > 0 is taken as given (clamped to [1, 512]). */
+FA_API int fa_decode_num_splits(int batch, int nq, int nheads_kv, long long ctx_bound, int num_splits);
+
+/* Floats of scratch fa_decode_launch needs for these sizes. */
+FA_API long long fa_decode_scratch_floats(int batch, int nq, int NH, int HD, int nsplit);
+
+/* ------------------------------------------------------------------------------------------
+ * LSE-merge of split-KV partial results (flash_attn_combine).
+ *   out_partial [nsplit, B, S, H, D] (dtype in_dtype), lse_partial [nsplit, B, H, S] fp32,
+ *   out [B, S, H, D] (dtype out_dtype), lse_out optional [B, H, S] fp32; all contiguous.
+ *   out = sum_s w_s*out_s / sum_s w_s with w_s = exp(lse_s - max_s lse_s); a row whose
+ *   partials are all -inf gives 0.
+ * -------------------------------------------------------------------------------------------*/
+typedef struct FaCombineParams {
+  unsigned int struct_size;
+  const void* out_partial; int in_dtype;
+  const float* lse_partial;
+  void* out; int out_dtype;
+  float* lse_out;
+  int nsplit, B, S, H, D;
+} FaCombineParams;
+
+FA_API int fa_combine_launch(const FaCombineParams* p, void* stream);
+
+/* ---- introspection ---- */
+FA_API int fa_abi_version(void);
+FA_API const char* fa_last_error(void);       /* message of the last failing call on this thread */
+/* Number of this library's kernels launched since load (all threads, all devices). */
+FA_API unsigned long long fa_kernel_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FABLE_ATTN_H */
