@@ -1,0 +1,400 @@
+"""Benchmark of the exact-attention hot path (one JSON line on rank 0).
+
+Headline: dense non-causal forward, batch 1, seqlen 16384, 32 heads,
+head_dim 128, bf16, scale 1/sqrt(128) -> TFLOP/s (4*B*H*S^2*D per step).  One step = one forward
+over the resident inputs (384 MiB of q/k/v, larger than the 126 MB L2, so no flush is needed).
+With N GPUs the 32 heads are split across ranks (no communication; total work fixed -> strong
+scaling) and `value` = total FLOPs / max-over-ranks time.
+
+Also reported in the same line:
+  e2e          the same metric through the public API (fable_attn.flash_attn_func) with pinned
+               host buffers: per step H2D of q/k/v, the call, D2H of the output
+  roofline     dominant kernel: algorithmic FLOPs / CUDA-event kernel time vs the measured bf16
+               peak (MEASURED_PEAKS.json), plus DRAM traffic from the committed ncu summary
+  cpu_baseline the reference's own fp64 CPU oracle (oracle/_ref, kernels/fa_common.hpp:102-134)
+               on a bounded sample of the same workload, all host threads
+  extra        config 3 (causal fwd+bwd fp16, dropout 0.1) and config 4 (paged decode) figures
+  clocks       nvidia-smi samples taken during the timed region
+
+`--impl reference` times only the reference's CPU implementation on the host cores (rank 0).
+"""
+import argparse
+import ctypes as C
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "flash-attention-rdna2_b200"))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "fwd/bwd TFLOP/s vs 2.25 PF tensor peak; paged-decode GB/s vs 8 TB/s HBM"
+CFG2 = dict(B=1, S=16384, H=32, D=128)
+
+
+def _dist():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def _peaks():
+    try:
+        return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        return None
+
+
+def _traffic(key):
+    """DRAM bytes per launch recorded from an ncu capture (profiles/ncu_traffic.txt: key bytes)."""
+    try:
+        for ln in open(os.path.join(ROOT, "profiles", "ncu_traffic.txt")):
+            parts = ln.split()
+            if len(parts) >= 2 and parts[0] == key:
+                return float(parts[1])
+    except Exception:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index, self.proc, self.lines = index, None, []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.lines.append(ln.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- CPU baseline
+def cpu_reference_sample(seconds=10.0, threads=None):
+    """Time the reference's fp64 CPU oracle (oracle/_ref; the restated oracle if absent) on rows of
+    the config-2 workload (one head, all 16384 keys; non-causal, so rows are independent), across
+    the host threads.  Returns (TFLOP/s, threads, kind, sample description)."""
+    from concurrent.futures import ThreadPoolExecutor
+    from oracle import oracle as O
+    S, D = CFG2["S"], CFG2["D"]
+    rng = np.random.default_rng(0)
+    k = rng.standard_normal((S, 1, D)).astype(np.float32)
+    v = rng.standard_normal((S, 1, D)).astype(np.float32)
+    kt = np.ascontiguousarray(k.transpose(1, 0, 2))
+    vt = np.ascontiguousarray(v.transpose(1, 0, 2))
+    R = O.ref_lib()
+    kind = "reference" if R is not None else "port"
+    threads = threads or os.cpu_count() or 1
+
+    def run_rows(nrows):
+        q = rng.standard_normal((nrows, 1, D)).astype(np.float32)
+        if R is not None:
+            o = np.zeros_like(q)
+            lse = np.zeros((1, nrows), np.float32)
+            # a row block of a non-causal problem is itself a valid (nrows x S) problem
+            R.ref_attention_c(q, kt, vt, o, lse, nrows, S, D, 1, 1, D ** -0.5, 0.0, -1, -1, 0, 0, None, 0)
+        else:
+            O.forward(q[None], k[None], v[None], D ** -0.5)
+
+    t0 = time.perf_counter()
+    run_rows(1)
+    per_row = max(time.perf_counter() - t0, 1e-4)
+    rows_per_thread = max(1, int(seconds / per_row))
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(threads) as ex:
+        list(ex.map(run_rows, [rows_per_thread] * threads))
+    wall = time.perf_counter() - t0
+    rows = rows_per_thread * threads
+    flops = 4.0 * rows * S * D
+    desc = (f"{rows} query rows x {S} keys x D={D} of config 2 (1 head, non-causal), "
+            f"{threads} threads, {wall:.1f} s wall")
+    return flops / wall / 1e12, threads, kind, desc
+
+
+# ----------------------------------------------------------------------------- GPU arms
+def _events():
+    return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+
+def bench_fwd_dense(args, ws, rank, dev):
+    import fable_attn as fa
+    from fable_attn import _C
+    B, S, H, D = CFG2["B"], CFG2["S"], CFG2["H"], CFG2["D"]
+    assert H % ws == 0, "heads must divide across ranks"
+    h = H // ws
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    q = torch.randn(B, S, h, D, device=dev, dtype=torch.bfloat16, generator=g)
+    k = torch.randn(B, S, h, D, device=dev, dtype=torch.bfloat16, generator=g)
+    v = torch.randn(B, S, h, D, device=dev, dtype=torch.bfloat16, generator=g)
+    qh, kh, vh = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
+    out = torch.empty(B, S, h, D, device=dev, dtype=torch.bfloat16).transpose(1, 2)
+    scale = D ** -0.5
+
+    def step():
+        _C.fwd(qh, kh, vh, scale, False, -1, -1, 0.0, None, 0.0, 0, 0, out)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    _barrier(ws)
+    l0 = _C.kernel_launch_count()
+    evs = [_events() for _ in range(args.steps)]
+    with ClockSampler(dev.index if dev.index is not None else 0) as clk:
+        torch.cuda.synchronize()
+        t_start, t_end = _events()
+        t_start.record()
+        for e0, e1 in evs:
+            e0.record()
+            step()
+            e1.record()
+        t_end.record()
+        torch.cuda.synchronize()
+    launches = _C.kernel_launch_count() - l0
+    total_ms = t_start.elapsed_time(t_end)
+    kern_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    total_ms = _max_over_ranks(total_ms, ws, dev)
+    flops_total = 4.0 * B * H * S * S * D            # whole job (all ranks)
+    ms_per_step = total_ms / args.steps
+    value = flops_total / (ms_per_step * 1e-3) / 1e12
+    flops_launch = 4.0 * B * h * S * S * D
+    achieved = flops_launch / (kern_ms * 1e-3) / 1e12
+
+    # e2e through the public API with host buffers (pinned), H2D + call + D2H each step
+    hq = q.cpu().pin_memory()
+    hk = k.cpu().pin_memory()
+    hv = v.cpu().pin_memory()
+    hout = torch.empty(B, S, h, D, dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        dq = hq.to(dev, non_blocking=True)
+        dk = hk.to(dev, non_blocking=True)
+        dv = hv.to(dev, non_blocking=True)
+        o = fa.flash_attn_func(dq, dk, dv, softmax_scale=scale)
+        hout.copy_(o, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    _barrier(ws)
+    a, b = _events()
+    a.record()
+    n_e2e = max(3, args.steps // 2)
+    for _ in range(n_e2e):
+        e2e_step()
+    b.record()
+    torch.cuda.synchronize()
+    e2e_ms = _max_over_ranks(a.elapsed_time(b) / n_e2e, ws, dev)
+    e2e = {"value": round(flops_total / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+           "h2d_bytes_per_step": 3 * B * S * H * D * 2, "d2h_bytes_per_step": B * S * H * D * 2,
+           "ms_per_step": round(e2e_ms, 3)}
+    return dict(value=value, ms_per_step=ms_per_step, achieved=achieved, kern_ms=kern_ms, flops_launch=flops_launch,
+                launches=launches, clocks=clk.summary(), e2e=e2e)
+
+
+def bench_fwd_bwd_causal(dev, steps=5, warmup=3):
+    """Config 3: B2 S4096 H32 D128 fp16 causal, dropout 0.1, fixed seed: fwd and bwd times."""
+    from fable_attn import _C
+    B, S, H, D = 2, 4096, 32, 128
+    g = torch.Generator(device=dev).manual_seed(7)
+    q, k, v, do = (torch.randn(B, S, H, D, device=dev, dtype=torch.float16, generator=g) for _ in range(4))
+    qh, kh, vh, doh = (t.transpose(1, 2) for t in (q, k, v, do))
+    out = torch.empty(B, S, H, D, device=dev, dtype=torch.float16).transpose(1, 2)
+    sc = D ** -0.5
+    for _ in range(warmup):
+        _, lse = _C.fwd(qh, kh, vh, sc, True, -1, 0, 0.0, None, 0.1, 777, 0, out)
+        _C.bwd(doh, qh, kh, vh, out, lse, sc, True, -1, 0, 0.0, None, 0.1, 777)
+    torch.cuda.synchronize()
+    f0, f1 = _events()
+    b0, b1 = _events()
+    tf, tb = 0.0, 0.0
+    for _ in range(steps):
+        f0.record()
+        _, lse = _C.fwd(qh, kh, vh, sc, True, -1, 0, 0.0, None, 0.1, 777, 0, out)
+        f1.record()
+        b0.record()
+        _C.bwd(doh, qh, kh, vh, out, lse, sc, True, -1, 0, 0.0, None, 0.1, 777)
+        b1.record()
+        torch.cuda.synchronize()
+        tf += f0.elapsed_time(f1)
+        tb += b0.elapsed_time(b1)
+    fwd_flops = 4.0 * D * B * H * S * (S + 1) / 2
+    fms, bms = tf / steps, tb / steps
+    return {"config": "causal fwd+bwd B2 S4096 H32 D128 fp16 dropout0.1", "fwd_ms": round(fms, 3),
+            "fwd_tflops": round(fwd_flops / fms / 1e9, 1), "bwd_ms": round(bms, 3),
+            "bwd_tflops": round(2.5 * fwd_flops / bms / 1e9, 1)}
+
+
+def bench_decode(dev, steps=20, warmup=5):
+    """Config 4: B16 Hq32 Hk8 D128 bf16, page 256, cache_seqlens ~ U[16384, 32768], permuted pages."""
+    from fable_attn import _C
+    B, Hq, Hk, D, page, maxctx = 16, 32, 8, 128, 256, 32768
+    nper = maxctx // page
+    g = torch.Generator(device=dev).manual_seed(11)
+    rng = np.random.default_rng(11)
+    kc = torch.randn(B * nper, page, Hk, D, device=dev, dtype=torch.bfloat16, generator=g)
+    vc = torch.randn(B * nper, page, Hk, D, device=dev, dtype=torch.bfloat16, generator=g)
+    bt = torch.from_numpy(rng.permutation(B * nper).astype(np.int32).reshape(B, nper)).to(dev)
+    lens = rng.integers(16384, 32769, size=B).astype(np.int32)
+    cs = torch.from_numpy(lens).to(dev)
+    q = torch.randn(B, 1, Hq, D, device=dev, dtype=torch.bfloat16, generator=g)
+    sc = D ** -0.5
+
+    def call():
+        return _C.dec(q, kc, vc, bt, cs, None, None, None, None, False, sc, -1, 0, None, False, 0.0, None, 0, None)
+
+    for _ in range(warmup):
+        call()
+    torch.cuda.synchronize()
+    a, b = _events()
+    a.record()
+    for _ in range(steps):
+        call()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    nbytes = float(lens.sum()) * Hk * D * 2 * 2
+    return {"config": "paged decode B16 Hq32 Hk8 D128 bf16 page256 L~U[16K,32K]", "ms": round(ms, 4),
+            "GBps": round(nbytes / ms / 1e6, 1), "bytes": nbytes}
+
+
+def _barrier(ws):
+    if ws > 1:
+        torch.distributed.barrier()
+
+
+def _max_over_ranks(x, ws, dev):
+    if ws == 1:
+        return x
+    t = torch.tensor([x], device=dev, dtype=torch.float64)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-extra", action="store_true", help="skip the config 3/4 figures")
+    ap.add_argument("--cpu-seconds", type=float, default=8.0)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    ws, rank, local = _dist()
+    config = {"workload": "dense non-causal forward B1 S16384 H32 D128 bf16 (BASELINE configs[1])",
+              "global_batch": CFG2["B"], "seq_len": CFG2["S"], "heads": CFG2["H"], "head_dim": CFG2["D"],
+              "parallelism": f"heads/{ws} per GPU" if ws > 1 else "single GPU",
+              "l2": "inputs (384 MiB) larger than L2, no flush"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        vals = []
+        for _ in range(args.warmup + args.steps):
+            val, cores, kind, desc = cpu_reference_sample(seconds=max(1.0, args.cpu_seconds / 4))
+            vals.append(val)
+        v = statistics.mean(vals[args.warmup:])
+        line = {"metric": METRIC, "value": round(v, 6), "unit": "TFLOP/s", "n_gpus": ws, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True, "impl": "reference",
+                "dtype": "f64", "data": "synthetic N(0,1), seeded", "config": config, "vs_baseline": None,
+                "cpu_baseline": {"value": round(v, 6), "unit": "TFLOP/s", "cores": cores, "kind": kind,
+                                 "sample": desc},
+                "e2e": {"value": round(v, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    if ws > 1:
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120))
+    dev = torch.device("cuda", local if ws > 1 else 0)
+    torch.cuda.set_device(dev)
+
+    r = bench_fwd_dense(args, ws, rank, dev)
+    extra = {}
+    if not args.no_extra and rank == 0:
+        try:
+            extra["fwd_bwd_causal"] = bench_fwd_bwd_causal(dev)
+        except Exception as e:  # keep the headline even if a secondary figure fails
+            extra["fwd_bwd_causal"] = {"error": f"{type(e).__name__}: {e}"[:200]}
+        try:
+            extra["decode_paged"] = bench_decode(dev)
+        except Exception as e:
+            extra["decode_paged"] = {"error": f"{type(e).__name__}: {e}"[:200]}
+    cpu = None
+    if rank == 0 and ws == 1:
+        val, cores, kind, desc = cpu_reference_sample(seconds=args.cpu_seconds)
+        cpu = {"value": round(val, 6), "unit": "TFLOP/s", "cores": cores, "kind": kind, "sample": desc}
+    peaks = _peaks()
+    if peaks and peaks.get("bf16_tflops"):
+        peak, peak_src = float(peaks["bf16_tflops"]), "MEASURED_PEAKS.json bf16_tflops (burst), of measured"
+    else:
+        peak, peak_src = 1590.0, "fallback 1.59 PFLOP/s, of fallback"
+    traffic = _traffic("fwd_dense_bf16_s16384_h32_d128")
+    if ws > 1 and traffic is not None:
+        traffic = traffic / ws
+    roofline = {"bound": "tensor", "achieved": round(r["achieved"], 1), "peak": peak, "unit": "TFLOP/s",
+                "frac": round(r["achieved"] / peak, 4), "traffic": traffic, "peak_source": peak_src,
+                "kernel_ms": round(r["kern_ms"], 4), "flops_per_launch": r["flops_launch"]}
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(r["value"], 2), "unit": "TFLOP/s", "n_gpus": ws, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(r["ms_per_step"], 4), "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic N(0,1), seeded (no dataset in the reference's benchmark)", "config": config,
+                "e2e": r["e2e"], "roofline": roofline, "cpu_baseline": cpu, "gpu_launches": int(r["launches"]),
+                "clocks": r["clocks"], "extra": extra}
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

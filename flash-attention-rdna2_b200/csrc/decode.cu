@@ -62,7 +62,13 @@ __device__ __forceinline__ void rotate_row(float* v, int rdim, int mode, const f
 // Page lookup with a bounds check; an invalid page index marks the position invisible and
 // raises the caller's error flag (the cache is never read out of bounds).
 __device__ __forceinline__ long long page_of(const FaDecParams& p, int b, int pos, int shift, bool& ok) {
-  const int blk = p.block_table[(long long)b * p.max_blocks + (pos >> shift)];
+  const int slot = pos >> shift;
+  if (pos < 0 || slot >= p.max_blocks) {   // position past the block table's row
+    ok = false;
+    if (p.err_flag) atomicExch(p.err_flag, 1);
+    return 0;
+  }
+  const int blk = p.block_table[(long long)b * p.max_blocks + slot];
   ok = blk >= 0 && (p.num_blocks <= 0 || blk < p.num_blocks);
   if (!ok && p.err_flag) atomicExch(p.err_flag, 1);
   return ok ? (long long)blk : 0;

@@ -1,6 +1,478 @@
-// fwd_sm100.cu — tcgen05 forward (being written; declines every request for now).
+// fwd_sm100.cu — exact attention forward on the Blackwell tensor cores (tcgen05 + TMEM + TMA).
+//
+// One CTA = one 128-row query tile of one head of one sequence.  Warp roles (192 threads):
+//   warps 0-3  softmax: thread t owns query row t (= TMEM lane t).  Reads its S row from TMEM,
+//              applies masks / softcap / alibi / Philox dropout, keeps the online-softmax state
+//              (lazy rescale: the reference max only moves when it grows by > 2^8), writes P as
+//              packed 16-bit pairs back into the same TMEM columns, and finally normalises O
+//              and writes O and LSE.
+//   warp 4     TMA producer: Q once, then K and V tiles (128 keys x D) into an NS-stage ring.
+//   warp 5     MMA issuer: owns the TMEM allocation; S_j = Q K_j^T into one of two S buffers
+//              (SS form), then O += P_j V_j with P read from TMEM (TS form).
+// TMEM columns: S0 [0,128), S1 [128,256), O [256, 256+D).  K/V tiles are 128-byte swizzled
+// (TMA SWIZZLE_128B, one 64-column box per 128-byte row chunk); S uses K-major Q and K operands,
+// PV uses an MN-major V operand.  Every mbarrier wait is bounded: on timeout the CTA records an
+// error (fa_device_error) and unwinds without touching TMEM or smem further.
+//
+// Semantics are identical to the CUDA-core kernel (fwd_simt.cu) and to the reference's forward
+// (kernels/fa_forward.hip:52-313): bottom-right causal / window / chunk masks, softcap, signed
+// alibi without diagonal offset, Philox dropout keyed (h*SQ+q)*SK+key, LSE in natural log,
+// empty rows -> O = 0 and LSE = -inf.
+#include <cudaTypedefs.h>
 #include "fa_common.cuh"
 #include "fa_launch.h"
+#include "sm100_ptx.cuh"
+
+namespace {
+
+using namespace sm100;
+
+constexpr int BM = 128, BN = 128, NTHREADS = 192;
+constexpr float LAZY_THRESH = 8.0f;   // log2 units: rescale O only when the max grows by > 2^8
+
+__device__ int g_fwd_error = 0;       // non-zero after a pipeline wait timed out
+
+template <int D>
+struct Cfg {
+  static constexpr int NS = (D <= 64) ? 4 : 2;                 // K/V ring depth
+  static constexpr int NCH = D / 64;                           // 64-column (128-byte) chunks per row
+  static constexpr int Q_BYTES = BM * D * 2;
+  static constexpr int KV_BYTES = BN * D * 2;                  // one K (or V) tile
+  static constexpr int CH_BYTES = BN * 128;                    // one 64-column chunk of a tile
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = Q_BYTES;
+  static constexpr int OFF_V = OFF_K + NS * KV_BYTES;
+  static constexpr int OFF_BAR = OFF_V + NS * KV_BYTES;
+  static constexpr int SMEM = OFF_BAR + 256 + 1024;            // barriers + alignment slack
+  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr uint32_t O_COL = 256;
+};
+
+struct Bars {   // mbarrier offsets inside the barrier block (8 bytes each)
+  static constexpr int Q_FULL = 0, K_FULL = 8, V_FULL = 48, KV_EMPTY = 88, S_FULL = 128, P_FULL = 144,
+                       O_DONE = 160, TMEM_ADDR = 168;
+};
+
+__device__ __forceinline__ void record_error(int code) { atomicOr(&g_fwd_error, code); }
+
+template <int D, bool BF16, bool FEAT>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                  const __grid_constant__ CUtensorMap tmV, const FaFwdParams p) {
+  using C = Cfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  uint8_t* sgen = smem_raw + (sbase - smem_u32(smem_raw));
+  const uint32_t sQ = sbase + C::OFF_Q, sK = sbase + C::OFF_K, sV = sbase + C::OFF_V;
+  const uint32_t bar = sbase + C::OFF_BAR;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sgen + C::OFF_BAR + Bars::TMEM_ADDR);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int z = blockIdx.z, h = blockIdx.y, kvh = h / p.gqa;
+  const bool varlen = p.cu_q != nullptr;
+
+  // ---- sequence geometry (uniform over the CTA; exits before any barrier or TMEM work)
+  int SQ = p.SQ, SK = p.SK, qtok0 = 0, ktok0 = 0;
+  if (varlen) {
+    qtok0 = p.cu_q[z];
+    ktok0 = p.cu_k[z];
+    SQ = p.cu_q[z + 1] - qtok0;
+    SK = p.cu_k[z + 1] - ktok0;
+    if (p.seqused_q && p.seqused_q[z] < SQ) SQ = p.seqused_q[z];
+    if (p.seqused_k && p.seqused_k[z] < SK) SK = p.seqused_k[z];
+    SQ = max(SQ, 0);
+    SK = max(SK, 0);
+  }
+  const int qb = (gridDim.x - 1 - blockIdx.x) * BM;   // heavy (late, causal) tiles first
+  if (qb >= SQ) return;
+  const int bcoord = varlen ? 0 : z;
+
+  int klo, khi, dmy;
+  fa_key_range(qb, SQ, SK, p.causal, p.win_left, p.win_right, p.attn_chunk, klo, dmy);
+  fa_key_range(min(qb + BM, SQ) - 1, SQ, SK, p.causal, p.win_left, p.win_right, p.attn_chunk, dmy, khi);
+  klo = max(klo, 0);
+  khi = min(khi, SK - 1);
+  const int t0 = klo / BN;
+  const int ntiles = (khi >= klo) ? (khi / BN - t0 + 1) : 0;
+
+  // ---- set-up: barriers (thread 0), TMEM (warp 5)
+  if (tid == 0) {
+    mbar_init(bar + Bars::Q_FULL, 1);
+    for (int s = 0; s < C::NS; ++s) {
+      mbar_init(bar + Bars::K_FULL + 8 * s, 1);
+      mbar_init(bar + Bars::V_FULL + 8 * s, 1);
+      mbar_init(bar + Bars::KV_EMPTY + 8 * s, 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bar + Bars::S_FULL + 8 * s, 1);
+      mbar_init(bar + Bars::P_FULL + 8 * s, BM);
+    }
+    mbar_init(bar + Bars::O_DONE, 1);
+    fence_barrier_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (warp == 4 && lane == 0) {
+    prefetch_tmap(&tmQ);
+    prefetch_tmap(&tmK);
+    prefetch_tmap(&tmV);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    // ======================= TMA producer
+    if (lane == 0 && ntiles > 0) {
+      mbar_expect_tx(bar + Bars::Q_FULL, C::Q_BYTES);
+      for (int c = 0; c < C::NCH; ++c)
+        tma_load_4d(sQ + c * (BM * 128), &tmQ, c * 64, qtok0 + qb, h, bcoord, bar + Bars::Q_FULL);
+      for (int j = 0; j < ntiles; ++j) {
+        const int s = j % C::NS;
+        if (j >= C::NS && !mbar_wait(bar + Bars::KV_EMPTY + 8 * s, ((j / C::NS) - 1) & 1)) {
+          record_error(1);
+          break;
+        }
+        const int krow = ktok0 + (t0 + j) * BN;
+        mbar_expect_tx(bar + Bars::K_FULL + 8 * s, C::KV_BYTES);
+        for (int c = 0; c < C::NCH; ++c)
+          tma_load_4d(sK + s * C::KV_BYTES + c * C::CH_BYTES, &tmK, c * 64, krow, kvh, bcoord,
+                      bar + Bars::K_FULL + 8 * s);
+        mbar_expect_tx(bar + Bars::V_FULL + 8 * s, C::KV_BYTES);
+        for (int c = 0; c < C::NCH; ++c)
+          tma_load_4d(sV + s * C::KV_BYTES + c * C::CH_BYTES, &tmV, c * 64, krow, kvh, bcoord,
+                      bar + Bars::V_FULL + 8 * s);
+      }
+      // do not leave while copies of this CTA are still landing in shared memory
+      for (int j = max(0, ntiles - C::NS); j < ntiles; ++j) {
+        const int s = j % C::NS;
+        mbar_wait(bar + Bars::K_FULL + 8 * s, (j / C::NS) & 1);
+        mbar_wait(bar + Bars::V_FULL + 8 * s, (j / C::NS) & 1);
+      }
+    }
+  } else if (warp == 5) {
+    // ======================= MMA issuer (whole warp follows; lane 0 issues)
+    constexpr uint32_t IDESC_S = idesc_f16(BF16 ? 1 : 0, BM, BN, 0, 0);
+    constexpr uint32_t IDESC_O = idesc_f16(BF16 ? 1 : 0, BM, D, 0, 1);
+    bool ok = ntiles == 0 || mbar_wait_warp(bar + Bars::Q_FULL, 0);
+    if (!ok) record_error(2);
+    auto issue_pv = [&](int i) -> bool {
+      const int s = i % C::NS;
+      if (!mbar_wait_warp(bar + Bars::P_FULL + 8 * (i & 1), (i >> 1) & 1)) return false;
+      if (!mbar_wait_warp(bar + Bars::V_FULL + 8 * s, (i / C::NS) & 1)) return false;
+      const int kb = (t0 + i) * BN;
+      if (varlen && kb + BN > SK) {
+        // rows past the sequence end belong to other sequences (or are unused): zero them so
+        // that P = 0 never meets a non-finite value
+        const int r0 = max(SK - kb, 0);
+        for (int e = r0 * 8 * C::NCH + lane; e < BN * 8 * C::NCH; e += 32) {
+          const int c = e / (BN * 8), rem = e % (BN * 8);
+          const int r = rem / 8, w16 = rem % 8;
+          if (r >= r0)
+            *reinterpret_cast<uint4*>(sgen + C::OFF_V + s * C::KV_BYTES + c * C::CH_BYTES + r * 128 + w16 * 16) =
+                make_uint4(0, 0, 0, 0);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+      }
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t pt = tmem + (uint32_t)(i & 1) * 128u;
+        const uint32_t vbase = sV + s * C::KV_BYTES;
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          // B = V tile, MN-major: 16 keys = 16 rows of 128 B; D spans NCH swizzle atoms (LBO apart)
+          const uint64_t bd = sdesc_sw128(vbase + kk * 16 * 128, C::CH_BYTES, 1024);
+          mma_ts(tmem + C::O_COL, pt + kk * 8, bd, IDESC_O, (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(bar + Bars::KV_EMPTY + 8 * s);
+        mma_commit(bar + Bars::O_DONE);
+      }
+      __syncwarp();
+      return true;
+    };
+    for (int j = 0; ok && j < ntiles; ++j) {
+      const int s = j % C::NS;
+      if (!mbar_wait_warp(bar + Bars::K_FULL + 8 * s, (j / C::NS) & 1)) { ok = false; break; }
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t st = tmem + (uint32_t)(j & 1) * 128u;
+        const uint32_t kbase = sK + s * C::KV_BYTES;
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const int c = kk / 4, off = (kk % 4) * 32;   // 16 columns = 32 bytes inside a 128-byte chunk
+          const uint64_t ad = sdesc_sw128(sQ + c * (BM * 128) + off, 16, 1024);
+          const uint64_t bd = sdesc_sw128(kbase + c * C::CH_BYTES + off, 16, 1024);
+          mma_ss(st, ad, bd, IDESC_S, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(bar + Bars::S_FULL + 8 * (j & 1));
+      }
+      __syncwarp();
+      if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+    }
+    if (ok && ntiles > 0 && !issue_pv(ntiles - 1)) ok = false;
+    if (!ok) record_error(4);
+  } else {
+    // ======================= softmax + epilogue (warps 0-3, thread = query row)
+    const int r = tid, q = qb + r;
+    const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+    int rlo, rhi;
+    fa_key_range(q, SQ, SK, p.causal, p.win_left, p.win_right, p.attn_chunk, rlo, rhi);
+    if (q >= SQ) { rlo = 1; rhi = 0; }
+    // CTA-uniform bounds used to classify tiles as fully visible
+    int lo_last, hi_first;
+    {
+      int a, b;
+      fa_key_range(min(qb + BM, SQ) - 1, SQ, SK, p.causal, p.win_left, p.win_right, p.attn_chunk, lo_last, a);
+      fa_key_range(qb, SQ, SK, p.causal, p.win_left, p.win_right, p.attn_chunk, b, hi_first);
+    }
+    const bool full_rows = qb + BM <= SQ;
+    const float scale2 = p.scale * FA_LOG2E;
+    const float slope2 = (FEAT && p.alibi_slopes) ? p.alibi_slopes[h] * FA_LOG2E : 0.f;
+    const bool drop = FEAT && p.dropout_p > 0.f;
+    const float inv_keep = drop ? 1.0f / (1.0f - p.dropout_p) : 1.f;
+    float m_ref = -INFINITY, l = 0.f;
+    bool ok = true;
+    float s[BN];
+    for (int j = 0; j < ntiles; ++j) {
+      if (!mbar_wait_warp(bar + Bars::S_FULL + 8 * (j & 1), (j >> 1) & 1)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t sa = lane_addr + (uint32_t)(j & 1) * 128u;
+#pragma unroll
+      for (int c = 0; c < BN; c += 32) tmem_ld32(sa + c, s + c);
+      tc_wait_ld();
+      const int kb = (t0 + j) * BN;
+      // ---- scores (log2 domain) and masks
+      float tmax = -INFINITY;
+      if constexpr (FEAT) {
+#pragma unroll
+        for (int c = 0; c < BN; ++c) {
+          const int key = kb + c;
+          float v;
+          if (p.softcap > 0.f) v = p.softcap * tanhf(s[c] * p.scale / p.softcap) * FA_LOG2E;
+          else v = s[c] * scale2;
+          v += slope2 * (float)(key - q);
+          s[c] = (key < rlo || key > rhi) ? -INFINITY : v;
+          tmax = fmaxf(tmax, s[c]);
+        }
+      } else {
+        const bool interior = full_rows && kb >= lo_last && kb + BN - 1 <= hi_first && kb + BN <= SK;
+        if (!interior) {
+#pragma unroll
+          for (int c = 0; c < BN; ++c) {
+            const int key = kb + c;
+            if (key < rlo || key > rhi) s[c] = -INFINITY;
+          }
+        }
+#pragma unroll
+        for (int c = 0; c < BN; ++c) tmax = fmaxf(tmax, s[c]);
+        tmax = (tmax == -INFINITY) ? -INFINITY : tmax * scale2;
+      }
+      // ---- lazy online-softmax update; the O rescale is done by whole warps (tcgen05.ld/st are
+      //      warp-collective), rows that do not move keep a factor of 1
+      const bool move = tmax > m_ref + LAZY_THRESH || (m_ref == -INFINITY && tmax != -INFINITY);
+      float corr = 1.f;
+      if (move) {
+        corr = ex2(m_ref - tmax);   // 0 when the row had no visible key yet (its O row is 0)
+        l *= corr;
+        m_ref = tmax;
+      }
+      if (j > 0 && __any_sync(0xffffffffu, move && corr != 1.f)) {
+        if (!mbar_wait_warp(bar + Bars::O_DONE, (j - 1) & 1)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < D; c += 32) {
+          float o[32];
+          tmem_ld32(lane_addr + C::O_COL + c, o);
+          tc_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= corr;
+          tmem_st32(lane_addr + C::O_COL + c, reinterpret_cast<const uint32_t*>(o));
+        }
+        tc_wait_st();
+      }
+      const float muse = (m_ref == -INFINITY) ? 0.f : m_ref;
+      const float sc = FEAT ? 1.f : scale2;
+      // ---- P = 2^(s - m): row sum (before dropout), dropout, 16-bit pairs into the first
+      //      BN/2 columns of the same S buffer (chunk c overwrites S columns already consumed)
+      float lsum = 0.f;
+#pragma unroll
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float a = ex2(fmaf(s[c0 + 2 * i], sc, -muse));
+          float b = ex2(fmaf(s[c0 + 2 * i + 1], sc, -muse));
+          lsum += a + b;
+          if (drop) {
+            const unsigned long long idx = ((unsigned long long)h * SQ + q) * SK + (kb + c0 + 2 * i);
+            a *= fa_dropout_mul(p.philox_seed, idx, p.dropout_p, inv_keep);
+            b *= fa_dropout_mul(p.philox_seed, idx + 1, p.dropout_p, inv_keep);
+          }
+          if constexpr (BF16) {
+            const __nv_bfloat162 t2 = __floats2bfloat162_rn(a, b);
+            pk[i] = *reinterpret_cast<const uint32_t*>(&t2);
+          } else {
+            const __half2 t2 = __floats2half2_rn(a, b);
+            pk[i] = *reinterpret_cast<const uint32_t*>(&t2);
+          }
+        }
+        tmem_st16(sa + c0 / 2, pk);
+      }
+      l += lsum;
+      tc_wait_st();
+      tc_fence_before();
+      mbar_arrive(bar + Bars::P_FULL + 8 * (j & 1));
+    }
+    if (!ok) record_error(8);
+    // ---- epilogue: O / l, LSE (TMEM reads by whole warps; stores only for real rows)
+    const bool have_o = ok && ntiles > 0;
+    if (have_o && !mbar_wait_warp(bar + Bars::O_DONE, (ntiles - 1) & 1)) record_error(16);
+    tc_fence_after();
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+    T* orow = (T*)p.O + (varlen ? (long long)qtok0 * p.sO.s : (long long)z * p.sO.b) + (long long)h * p.sO.h +
+              (long long)q * p.sO.s;
+#pragma unroll
+    for (int c = 0; c < D; c += 32) {
+      float o[32];
+      if (have_o) {
+        tmem_ld32(lane_addr + C::O_COL + c, o);
+        tc_wait_ld();
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] = 0.f;
+      }
+      if (q < SQ) {
+        uint32_t w[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          if constexpr (BF16) {
+            const __nv_bfloat162 t2 = __floats2bfloat162_rn(o[2 * i] * inv, o[2 * i + 1] * inv);
+            w[i] = *reinterpret_cast<const uint32_t*>(&t2);
+          } else {
+            const __half2 t2 = __floats2half2_rn(o[2 * i] * inv, o[2 * i + 1] * inv);
+            w[i] = *reinterpret_cast<const uint32_t*>(&t2);
+          }
+        }
+        uint4* dst = reinterpret_cast<uint4*>(orow + c);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+      }
+    }
+    if (q < SQ && p.LSE) {
+      const long long li = fa_lse_index(varlen, z, h, p.NH, p.SQ, qtok0, p.lse_total_q, q);
+      p.LSE[li] = l > 0.f ? m_ref * FA_LN2 + logf(l) : -INFINITY;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (PFN_cuTensorMapEncodeTiled_v12000)ptr;
+  }
+  return fn;
+}
+
+// 4-D view [B][H][S][D] (dim 0 innermost) with 128-byte swizzled boxes of 64 x rows
+bool make_map(CUtensorMap* m, const void* base, bool bf16, long long D, long long S, long long H, long long B,
+              const FaStrides& st, int box_rows) {
+  auto enc = encode_fn();
+  if (!enc) return false;
+  const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)H, (cuuint64_t)B};
+  // with a single batch entry the batch stride is never used: give it a valid (aligned) value
+  const long long sb = (B > 1) ? st.b : ((st.s * S > st.h * H ? st.s * S : st.h * H) + 7) / 8 * 8;
+  const cuuint64_t strides[3] = {(cuuint64_t)st.s * 2, (cuuint64_t)st.h * 2, (cuuint64_t)sb * 2};
+  const cuuint32_t box[4] = {64, (cuuint32_t)box_rows, 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  for (int i = 0; i < 3; ++i)
+    if (strides[i] % 16 != 0 || strides[i] >= (1ull << 40)) return false;
+  if (((uintptr_t)base) % 16 != 0) return false;
+  const CUresult r = enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                         const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int D, bool BF16, bool FEAT>
+int launch(const FaFwdParams& p, cudaStream_t st, const CUtensorMap& mq, const CUtensorMap& mk,
+           const CUtensorMap& mv) {
+  using C = Cfg<D>;
+  static unsigned long long done = 0;
+  if (int rc = fa::ensure_smem((const void*)fwd_tc_kernel<D, BF16, FEAT>, C::SMEM, &done)) return rc;
+  dim3 grid((p.SQ + BM - 1) / BM, p.NH, p.batch);
+  fwd_tc_kernel<D, BF16, FEAT><<<grid, NTHREADS, C::SMEM, st>>>(mq, mk, mv, p);
+  fa::count_launch();
+  return fa::cuda_status(cudaGetLastError(), "fwd_sm100 launch");
+}
+
+template <bool BF16, bool FEAT>
+int launch_d(const FaFwdParams& p, cudaStream_t st, const CUtensorMap& mq, const CUtensorMap& mk,
+             const CUtensorMap& mv) {
+  if (p.HD == 64) return launch<64, BF16, FEAT>(p, st, mq, mk, mv);
+  return launch<128, BF16, FEAT>(p, st, mq, mk, mv);
+}
+
+}  // namespace
+
 namespace fa {
-int fwd_sm100(const FaFwdParams&, int, cudaStream_t, bool* taken) { *taken = false; return FA_OK; }
+
+// Takes fp16/bf16 requests with head_dim 64 or 128, 16-byte aligned rows and strides;
+// everything else is left to the CUDA-core kernel (*taken = false).
+int fwd_sm100(const FaFwdParams& p, int dtype, cudaStream_t st, bool* taken) {
+  *taken = false;
+  if (p.HD != 64 && p.HD != 128) return FA_OK;
+  if (getenv("FABLE_ATTN_DISABLE_TC")) return FA_OK;
+  int dev = current_device(), major = 0, minor = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  if (major != 10 || minor != 0) return FA_OK;
+  const bool bf16 = dtype == FA_DTYPE_BF16;
+  const bool varlen = p.cu_q != nullptr;
+  // varlen tensors are (total, H, D): a 4-D map with one batch entry, rows = tokens; the row
+  // extent is taken from the largest token index any sequence can address
+  long long rows_q, rows_k;
+  if (varlen) {
+    rows_q = rows_k = (1ll << 31) - 1;   // bounded by the allocation, see below
+    return FA_OK;                        // varlen on the tensor cores: not yet enabled
+  } else {
+    rows_q = p.SQ;
+    rows_k = p.SK;
+  }
+  const int NKV = p.NH / p.gqa;
+  CUtensorMap mq, mk, mv;
+  if (!make_map(&mq, p.Q, bf16, p.HD, rows_q, p.NH, varlen ? 1 : p.batch, p.sQ, BM)) return FA_OK;
+  if (!make_map(&mk, p.K, bf16, p.HD, rows_k, NKV, varlen ? 1 : p.batch, p.sK, BN)) return FA_OK;
+  if (!make_map(&mv, p.V, bf16, p.HD, rows_k, NKV, varlen ? 1 : p.batch, p.sV, BN)) return FA_OK;
+  if (((uintptr_t)p.O) % 16 || (p.sO.s % 8) || (p.sO.h % 8) || (!varlen && p.sO.b % 8)) return FA_OK;
+  *taken = true;
+  const bool feat = p.softcap > 0.f || p.alibi_slopes != nullptr || p.dropout_p > 0.f;
+  if (bf16) return feat ? launch_d<true, true>(p, st, mq, mk, mv) : launch_d<true, false>(p, st, mq, mk, mv);
+  return feat ? launch_d<false, true>(p, st, mq, mk, mv) : launch_d<false, false>(p, st, mq, mk, mv);
+}
+
+}  // namespace fa
+
+extern "C" FA_API int fa_device_error(int clear) {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_fwd_error, sizeof(int));
+  if (clear) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_fwd_error, &zero, sizeof(int));
+  }
+  return v;
 }

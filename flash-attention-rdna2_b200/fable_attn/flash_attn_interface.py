@@ -412,14 +412,14 @@ def flash_attn_with_kvcache(q, k_cache, v_cache, k=None, v=None, qv=None, rotary
     _accept_hints(num_splits, pack_gqa, sm_margin)
     if q.dim() != 4:
         raise ValueError(f"fable_attn: decode expects q as (batch, seqlen_q, nheads, headdim), got {tuple(q.shape)}")
-    if not q.is_cuda:
-        raise ValueError("fable_attn: tensors must be on a CUDA device (q.is_cuda is False)")
     if softmax_scale is None:
         softmax_scale = (q.shape[-1] + (qv.shape[-1] if qv is not None else 0)) ** -0.5
     del scheduler_metadata  # precomputed FA-3 schedules are not needed: the launcher plans per call
     if cu_seqlens_k_new is not None:
         raise NotImplementedError("fable_attn: cu_seqlens_k_new (ragged append) is not supported; append the "
                                   "same number of tokens to every sequence")
+    if not q.is_cuda:
+        raise ValueError("fable_attn: tensors must be on a CUDA device (q.is_cuda is False)")
     if cu_seqlens_q is not None:
         cu = cu_seqlens_q.to(torch.int32).cpu()
         outs, lses = [], []

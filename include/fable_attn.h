@@ -198,6 +198,10 @@ FA_API int fa_combine_launch(const FaCombineParams* p, void* stream);
 /* ---- introspection ---- */
 FA_API int fa_abi_version(void);
 FA_API const char* fa_last_error(void);       /* message of the last failing call on this thread */
+/* Error bits recorded by device-side pipeline waits that gave up (0 = none).  A bounded wait in
+ * a tensor-core kernel that times out records a bit here and the kernel unwinds instead of
+ * hanging.  Synchronous (device -> host copy); clear != 0 resets the bits. */
+FA_API int fa_device_error(int clear);
 /* Number of this library's kernels launched since load (all threads, all devices). */
 FA_API unsigned long long fa_kernel_launch_count(void);
 

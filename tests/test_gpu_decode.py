@@ -1,0 +1,185 @@
+"""GPU parity of paged-KV decode (append + split-K partial + merge) and of the combine kernel,
+through the C ABI, against the oracle (kernels/fa_decode_gate.inc:66-96 restated).
+
+Case table: the reference's decode gate (kernels/fa_decode_gate.inc:159-192) — paged GQA, NeoX
+and interleaved rotary, window, append(+rotary), leftpad(+window), softcap, alibi, nq = 3..8,
+every head dim — on a 2-sequence batch with a RANDOM permutation block table (the reference uses
+the identity), plus gqa values the reference's kernel cannot map (3, 6, 16), bit-exact append
+placement, split-count invariance, and out-of-range page detection."""
+import ctypes as C
+import zlib
+
+import numpy as np
+import pytest
+import torch
+
+import fa_abi as A
+from gpu_util import TDT, TOL, randn, stream, to_np
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+# (name, HD, NH, gqa, ctx, window, rotary, append, leftpad, nq, softcap, alibi)
+CASES = [
+    ("paged_gqa4_ctx333", 128, 32, 4, 333, -1, 0, False, 0, 1, 0.0, False),
+    ("paged_gqa1_ctx200", 128, 8, 1, 200, -1, 0, False, 0, 1, 0.0, False),
+    ("rotary_neox", 128, 32, 4, 256, -1, 1, False, 0, 1, 0.0, False),
+    ("rotary_interleaved", 128, 32, 4, 256, -1, 2, False, 0, 1, 0.0, False),
+    ("window64", 128, 32, 4, 500, 64, 0, False, 0, 1, 0.0, False),
+    ("append_rotary", 128, 32, 4, 257, -1, 1, True, 0, 1, 0.0, False),
+    ("leftpad100", 128, 32, 4, 400, -1, 0, False, 100, 1, 0.0, False),
+    ("leftpad37_gqa1", 128, 8, 1, 333, -1, 0, False, 37, 1, 0.0, False),
+    ("leftpad_window", 128, 32, 4, 500, 64, 0, False, 50, 1, 0.0, False),
+    ("softcap30", 128, 32, 4, 333, -1, 0, False, 0, 1, 30.0, False),
+    ("softcap50_append", 128, 32, 4, 257, -1, 0, True, 0, 1, 50.0, False),
+    ("alibi", 128, 32, 4, 333, -1, 0, False, 0, 1, 0.0, True),
+    ("alibi_window", 128, 32, 4, 500, 128, 0, False, 0, 1, 0.0, True),
+    ("nq4_no_append", 128, 32, 4, 300, -1, 0, False, 0, 4, 0.0, False),
+    ("nq4_append", 128, 32, 4, 300, -1, 0, True, 0, 4, 0.0, False),
+    ("nq8_append_rotary", 128, 32, 4, 257, -1, 1, True, 0, 8, 0.0, False),
+    ("nq5_gqa1_window", 128, 8, 1, 400, 96, 0, True, 0, 5, 0.0, False),
+    ("nq3_softcap_alibi", 128, 32, 4, 300, -1, 0, True, 0, 3, 30.0, True),
+    ("hd64", 64, 32, 4, 300, -1, 0, False, 0, 1, 0.0, False),
+    ("hd256", 256, 8, 4, 300, -1, 0, False, 0, 1, 0.0, False),
+    ("hd16", 16, 32, 4, 200, -1, 0, False, 0, 1, 0.0, False),
+    ("hd32", 32, 32, 4, 200, -1, 0, False, 0, 1, 0.0, False),
+    ("hd48", 48, 32, 4, 200, -1, 0, False, 0, 1, 0.0, False),
+    ("hd80", 80, 32, 4, 200, -1, 0, False, 0, 1, 0.0, False),
+    ("hd96", 96, 32, 4, 200, -1, 0, False, 0, 1, 0.0, False),
+    ("hd112", 112, 32, 4, 200, -1, 0, False, 0, 1, 0.0, False),
+    ("hd160", 160, 8, 4, 200, -1, 0, False, 0, 1, 0.0, False),
+    ("hd192", 192, 8, 4, 200, -1, 0, False, 0, 1, 0.0, False),
+    ("hd224", 224, 8, 4, 200, -1, 0, False, 0, 1, 0.0, False),
+    ("gqa3", 64, 12, 3, 300, -1, 0, False, 0, 1, 0.0, False),
+    ("gqa6_append", 64, 12, 6, 300, -1, 0, True, 0, 2, 0.0, False),
+    ("gqa16_mqa", 64, 16, 16, 300, -1, 0, False, 0, 1, 0.0, False),
+]
+
+PAGE = 16
+
+
+def _setup(case, dt, nsplit=0, batch=2):
+    name, HD, NH, gqa, ctx, window, rotary, append, leftpad, nq, sc, al = case
+    rng = np.random.default_rng(zlib.crc32(name.encode()))
+    NKV = NH // gqa
+    ctxs = np.array([ctx, max(ctx // 2 + 7, 1)][:batch], dtype=np.int32)
+    total = ctxs + (nq if append else 0)
+    max_blocks = int((total.max() + PAGE - 1) // PAGE)
+    nblocks = batch * max_blocks + 3
+    bt = rng.permutation(nblocks)[: batch * max_blocks].astype(np.int32).reshape(batch, max_blocks)
+    kcn, kc = randn(rng, (nblocks, PAGE, NKV, HD), dt)
+    vcn, vc = randn(rng, (nblocks, PAGE, NKV, HD), dt)
+    qn, q = randn(rng, (batch, nq, NH, HD), dt)
+    nkn = nvn = nk = nv = None
+    if append:
+        nkn, nk = randn(rng, (batch, nq, NKV, HD), dt)
+        nvn, nv = randn(rng, (batch, nq, NKV, HD), dt)
+    seqro = int(total.max()) + 8
+    ang = np.arange(seqro)[:, None] * (10000.0 ** (-2.0 * np.arange(HD // 2) / HD))[None]
+    cos, sin = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+    slopes = (-(2.0 ** (-(8.0 * (np.arange(NH) + 1) / NH)))).astype(np.float32) if al else None
+    lp = np.full(batch, leftpad, np.int32) if leftpad else None
+    if nsplit <= 0:
+        nsplit = A.lib().fa_decode_num_splits(batch, nq, NKV, max_blocks * PAGE, 0)
+    o = torch.empty_like(q)
+    lse = torch.empty((batch, nq, NH), device="cuda", dtype=torch.float32)
+    scratch = torch.empty(A.lib().fa_decode_scratch_floats(batch, nq, NH, HD, nsplit), device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    keep = dict(bt=torch.from_numpy(bt).cuda(), ctx=torch.from_numpy(ctxs).cuda(),
+                cos=torch.from_numpy(cos).cuda(), sin=torch.from_numpy(sin).cuda(),
+                al=torch.from_numpy(slopes).cuda() if al else None,
+                lp=torch.from_numpy(lp).cuda() if lp is not None else None)
+    p = A.FaDecParams()
+    p.struct_size = C.sizeof(A.FaDecParams)
+    p.q, p.Kc, p.Vc, p.block_table, p.o = A.ptr(q), A.ptr(kc), A.ptr(vc), A.ptr(keep["bt"]), A.ptr(o)
+    p.scratch, p.ctx_len = A.ptr(scratch), A.ptr(keep["ctx"])
+    if rotary:
+        p.cos, p.sin = A.ptr(keep["cos"]), A.ptr(keep["sin"])
+    p.batch, p.NH, p.gqa, p.HD, p.page, p.max_blocks, p.nsplit, p.window = (batch, NH, gqa, HD, PAGE, max_blocks,
+                                                                             nsplit, window)
+    p.rotary, p.scale, p.leftpad, p.lse_out = rotary, HD ** -0.5, A.ptr(keep["lp"]), A.ptr(lse)
+    p.softcap, p.alibi, p.nq = sc, A.ptr(keep["al"]), nq
+    p.num_blocks, p.err_flag = nblocks, A.ptr(err)
+    ref = O.decode(qn, kcn, vcn, bt, ctxs, nkn, nvn, cos if rotary else None, sin if rotary else None, rotary, 0,
+                   None, lp, slopes, window, HD ** -0.5, sc)
+    return dict(p=p, keep=keep, q=q, kc=kc, vc=vc, nk=nk, nv=nv, o=o, lse=lse, err=err, ref=ref, bt=bt, ctxs=ctxs,
+                nkn=nkn, nvn=nvn, kcn=kcn, vcn=vcn)
+
+
+def _launch(s, dt):
+    A.check(A.lib().fa_decode_launch(C.byref(s["p"]), A.DT[dt], stream(), A.ptr(s["nk"]), A.ptr(s["nv"])))
+    torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("dt", ["fp16", "bf16", "fp32"])
+@pytest.mark.parametrize("case", CASES, ids=[c[0] for c in CASES])
+def test_decode_gate_table(case, dt):
+    s = _setup(case, dt)
+    _launch(s, dt)
+    ro, rl = s["ref"]
+    e = O.rel_rms(to_np(s["o"]), ro)
+    assert e < TOL[dt], f"O rel_rms {e:.3e}"
+    el = O.rel_rms(s["lse"].cpu().numpy(), rl)
+    assert el < TOL[dt], f"LSE rel_rms {el:.3e}"
+    assert int(s["err"].item()) == 0
+
+
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+def test_decode_append_placement_bit_exact(dt):
+    """New V rows land verbatim at block_table[b][pos//page], slot pos%page, pos = ctx+tk;
+    un-rotated K rows likewise; every other cache byte is untouched."""
+    case = ("placement", 64, 8, 2, 45, -1, 0, True, 0, 4, 0.0, False)
+    s = _setup(case, dt)
+    kc0, vc0 = s["kc"].clone(), s["vc"].clone()
+    _launch(s, dt)
+    kexp, vexp = kc0.clone(), vc0.clone()
+    for b in range(2):
+        for tk in range(4):
+            pos = int(s["ctxs"][b]) + tk
+            blk, slot = int(s["bt"][b][pos // PAGE]), pos % PAGE
+            kexp[blk, slot] = s["nk"][b, tk]
+            vexp[blk, slot] = s["nv"][b, tk]
+    assert torch.equal(s["kc"].view(torch.int16), kexp.view(torch.int16))
+    assert torch.equal(s["vc"].view(torch.int16), vexp.view(torch.int16))
+
+
+@pytest.mark.parametrize("nsplit", [1, 2, 7, 40])
+def test_decode_split_count_invariance(nsplit):
+    case = CASES[0]
+    s = _setup(case, "bf16", nsplit=nsplit)
+    _launch(s, "bf16")
+    assert O.rel_rms(to_np(s["o"]), s["ref"][0]) < TOL["bf16"]
+
+
+def test_decode_bad_page_index_sets_flag():
+    """A block-table entry past the cache is never dereferenced: the position is skipped and the
+    caller's error flag is raised."""
+    case = CASES[1]
+    s = _setup(case, "bf16")
+    s["keep"]["bt"][0, 2] = 1 << 30
+    _launch(s, "bf16")
+    assert int(s["err"].item()) == 1
+
+
+@pytest.mark.parametrize("in_dt,out_dt", [("fp32", "bf16"), ("fp32", "fp16"), ("bf16", "bf16"), ("fp32", "fp32")])
+def test_combine_kernel(in_dt, out_dt):
+    rng = np.random.default_rng(17)
+    ns, B, S, H, D = 5, 2, 3, 8, 128
+    opn, op = randn(rng, (ns, B, S, H, D), in_dt)
+    lpn = (rng.standard_normal((ns, B, H, S)) * 3).astype(np.float32)
+    lpn[:, 1, 2, 0] = -np.inf
+    lp = torch.from_numpy(lpn).cuda()
+    out = torch.empty((B, S, H, D), device="cuda", dtype=TDT[out_dt])
+    lse = torch.empty((B, H, S), device="cuda", dtype=torch.float32)
+    p = A.FaCombineParams()
+    p.struct_size = C.sizeof(A.FaCombineParams)
+    p.out_partial, p.in_dtype, p.lse_partial = A.ptr(op), A.DT[in_dt], A.ptr(lp)
+    p.out, p.out_dtype, p.lse_out = A.ptr(out), A.DT[out_dt], A.ptr(lse)
+    p.nsplit, p.B, p.S, p.H, p.D = ns, B, S, H, D
+    A.check(A.lib().fa_combine_launch(C.byref(p), stream()))
+    torch.cuda.synchronize()
+    ro, rl = O.combine(opn, lpn)
+    assert O.rel_rms(to_np(out), ro) < TOL[out_dt]
+    got_l = lse.cpu().numpy()
+    assert np.array_equal(np.isfinite(got_l), np.isfinite(rl))
+    assert np.abs(got_l[np.isfinite(rl)] - rl[np.isfinite(rl)]).max() < 1e-4

@@ -1,0 +1,184 @@
+"""CPU tests of the oracle itself: pinned to the reference's own numbers before it is trusted.
+
+1. golden fixtures produced by the reference's ref_attention / philox (tests/golden)
+2. the reference's oracle compiled here (oracle/_ref), when present
+3. independent cross-checks: backward vs float64 torch autograd, decode vs the dense forward,
+   combine vs the closed form.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+
+GOLD = os.path.join(os.path.dirname(__file__), "golden", "reference_oracle.npz")
+
+
+@pytest.fixture(scope="module")
+def gold():
+    return np.load(GOLD)
+
+
+def _fwd_cases(gold):
+    return sorted({k.split("/")[1] for k in gold.files if k.startswith("fwd/")})
+
+
+def test_philox_known_answer():
+    # known answer quoted for the reference generator: philox(777, 12345) = (e8c223b1, 0e6d9111)
+    assert O.philox_r0(777, 12345) == 0xE8C223B1
+    assert abs(O.lib().fa_oracle_dropout_mul(777, 12345, 0.1) - 1.0 / 0.9) < 1e-6
+
+
+def test_philox_matches_reference_golden(gold):
+    for seed, idx, r0, _r1 in gold["philox/kat"].tolist():
+        assert O.philox_r0(int(seed), int(idx)) == int(r0)
+
+
+def test_dropout_mask_matches_reference_golden(gold):
+    ref = gold["philox/mask_h3_24x40_p0.2_seed777"]
+    got = O.dropout_mask(777, 3, 24, 40, 0.2)
+    assert np.array_equal(got, ref)
+    assert 0.1 < 1 - got.mean() < 0.3
+
+
+def test_forward_matches_reference_golden(gold):
+    for name in _fwd_cases(gold):
+        p = f"fwd/{name}/"
+        SQ, SK, D, NH, g, causal, al, wl, wr, sc, ch = gold[p + "cfg"].tolist()
+        q = gold[p + "q"].astype(np.float32)[None]
+        k = gold[p + "k"].astype(np.float32)[None]
+        v = gold[p + "v"].astype(np.float32)[None]
+        slopes = gold[p + "slopes"] if al else None
+        o, lse = O.forward(q, k, v, int(D) ** -0.5, bool(causal), int(wl), int(wr), sc, slopes, int(ch))
+        assert O.rel_rms(o[0], gold[p + "o"]) < 1e-6, name
+        ref_l = gold[p + "lse"]
+        fin = np.isfinite(ref_l)
+        assert np.array_equal(fin, np.isfinite(lse[0])), name
+        if fin.any():
+            assert np.abs(lse[0][fin] - ref_l[fin]).max() < 2e-5, name
+
+
+@pytest.mark.skipif(O.ref_lib() is None, reason="reference oracle not built (reference sources absent)")
+@pytest.mark.parametrize("causal,wl,wr,softcap,alibi,chunk,SQ,SK", [
+    (True, -1, -1, 0.0, False, 0, 96, 96), (False, -1, -1, 0.0, False, 0, 80, 112),
+    (True, 31, 0, 0.0, False, 0, 96, 96), (False, 16, 16, 0.0, False, 0, 64, 64),
+    (True, -1, -1, 30.0, True, 0, 72, 72), (True, -1, -1, 0.0, False, 37, 96, 96),
+    (True, -1, -1, 0.0, False, 0, 96, 40)])
+def test_forward_matches_reference_build(causal, wl, wr, softcap, alibi, chunk, SQ, SK):
+    rng = np.random.default_rng(SQ * 7 + SK)
+    NH, g, D = 4, 2, 64
+    q = rng.standard_normal((SQ, NH, D)).astype(np.float32)
+    k = rng.standard_normal((SK, NH // g, D)).astype(np.float32)
+    v = rng.standard_normal((SK, NH // g, D)).astype(np.float32)
+    slopes = (-0.1 * (np.arange(NH) + 1)).astype(np.float32) if alibi else None
+    o1, l1 = O.forward(q[None], k[None], v[None], D ** -0.5, causal, wl, wr, softcap, slopes, chunk)
+    o2, l2 = O.ref_forward(q, k, v, D ** -0.5, causal, wl, wr, softcap, slopes, chunk)
+    assert O.rel_rms(o1[0], o2) < 1e-6
+    fin = np.isfinite(l2)
+    assert np.array_equal(fin, np.isfinite(l1[0]))
+    assert np.abs(l1[0][fin] - l2[fin]).max() < 2e-5
+
+
+def _torch_attention_f64(q, k, v, scale, causal, wl, wr, softcap, alibi, dropout_p, seed):
+    """Independent float64 torch formulation (B,S,H,D) with the oracle's keep mask."""
+    B, SQ, NH, D = q.shape
+    SK, NKV = k.shape[1], k.shape[2]
+    kk = k.repeat_interleave(NH // NKV, dim=2)
+    vv = v.repeat_interleave(NH // NKV, dim=2)
+    s = torch.einsum("bqhd,bkhd->bhqk", q, kk) * scale
+    if softcap > 0:
+        s = softcap * torch.tanh(s / softcap)
+    qi = torch.arange(SQ).view(-1, 1)
+    ki = torch.arange(SK).view(1, -1)
+    if alibi is not None:
+        s = s + torch.tensor(alibi, dtype=torch.float64).view(1, NH, 1, 1) * (ki - qi)
+    hide = torch.zeros(SQ, SK, dtype=torch.bool)
+    diag = qi + SK - SQ
+    if causal:
+        hide |= ki > diag
+    if wl >= 0:
+        hide |= ki < diag - wl
+    if wr >= 0:
+        hide |= ki > diag + wr
+    p = torch.nan_to_num(torch.softmax(s.masked_fill(hide, float("-inf")), -1), nan=0.0)
+    if dropout_p > 0:
+        z = torch.stack([torch.from_numpy(O.dropout_mask(seed, h, SQ, SK, dropout_p)).double() for h in range(NH)])
+        p = p * z.unsqueeze(0) / (1 - dropout_p)
+    return torch.einsum("bhqk,bkhd->bqhd", p, vv)
+
+
+@pytest.mark.parametrize("causal,wl,wr,softcap,alibi,dropout_p", [
+    (True, -1, -1, 0.0, False, 0.0), (False, 7, 3, 0.0, False, 0.0), (True, -1, -1, 20.0, True, 0.0),
+    (False, -1, -1, 0.0, False, 0.2)])
+def test_backward_oracle_vs_torch_autograd(causal, wl, wr, softcap, alibi, dropout_p):
+    rng = np.random.default_rng(5)
+    B, SQ, SK, NH, NKV, D = 1, 20, 24, 4, 2, 16
+    q = rng.standard_normal((B, SQ, NH, D)).astype(np.float32)
+    k = rng.standard_normal((B, SK, NKV, D)).astype(np.float32)
+    v = rng.standard_normal((B, SK, NKV, D)).astype(np.float32)
+    do = rng.standard_normal((B, SQ, NH, D)).astype(np.float32)
+    slopes = (-0.1 * (np.arange(NH) + 1)).astype(np.float32) if alibi else None
+    scale = D ** -0.5
+    dq, dk, dv = O.backward(q, k, v, do, scale, causal, wl, wr, softcap, slopes, dropout_p, 99)
+    tq, tk, tv = (torch.tensor(x, dtype=torch.float64, requires_grad=True) for x in (q, k, v))
+    out = _torch_attention_f64(tq, tk, tv, scale, causal, wl, wr, softcap, slopes, dropout_p, 99)
+    out.backward(torch.tensor(do, dtype=torch.float64))
+    # the rounding of the float32 slopes/inv_keep inside the oracle bounds the agreement
+    for got, ref in ((dq, tq.grad), (dk, tk.grad), (dv, tv.grad)):
+        assert O.rel_rms(got, ref.numpy()) < 2e-6
+    o, _ = O.forward(q, k, v, scale, causal, wl, wr, softcap, slopes, 0, dropout_p, 99)
+    assert O.rel_rms(o, out.detach().numpy()) < 2e-6
+
+
+def test_decode_oracle_vs_dense_forward():
+    """A paged cache read through a permuted block table equals dense attention of the gathered
+    rows (no append: the new token's window is the whole cache, non-causal)."""
+    rng = np.random.default_rng(11)
+    B, NH, NKV, D, page, nblk = 2, 8, 2, 32, 16, 12
+    ctx = np.array([150, 77], dtype=np.int32)
+    kc = rng.standard_normal((B * nblk, page, NKV, D)).astype(np.float32)
+    vc = rng.standard_normal((B * nblk, page, NKV, D)).astype(np.float32)
+    bt = rng.permutation(B * nblk).astype(np.int32).reshape(B, nblk)
+    q = rng.standard_normal((B, 1, NH, D)).astype(np.float32)
+    o, lse = O.decode(q, kc, vc, bt, ctx)
+    for b in range(B):
+        L = int(ctx[b])
+        kd = kc[bt[b]].reshape(-1, NKV, D)[:L][None]
+        vd = vc[bt[b]].reshape(-1, NKV, D)[:L][None]
+        od, ld = O.forward(q[b:b + 1], kd, vd, D ** -0.5)
+        assert O.rel_rms(o[b], od[0]) < 1e-6
+        assert np.abs(lse[b, 0] - ld[0, :, 0]).max() < 1e-5
+
+
+def test_decode_oracle_append_causal_among_new_tokens():
+    rng = np.random.default_rng(12)
+    NH, NKV, D, page, nblk, ctx, nq = 4, 2, 16, 8, 8, 29, 3
+    kc = rng.standard_normal((nblk, page, NKV, D)).astype(np.float32)
+    vc = rng.standard_normal((nblk, page, NKV, D)).astype(np.float32)
+    bt = np.arange(nblk, dtype=np.int32)[None]
+    q = rng.standard_normal((1, nq, NH, D)).astype(np.float32)
+    nk = rng.standard_normal((1, nq, NKV, D)).astype(np.float32)
+    nv = rng.standard_normal((1, nq, NKV, D)).astype(np.float32)
+    o, _ = O.decode(q, kc, vc, bt, np.array([ctx], np.int32), new_k=nk, new_v=nv)
+    for tk in range(nq):
+        kd = np.concatenate([kc.reshape(-1, NKV, D)[:ctx], nk[0, :tk + 1]])[None]
+        vd = np.concatenate([vc.reshape(-1, NKV, D)[:ctx], nv[0, :tk + 1]])[None]
+        od, _ = O.forward(q[:, tk:tk + 1], kd, vd, D ** -0.5)
+        assert O.rel_rms(o[0, tk], od[0, 0]) < 1e-6
+
+
+def test_combine_oracle_closed_form():
+    rng = np.random.default_rng(13)
+    ns, B, S, H, D = 3, 2, 5, 4, 8
+    op = rng.standard_normal((ns, B, S, H, D)).astype(np.float32)
+    lp = rng.standard_normal((ns, B, H, S)).astype(np.float32)
+    lp[:, 0, 0, 0] = -np.inf   # a row with no keys anywhere -> zeros, -inf
+    out, lse = O.combine(op, lp)
+    w = np.exp(lp - np.nanmax(np.where(np.isfinite(lp), lp, np.nan), axis=0, keepdims=True))
+    w = np.nan_to_num(w)
+    ref = (op * np.transpose(w, (0, 1, 3, 2))[..., None]).sum(0) / np.maximum(
+        np.transpose(w.sum(0), (0, 2, 1))[..., None], 1e-30)
+    assert np.allclose(out, ref, atol=1e-5)
+    assert out[0, 0, 0].tolist() == [0.0] * D and lse[0, 0, 0] == -np.inf
