@@ -67,31 +67,43 @@ def _traffic(key):
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle-reason samples during the timed region."""
+    """nvidia-smi clock / throttle-reason samples; only samples taken between mark_start() and
+    mark_stop() (the timed region) are summarised."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index):
-        self.index, self.proc, self.lines = index, None, []
+    def __init__(self, index, period_ms=50):
+        self.index, self.period, self.proc, self.lines = index, period_ms, None, []
+        self.t_start = self.t_stop = None
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", str(self.period)],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            t0 = time.time()
+            while not self.lines and time.time() - t0 < 5.0:   # sampler is live before timing starts
+                time.sleep(0.02)
         except Exception:
             self.proc = None
         return self
 
     def _read(self):
         for ln in self.proc.stdout:
-            self.lines.append(ln.strip())
+            self.lines.append((time.time(), ln.strip()))
+
+    def mark_start(self):
+        self.t_start = time.time()
+
+    def mark_stop(self):
+        self.t_stop = time.time()
 
     def __exit__(self, *a):
         if self.proc is not None:
+            time.sleep(2 * self.period / 1000.0)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -101,7 +113,9 @@ class ClockSampler:
     def summary(self):
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ts, ln in self.lines:
+            if self.t_start is not None and not (self.t_start <= ts <= (self.t_stop or ts)):
+                continue
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
@@ -181,14 +195,15 @@ def bench_fwd_dense(args, ws, rank, dev):
     def step():
         _C.fwd(qh, kh, vh, scale, False, -1, -1, 0.0, None, 0.0, 0, 0, out)
 
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    _barrier(ws)
-    l0 = _C.kernel_launch_count()
     evs = [_events() for _ in range(args.steps)]
     with ClockSampler(dev.index if dev.index is not None else 0) as clk:
+        for _ in range(args.warmup):
+            step()
         torch.cuda.synchronize()
+        _barrier(ws)
+        torch.cuda.synchronize()
+        l0 = _C.kernel_launch_count()
+        clk.mark_start()
         t_start, t_end = _events()
         t_start.record()
         for e0, e1 in evs:
@@ -197,7 +212,9 @@ def bench_fwd_dense(args, ws, rank, dev):
             e1.record()
         t_end.record()
         torch.cuda.synchronize()
-    launches = _C.kernel_launch_count() - l0
+        clk.mark_stop()
+        launches = _C.kernel_launch_count() - l0
+        _barrier(ws)
     total_ms = t_start.elapsed_time(t_end)
     kern_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
     total_ms = _max_over_ranks(total_ms, ws, dev)
@@ -226,7 +243,7 @@ def bench_fwd_dense(args, ws, rank, dev):
     _barrier(ws)
     a, b = _events()
     a.record()
-    n_e2e = max(3, args.steps // 2)
+    n_e2e = max(3, min(20, args.steps // 2))
     for _ in range(n_e2e):
         e2e_step()
     b.record()
@@ -321,8 +338,8 @@ def _max_over_ranks(x, ws, dev):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
-    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-extra", action="store_true", help="skip the config 3/4 figures")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)

@@ -172,7 +172,10 @@ __global__ void __launch_bounds__(DEC_THREADS) dec_partial_kernel(const FaDecPar
   const int shift = __ffs(p.page) - 1, pmask = p.page - 1;
   const T* Kc = (const T*)p.Kc;
   const T* Vc = (const T*)p.Vc;
-  for (int base = start + rg; base < end; base += NRG * U) {
+  // the trip count is the same for every lane of the CTA (the shuffles below are full-warp);
+  // positions past the split end are simply invisible
+  for (int base0 = start; base0 < end; base0 += NRG * U) {
+    const int base = base0 + rg;
     float kf[U][8], vf[U][8];
     bool vis[U];
 #pragma unroll

@@ -34,23 +34,24 @@ __device__ int g_fwd_error = 0;       // non-zero after a pipeline wait timed ou
 
 template <int D>
 struct Cfg {
-  static constexpr int NS = (D <= 64) ? 4 : 2;                 // K/V ring depth
+  static constexpr int NSK = (D <= 64) ? 4 : 3;                // K ring depth (freed after S)
+  static constexpr int NSV = (D <= 64) ? 4 : 2;                // V ring depth (freed after PV)
   static constexpr int NCH = D / 64;                           // 64-column (128-byte) chunks per row
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int KV_BYTES = BN * D * 2;                  // one K (or V) tile
   static constexpr int CH_BYTES = BN * 128;                    // one 64-column chunk of a tile
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = Q_BYTES;
-  static constexpr int OFF_V = OFF_K + NS * KV_BYTES;
-  static constexpr int OFF_BAR = OFF_V + NS * KV_BYTES;
+  static constexpr int OFF_V = OFF_K + NSK * KV_BYTES;
+  static constexpr int OFF_BAR = OFF_V + NSV * KV_BYTES;
   static constexpr int SMEM = OFF_BAR + 256 + 1024;            // barriers + alignment slack
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t O_COL = 256;
 };
 
-struct Bars {   // mbarrier offsets inside the barrier block (8 bytes each)
-  static constexpr int Q_FULL = 0, K_FULL = 8, V_FULL = 48, KV_EMPTY = 88, S_FULL = 128, P_FULL = 144,
-                       O_DONE = 160, TMEM_ADDR = 168;
+struct Bars {   // mbarrier offsets inside the barrier block (8 bytes each; rings of up to 4)
+  static constexpr int Q_FULL = 0, K_FULL = 8, K_EMPTY = 40, V_FULL = 72, V_EMPTY = 104, S_FULL = 136,
+                       P_FULL = 152, O_DONE = 168, MMA_DRAIN = 176, TMEM_ADDR = 184;
 };
 
 __device__ __forceinline__ void record_error(int code) { atomicOr(&g_fwd_error, code); }
@@ -98,16 +99,20 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   // ---- set-up: barriers (thread 0), TMEM (warp 5)
   if (tid == 0) {
     mbar_init(bar + Bars::Q_FULL, 1);
-    for (int s = 0; s < C::NS; ++s) {
+    for (int s = 0; s < C::NSK; ++s) {
       mbar_init(bar + Bars::K_FULL + 8 * s, 1);
+      mbar_init(bar + Bars::K_EMPTY + 8 * s, 1);
+    }
+    for (int s = 0; s < C::NSV; ++s) {
       mbar_init(bar + Bars::V_FULL + 8 * s, 1);
-      mbar_init(bar + Bars::KV_EMPTY + 8 * s, 1);
+      mbar_init(bar + Bars::V_EMPTY + 8 * s, 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(bar + Bars::S_FULL + 8 * s, 1);
       mbar_init(bar + Bars::P_FULL + 8 * s, BM);
     }
     mbar_init(bar + Bars::O_DONE, 1);
+    mbar_init(bar + Bars::MMA_DRAIN, 1);
     fence_barrier_init();
   }
   if (warp == 5) {
@@ -131,28 +136,32 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       for (int c = 0; c < C::NCH; ++c)
         tma_load_4d(sQ + c * (BM * 128), &tmQ, c * 64, qtok0 + qb, h, bcoord, bar + Bars::Q_FULL);
       for (int j = 0; j < ntiles; ++j) {
-        const int s = j % C::NS;
-        if (j >= C::NS && !mbar_wait(bar + Bars::KV_EMPTY + 8 * s, ((j / C::NS) - 1) & 1)) {
+        const int krow = ktok0 + (t0 + j) * BN;
+        const int sk = j % C::NSK, sv = j % C::NSV;
+        if (j >= C::NSK && !mbar_wait(bar + Bars::K_EMPTY + 8 * sk, ((j / C::NSK) - 1) & 1)) {
           record_error(1);
           break;
         }
-        const int krow = ktok0 + (t0 + j) * BN;
-        mbar_expect_tx(bar + Bars::K_FULL + 8 * s, C::KV_BYTES);
+        mbar_expect_tx(bar + Bars::K_FULL + 8 * sk, C::KV_BYTES);
         for (int c = 0; c < C::NCH; ++c)
-          tma_load_4d(sK + s * C::KV_BYTES + c * C::CH_BYTES, &tmK, c * 64, krow, kvh, bcoord,
-                      bar + Bars::K_FULL + 8 * s);
-        mbar_expect_tx(bar + Bars::V_FULL + 8 * s, C::KV_BYTES);
+          tma_load_4d(sK + sk * C::KV_BYTES + c * C::CH_BYTES, &tmK, c * 64, krow, kvh, bcoord,
+                      bar + Bars::K_FULL + 8 * sk);
+        if (j >= C::NSV && !mbar_wait(bar + Bars::V_EMPTY + 8 * sv, ((j / C::NSV) - 1) & 1)) {
+          record_error(1);
+          break;
+        }
+        mbar_expect_tx(bar + Bars::V_FULL + 8 * sv, C::KV_BYTES);
         for (int c = 0; c < C::NCH; ++c)
-          tma_load_4d(sV + s * C::KV_BYTES + c * C::CH_BYTES, &tmV, c * 64, krow, kvh, bcoord,
-                      bar + Bars::V_FULL + 8 * s);
+          tma_load_4d(sV + sv * C::KV_BYTES + c * C::CH_BYTES, &tmV, c * 64, krow, kvh, bcoord,
+                      bar + Bars::V_FULL + 8 * sv);
       }
       // do not leave while copies of this CTA are still landing in shared memory
-      for (int j = max(0, ntiles - C::NS); j < ntiles; ++j) {
-        const int s = j % C::NS;
-        mbar_wait(bar + Bars::K_FULL + 8 * s, (j / C::NS) & 1);
-        mbar_wait(bar + Bars::V_FULL + 8 * s, (j / C::NS) & 1);
-      }
+      for (int j = max(0, ntiles - C::NSK); j < ntiles; ++j)
+        mbar_wait(bar + Bars::K_FULL + 8 * (j % C::NSK), (j / C::NSK) & 1);
+      for (int j = max(0, ntiles - C::NSV); j < ntiles; ++j)
+        mbar_wait(bar + Bars::V_FULL + 8 * (j % C::NSV), (j / C::NSV) & 1);
     }
+    __syncwarp();
   } else if (warp == 5) {
     // ======================= MMA issuer (whole warp follows; lane 0 issues)
     constexpr uint32_t IDESC_S = idesc_f16(BF16 ? 1 : 0, BM, BN, 0, 0);
@@ -160,9 +169,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     bool ok = ntiles == 0 || mbar_wait_warp(bar + Bars::Q_FULL, 0);
     if (!ok) record_error(2);
     auto issue_pv = [&](int i) -> bool {
-      const int s = i % C::NS;
+      const int s = i % C::NSV;
       if (!mbar_wait_warp(bar + Bars::P_FULL + 8 * (i & 1), (i >> 1) & 1)) return false;
-      if (!mbar_wait_warp(bar + Bars::V_FULL + 8 * s, (i / C::NS) & 1)) return false;
+      if (!mbar_wait_warp(bar + Bars::V_FULL + 8 * s, (i / C::NSV) & 1)) return false;
       const int kb = (t0 + i) * BN;
       if (varlen && kb + BN > SK) {
         // rows past the sequence end belong to other sequences (or are unused): zero them so
@@ -187,15 +196,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           const uint64_t bd = sdesc_sw128(vbase + kk * 16 * 128, C::CH_BYTES, 1024);
           mma_ts(tmem + C::O_COL, pt + kk * 8, bd, IDESC_O, (i > 0 || kk > 0) ? 1u : 0u);
         }
-        mma_commit(bar + Bars::KV_EMPTY + 8 * s);
+        mma_commit(bar + Bars::V_EMPTY + 8 * s);
         mma_commit(bar + Bars::O_DONE);
       }
       __syncwarp();
       return true;
     };
     for (int j = 0; ok && j < ntiles; ++j) {
-      const int s = j % C::NS;
-      if (!mbar_wait_warp(bar + Bars::K_FULL + 8 * s, (j / C::NS) & 1)) { ok = false; break; }
+      const int s = j % C::NSK;
+      if (!mbar_wait_warp(bar + Bars::K_FULL + 8 * s, (j / C::NSK) & 1)) { ok = false; break; }
       tc_fence_after();
       if (lane == 0) {
         const uint32_t st = tmem + (uint32_t)(j & 1) * 128u;
@@ -207,12 +216,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           mma_ss(st, ad, bd, IDESC_S, kk > 0 ? 1u : 0u);
         }
         mma_commit(bar + Bars::S_FULL + 8 * (j & 1));
+        mma_commit(bar + Bars::K_EMPTY + 8 * s);
       }
       __syncwarp();
       if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
     }
     if (ok && ntiles > 0 && !issue_pv(ntiles - 1)) ok = false;
     if (!ok) record_error(4);
+    // every MMA this warp issued has completed before TMEM can be released (also on error paths)
+    if (lane == 0) mma_commit(bar + Bars::MMA_DRAIN);
+    __syncwarp();
+    if (!mbar_wait_warp(bar + Bars::MMA_DRAIN, 0)) record_error(32);
   } else {
     // ======================= softmax + epilogue (warps 0-3, thread = query row)
     const int r = tid, q = qb + r;
@@ -269,28 +283,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         for (int c = 0; c < BN; ++c) tmax = fmaxf(tmax, s[c]);
         tmax = (tmax == -INFINITY) ? -INFINITY : tmax * scale2;
       }
-      // ---- lazy online-softmax update; the O rescale is done by whole warps (tcgen05.ld/st are
-      //      warp-collective), rows that do not move keep a factor of 1
+      // ---- lazy online-softmax update: the reference max moves only when it grows by > 2^8
       const bool move = tmax > m_ref + LAZY_THRESH || (m_ref == -INFINITY && tmax != -INFINITY);
       float corr = 1.f;
       if (move) {
         corr = ex2(m_ref - tmax);   // 0 when the row had no visible key yet (its O row is 0)
         l *= corr;
         m_ref = tmax;
-      }
-      if (j > 0 && __any_sync(0xffffffffu, move && corr != 1.f)) {
-        if (!mbar_wait_warp(bar + Bars::O_DONE, (j - 1) & 1)) { ok = false; break; }
-        tc_fence_after();
-#pragma unroll
-        for (int c = 0; c < D; c += 32) {
-          float o[32];
-          tmem_ld32(lane_addr + C::O_COL + c, o);
-          tc_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] *= corr;
-          tmem_st32(lane_addr + C::O_COL + c, reinterpret_cast<const uint32_t*>(o));
-        }
-        tc_wait_st();
       }
       const float muse = (m_ref == -INFINITY) ? 0.f : m_ref;
       const float sc = FEAT ? 1.f : scale2;
@@ -319,6 +318,24 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           }
         }
         tmem_st16(sa + c0 / 2, pk);
+      }
+      // ---- O rescale.  Every tile j >= 1 waits exactly once for PV_{j-1} (so the parity wait
+      //      can never alias an older phase); PV_{j-1} normally finished while P_j was computed.
+      //      tcgen05.ld/st are warp-collective: rows that did not move scale by 1.
+      if (j > 0) {
+        if (!mbar_wait_warp(bar + Bars::O_DONE, (j - 1) & 1)) { ok = false; break; }
+        if (__any_sync(0xffffffffu, corr != 1.f)) {
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < D; c += 32) {
+            float o[32];
+            tmem_ld32(lane_addr + C::O_COL + c, o);
+            tc_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] *= corr;
+            tmem_st32(lane_addr + C::O_COL + c, reinterpret_cast<const uint32_t*>(o));
+          }
+        }
       }
       l += lsum;
       tc_wait_st();

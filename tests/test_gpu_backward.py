@@ -79,6 +79,8 @@ def _run_case(case, dt):
     A.check(A.lib().fable_attn_backward_launch(C.byref(p), A.DT[dt], stream()))
     torch.cuda.synchronize()
     refs = O.backward(qn, kn, vn, don, scale, causal, wl, wr, sc, slopes, pd, seed)
+    # the parameter block holds raw pointers: keep every tensor it names alive with it
+    p._keep = (q, k, v, o, do, lse, dsum, al_t, dq, dk, dv)
     return p, (dq, dk, dv), refs
 
 

@@ -102,6 +102,7 @@ def _setup(case, dt, nsplit=0, batch=2):
     p.num_blocks, p.err_flag = nblocks, A.ptr(err)
     ref = O.decode(qn, kcn, vcn, bt, ctxs, nkn, nvn, cos if rotary else None, sin if rotary else None, rotary, 0,
                    None, lp, slopes, window, HD ** -0.5, sc)
+    keep["scratch"] = scratch   # the parameter block holds raw pointers: keep them alive
     return dict(p=p, keep=keep, q=q, kc=kc, vc=vc, nk=nk, nv=nv, o=o, lse=lse, err=err, ref=ref, bt=bt, ctxs=ctxs,
                 nkn=nkn, nvn=nvn, kcn=kcn, vcn=vcn)
 
