@@ -335,6 +335,24 @@ def _max_over_ranks(x, ws, dev):
     return float(t.item())
 
 
+def profile_case(which, dev):
+    """Reduced cases for ncu captures (inputs still larger than L2): three launches of one kernel."""
+    from fable_attn import _C
+    if which == "fwd":   # dense bf16 forward, B1 S16384 H16 D128 (192 MiB of q/k/v)
+        g = torch.Generator(device=dev).manual_seed(1)
+        q, k, v = (torch.randn(1, 16384, 16, 128, device=dev, dtype=torch.bfloat16, generator=g).transpose(1, 2)
+                   for _ in range(3))
+        for _ in range(3):
+            _C.fwd(q, k, v, 128 ** -0.5, False, -1, -1, 0.0, None, 0.0, 0, 0, None)
+    elif which == "decode":
+        for _ in range(1):
+            bench_decode(dev, steps=3, warmup=0)
+    elif which == "bwd":
+        bench_fwd_bwd_causal(dev, steps=1, warmup=0)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile": which, "ok": True}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -343,7 +361,11 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-extra", action="store_true", help="skip the config 3/4 figures")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
+    ap.add_argument("--profile", choices=["fwd", "decode", "bwd"], help="run one reduced case for ncu and exit")
     args = ap.parse_args()
+    if args.profile:
+        profile_case(args.profile, torch.device("cuda", 0))
+        return
     args.warmup = max(args.warmup, 3)
     ws, rank, local = _dist()
     config = {"workload": "dense non-causal forward B1 S16384 H32 D128 bf16 (BASELINE configs[1])",
