@@ -402,3 +402,44 @@ int combine_run(const FaCombineParams& p, cudaStream_t st) {
   return combine_out<float>(p, st);
 }
 }  // namespace fa
+
+// ---------------------------------------------------------------- decode without allocation
+// Split-K scratch for fa_decode_launch_noalloc: a fixed device array (16 MiB) owned by the
+// library, so callers that cannot allocate device memory can still decode.  Device code could
+// name it directly; host code only holds a stand-in symbol, so the launcher passes the real
+// device address, looked up once per device with that device current.
+static __device__ __align__(256) float g_noalloc_scratch[FA_DECODE_NOALLOC_MAX_SCRATCH_FLOATS];
+
+extern "C" FA_API int fa_decode_launch_noalloc(const FaDecParams* pp, int dtype, void* stream, const void* new_k,
+                                               const void* new_v) {
+  if (!pp) {
+    fa::set_error("decode (no-alloc): null parameter block");
+    return FA_ERR_INVALID;
+  }
+  if (pp->struct_size != sizeof(FaDecParams)) {
+    fa::set_error("decode (no-alloc): struct_size %u != %zu", pp->struct_size, sizeof(FaDecParams));
+    return FA_ERR_ABI;
+  }
+  FaDecParams p = *pp;
+  const long long need = fa_decode_scratch_floats(p.batch, p.nq < 1 ? 1 : p.nq, p.NH, p.HD, p.nsplit);
+  if (need > FA_DECODE_NOALLOC_MAX_SCRATCH_FLOATS || need < 0) {
+    fa::set_error("decode (no-alloc): needs %lld scratch floats for batch=%d nq=%d NH=%d HD=%d nsplit=%d, above the "
+                  "fixed maximum %lld; lower nsplit", need, p.batch, p.nq, p.NH, p.HD, p.nsplit,
+                  (long long)FA_DECODE_NOALLOC_MAX_SCRATCH_FLOATS);
+    return FA_ERR_SIZE;
+  }
+  static float* dev_ptr[64] = {nullptr};
+  const int d = fa::current_device();
+  if (d < 0 || d >= 64) {
+    fa::set_error("decode (no-alloc): device ordinal %d out of range", d);
+    return FA_ERR_INVALID;
+  }
+  if (!dev_ptr[d]) {
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) return fa::cuda_status(e, "decode (no-alloc): cudaGetSymbolAddress");
+    dev_ptr[d] = (float*)ptr;
+  }
+  p.scratch = dev_ptr[d];
+  return fa_decode_launch(&p, dtype, stream, new_k, new_v);
+}

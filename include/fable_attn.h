@@ -170,6 +170,33 @@ typedef struct FaDecParams {
 FA_API int fa_decode_launch(const FaDecParams* p, int dtype, void* stream,
                      const void* new_k, const void* new_v);
 
+/* ------------------------------------------------------------------------------------------
+ * fa_decode_launch_noalloc — the same decode, for callers that cannot allocate device memory at
+ * call time.  No counterpart in the reference: its decode always allocates its split-K scratch
+ * through torch (package/csrc/dispatch.cpp:203).
+ *
+ * Who needs it: hosts that bind only this C ABI from another runtime (a Go, Java or Rust serving
+ * process with no CUDA allocator of its own), processes whose device memory is reserved up front
+ * by a pool (a KV-cache manager or caching allocator holding most of HBM, where one more
+ * cudaMalloc can fail), and decode loops that cannot afford cudaMalloc/cudaFree in the step
+ * (cudaFree synchronises the device).  The caller still passes every input and output; only the
+ * split-K scratch is taken from a fixed device array of FA_DECODE_NOALLOC_MAX_SCRATCH_FLOATS
+ * floats (16 MiB) inside the library, which every GPU that loads the library holds until exit.
+ *   - p->scratch is ignored (may be null).  Requests needing more scratch than the array holds
+ *     (fa_decode_scratch_floats(batch, nq, NH, HD, nsplit) > the maximum) are refused with
+ *     FA_ERR_SIZE before any work; lower nsplit to fit.
+ *   - The first call on each device looks up the array's device address (cudaGetSymbolAddress,
+ *     with that device current) and caches it; make that first call before any stream capture.
+ *   - No allocation of any kind: no cudaMalloc/cudaFree, no library allocator.
+ *   - All calls share the one array and it keeps the last call's contents.  Nothing in it needs
+ *     to start at zero (every split writes its whole slot before the merge reads it), but calls
+ *     whose kernels overlap on the GPU (different streams, or several host threads) race on it:
+ *     serialise them on one stream.
+ * -------------------------------------------------------------------------------------------*/
+#define FA_DECODE_NOALLOC_MAX_SCRATCH_FLOATS (4LL << 20)
+FA_API int fa_decode_launch_noalloc(const FaDecParams* p, int dtype, void* stream, const void* new_k,
+                                    const void* new_v);
+
 /* Default split count: enough CTAs to fill the GPU, each split at least 256 positions, at most
  * 512 splits; num_splits > 0 is taken as given (clamped to [1, 512]). */
 FA_API int fa_decode_num_splits(int batch, int nq, int nheads_kv, long long ctx_bound, int num_splits);
