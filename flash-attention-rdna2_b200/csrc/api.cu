@@ -124,6 +124,9 @@ extern "C" int fable_attn_backward_launch(const FaBwdParams* pp, int dtype, void
   }
   if (p.cu_q) FA_CHECK_ARG(p.lse_total_q > 0, "backward: varlen needs lse_total_q");
   if (p.B == 0 || p.SQ == 0 || p.SK == 0) return FA_OK;
+  bool taken = false;
+  const int rc = fa::bwd_sm100(p, dtype, (cudaStream_t)stream, &taken);
+  if (taken || rc) return rc;
   return fa::bwd_simt(p, dtype, (cudaStream_t)stream);
 }
 

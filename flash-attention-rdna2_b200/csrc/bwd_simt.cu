@@ -317,6 +317,14 @@ int launch_t(const FaBwdParams& p, cudaStream_t st) {
 }  // namespace
 
 namespace fa {
+int bwd_dsum(const FaBwdParams& p, int dtype, cudaStream_t st) {
+  const dim3 grid((p.SQ + 7) / 8, p.Hq, p.B);
+  if (dtype == FA_DTYPE_F16) bwd_pre_kernel<__half><<<grid, 256, 0, st>>>(p);
+  else if (dtype == FA_DTYPE_BF16) bwd_pre_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(p);
+  else bwd_pre_kernel<float><<<grid, 256, 0, st>>>(p);
+  count_launch();
+  return cuda_status(cudaGetLastError(), "bwd dsum launch");
+}
 int bwd_simt(const FaBwdParams& p, int dtype, cudaStream_t st) {
   if (dtype == FA_DTYPE_F16) return launch_t<__half>(p, st);
   if (dtype == FA_DTYPE_BF16) return launch_t<__nv_bfloat16>(p, st);

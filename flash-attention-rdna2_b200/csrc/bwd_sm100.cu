@@ -1,0 +1,662 @@
+// bwd_sm100.cu — exact attention backward on the Blackwell tensor cores (tcgen05 + TMEM + TMA),
+// deterministic: no atomics, every output element is produced by exactly one CTA in a fixed
+// order (the decomposition of the reference, kernels/backward.hip:86-387).
+//
+//   dq kernel   : one CTA per 128-row query tile; loops over 64-key tiles
+//                 S = Q K^T, dP = dO V^T (SS MMAs into TMEM, double-buffered);
+//                 softmax warps (thread = query row) form dS = P (Z dP - dsum) (1 - tanh^2);
+//                 dQ += dS K (TS MMA, dS read from TMEM).
+//   dkdv kernel : one CTA per 128-key tile of one kv head; loops over every query head of the
+//                 group and every 64-row query tile that can see the keys
+//                 S^T = K Q^T, dP^T = V dO^T (SS), thread = key row forms P~^T = Z P^T and dS^T;
+//                 dV += P~^T dO, dK += dS^T Q (TS).
+// dS feeds its MMAs as a pair of 16-bit numbers hi + lo (lo = dS - hi), two MMAs each, so the
+// 16-bit rounding of dS does not reach dQ/dK; P~ goes in as one 16-bit number.  The preprocess
+// dsum = rowsum(O*dO) is the CUDA-core kernel of bwd_simt.cu.  Every mbarrier wait is bounded.
+#include <cudaTypedefs.h>
+#include "fa_common.cuh"
+#include "fa_launch.h"
+#include "sm100_ptx.cuh"
+
+namespace {
+
+using namespace sm100;
+
+constexpr int NTHREADS = 192;        // warps 0-3 elementwise, 4 TMA, 5 MMA
+__device__ int g_bwd_error = 0;
+__device__ __forceinline__ void record_error(int code) { atomicOr(&g_bwd_error, code); }
+
+// named barrier 1 over the 128 elementwise threads, AND-reducing a predicate (uniform break)
+__device__ __forceinline__ bool bar_and_128(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\t"
+      "setp.ne.u32 pi, %1, 0;\n\t"
+      "bar.red.and.pred po, 1, 128, pi;\n\t"
+      "selp.u32 %0, 1, 0, po;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v)
+      : "memory");
+  return r != 0;
+}
+
+// 16-bit pair packing
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  if constexpr (BF16) {
+    const __nv_bfloat162 t = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&t);
+  } else {
+    const __half2 t = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&t);
+  }
+}
+template <bool BF16>
+__device__ __forceinline__ float round16(float a) {
+  if constexpr (BF16) return __bfloat162float(__float2bfloat16_rn(a));
+  else return __half2float(__float2half_rn(a));
+}
+
+// logit and softcap derivative of one raw score (natural units)
+__device__ __forceinline__ void logit_of(float raw, float scale, float softcap, float& logit, float& deriv) {
+  const float g0 = raw * scale;
+  if (softcap > 0.f) {
+    const float tn = tanhf(g0 / softcap);
+    logit = softcap * tn;
+    deriv = 1.f - tn * tn;
+  } else {
+    logit = g0;
+    deriv = 1.f;
+  }
+}
+
+// K-major / MN-major descriptors of a [rows][D] tile stored as D/64 chunks of rows x 128 B
+// (TMA SWIZZLE_128B boxes).  kstep = 16-element step along the contracted dimension.
+__device__ __forceinline__ uint64_t desc_kmajor(uint32_t tile, int rows, int kstep) {
+  const int c = kstep / 4, off = (kstep % 4) * 32;
+  return sdesc_sw128(tile + c * rows * 128 + off, 16, 1024);
+}
+__device__ __forceinline__ uint64_t desc_mnmajor(uint32_t tile, int rows, int kstep) {
+  // contracted dim = rows: 16 rows per step; the D (N) dim spans chunks rows*128 bytes apart
+  return sdesc_sw128(tile + kstep * 16 * 128, rows * 128, 1024);
+}
+
+// =====================================================================================
+// dQ kernel
+// =====================================================================================
+template <int D>
+struct DqCfg {
+  static constexpr int BM = 128, BN = 64, NS = 4, NCH = D / 64;
+  static constexpr int Q_BYTES = BM * D * 2, KV_BYTES = BN * D * 2;
+  static constexpr int OFF_Q = 0, OFF_DO = Q_BYTES, OFF_K = 2 * Q_BYTES, OFF_V = OFF_K + NS * KV_BYTES;
+  static constexpr int OFF_BAR = OFF_V + NS * KV_BYTES;
+  static constexpr int SMEM = OFF_BAR + 256 + 1024;
+  // TMEM columns: S[2] at 0/64, dP[2] at 128/192, dQ at 256
+  static constexpr uint32_t S_COL = 0, DP_COL = 128, DQ_COL = 256;
+};
+struct DqBars {
+  static constexpr int Q_FULL = 0, K_FULL = 8, K_EMPTY = 40, V_FULL = 72, V_EMPTY = 104, SP_FULL = 136,
+                       DS_FULL = 152, DQ_DONE = 168, DRAIN = 176, TMEM_ADDR = 184;
+};
+
+template <int D, bool BF16, bool FEAT>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
+                     const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                     const FaBwdParams p) {
+  using C = DqCfg<D>;
+  using Bz = DqBars;
+  constexpr int BM = C::BM, BN = C::BN;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  uint8_t* sgen = smem_raw + (sbase - smem_u32(smem_raw));
+  const uint32_t sQ = sbase + C::OFF_Q, sDO = sbase + C::OFF_DO, sK = sbase + C::OFF_K, sV = sbase + C::OFF_V;
+  const uint32_t bar = sbase + C::OFF_BAR;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sgen + C::OFF_BAR + Bz::TMEM_ADDR);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int z = blockIdx.z, h = blockIdx.y, kvh = h / p.gqa;
+  const int SQ = p.SQ, SK = p.SK;
+  const int qb = (gridDim.x - 1 - blockIdx.x) * BM;
+  if (qb >= SQ) return;
+
+  int klo, khi, dmy;
+  fa_key_range(qb, SQ, SK, p.causal, p.win_left, p.win_right, 0, klo, dmy);
+  fa_key_range(min(qb + BM, SQ) - 1, SQ, SK, p.causal, p.win_left, p.win_right, 0, dmy, khi);
+  klo = max(klo, 0);
+  khi = min(khi, SK - 1);
+  const int t0 = klo / BN;
+  const int ntiles = (khi >= klo) ? (khi / BN - t0 + 1) : 0;
+
+  if (tid == 0) {
+    mbar_init(bar + Bz::Q_FULL, 1);
+    for (int s = 0; s < C::NS; ++s) {
+      mbar_init(bar + Bz::K_FULL + 8 * s, 1);
+      mbar_init(bar + Bz::K_EMPTY + 8 * s, 1);
+      mbar_init(bar + Bz::V_FULL + 8 * s, 1);
+      mbar_init(bar + Bz::V_EMPTY + 8 * s, 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bar + Bz::SP_FULL + 8 * s, 1);
+      mbar_init(bar + Bz::DS_FULL + 8 * s, BM);
+    }
+    mbar_init(bar + Bz::DQ_DONE, 1);
+    mbar_init(bar + Bz::DRAIN, 1);
+    fence_barrier_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0 && ntiles > 0) {
+      mbar_expect_tx(bar + Bz::Q_FULL, 2 * C::Q_BYTES);
+      for (int c = 0; c < C::NCH; ++c) {
+        tma_load_4d(sQ + c * BM * 128, &tmQ, c * 64, qb, h, z, bar + Bz::Q_FULL);
+        tma_load_4d(sDO + c * BM * 128, &tmDO, c * 64, qb, h, z, bar + Bz::Q_FULL);
+      }
+      for (int j = 0; j < ntiles; ++j) {
+        const int s = j % C::NS, krow = (t0 + j) * BN;
+        if (j >= C::NS && !mbar_wait(bar + Bz::K_EMPTY + 8 * s, ((j / C::NS) - 1) & 1)) { record_error(1); break; }
+        mbar_expect_tx(bar + Bz::K_FULL + 8 * s, C::KV_BYTES);
+        for (int c = 0; c < C::NCH; ++c)
+          tma_load_4d(sK + s * C::KV_BYTES + c * BN * 128, &tmK, c * 64, krow, kvh, z, bar + Bz::K_FULL + 8 * s);
+        if (j >= C::NS && !mbar_wait(bar + Bz::V_EMPTY + 8 * s, ((j / C::NS) - 1) & 1)) { record_error(1); break; }
+        mbar_expect_tx(bar + Bz::V_FULL + 8 * s, C::KV_BYTES);
+        for (int c = 0; c < C::NCH; ++c)
+          tma_load_4d(sV + s * C::KV_BYTES + c * BN * 128, &tmV, c * 64, krow, kvh, z, bar + Bz::V_FULL + 8 * s);
+      }
+      for (int j = max(0, ntiles - C::NS); j < ntiles; ++j) {
+        mbar_wait(bar + Bz::K_FULL + 8 * (j % C::NS), (j / C::NS) & 1);
+        mbar_wait(bar + Bz::V_FULL + 8 * (j % C::NS), (j / C::NS) & 1);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer
+    constexpr uint32_t ID_S = idesc_f16(BF16 ? 1 : 0, BM, BN, 0, 0);   // S, dP: 128 x 64
+    constexpr uint32_t ID_Q = idesc_f16(BF16 ? 1 : 0, BM, D, 0, 1);    // dQ += dS K: 128 x D, K MN-major
+    bool ok = ntiles == 0 || mbar_wait_warp(bar + Bz::Q_FULL, 0);
+    auto issue_dq = [&](int i) -> bool {
+      if (!mbar_wait_warp(bar + Bz::DS_FULL + 8 * (i & 1), (i >> 1) & 1)) return false;
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t kt = sK + (i % C::NS) * C::KV_BYTES;
+        const uint32_t hi = tmem + C::S_COL + (i & 1) * 64, lo = tmem + C::DP_COL + (i & 1) * 64;
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint64_t bd = desc_mnmajor(kt, BN, kk);
+          mma_ts(tmem + C::DQ_COL, hi + kk * 8, bd, ID_Q, (i > 0 || kk > 0) ? 1u : 0u);
+          mma_ts(tmem + C::DQ_COL, lo + kk * 8, bd, ID_Q, 1u);
+        }
+        mma_commit(bar + Bz::K_EMPTY + 8 * (i % C::NS));
+      }
+      __syncwarp();
+      return true;
+    };
+    for (int j = 0; ok && j < ntiles; ++j) {
+      const int s = j % C::NS;
+      if (!mbar_wait_warp(bar + Bz::K_FULL + 8 * s, (j / C::NS) & 1) ||
+          !mbar_wait_warp(bar + Bz::V_FULL + 8 * s, (j / C::NS) & 1)) { ok = false; break; }
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t kt = sK + s * C::KV_BYTES, vt = sV + s * C::KV_BYTES;
+        for (int kk = 0; kk < D / 16; ++kk) {
+          mma_ss(tmem + C::S_COL + (j & 1) * 64, desc_kmajor(sQ, BM, kk), desc_kmajor(kt, BN, kk), ID_S, kk > 0);
+          mma_ss(tmem + C::DP_COL + (j & 1) * 64, desc_kmajor(sDO, BM, kk), desc_kmajor(vt, BN, kk), ID_S, kk > 0);
+        }
+        mma_commit(bar + Bz::SP_FULL + 8 * (j & 1));
+        mma_commit(bar + Bz::V_EMPTY + 8 * s);
+      }
+      __syncwarp();
+      if (j >= 1 && !issue_dq(j - 1)) { ok = false; break; }
+    }
+    if (ok && ntiles > 0 && !issue_dq(ntiles - 1)) ok = false;
+    if (!ok) record_error(2);
+    if (lane == 0) { mma_commit(bar + Bz::DQ_DONE); mma_commit(bar + Bz::DRAIN); }
+    __syncwarp();
+    if (!mbar_wait_warp(bar + Bz::DRAIN, 0)) record_error(4);
+  } else {
+    // ------------------------------------------------------------ elementwise (thread = query row)
+    const int q = qb + tid;
+    const uint32_t la = tmem + ((uint32_t)(warp * 32) << 16);
+    int rlo, rhi;
+    fa_key_range(q, SQ, SK, p.causal, p.win_left, p.win_right, 0, rlo, rhi);
+    float lse2 = 0.f, dsum = 0.f;
+    if (q < SQ) {
+      const long long li = fa_lse_index(false, z, h, p.Hq, SQ, 0, 0, q);
+      lse2 = p.lse[li] * FA_LOG2E;
+      dsum = p.dsum[li];
+      if (!(lse2 > -INFINITY)) { rlo = 1; rhi = 0; }   // row saw no key in the forward
+    } else {
+      rlo = 1; rhi = 0;
+    }
+    const float slope = (FEAT && p.alibi) ? p.alibi[h] : 0.f;
+    const bool drop = FEAT && p.dropout;
+    bool ok = true;
+    for (int j = 0; j < ntiles; ++j) {
+      if (!mbar_wait_warp(bar + Bz::SP_FULL + 8 * (j & 1), (j >> 1) & 1)) { ok = false; break; }
+      tc_fence_after();
+      float s[BN], dp[BN];
+      tmem_ld32(la + C::S_COL + (j & 1) * 64, s);
+      tmem_ld32(la + C::S_COL + (j & 1) * 64 + 32, s + 32);
+      tmem_ld32(la + C::DP_COL + (j & 1) * 64, dp);
+      tmem_ld32(la + C::DP_COL + (j & 1) * 64 + 32, dp + 32);
+      tc_wait_ld();
+      const int kb = (t0 + j) * BN;
+#pragma unroll
+      for (int h32 = 0; h32 < BN; h32 += 32) {   // 16 packed columns per chunk; inputs already in registers
+        uint32_t hi[16], lo[16];
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) {
+          float dsv[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int cc = h32 + c + u, key = kb + cc;
+            float logit, deriv;
+            if constexpr (FEAT) {
+              logit_of(s[cc], p.scale, p.softcap, logit, deriv);
+              logit += slope * (float)(key - q);
+            } else {
+              logit = s[cc] * p.scale;
+              deriv = 1.f;
+            }
+            const float pr = (key >= rlo && key <= rhi) ? ex2(fmaf(logit, FA_LOG2E, -lse2)) : 0.f;
+            float zm = 1.f;
+            if (drop && pr != 0.f)
+              zm = fa_dropout_mul(p.drop_seed, ((unsigned long long)h * SQ + q) * SK + key, p.dropout_p, p.keep_scale);
+            dsv[u] = pr * (zm * dp[cc] - dsum) * deriv;
+          }
+          const float h0 = round16<BF16>(dsv[0]), h1 = round16<BF16>(dsv[1]);
+          hi[c / 2] = pack2<BF16>(h0, h1);
+          lo[c / 2] = pack2<BF16>(dsv[0] - h0, dsv[1] - h1);
+        }
+        tmem_st16(la + C::S_COL + (j & 1) * 64 + h32 / 2, hi);
+        tmem_st16(la + C::DP_COL + (j & 1) * 64 + h32 / 2, lo);
+      }
+      tc_wait_st();
+      tc_fence_before();
+      mbar_arrive(bar + Bz::DS_FULL + 8 * (j & 1));
+    }
+    if (!ok) record_error(8);
+    const bool have = ok && ntiles > 0;
+    if (have && !mbar_wait_warp(bar + Bz::DQ_DONE, 0)) record_error(16);
+    tc_fence_after();
+    using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+    T* qrow = (T*)p.dQ + (long long)z * p.dqs.b + (long long)h * p.dqs.h + (long long)q * p.dqs.s;
+#pragma unroll
+    for (int c = 0; c < D; c += 32) {
+      float o[32];
+      if (have) {
+        tmem_ld32(la + C::DQ_COL + c, o);
+        tc_wait_ld();
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] = 0.f;
+      }
+      if (q < SQ) {
+        uint32_t w[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) w[i] = pack2<BF16>(o[2 * i] * p.scale, o[2 * i + 1] * p.scale);
+        uint4* dst = reinterpret_cast<uint4*>(qrow + c);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// =====================================================================================
+// dK / dV kernel
+// =====================================================================================
+template <int D>
+struct DkvCfg {
+  static constexpr int BK = 128, BQ = 64, NS = 3, NCH = D / 64;
+  static constexpr int KV_BYTES = BK * D * 2, QT_BYTES = BQ * D * 2;
+  static constexpr int OFF_K = 0, OFF_V = KV_BYTES, OFF_Q = 2 * KV_BYTES, OFF_DO = OFF_Q + NS * QT_BYTES;
+  static constexpr int OFF_ST = OFF_DO + NS * QT_BYTES;      // lse2 / dsum per query tile: [2][2][64] f32
+  static constexpr int OFF_BAR = OFF_ST + 2 * 2 * 64 * 4;
+  static constexpr int SMEM = OFF_BAR + 256 + 1024;
+  // TMEM: dV [0,128), dK [128,256), S^T[2] at 256/320, dP^T[2] at 384/448
+  static constexpr uint32_t DV_COL = 0, DK_COL = 128, S_COL = 256, DP_COL = 384;
+};
+struct DkvBars {
+  static constexpr int KV_FULL = 0, Q_FULL = 8, Q_EMPTY = 40, SP_FULL = 72, DS_FULL = 88, DONE = 104,
+                       DRAIN = 112, TMEM_ADDR = 120;
+};
+
+template <int D, bool BF16, bool FEAT>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
+                       const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                       const FaBwdParams p) {
+  using C = DkvCfg<D>;
+  using Bz = DkvBars;
+  constexpr int BK = C::BK, BQ = C::BQ;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  uint8_t* sgen = smem_raw + (sbase - smem_u32(smem_raw));
+  const uint32_t sK = sbase + C::OFF_K, sV = sbase + C::OFF_V, sQ = sbase + C::OFF_Q, sDO = sbase + C::OFF_DO;
+  float* st = reinterpret_cast<float*>(sgen + C::OFF_ST);   // [buf][lse2|dsum][64]
+  const uint32_t bar = sbase + C::OFF_BAR;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sgen + C::OFF_BAR + Bz::TMEM_ADDR);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int z = blockIdx.z, kvh = blockIdx.y;
+  const int SQ = p.SQ, SK = p.SK;
+  const int kb = blockIdx.x * BK;
+  if (kb >= SK) return;
+
+  // query rows that can see a key of [kb, kb+BK): same bounds as the CUDA-core kernel
+  const int delta = SK - SQ, kend = min(kb + BK, SK) - 1;
+  int qstart = 0, qend = SQ - 1;
+  if (p.causal) qstart = max(qstart, kb - delta);
+  if (p.win_right >= 0) qstart = max(qstart, kb - delta - p.win_right);
+  if (p.win_left >= 0) qend = min(qend, kend - delta + p.win_left);
+  const int qt0 = qstart / BQ;
+  const int nqt = (qend >= qstart) ? (qend / BQ - qt0 + 1) : 0;
+  const int niter = nqt * p.gqa;   // (query head of the group, query tile) pairs, head-major
+
+  if (tid == 0) {
+    mbar_init(bar + Bz::KV_FULL, 1);
+    for (int s = 0; s < C::NS; ++s) {
+      mbar_init(bar + Bz::Q_FULL + 8 * s, 1);
+      mbar_init(bar + Bz::Q_EMPTY + 8 * s, 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bar + Bz::SP_FULL + 8 * s, 1);
+      mbar_init(bar + Bz::DS_FULL + 8 * s, BK);
+    }
+    mbar_init(bar + Bz::DONE, 1);
+    mbar_init(bar + Bz::DRAIN, 1);
+    fence_barrier_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    if (lane == 0 && niter > 0) {
+      mbar_expect_tx(bar + Bz::KV_FULL, 2 * C::KV_BYTES);
+      for (int c = 0; c < C::NCH; ++c) {
+        tma_load_4d(sK + c * BK * 128, &tmK, c * 64, kb, kvh, z, bar + Bz::KV_FULL);
+        tma_load_4d(sV + c * BK * 128, &tmV, c * 64, kb, kvh, z, bar + Bz::KV_FULL);
+      }
+      for (int i = 0; i < niter; ++i) {
+        const int s = i % C::NS, h = kvh * p.gqa + i / nqt, qrow = (qt0 + i % nqt) * BQ;
+        if (i >= C::NS && !mbar_wait(bar + Bz::Q_EMPTY + 8 * s, ((i / C::NS) - 1) & 1)) { record_error(1); break; }
+        mbar_expect_tx(bar + Bz::Q_FULL + 8 * s, 2 * C::QT_BYTES);
+        for (int c = 0; c < C::NCH; ++c) {
+          tma_load_4d(sQ + s * C::QT_BYTES + c * BQ * 128, &tmQ, c * 64, qrow, h, z, bar + Bz::Q_FULL + 8 * s);
+          tma_load_4d(sDO + s * C::QT_BYTES + c * BQ * 128, &tmDO, c * 64, qrow, h, z, bar + Bz::Q_FULL + 8 * s);
+        }
+      }
+      for (int i = max(0, niter - C::NS); i < niter; ++i) mbar_wait(bar + Bz::Q_FULL + 8 * (i % C::NS), (i / C::NS) & 1);
+    }
+    __syncwarp();
+  } else if (warp == 5) {
+    constexpr uint32_t ID_S = idesc_f16(BF16 ? 1 : 0, BK, BQ, 0, 0);   // S^T, dP^T: 128 x 64
+    constexpr uint32_t ID_O = idesc_f16(BF16 ? 1 : 0, BK, D, 0, 1);    // dV, dK: 128 x D, B MN-major
+    bool ok = niter == 0 || mbar_wait_warp(bar + Bz::KV_FULL, 0);
+    auto issue_kv = [&](int i) -> bool {
+      if (!mbar_wait_warp(bar + Bz::DS_FULL + 8 * (i & 1), (i >> 1) & 1)) return false;
+      tc_fence_after();
+      if (lane == 0) {
+        const int s = i % C::NS;
+        const uint32_t qt = sQ + s * C::QT_BYTES, dot = sDO + s * C::QT_BYTES;
+        const uint32_t pb = tmem + C::S_COL + (i & 1) * 64;        // P~^T at [0,32), dS^T hi at [32,64)
+        const uint32_t lo = tmem + C::DP_COL + (i & 1) * 64;       // dS^T lo at [0,32)
+        for (int kk = 0; kk < BQ / 16; ++kk) {
+          mma_ts(tmem + C::DV_COL, pb + kk * 8, desc_mnmajor(dot, BQ, kk), ID_O, (i > 0 || kk > 0) ? 1u : 0u);
+          mma_ts(tmem + C::DK_COL, pb + 32 + kk * 8, desc_mnmajor(qt, BQ, kk), ID_O, (i > 0 || kk > 0) ? 1u : 0u);
+          mma_ts(tmem + C::DK_COL, lo + kk * 8, desc_mnmajor(qt, BQ, kk), ID_O, 1u);
+        }
+        mma_commit(bar + Bz::Q_EMPTY + 8 * s);
+      }
+      __syncwarp();
+      return true;
+    };
+    for (int i = 0; ok && i < niter; ++i) {
+      const int s = i % C::NS;
+      if (!mbar_wait_warp(bar + Bz::Q_FULL + 8 * s, (i / C::NS) & 1)) { ok = false; break; }
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t qt = sQ + s * C::QT_BYTES, dot = sDO + s * C::QT_BYTES;
+        for (int kk = 0; kk < D / 16; ++kk) {
+          mma_ss(tmem + C::S_COL + (i & 1) * 64, desc_kmajor(sK, BK, kk), desc_kmajor(qt, BQ, kk), ID_S, kk > 0);
+          mma_ss(tmem + C::DP_COL + (i & 1) * 64, desc_kmajor(sV, BK, kk), desc_kmajor(dot, BQ, kk), ID_S, kk > 0);
+        }
+        mma_commit(bar + Bz::SP_FULL + 8 * (i & 1));
+      }
+      __syncwarp();
+      if (i >= 1 && !issue_kv(i - 1)) { ok = false; break; }
+    }
+    if (ok && niter > 0 && !issue_kv(niter - 1)) ok = false;
+    if (!ok) record_error(32);
+    if (lane == 0) { mma_commit(bar + Bz::DONE); mma_commit(bar + Bz::DRAIN); }
+    __syncwarp();
+    if (!mbar_wait_warp(bar + Bz::DRAIN, 0)) record_error(64);
+  } else {
+    // ------------------------------------------------------------ elementwise (thread = key row)
+    const int key = kb + tid;
+    const uint32_t la = tmem + ((uint32_t)(warp * 32) << 16);
+    const bool drop = FEAT && p.dropout;
+    bool ok = true;
+    for (int i = 0; i < niter; ++i) {
+      const int h = kvh * p.gqa + i / nqt, qbase = (qt0 + i % nqt) * BQ;
+      float* stb = st + (i & 1) * 128;
+      // this tile's lse2 / dsum (threads 0-63 and 64-127); the named barrier publishes them to the
+      // 4 warps and AND-reduces the wait outcome, so a timeout ends every warp at the same point
+      {
+        const int qi = tid & 63, q = qbase + qi;
+        float v = 0.f;
+        if (q < SQ) {
+          const long long li = fa_lse_index(false, z, h, p.Hq, SQ, 0, 0, q);
+          v = (tid < 64) ? p.lse[li] * FA_LOG2E : p.dsum[li];
+        } else if (tid < 64) {
+          v = -INFINITY;
+        }
+        stb[(tid < 64 ? 0 : 64) + qi] = v;
+      }
+      const bool got = mbar_wait_warp(bar + Bz::SP_FULL + 8 * (i & 1), (i >> 1) & 1);
+      if (!bar_and_128(got)) { ok = false; break; }
+      tc_fence_after();
+      float s[BQ], dp[BQ];
+      tmem_ld32(la + C::S_COL + (i & 1) * 64, s);
+      tmem_ld32(la + C::S_COL + (i & 1) * 64 + 32, s + 32);
+      tmem_ld32(la + C::DP_COL + (i & 1) * 64, dp);
+      tmem_ld32(la + C::DP_COL + (i & 1) * 64 + 32, dp + 32);
+      tc_wait_ld();
+      const float slope = (FEAT && p.alibi) ? p.alibi[h] : 0.f;
+#pragma unroll
+      for (int h32 = 0; h32 < BQ; h32 += 32) {   // inputs are all in registers: in-place outputs are safe
+        uint32_t pk[16], hi[16], lo[16];
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) {
+          float pv[2], dsv[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int cc = h32 + c + u, q = qbase + cc;
+            int lo_q, hi_q;
+            fa_key_range(q, SQ, SK, p.causal, p.win_left, p.win_right, 0, lo_q, hi_q);
+            const float l2 = stb[cc];
+            const bool vis = q < SQ && key < SK && key >= lo_q && key <= hi_q && l2 > -INFINITY;
+            float logit, deriv;
+            if constexpr (FEAT) {
+              logit_of(s[cc], p.scale, p.softcap, logit, deriv);
+              logit += slope * (float)(key - q);
+            } else {
+              logit = s[cc] * p.scale;
+              deriv = 1.f;
+            }
+            const float pr = vis ? ex2(fmaf(logit, FA_LOG2E, -l2)) : 0.f;
+            float zm = 1.f;
+            if (drop && pr != 0.f)
+              zm = fa_dropout_mul(p.drop_seed, ((unsigned long long)h * SQ + q) * SK + key, p.dropout_p, p.keep_scale);
+            pv[u] = zm * pr;
+            dsv[u] = pr * (zm * dp[cc] - stb[64 + cc]) * deriv;
+          }
+          pk[c / 2] = pack2<BF16>(pv[0], pv[1]);
+          const float h0 = round16<BF16>(dsv[0]), h1 = round16<BF16>(dsv[1]);
+          hi[c / 2] = pack2<BF16>(h0, h1);
+          lo[c / 2] = pack2<BF16>(dsv[0] - h0, dsv[1] - h1);
+        }
+        tmem_st16(la + C::S_COL + (i & 1) * 64 + h32 / 2, pk);
+        tmem_st16(la + C::S_COL + (i & 1) * 64 + 32 + h32 / 2, hi);
+        tmem_st16(la + C::DP_COL + (i & 1) * 64 + h32 / 2, lo);
+      }
+      tc_wait_st();
+      tc_fence_before();
+      mbar_arrive(bar + Bz::DS_FULL + 8 * (i & 1));
+    }
+    if (!ok) record_error(128);
+    const bool have = ok && niter > 0;
+    if (have && !mbar_wait_warp(bar + Bz::DONE, 0)) record_error(256);
+    tc_fence_after();
+    using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+    T* vrow = (T*)p.dV + (long long)z * p.dvs.b + (long long)kvh * p.dvs.h + (long long)key * p.dvs.s;
+    T* krow = (T*)p.dK + (long long)z * p.dks.b + (long long)kvh * p.dks.h + (long long)key * p.dks.s;
+#pragma unroll
+    for (int part = 0; part < 2; ++part) {
+      const uint32_t col = part == 0 ? C::DV_COL : C::DK_COL;
+      const float mul = part == 0 ? 1.f : p.scale;
+      T* row = part == 0 ? vrow : krow;
+#pragma unroll
+      for (int c = 0; c < D; c += 32) {
+        float o[32];
+        if (have) {
+          tmem_ld32(la + col + c, o);
+          tc_wait_ld();
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = 0.f;
+        }
+        if (key < SK) {
+          uint32_t w[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) w[i] = pack2<BF16>(o[2 * i] * mul, o[2 * i + 1] * mul);
+          uint4* dst = reinterpret_cast<uint4*>(row + c);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 bwd_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (PFN_cuTensorMapEncodeTiled_v12000)ptr;
+  }
+  return fn;
+}
+
+bool map4(CUtensorMap* m, const void* base, bool bf16, long long D, long long S, long long H, long long B,
+          const FaStrides& st, int box_rows) {
+  auto enc = bwd_encode_fn();
+  if (!enc || ((uintptr_t)base) % 16) return false;
+  const long long sb = (B > 1) ? st.b : ((st.s * S > st.h * H ? st.s * S : st.h * H) + 7) / 8 * 8;
+  const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)H, (cuuint64_t)B};
+  const cuuint64_t strides[3] = {(cuuint64_t)st.s * 2, (cuuint64_t)st.h * 2, (cuuint64_t)sb * 2};
+  for (int i = 0; i < 3; ++i)
+    if (strides[i] % 16 || strides[i] >= (1ull << 40)) return false;
+  const cuuint32_t box[4] = {64, (cuuint32_t)box_rows, 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  return enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base),
+             dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool out_ok(const void* ptr, const FaStrides& s, int B) {
+  return ((uintptr_t)ptr) % 16 == 0 && s.s % 8 == 0 && s.h % 8 == 0 && (B <= 1 || s.b % 8 == 0);
+}
+
+template <bool BF16, bool FEAT>
+int launch_all(const FaBwdParams& p, cudaStream_t st, const CUtensorMap* maps) {
+  const CUtensorMap &mq128 = maps[0], &mdo128 = maps[1], &mk64 = maps[2], &mv64 = maps[3];
+  const CUtensorMap &mq64 = maps[4], &mdo64 = maps[5], &mk128 = maps[6], &mv128 = maps[7];
+  using Cq = DqCfg<128>;
+  using Ck = DkvCfg<128>;
+  static unsigned long long done_q = 0, done_k = 0;
+  if (int rc = fa::ensure_smem((const void*)bwd_dq_tc_kernel<128, BF16, FEAT>, Cq::SMEM, &done_q)) return rc;
+  if (int rc = fa::ensure_smem((const void*)bwd_dkdv_tc_kernel<128, BF16, FEAT>, Ck::SMEM, &done_k)) return rc;
+  bwd_dkdv_tc_kernel<128, BF16, FEAT><<<dim3((p.SK + Ck::BK - 1) / Ck::BK, p.Hk, p.B), NTHREADS, Ck::SMEM, st>>>(
+      mq64, mdo64, mk128, mv128, p);
+  bwd_dq_tc_kernel<128, BF16, FEAT><<<dim3((p.SQ + Cq::BM - 1) / Cq::BM, p.Hq, p.B), NTHREADS, Cq::SMEM, st>>>(
+      mq128, mdo128, mk64, mv64, p);
+  fa::count_launch(2);
+  return fa::cuda_status(cudaGetLastError(), "bwd_sm100 launch");
+}
+
+}  // namespace
+
+namespace fa {
+
+// fp16/bf16, dense (no varlen), head_dim 128, 16-byte aligned rows: dsum on the CUDA cores, then
+// the dK/dV and dQ tensor-core kernels.  Anything else: *taken = false.
+int bwd_sm100(const FaBwdParams& p, int dtype, cudaStream_t st, bool* taken) {
+  *taken = false;
+  if (p.D != 128 || p.cu_q != nullptr || dtype == FA_DTYPE_F32) return FA_OK;
+  if (getenv("FABLE_ATTN_DISABLE_TC")) return FA_OK;
+  int dev = current_device(), major = 0, minor = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  if (major != 10 || minor != 0) return FA_OK;
+  const bool bf16 = dtype == FA_DTYPE_BF16;
+  CUtensorMap maps[8];
+  if (!map4(&maps[0], p.Q, bf16, p.D, p.SQ, p.Hq, p.B, p.qs, 128) ||
+      !map4(&maps[1], p.dO, bf16, p.D, p.SQ, p.Hq, p.B, p.dos, 128) ||
+      !map4(&maps[2], p.K, bf16, p.D, p.SK, p.Hk, p.B, p.ks, 64) ||
+      !map4(&maps[3], p.V, bf16, p.D, p.SK, p.Hk, p.B, p.vs, 64) ||
+      !map4(&maps[4], p.Q, bf16, p.D, p.SQ, p.Hq, p.B, p.qs, 64) ||
+      !map4(&maps[5], p.dO, bf16, p.D, p.SQ, p.Hq, p.B, p.dos, 64) ||
+      !map4(&maps[6], p.K, bf16, p.D, p.SK, p.Hk, p.B, p.ks, 128) ||
+      !map4(&maps[7], p.V, bf16, p.D, p.SK, p.Hk, p.B, p.vs, 128))
+    return FA_OK;
+  if (!out_ok(p.dQ, p.dqs, p.B) || !out_ok(p.dK, p.dks, p.B) || !out_ok(p.dV, p.dvs, p.B)) return FA_OK;
+  *taken = true;
+  if (int rc = bwd_dsum(p, dtype, st)) return rc;
+  const bool feat = p.softcap > 0.f || p.alibi != nullptr || p.dropout;
+  if (bf16) return feat ? launch_all<true, true>(p, st, maps) : launch_all<true, false>(p, st, maps);
+  return feat ? launch_all<false, true>(p, st, maps) : launch_all<false, false>(p, st, maps);
+}
+
+int bwd_device_error(int clear) {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_bwd_error, sizeof(int));
+  if (clear) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_bwd_error, &zero, sizeof(int));
+  }
+  return v;
+}
+
+}  // namespace fa

@@ -13,8 +13,10 @@
 // loop has no block-wide synchronisation; the row groups are merged once at the end.  Scores
 // are kept in the log2 domain; the scratch holds (m, l, acc[HD]) per (token, head, split)
 // with m in log2 units.
+#include <cudaTypedefs.h>
 #include "fa_common.cuh"
 #include "fa_launch.h"
+#include "sm100_ptx.cuh"
 
 namespace {
 
@@ -293,8 +295,319 @@ __global__ void dec_merge_kernel(const FaDecParams p) {
     p.lse_out[(long long)row * p.NH + h] = L > 0.f ? M * FA_LN2 + logf(L) : -INFINITY;
 }
 
+
+// ---------------------------------------------------------------- split-K partial, TMA-fed
+// fp16/bf16 caches.  The page slices of K and V of one kv head (rows of HD elements, NKV*HD
+// apart) are streamed by the TMA engine into an NS-stage shared-memory ring, 64 positions per
+// tile, while the 8 warps work on the previous tile in three phases:
+//   A  scores s[g][pos] = q_g . k_pos (row groups of HD/8 lanes, 16-byte smem reads, shuffle sums)
+//   B  per-head online softmax of the tile (warp g owns head g: tile max, rescale factor,
+//      2^(s - m) once per score)
+//   C  O_g += p[g][pos] * V[pos] (thread = head x 8-dim chunk x position group)
+// Positions outside the split are never read, so stale or unloaded rows cannot leak in.
+constexpr int DEC_TILE = 64;
+
+template <int HD>
+struct DecTmaCfg {
+  static constexpr int NS = (HD <= 128) ? 4 : 3;
+  static constexpr int ROW = HD * 2;                     // bytes per cached row (2-byte types)
+  static constexpr int TILE = DEC_TILE * ROW;            // one K (or V) tile
+  static constexpr int STAGE = 2 * TILE;
+  static constexpr int OFF_S = NS * STAGE;               // scores     [8][64] f32
+  static constexpr int OFF_P = OFF_S + 8 * 64 * 4;       // 2^(s - m)  [8][64] f32
+  static constexpr int OFF_Q = OFF_P + 8 * 64 * 4;       // q          [8][HD] f32
+  static constexpr int OFF_C = OFF_Q + 8 * HD * 4;       // rescale    [8] f32
+  static constexpr int OFF_BAR = OFF_C + 64;
+  static constexpr int SMEM = OFF_BAR + 8 * NS + 256;    // + alignment slack
+};
+
+template <typename T>
+__device__ __forceinline__ void cvt8(const uint4& r, float* f) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) { f[2 * i] = __uint_as_float(w[i] << 16); f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u); }
+  } else {
+    const __half2* h = reinterpret_cast<const __half2*>(&r);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) { const float2 v = __half22float2(h[i]); f[2 * i] = v.x; f[2 * i + 1] = v.y; }
+  }
+}
+
+__device__ int g_dec_error = 0;
+
+template <typename T, int HD, int G>
+__global__ void __launch_bounds__(DEC_THREADS, 1)
+    dec_tma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                   const FaDecParams p, int groups) {
+  using C = DecTmaCfg<HD>;
+  constexpr int LPR = (HD / 8 <= 2) ? 2 : (HD / 8 <= 4) ? 4 : (HD / 8 <= 8) ? 8 : (HD / 8 <= 16) ? 16 : 32;
+  constexpr int RPW = 32 / LPR, NRG = (DEC_THREADS / 32) * RPW;
+  constexpr int D8 = HD / 8, TPH = DEC_THREADS / G, NPG = TPH / D8;   // PV: threads per head, position groups
+  extern __shared__ uint8_t dsm_raw[];
+  const uint32_t sbase = (sm100::smem_u32(dsm_raw) + 127u) & ~127u;
+  uint8_t* sg = dsm_raw + (sbase - sm100::smem_u32(dsm_raw));
+  float* s_sc = reinterpret_cast<float*>(sg + C::OFF_S);
+  float* s_p = reinterpret_cast<float*>(sg + C::OFF_P);
+  float* s_q = reinterpret_cast<float*>(sg + C::OFF_Q);
+  float* s_corr = reinterpret_cast<float*>(sg + C::OFF_C);
+  const uint32_t bar0 = sbase + C::OFF_BAR;
+
+  const int bx = blockIdx.x, kvh = blockIdx.y / groups, grp = blockIdx.y % groups, sp = blockIdx.z;
+  const int b = bx / p.nq, tk = bx % p.nq;
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int hbase = kvh * p.gqa + grp * G;
+  const int nh = min(G, p.gqa - grp * G);
+
+  const int ctx0 = p.ctx_len[b];
+  const int qpos = ctx0 + tk;
+  const int ctx = ctx0 + (p.append ? tk + 1 : 0);
+  int lo = p.leftpad ? p.leftpad[b] : 0;
+  if (p.window >= 0) lo = max(lo, qpos - p.window + 1);
+  lo = max(lo, 0);
+  const int n = max(ctx - lo, 0);
+  const int chunk = (((n + p.nsplit - 1) / p.nsplit) + DEC_TILE - 1) / DEC_TILE * DEC_TILE;
+  const int start = lo + sp * chunk, end = min(start + chunk, ctx);
+  float* out_base = p.scratch + ((long long)(b * p.nq + tk) * p.NH) * (long long)p.nsplit * (HD + 2);
+  if (start >= end) {   // empty split (CTA-uniform): neutral partial
+    for (int e = t; e < nh * (HD + 2); e += DEC_THREADS) {
+      const int g = e / (HD + 2), k = e % (HD + 2);
+      out_base[((long long)(hbase + g) * p.nsplit + sp) * (HD + 2) + k] = (k == 0) ? -INFINITY : 0.f;
+    }
+    return;
+  }
+  const int start_al = start & ~(DEC_TILE - 1);
+  const int ntile = (end - start_al + DEC_TILE - 1) / DEC_TILE;
+  const int shift = __ffs(p.page) - 1, pmask = p.page - 1;
+  const int R = p.page < DEC_TILE ? p.page : DEC_TILE;     // rows per TMA box (one page slice)
+
+  if (t == 0) {
+    for (int s = 0; s < C::NS; ++s) sm100::mbar_init(bar0 + 8 * s, 1);
+    sm100::fence_barrier_init();
+  }
+  // q (+ rotary) -> fp32 smem
+  const T* qg = (const T*)p.q + ((long long)(b * p.nq + tk) * p.NH + hbase) * HD;
+  for (int e = t; e < G * HD; e += DEC_THREADS) {
+    const int g = e / HD, d = e % HD;
+    s_q[g * HD + d] = (g < nh) ? Elem<T>::to_f(qg[(long long)g * HD + d]) : 0.f;
+  }
+  __syncthreads();
+  if (p.rotary && t < nh) {
+    const int rdim = p.rotary_dim > 0 ? p.rotary_dim : HD;
+    const int rp = (p.rotary_pos ? p.rotary_pos[b] : ctx0) + tk;
+    rotate_row(s_q + t * HD, rdim, p.rotary, p.cos + (long long)rp * (rdim / 2), p.sin + (long long)rp * (rdim / 2));
+  }
+
+  // one tile = up to 64/R page slices of K and V; slices wholly outside [start, end) or with an
+  // invalid page are not loaded (their rows are never read)
+  auto issue = [&](int ti) {
+    const int s = ti % C::NS;
+    const int base = start_al + ti * DEC_TILE;
+    const uint32_t kdst = sbase + s * C::STAGE, vdst = kdst + C::TILE;
+    uint32_t bytes = 0;
+    for (int i = 0; i < DEC_TILE / R; ++i) {
+      const int pos0 = base + i * R;
+      if (pos0 >= end || pos0 + R <= start) continue;
+      bool ok;
+      page_of(p, b, pos0, shift, ok);
+      if (ok) bytes += 2u * R * C::ROW;
+    }
+    sm100::mbar_expect_tx(bar0 + 8 * s, bytes);
+    for (int i = 0; i < DEC_TILE / R; ++i) {
+      const int pos0 = base + i * R;
+      if (pos0 >= end || pos0 + R <= start) continue;
+      bool ok;
+      const long long blk = page_of(p, b, pos0, shift, ok);
+      if (!ok) continue;
+      const int row = (int)(blk * p.page + (pos0 & pmask));
+      sm100::tma_load_3d(kdst + i * R * C::ROW, &tmK, 0, kvh, row, bar0 + 8 * s);
+      sm100::tma_load_3d(vdst + i * R * C::ROW, &tmV, 0, kvh, row, bar0 + 8 * s);
+    }
+  };
+  __syncthreads();   // barriers initialised, q rotated
+  int issued = 0;   // tiles whose loads thread 0 has issued
+  if (t == 0)
+    for (; issued < min(ntile, C::NS); ++issued) issue(issued);
+
+  // ---- per-thread roles
+  const int rg = warp * RPW + lane / LPR, li = lane % LPR, d0 = li * 8;
+  const bool dlive = d0 < HD;
+  float qr[G][8];
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) qr[g][i] = dlive ? s_q[g * HD + d0 + i] : 0.f;
+  const float scale2 = p.scale * FA_LOG2E;
+  const int gp = t / TPH, cchunk = (t % TPH) % D8, pg = (t % TPH) / D8;   // PV role
+  const bool pv_live = (t % TPH) < NPG * D8;   // HD/8 need not divide the threads of a head
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  float m_run = -INFINITY, l_run = 0.f;   // softmax stats, meaningful in warp g < G
+  bool ok = true;
+
+  for (int ti = 0; ti < ntile; ++ti) {
+    const int s = ti % C::NS;
+    const bool got = sm100::mbar_wait(bar0 + 8 * s, (ti / C::NS) & 1);
+    if (!__syncthreads_and(got)) { ok = false; break; }
+    // every thread is past phase C of tile ti-1: its stage can be refilled
+    if (t == 0 && ti >= 1 && ti - 1 + C::NS < ntile) issue(issued++);
+    const uint8_t* Kt = sg + s * C::STAGE;
+    const uint8_t* Vt = Kt + C::TILE;
+    const int base = start_al + ti * DEC_TILE;
+    const int v0 = max(start - base, 0), v1 = min(end - base, DEC_TILE);
+    // phase A: scores (trip count uniform: the shuffles are full-warp)
+    for (int pp = 0; pp < DEC_TILE; pp += NRG) {
+      const int pr = pp + rg;
+      const bool vis = pr < DEC_TILE && pr >= v0 && pr < v1;
+      float kf[8];
+      if (vis && dlive) cvt8<T>(*reinterpret_cast<const uint4*>(Kt + pr * C::ROW + d0 * 2), kf);
+      else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) kf[i] = 0.f;
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float a = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) a = fmaf(qr[g][i], kf[i], a);
+#pragma unroll
+        for (int o = LPR / 2; o >= 1; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+        if (li == 0 && pr < DEC_TILE) {
+          float v = -INFINITY;
+          if (vis && g < nh) {
+            v = (p.softcap > 0.f) ? p.softcap * tanhf(a * p.scale / p.softcap) * FA_LOG2E : a * scale2;
+            if (p.alibi) v += p.alibi[hbase + g] * (float)(base + pr - qpos) * FA_LOG2E;
+          }
+          s_sc[g * DEC_TILE + pr] = v;
+        }
+      }
+    }
+    __syncthreads();
+    // phase B: per-head tile softmax (warp g = head g)
+    if (warp < G) {
+      const int g = warp;
+      const float a = s_sc[g * DEC_TILE + lane], c = s_sc[g * DEC_TILE + lane + 32];
+      float tm = fmaxf(a, c);
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, o));
+      const float mn = fmaxf(m_run, tm);
+      const float muse = (mn == -INFINITY) ? 0.f : mn;
+      const float corr = (mn == -INFINITY) ? 1.f : exp2f(m_run - mn);
+      const float pa = exp2f(a - muse), pc = exp2f(c - muse);
+      float sum = pa + pc;
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      l_run = l_run * corr + sum;
+      m_run = mn;
+      s_p[g * DEC_TILE + lane] = pa;
+      s_p[g * DEC_TILE + lane + 32] = pc;
+      if (lane == 0) s_corr[g] = corr;
+    }
+    __syncthreads();
+    // phase C: O += p V over the visible positions of this thread's group
+    if (pv_live) {
+      const float corr = s_corr[gp];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] *= corr;
+      for (int pr = v0 + ((pg - v0 % NPG) + NPG) % NPG; pr < v1; pr += NPG) {
+        const float w = s_p[gp * DEC_TILE + pr];
+        float vf[8];
+        cvt8<T>(*reinterpret_cast<const uint4*>(Vt + pr * C::ROW + cchunk * 16), vf);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = fmaf(w, vf[i], acc[i]);
+      }
+    }
+  }
+  if (!ok && t == 0) {
+    atomicOr(&g_dec_error, 1);
+    // no copy of this CTA may still be landing when its shared memory is reused or released
+    for (int tj = 0; tj < issued; ++tj) sm100::mbar_wait(bar0 + 8 * (tj % C::NS), (tj / C::NS) & 1, 1000000000ull);
+  }
+  __syncthreads();
+  // reduce the position groups (stage 0 is free: every issued tile was consumed or timed out)
+  float* red = reinterpret_cast<float*>(sg);   // [G][NPG][HD]
+  if (pv_live) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) red[(gp * NPG + pg) * HD + cchunk * 8 + i] = acc[i];
+  }
+  if (warp < G && lane == 0) {
+    s_sc[warp] = ok ? m_run : -INFINITY;
+    s_sc[8 + warp] = ok ? l_run : 0.f;
+  }
+  __syncthreads();
+  for (int e = t; e < nh * HD; e += DEC_THREADS) {
+    const int g = e / HD, d = e % HD;
+    float a = 0.f;
+    for (int r = 0; r < NPG; ++r) a += red[(g * NPG + r) * HD + d];
+    float* out = out_base + ((long long)(hbase + g) * p.nsplit + sp) * (HD + 2);
+    out[2 + d] = ok ? a : 0.f;
+    if (d == 0) { out[0] = s_sc[g]; out[1] = s_sc[8 + g]; }
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 dec_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (PFN_cuTensorMapEncodeTiled_v12000)ptr;
+  }
+  return fn;
+}
+
+// cache [num_blocks*page rows][NKV][HD] viewed as 3-D (HD, NKV, rows); box = one page slice
+bool dec_map(CUtensorMap* m, const void* base, bool bf16, int HD, int NKV, long long rows, int box_rows) {
+  auto enc = dec_encode_fn();
+  if (!enc || ((uintptr_t)base) % 16) return false;
+  const cuuint64_t dims[3] = {(cuuint64_t)HD, (cuuint64_t)NKV, (cuuint64_t)rows};
+  const cuuint64_t strides[2] = {(cuuint64_t)HD * 2, (cuuint64_t)NKV * HD * 2};
+  const cuuint32_t box[3] = {(cuuint32_t)HD, 1, (cuuint32_t)box_rows};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base),
+             dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <typename T, int HD>
+int launch_tma(const FaDecParams& p, cudaStream_t st, bool* taken) {
+  *taken = false;
+  const int NKV = p.NH / p.gqa;
+  const long long rows = p.num_blocks * (long long)p.page;
+  if (p.num_blocks <= 0 || rows >= (1ll << 31) || getenv("FABLE_ATTN_DECODE_NO_TMA")) return FA_OK;
+  CUtensorMap mk, mv;
+  const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+  const int R = p.page < DEC_TILE ? p.page : DEC_TILE;
+  if (!dec_map(&mk, p.Kc, bf16, HD, NKV, rows, R) || !dec_map(&mv, p.Vc, bf16, HD, NKV, rows, R)) return FA_OK;
+  *taken = true;
+  using Cf = DecTmaCfg<HD>;
+  dim3 grid(p.batch * p.nq, 1, p.nsplit);
+#define FA_DEC_TMA(GG)                                                                       \
+  {                                                                                          \
+    const int groups = (p.gqa + GG - 1) / GG;                                                \
+    grid.y = NKV * groups;                                                                   \
+    static unsigned long long done = 0;                                                      \
+    if (int rc = fa::ensure_smem((const void*)dec_tma_kernel<T, HD, GG>, Cf::SMEM, &done)) return rc; \
+    dec_tma_kernel<T, HD, GG><<<grid, DEC_THREADS, Cf::SMEM, st>>>(mk, mv, p, groups);       \
+  }
+  if (p.gqa <= 1) FA_DEC_TMA(1)
+  else if (p.gqa <= 2) FA_DEC_TMA(2)
+  else if (p.gqa <= 4) FA_DEC_TMA(4)
+  else FA_DEC_TMA(8)
+#undef FA_DEC_TMA
+  fa::count_launch();
+  return fa::cuda_status(cudaGetLastError(), "decode partial (TMA) launch");
+}
+
 template <typename T, int HD>
 int launch_partial(const FaDecParams& p, cudaStream_t st) {
+  if constexpr (!std::is_same<T, float>::value) {
+    bool taken = false;
+    const int rc = launch_tma<T, HD>(p, st, &taken);
+    if (taken || rc) return rc;
+  }
   const int NKV = p.NH / p.gqa;
   const int gq = p.gqa;
   dim3 grid(p.batch * p.nq, 1, p.nsplit);
@@ -391,6 +704,15 @@ int combine_out(const FaCombineParams& p, cudaStream_t st) {
 }  // namespace
 
 namespace fa {
+int dec_device_error(int clear) {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_dec_error, sizeof(int));
+  if (clear) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_dec_error, &zero, sizeof(int));
+  }
+  return v;
+}
 int dec_run(const FaDecParams& p, int dtype, cudaStream_t st, const void* nk, const void* nv) {
   if (dtype == FA_DTYPE_F16) return launch_t<__half>(p, st, nk, nv);
   if (dtype == FA_DTYPE_BF16) return launch_t<__nv_bfloat16>(p, st, nk, nv);

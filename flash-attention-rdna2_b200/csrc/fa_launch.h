@@ -8,8 +8,12 @@ namespace fa {
 int fwd_simt(const FaFwdParams& p, int dtype, cudaStream_t st);
 int fwd_sm100(const FaFwdParams& p, int dtype, cudaStream_t st, bool* taken);
 int bwd_simt(const FaBwdParams& p, int dtype, cudaStream_t st);
+int bwd_dsum(const FaBwdParams& p, int dtype, cudaStream_t st);
+int bwd_sm100(const FaBwdParams& p, int dtype, cudaStream_t st, bool* taken);
+int bwd_device_error(int clear);   // bits of the tensor-core backward's timed-out waits
 int dec_run(const FaDecParams& p, int dtype, cudaStream_t st, const void* new_k, const void* new_v);
 int combine_run(const FaCombineParams& p, cudaStream_t st);
+int dec_device_error(int clear);   // bit 0: a decode pipeline wait timed out
 
 int current_device();
 // Raise the dynamic shared-memory limit of `func` to `bytes` once per device.

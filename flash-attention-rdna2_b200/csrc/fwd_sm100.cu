@@ -491,5 +491,5 @@ extern "C" FA_API int fa_device_error(int clear) {
     const int zero = 0;
     cudaMemcpyToSymbol(g_fwd_error, &zero, sizeof(int));
   }
-  return v;
+  return v | (fa::dec_device_error(clear) ? 64 : 0) | (fa::bwd_device_error(clear) ? 128 : 0);
 }
