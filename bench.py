@@ -256,8 +256,9 @@ def bench_fwd_dense(args, ws, rank, dev):
                 launches=launches, clocks=clk.summary(), e2e=e2e)
 
 
-def bench_fwd_bwd_causal(dev, steps=5, warmup=3):
-    """Config 3: B2 S4096 H32 D128 fp16 causal, dropout 0.1, fixed seed: fwd and bwd times."""
+def bench_fwd_bwd_causal(dev, steps=5, warmup=3, dropout_p=0.1):
+    """Config 3: B2 S4096 H32 D128 fp16 causal, dropout 0.1, fixed seed: fwd and bwd times (the
+    keep mask is generated once per step, as the autograd path does, and its time is included)."""
     from fable_attn import _C
     B, S, H, D = 2, 4096, 32, 128
     g = torch.Generator(device=dev).manual_seed(7)
@@ -265,26 +266,33 @@ def bench_fwd_bwd_causal(dev, steps=5, warmup=3):
     qh, kh, vh, doh = (t.transpose(1, 2) for t in (q, k, v, do))
     out = torch.empty(B, S, H, D, device=dev, dtype=torch.float16).transpose(1, 2)
     sc = D ** -0.5
+    pd = float(dropout_p)
+
+    def mask():
+        return _C.dropout_mask(qh, 777, pd, H, S, S, True, -1, 0) if pd > 0 else None
+
     for _ in range(warmup):
-        _, lse = _C.fwd(qh, kh, vh, sc, True, -1, 0, 0.0, None, 0.1, 777, 0, out)
-        _C.bwd(doh, qh, kh, vh, out, lse, sc, True, -1, 0, 0.0, None, 0.1, 777)
+        bits = mask()
+        _, lse = _C.fwd(qh, kh, vh, sc, True, -1, 0, 0.0, None, pd, 777, 0, out, bits)
+        _C.bwd(doh, qh, kh, vh, out, lse, sc, True, -1, 0, 0.0, None, pd, 777, bits)
     torch.cuda.synchronize()
     f0, f1 = _events()
     b0, b1 = _events()
     tf, tb = 0.0, 0.0
     for _ in range(steps):
         f0.record()
-        _, lse = _C.fwd(qh, kh, vh, sc, True, -1, 0, 0.0, None, 0.1, 777, 0, out)
+        bits = mask()
+        _, lse = _C.fwd(qh, kh, vh, sc, True, -1, 0, 0.0, None, pd, 777, 0, out, bits)
         f1.record()
         b0.record()
-        _C.bwd(doh, qh, kh, vh, out, lse, sc, True, -1, 0, 0.0, None, 0.1, 777)
+        _C.bwd(doh, qh, kh, vh, out, lse, sc, True, -1, 0, 0.0, None, pd, 777, bits)
         b1.record()
         torch.cuda.synchronize()
         tf += f0.elapsed_time(f1)
         tb += b0.elapsed_time(b1)
     fwd_flops = 4.0 * D * B * H * S * (S + 1) / 2
     fms, bms = tf / steps, tb / steps
-    return {"config": "causal fwd+bwd B2 S4096 H32 D128 fp16 dropout0.1", "fwd_ms": round(fms, 3),
+    return {"config": f"causal fwd+bwd B2 S4096 H32 D128 fp16 dropout{pd:g}", "fwd_ms": round(fms, 3),
             "fwd_tflops": round(fwd_flops / fms / 1e9, 1), "bwd_ms": round(bms, 3),
             "bwd_tflops": round(2.5 * fwd_flops / bms / 1e9, 1)}
 
@@ -403,6 +411,10 @@ def main():
             extra["fwd_bwd_causal"] = bench_fwd_bwd_causal(dev)
         except Exception as e:  # keep the headline even if a secondary figure fails
             extra["fwd_bwd_causal"] = {"error": f"{type(e).__name__}: {e}"[:200]}
+        try:
+            extra["fwd_bwd_causal_no_dropout"] = bench_fwd_bwd_causal(dev, dropout_p=0.0)
+        except Exception as e:
+            extra["fwd_bwd_causal_no_dropout"] = {"error": f"{type(e).__name__}: {e}"[:200]}
         try:
             extra["decode_paged"] = bench_decode(dev)
         except Exception as e:

@@ -97,6 +97,7 @@ extern "C" int fa_forward_launch(const FaFwdParams* pp, int dtype, void* stream)
     return FA_ERR_UNSUPPORTED;
   }
   if (p.cu_q && p.LSE) FA_CHECK_ARG(p.lse_total_q > 0, "forward: varlen LSE needs lse_total_q");
+  FA_CHECK_ARG(!(p.dropout_bits && p.cu_q), "forward: dropout_bits is for dense layouts only");
   if (p.batch == 0 || p.SQ == 0) return FA_OK;
   cudaStream_t st = (cudaStream_t)stream;
   bool taken = false;
@@ -123,6 +124,7 @@ extern "C" int fable_attn_backward_launch(const FaBwdParams* pp, int dtype, void
     return FA_ERR_UNSUPPORTED;
   }
   if (p.cu_q) FA_CHECK_ARG(p.lse_total_q > 0, "backward: varlen needs lse_total_q");
+  FA_CHECK_ARG(!(p.dropout_bits && p.cu_q), "backward: dropout_bits is for dense layouts only");
   if (p.B == 0 || p.SQ == 0 || p.SK == 0) return FA_OK;
   bool taken = false;
   const int rc = fa::bwd_sm100(p, dtype, (cudaStream_t)stream, &taken);

@@ -91,8 +91,7 @@ __device__ __forceinline__ void fill_pds(const FaBwdParams& p, const float* Qs, 
         const float pr = exp2f((logit - lse[i]) * FA_LOG2E);
         float zm = 1.f;
         if (p.dropout) {
-          const unsigned long long idx = ((unsigned long long)h * SQ + q) * SK + k;
-          zm = fa_dropout_mul(p.drop_seed, idx, p.dropout_p, inv_keep);
+          zm = fa_keep_mul(p.dropout_bits, p.drop_seed, h, SQ, SK, q, k, p.dropout_p, inv_keep);
         }
         pv = zm * pr;
         dsv = pr * (zm * dp[a][b] - dsum[i]) * deriv;

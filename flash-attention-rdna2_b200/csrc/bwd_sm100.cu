@@ -14,6 +14,7 @@
 // 16-bit rounding of dS does not reach dQ/dK; P~ goes in as one 16-bit number.  The preprocess
 // dsum = rowsum(O*dO) is the CUDA-core kernel of bwd_simt.cu.  Every mbarrier wait is bounded.
 #include <cudaTypedefs.h>
+#include <type_traits>
 #include "fa_common.cuh"
 #include "fa_launch.h"
 #include "sm100_ptx.cuh"
@@ -55,19 +56,6 @@ template <bool BF16>
 __device__ __forceinline__ float round16(float a) {
   if constexpr (BF16) return __bfloat162float(__float2bfloat16_rn(a));
   else return __half2float(__float2half_rn(a));
-}
-
-// logit and softcap derivative of one raw score (natural units)
-__device__ __forceinline__ void logit_of(float raw, float scale, float softcap, float& logit, float& deriv) {
-  const float g0 = raw * scale;
-  if (softcap > 0.f) {
-    const float tn = tanhf(g0 / softcap);
-    logit = softcap * tn;
-    deriv = 1.f - tn * tn;
-  } else {
-    logit = g0;
-    deriv = 1.f;
-  }
 }
 
 // K-major / MN-major descriptors of a [rows][D] tile stored as D/64 chunks of rows x 128 B
@@ -238,8 +226,26 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
     const float slope = (FEAT && p.alibi) ? p.alibi[h] : 0.f;
     const bool drop = FEAT && p.dropout;
+    const bool use_bits = drop && p.dropout_bits != nullptr;
+    const int mask_w = (SK + 31) / 32;
+    const uint32_t thresh = fa_drop_thresh(p.dropout_p);
+    const bool cap_on = FEAT && p.softcap > 0.f;
+    const float cap_in = cap_on ? p.scale / p.softcap : 0.f;
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
+      const int kb = (t0 + j) * BN;
+      // keep bits of this row for the tile (bit b of word i <-> key kb + 32i + b), prepared ahead
+      // of the wait: loaded from the mask (coalesced over rows) or evaluated with Philox
+      uint32_t dw[BN / 32];
+#pragma unroll
+      for (int i = 0; i < BN / 32; ++i) {
+        const int kw = kb / 32 + i;
+        dw[i] = 0u;
+        if (drop && q < SQ && kw < mask_w)
+          dw[i] = use_bits ? __ldg(p.dropout_bits + fa_mask_word(h, SQ, SK, q, kw))
+                           : fa_keep_word(p.drop_seed, ((uint64_t)h * SQ + q) * SK + 32 * kw, 1, thresh,
+                                          SK - 32 * kw);
+      }
       if (!mbar_wait_warp(bar + Bz::SP_FULL + 8 * (j & 1), (j >> 1) & 1)) { ok = false; break; }
       tc_fence_after();
       float s[BN], dp[BN];
@@ -248,36 +254,47 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       tmem_ld32(la + C::DP_COL + (j & 1) * 64, dp);
       tmem_ld32(la + C::DP_COL + (j & 1) * 64 + 32, dp + 32);
       tc_wait_ld();
-      const int kb = (t0 + j) * BN;
+      const float d0 = (float)(kb - q);   // key - q = d0 + cc, exact in fp32
+      // dS = P o (Z dP - dsum) o dlogit/ds, with Z the keep multiplier; one unrolled body per
+      // softcap setting so that neither carries the other's code
+      auto body = [&](auto cap_tag) {
+        constexpr bool kCap = decltype(cap_tag)::value;
 #pragma unroll
-      for (int h32 = 0; h32 < BN; h32 += 32) {   // 16 packed columns per chunk; inputs already in registers
-        uint32_t hi[16], lo[16];
+        for (int h32 = 0; h32 < BN; h32 += 32) {   // 16 packed columns per chunk; inputs in registers
+          uint32_t hi[16], lo[16];
 #pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          float dsv[2];
+          for (int c = 0; c < 32; c += 2) {
+            float dsv[2];
 #pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int cc = h32 + c + u, key = kb + cc;
-            float logit, deriv;
-            if constexpr (FEAT) {
-              logit_of(s[cc], p.scale, p.softcap, logit, deriv);
-              logit += slope * (float)(key - q);
-            } else {
-              logit = s[cc] * p.scale;
-              deriv = 1.f;
+            for (int u = 0; u < 2; ++u) {
+              const int cc = h32 + c + u, key = kb + cc;
+              float logit, deriv = 1.f;
+              if constexpr (kCap) {
+                const float tn = fa_tanh(s[cc] * cap_in);
+                logit = fmaf(p.softcap, tn, slope * (d0 + (float)cc));
+                deriv = 1.f - tn * tn;
+              } else if constexpr (FEAT) {
+                logit = fmaf(s[cc], p.scale, slope * (d0 + (float)cc));
+              } else {
+                logit = s[cc] * p.scale;
+              }
+              const float pr = (key >= rlo && key <= rhi) ? ex2(fmaf(logit, FA_LOG2E, -lse2)) : 0.f;
+              const float zm = drop ? (((dw[cc / 32] >> (cc % 32)) & 1u) ? p.keep_scale : 0.f) : 1.f;
+              dsv[u] = pr * (zm * dp[cc] - dsum) * deriv;
             }
-            const float pr = (key >= rlo && key <= rhi) ? ex2(fmaf(logit, FA_LOG2E, -lse2)) : 0.f;
-            float zm = 1.f;
-            if (drop && pr != 0.f)
-              zm = fa_dropout_mul(p.drop_seed, ((unsigned long long)h * SQ + q) * SK + key, p.dropout_p, p.keep_scale);
-            dsv[u] = pr * (zm * dp[cc] - dsum) * deriv;
+            const float h0 = round16<BF16>(dsv[0]), h1 = round16<BF16>(dsv[1]);
+            hi[c / 2] = pack2<BF16>(h0, h1);
+            lo[c / 2] = pack2<BF16>(dsv[0] - h0, dsv[1] - h1);
           }
-          const float h0 = round16<BF16>(dsv[0]), h1 = round16<BF16>(dsv[1]);
-          hi[c / 2] = pack2<BF16>(h0, h1);
-          lo[c / 2] = pack2<BF16>(dsv[0] - h0, dsv[1] - h1);
+          tmem_st16(la + C::S_COL + (j & 1) * 64 + h32 / 2, hi);
+          tmem_st16(la + C::DP_COL + (j & 1) * 64 + h32 / 2, lo);
         }
-        tmem_st16(la + C::S_COL + (j & 1) * 64 + h32 / 2, hi);
-        tmem_st16(la + C::DP_COL + (j & 1) * 64 + h32 / 2, lo);
+      };
+      if constexpr (FEAT) {
+        if (cap_on) body(std::true_type{});
+        else body(std::false_type{});
+      } else {
+        body(std::false_type{});
       }
       tc_wait_st();
       tc_fence_before();
@@ -457,9 +474,35 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int key = kb + tid;
     const uint32_t la = tmem + ((uint32_t)(warp * 32) << 16);
     const bool drop = FEAT && p.dropout;
+    const bool use_bits = drop && p.dropout_bits != nullptr;
+    const uint32_t thresh = fa_drop_thresh(p.dropout_p);
+    const bool cap_on = FEAT && p.softcap > 0.f;
+    const float cap_in = cap_on ? p.scale / p.softcap : 0.f;
+    // the warp's 32 keys are one mask word column (kb is a multiple of 128)
+    const int kw = kb / 32 + warp;
+    const bool kw_ok = kw < (SK + 31) / 32;
+    // query rows that see this key (empty for keys past SK)
+    int qlo, qhi;
+    fa_query_range(key, SQ, SK, p.causal, p.win_left, p.win_right, qlo, qhi);
+    if (key >= SK) { qlo = 1; qhi = 0; }
     bool ok = true;
     for (int i = 0; i < niter; ++i) {
       const int h = kvh * p.gqa + i / nqt, qbase = (qt0 + i % nqt) * BQ;
+      // keep bits of this key over the tile's query rows: cw[hq] bit r <-> row qbase + 32hq + r.
+      // From the mask, lane l loads the word of row qbase + 32hq + l (one line per warp) and a
+      // ballot transpose after the wait turns rows-of-keys into keys-of-rows; without a mask,
+      // Philox is evaluated here, down the key's column (counter stride SK).
+      uint32_t cw[BQ / 32];
+#pragma unroll
+      for (int hq = 0; hq < BQ / 32; ++hq) {
+        const int q0 = qbase + 32 * hq;
+        cw[hq] = 0u;
+        if (use_bits) {
+          if (kw_ok && q0 + lane < SQ) cw[hq] = __ldg(p.dropout_bits + fa_mask_word(h, SQ, SK, q0 + lane, kw));
+        } else if (drop && key < SK && q0 < SQ) {
+          cw[hq] = fa_keep_word(p.drop_seed, ((uint64_t)h * SQ + q0) * SK + key, (uint64_t)SK, thresh, SQ - q0);
+        }
+      }
       float* stb = st + (i & 1) * 128;
       // this tile's lse2 / dsum (threads 0-63 and 64-127); the named barrier publishes them to the
       // 4 warps and AND-reduces the wait outcome, so a timeout ends every warp at the same point
@@ -483,43 +526,63 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       tmem_ld32(la + C::DP_COL + (i & 1) * 64, dp);
       tmem_ld32(la + C::DP_COL + (i & 1) * 64 + 32, dp + 32);
       tc_wait_ld();
-      const float slope = (FEAT && p.alibi) ? p.alibi[h] : 0.f;
+      if (use_bits) {   // warp-uniform: every lane takes part in the ballots
 #pragma unroll
-      for (int h32 = 0; h32 < BQ; h32 += 32) {   // inputs are all in registers: in-place outputs are safe
-        uint32_t pk[16], hi[16], lo[16];
+        for (int hq = 0; hq < BQ / 32; ++hq) {
+          uint32_t t = 0u;
 #pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          float pv[2], dsv[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int cc = h32 + c + u, q = qbase + cc;
-            int lo_q, hi_q;
-            fa_key_range(q, SQ, SK, p.causal, p.win_left, p.win_right, 0, lo_q, hi_q);
-            const float l2 = stb[cc];
-            const bool vis = q < SQ && key < SK && key >= lo_q && key <= hi_q && l2 > -INFINITY;
-            float logit, deriv;
-            if constexpr (FEAT) {
-              logit_of(s[cc], p.scale, p.softcap, logit, deriv);
-              logit += slope * (float)(key - q);
-            } else {
-              logit = s[cc] * p.scale;
-              deriv = 1.f;
-            }
-            const float pr = vis ? ex2(fmaf(logit, FA_LOG2E, -l2)) : 0.f;
-            float zm = 1.f;
-            if (drop && pr != 0.f)
-              zm = fa_dropout_mul(p.drop_seed, ((unsigned long long)h * SQ + q) * SK + key, p.dropout_p, p.keep_scale);
-            pv[u] = zm * pr;
-            dsv[u] = pr * (zm * dp[cc] - stb[64 + cc]) * deriv;
+          for (int b = 0; b < 32; ++b) {
+            const uint32_t m = __ballot_sync(0xffffffffu, (cw[hq] >> b) & 1u);   // rows keeping key 32kw + b
+            t = (lane == b) ? m : t;
           }
-          pk[c / 2] = pack2<BF16>(pv[0], pv[1]);
-          const float h0 = round16<BF16>(dsv[0]), h1 = round16<BF16>(dsv[1]);
-          hi[c / 2] = pack2<BF16>(h0, h1);
-          lo[c / 2] = pack2<BF16>(dsv[0] - h0, dsv[1] - h1);
+          cw[hq] = t;
         }
-        tmem_st16(la + C::S_COL + (i & 1) * 64 + h32 / 2, pk);
-        tmem_st16(la + C::S_COL + (i & 1) * 64 + 32 + h32 / 2, hi);
-        tmem_st16(la + C::DP_COL + (i & 1) * 64 + h32 / 2, lo);
+      }
+      const float slope = (FEAT && p.alibi) ? p.alibi[h] : 0.f;
+      const float d0 = (float)(key - qbase);   // key - q = d0 - cc, exact in fp32
+      auto body = [&](auto cap_tag) {
+        constexpr bool kCap = decltype(cap_tag)::value;
+#pragma unroll
+        for (int h32 = 0; h32 < BQ; h32 += 32) {   // inputs are all in registers: in-place outputs are safe
+          uint32_t pk[16], hi[16], lo[16];
+#pragma unroll
+          for (int c = 0; c < 32; c += 2) {
+            float pv[2], dsv[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int cc = h32 + c + u, q = qbase + cc;
+              const float l2 = stb[cc];
+              const bool vis = q >= qlo && q <= qhi && l2 > -INFINITY;
+              float logit, deriv = 1.f;
+              if constexpr (kCap) {
+                const float tn = fa_tanh(s[cc] * cap_in);
+                logit = fmaf(p.softcap, tn, slope * (d0 - (float)cc));
+                deriv = 1.f - tn * tn;
+              } else if constexpr (FEAT) {
+                logit = fmaf(s[cc], p.scale, slope * (d0 - (float)cc));
+              } else {
+                logit = s[cc] * p.scale;
+              }
+              const float pr = vis ? ex2(fmaf(logit, FA_LOG2E, -l2)) : 0.f;
+              const float zm = drop ? (((cw[h32 / 32] >> (c + u)) & 1u) ? p.keep_scale : 0.f) : 1.f;
+              pv[u] = zm * pr;
+              dsv[u] = pr * (zm * dp[cc] - stb[64 + cc]) * deriv;
+            }
+            pk[c / 2] = pack2<BF16>(pv[0], pv[1]);
+            const float h0 = round16<BF16>(dsv[0]), h1 = round16<BF16>(dsv[1]);
+            hi[c / 2] = pack2<BF16>(h0, h1);
+            lo[c / 2] = pack2<BF16>(dsv[0] - h0, dsv[1] - h1);
+          }
+          tmem_st16(la + C::S_COL + (i & 1) * 64 + h32 / 2, pk);
+          tmem_st16(la + C::S_COL + (i & 1) * 64 + 32 + h32 / 2, hi);
+          tmem_st16(la + C::DP_COL + (i & 1) * 64 + h32 / 2, lo);
+        }
+      };
+      if constexpr (FEAT) {
+        if (cap_on) body(std::true_type{});
+        else body(std::false_type{});
+      } else {
+        body(std::false_type{});
       }
       tc_wait_st();
       tc_fence_before();

@@ -53,11 +53,43 @@ const int* opt_i32(const c10::optional<torch::Tensor>& t) {
   return t->data_ptr<int>();
 }
 
+// ------------------------------------------------------------------ dropout keep mask
+constexpr long long kMaxMaskBytes = 1ll << 30;   // above this the kernels evaluate Philox themselves
+
+c10::optional<torch::Tensor> make_mask(const torch::Tensor& like, int64_t seed, double dropout_p, int NH, int SQ,
+                                       int SK, bool causal, int64_t wl, int64_t wr) {
+  const long long words = fa_dropout_mask_words(NH, SQ, SK);
+  if (!(dropout_p > 0) || words * 4 > kMaxMaskBytes || words == 0) return c10::nullopt;
+  auto bits = torch::empty({words}, like.options().dtype(torch::kInt32));
+  check(fa_dropout_mask_launch((unsigned long long)seed, (float)dropout_p, NH, SQ, SK, causal ? 1 : 0, (int)wl,
+                               (int)wr, (unsigned int*)bits.data_ptr<int>(), cur_stream(like)),
+        "dropout mask");
+  return bits;
+}
+
+torch::Tensor dropout_mask(torch::Tensor like, int64_t seed, double dropout_p, int64_t NH, int64_t SQ, int64_t SK,
+                           bool causal, int64_t wl, int64_t wr) {
+  const c10::cuda::CUDAGuard guard(like.device());
+  auto m = make_mask(like, seed, dropout_p, (int)NH, (int)SQ, (int)SK, causal, wl, wr);
+  return m.has_value() ? *m : torch::empty({0}, like.options().dtype(torch::kInt32));
+}
+
+// the kernels index the mask as [NH][SQ][ceil(SK/32)] words: a mask of any other size is refused
+const unsigned int* mask_ptr(const c10::optional<torch::Tensor>& m, int NH, int SQ, int SK) {
+  if (!m.has_value() || !m->defined() || m->numel() == 0) return nullptr;
+  TORCH_CHECK_VALUE(m->scalar_type() == torch::kInt32 && m->is_contiguous(), "fable_attn: dropout_bits must be int32");
+  TORCH_CHECK_VALUE(m->numel() == fa_dropout_mask_words(NH, SQ, SK),
+                    "fable_attn: dropout_bits has ", m->numel(), " words, expected ", fa_dropout_mask_words(NH, SQ, SK),
+                    " for nheads=", NH, " seqlen_q=", SQ, " seqlen_k=", SK);
+  return (const unsigned int*)m->data_ptr<int>();
+}
+
 // ------------------------------------------------------------------ forward (dense)
 std::vector<torch::Tensor> fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, double scale, bool causal,
                                int64_t win_left, int64_t win_right, double softcap,
                                c10::optional<torch::Tensor> alibi, double dropout_p, int64_t seed,
-                               int64_t attn_chunk, c10::optional<torch::Tensor> out_opt) {
+                               int64_t attn_chunk, c10::optional<torch::Tensor> out_opt,
+                               c10::optional<torch::Tensor> dropout_bits) {
   need_cuda_lastdim(q, "q"); need_cuda_lastdim(k, "k"); need_cuda_lastdim(v, "v");
   TORCH_CHECK_VALUE(q.dim() == 4 && k.dim() == 4 && v.dim() == 4, "fable_attn: fwd expects [B,H,S,D]");
   const c10::cuda::CUDAGuard guard(q.device());
@@ -79,6 +111,10 @@ std::vector<torch::Tensor> fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v
   p.causal = causal ? 1 : 0; p.win_left = (int)win_left; p.win_right = (int)win_right;
   p.attn_chunk = (int)attn_chunk; p.alibi_slopes = opt_f32(alibi);
   p.dropout_p = (float)dropout_p; p.philox_seed = (unsigned long long)seed;
+  c10::optional<torch::Tensor> bits = dropout_bits;
+  if (dropout_p > 0 && !mask_ptr(bits, Hq, SQ, SK))
+    bits = make_mask(q, seed, dropout_p, Hq, SQ, SK, causal, win_left, win_right);
+  p.dropout_bits = mask_ptr(bits, Hq, SQ, SK);
   check(fa_forward_launch(&p, dt_of(q), cur_stream(q)), "forward");
   return {out, lse};
 }
@@ -136,7 +172,7 @@ FaBwdParams bwd_common(torch::Tensor& dout, torch::Tensor& q, torch::Tensor& k, 
 std::vector<torch::Tensor> bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
                                torch::Tensor out, torch::Tensor lse, double scale, bool causal, int64_t win_left,
                                int64_t win_right, double softcap, c10::optional<torch::Tensor> alibi,
-                               double dropout_p, int64_t seed) {
+                               double dropout_p, int64_t seed, c10::optional<torch::Tensor> dropout_bits) {
   for (auto* t : {&dout, &q, &k, &v, &out}) need_cuda_lastdim(*t, "backward input");
   TORCH_CHECK_VALUE(lse.is_contiguous() && lse.scalar_type() == torch::kFloat32, "fable_attn: lse must be contiguous fp32");
   const c10::cuda::CUDAGuard guard(q.device());
@@ -148,6 +184,10 @@ std::vector<torch::Tensor> bwd(torch::Tensor dout, torch::Tensor q, torch::Tenso
   p.qs = S4(q); p.ks = S4(k); p.vs = S4(v); p.os = S4(out); p.dos = S4(dout);
   p.dqs = S4(dq); p.dks = S4(dk); p.dvs = S4(dv);
   p.B = B; p.Hq = Hq; p.Hk = Hk; p.SQ = SQ; p.SK = SK; p.D = D; p.gqa = Hq / Hk;
+  c10::optional<torch::Tensor> bits = dropout_bits;
+  if (dropout_p > 0 && !mask_ptr(bits, Hq, SQ, SK))
+    bits = make_mask(q, seed, dropout_p, Hq, SQ, SK, causal, win_left, win_right);
+  p.dropout_bits = mask_ptr(bits, Hq, SQ, SK);
   check(fable_attn_backward_launch(&p, dt_of(q), cur_stream(q)), "backward");
   return {dq, dk, dv};
 }
@@ -253,10 +293,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "fable_attn sm_100a attention kernels (binds the C ABI of include/fable_attn.h)";
   m.def("fwd", &fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("scale"), py::arg("causal"),
         py::arg("win_left"), py::arg("win_right"), py::arg("softcap"), py::arg("alibi"), py::arg("dropout_p"),
-        py::arg("seed"), py::arg("attn_chunk") = 0, py::arg("out") = c10::optional<torch::Tensor>());
+        py::arg("seed"), py::arg("attn_chunk") = 0, py::arg("out") = c10::optional<torch::Tensor>(),
+        py::arg("dropout_bits") = c10::optional<torch::Tensor>());
   m.def("bwd", &bwd, py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"), py::arg("out"), py::arg("lse"),
         py::arg("scale"), py::arg("causal"), py::arg("win_left"), py::arg("win_right"), py::arg("softcap"),
-        py::arg("alibi"), py::arg("dropout_p"), py::arg("seed"));
+        py::arg("alibi"), py::arg("dropout_p"), py::arg("seed"), py::arg("dropout_bits") = c10::optional<torch::Tensor>());
+  m.def("dropout_mask", &dropout_mask, py::arg("like"), py::arg("seed"), py::arg("dropout_p"), py::arg("nheads"),
+        py::arg("seqlen_q"), py::arg("seqlen_k"), py::arg("causal"), py::arg("win_left"), py::arg("win_right"));
   m.def("fwd_varlen", &fwd_varlen, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("cu_q"), py::arg("cu_k"),
         py::arg("max_sq"), py::arg("max_sk"), py::arg("scale"), py::arg("causal"), py::arg("win_left"),
         py::arg("win_right"), py::arg("softcap"), py::arg("alibi"), py::arg("dropout_p"), py::arg("seed"),

@@ -1,0 +1,61 @@
+// dropout.cu — the dropout keep mask as bits (see fa_dropout_mask_launch in fable_attn.h).
+//
+// One thread per 32-bit word = 32 consecutive keys of one (head, query row); consecutive threads
+// take consecutive query rows, so stores are coalesced in the [NH][ceil(SK/32)][SQ] layout.  The
+// 32 Philox evaluations of a word are independent and are issued 8 at a time to keep the integer
+// pipes busy (fa_keep_word).  The keep decision is the reference's (kernels/fa_common.hpp:71-88),
+// u = (r0 >> 8) / 2^24, keep iff u >= p, evaluated as the equivalent integer test of
+// fa_drop_thresh.  Words that hold no key the row can see (causal / window) are skipped: no
+// consumer reads them.
+#include "fa_common.cuh"
+#include "fa_launch.h"
+
+namespace {
+
+__global__ void __launch_bounds__(256) dropout_mask_kernel(unsigned long long seed, unsigned int thresh, int NH,
+                                                           int SQ, int SK, int causal, int wl, int wr,
+                                                           unsigned int* bits) {
+  const int W = (SK + 31) / 32;
+  const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long total = (long long)NH * SQ * W;
+  if (gid >= total) return;
+  const int q = (int)(gid % SQ);
+  const long long hw = gid / SQ;            // h*W + kw
+  const int kw = (int)(hw % W), h = (int)(hw / W);
+  int lo, hi;
+  fa_key_range(q, SQ, SK, causal, wl, wr, 0, lo, hi);
+  const int k0 = kw * 32;
+  if (hi < k0 || lo > k0 + 31 || lo > hi) return;
+  bits[gid] = fa_keep_word(seed, ((uint64_t)h * SQ + q) * SK + k0, 1, thresh, SK - k0);
+}
+
+}  // namespace
+
+extern "C" FA_API long long fa_dropout_mask_words(int NH, int SQ, int SK) {
+  if (NH <= 0 || SQ <= 0 || SK <= 0) return 0;
+  return (long long)NH * SQ * ((SK + 31) / 32);
+}
+
+extern "C" FA_API int fa_dropout_mask_launch(unsigned long long seed, float p, int NH, int SQ, int SK, int causal,
+                                             int win_left, int win_right, unsigned int* bits, void* stream) {
+  if (!bits) {
+    fa::set_error("dropout mask: null output");
+    return FA_ERR_INVALID;
+  }
+  if (!(p > 0.f && p < 1.f) || NH <= 0 || SQ < 0 || SK < 0) {
+    fa::set_error("dropout mask: p=%f NH=%d SQ=%d SK=%d", p, NH, SQ, SK);
+    return FA_ERR_INVALID;
+  }
+  const long long total = fa_dropout_mask_words(NH, SQ, SK);
+  if (total == 0) return FA_OK;
+  const long long blocks = (total + 255) / 256;
+  if (blocks >= (1ll << 31)) {
+    fa::set_error("dropout mask: %lld words is too large", total);
+    return FA_ERR_SIZE;
+  }
+  const unsigned int thresh = fa_drop_thresh(p);
+  dropout_mask_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(seed, thresh, NH, SQ, SK, causal,
+                                                                         win_left, win_right, bits);
+  fa::count_launch();
+  return fa::cuda_status(cudaGetLastError(), "dropout mask launch");
+}

@@ -58,6 +58,46 @@ __host__ __device__ __forceinline__ float fa_dropout_mul(uint64_t seed, uint64_t
   return (u >= p) ? inv_keep : 0.0f;
 }
 
+// Integer form of the keep test: u = (r0 >> 8) / 2^24 >= p  <=>  (r0 >> 8) >= ceil(p * 2^24).
+// Both sides of the float test are exact (r0 >> 8 < 2^24 and scaling by 2^-24 is exact), and
+// p * 2^24 is exact in fp32, so the two tests decide identically.  Result in 1 .. 2^24.
+__host__ __device__ __forceinline__ uint32_t fa_drop_thresh(float p) {
+  return (uint32_t)ceilf(p * 16777216.0f);
+}
+
+// Keep bits of the Philox counters base + b*stride, b = 0..31 (bit b set iff that score is
+// kept); bits b >= nvalid are 0.  Not inlined: the attention kernels call it once per 32
+// scores, and a single copy keeps their unrolled element loops small.  The 32 evaluations are
+// independent and are issued 8 at a time to keep the integer pipes busy.
+static __device__ __noinline__ uint32_t fa_keep_word(uint64_t seed, uint64_t base, uint64_t stride, uint32_t thresh,
+                                              int nvalid) {
+  uint32_t word = 0;
+#pragma unroll 1
+  for (int b0 = 0; b0 < 32; b0 += 8) {
+    uint32_t r[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) r[u] = fa_philox_r0(seed, base + (uint64_t)(b0 + u) * stride);
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if ((r[u] >> 8) >= thresh && b0 + u < nvalid) word |= 1u << (b0 + u);
+  }
+  return word;
+}
+
+// index of the keep-mask word holding keys [32*kw, 32*kw + 31] of query row q of head h: the
+// fa_dropout_mask_launch layout [NH][ceil(SK/32)][SQ], query row fastest
+__host__ __device__ __forceinline__ long long fa_mask_word(int h, int SQ, int SK, int q, int kw) {
+  return ((long long)h * ((SK + 31) / 32) + kw) * SQ + q;
+}
+
+// keep multiplier of score (q, k) of query head h: from the precomputed bit mask when given,
+// else Philox evaluated here; both give the same decision
+__device__ __forceinline__ float fa_keep_mul(const unsigned int* bits, uint64_t seed, int h, int SQ, int SK, int q,
+                                             int k, float p, float inv_keep) {
+  if (bits) return ((bits[fa_mask_word(h, SQ, SK, q, k / 32)] >> (k % 32)) & 1u) ? inv_keep : 0.0f;
+  return fa_dropout_mul(seed, ((uint64_t)h * SQ + q) * SK + k, p, inv_keep);
+}
+
 // ---------------------------------------------------------------- sequence geometry
 // Resolves, for batch index / sequence z, the lengths and the element offsets of row 0 of the
 // q / k / o tensors.  Dense: offsets from the batch stride.  Varlen: token offsets from
@@ -112,6 +152,33 @@ __host__ __device__ __forceinline__ void fa_key_range(int q, int SQ, int SK, int
     if (cs > lo) lo = cs;
     if (cs + chunk - 1 < hi) hi = cs + chunk - 1;
   }
+}
+
+// Query rows [qlo, qhi] that see key k under (causal, wl, wr), without attention chunks: the
+// inverse of fa_key_range.  Row q's diagonal is key q + SK - SQ, so with off = SQ - SK
+//   causal: k <= q - off    <=>  q >= k + off
+//   wl>=0:  k >= diag - wl  <=>  q <= k + wl + off
+//   wr>=0:  k <= diag + wr  <=>  q >= k - wr + off
+// Empty when qlo > qhi.  Computed in 64 bits and clamped to [0, SQ] / [-1, SQ-1].
+__host__ __device__ __forceinline__ void fa_query_range(int k, int SQ, int SK, int causal, int wl, int wr,
+                                                        int& qlo, int& qhi) {
+  const long long off = (long long)SQ - SK;
+  long long lo = 0, hi = SQ - 1;
+  if (causal && k + off > lo) lo = k + off;
+  if (wr >= 0 && k - wr + off > lo) lo = k - wr + off;
+  if (wl >= 0 && k + wl + off < hi) hi = k + wl + off;
+  qlo = (int)(lo > SQ ? SQ : lo);
+  qhi = (int)(hi < -1 ? -1 : hi);
+}
+
+// tanh from the identity tanh x = 1 - 2 / (e^(2x) + 1), with e^(2x) = 2^(2x log2 e) on the SFU.
+// The exponent is clamped so the power stays finite (tanh is 1 in fp32 long before); below, the
+// power flushes to 0 and the result is -1.  Absolute error is a few ulp of 1, which is what the
+// softcapped logit cap * tanh(.) needs: its error is then a few ulp of cap.
+__device__ __forceinline__ float fa_tanh(float x) {
+  float e;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(fminf(2.f * FA_LOG2E * x, 64.f)));
+  return 1.f - __fdividef(2.f, e + 1.f);
 }
 
 // ---------------------------------------------------------------- host bookkeeping

@@ -123,8 +123,8 @@ __global__ void __launch_bounds__(256) fwd_simt_kernel(const FaFwdParams p) {
 #pragma unroll
           for (int j = 0; j < 2; ++j) {
             const int key = kb + tx + 16 * j;
-            const unsigned long long idx = ((unsigned long long)h * SQ + q) * SK + key;
-            pj[j] *= fa_dropout_mul(p.philox_seed, idx, p.dropout_p, inv_keep);
+            if (q < SQ && key < SK)
+              pj[j] *= fa_keep_mul(p.dropout_bits, p.philox_seed, h, SQ, SK, q, key, p.dropout_p, inv_keep);
           }
         }
       }

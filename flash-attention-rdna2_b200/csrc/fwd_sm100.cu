@@ -249,40 +249,58 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     float m_ref = -INFINITY, l = 0.f;
     bool ok = true;
     float s[BN];
+    const bool use_bits = drop && p.dropout_bits != nullptr;
+    const int mask_w = (SK + 31) / 32;
+    const uint32_t thresh = fa_drop_thresh(p.dropout_p);
+    const bool cap_on = FEAT && p.softcap > 0.f;
+    const float cap_in = cap_on ? p.scale / p.softcap : 0.f, cap2 = p.softcap * FA_LOG2E;
     for (int j = 0; j < ntiles; ++j) {
+      const int kb = (t0 + j) * BN;
+      // this tile's keep bits, one word per 32 keys (bit b <-> key kb + 32i + b), prepared before
+      // the wait so that they overlap it: loaded from the mask (its layout puts the warp's 32 rows
+      // on one line) or evaluated with Philox.  Mask words past the row's visible keys may be
+      // unwritten: they only multiply probabilities that are already 0.
+      uint32_t dw[BN / 32];
+#pragma unroll
+      for (int i = 0; i < BN / 32; ++i) {
+        const int kw = kb / 32 + i;
+        dw[i] = 0u;
+        if (drop && q < SQ && kw < mask_w)
+          dw[i] = use_bits ? __ldg(p.dropout_bits + fa_mask_word(h, SQ, SK, q, kw))
+                           : fa_keep_word(p.philox_seed, ((uint64_t)h * SQ + q) * SK + 32 * kw, 1, thresh,
+                                          SK - 32 * kw);
+      }
       if (!mbar_wait_warp(bar + Bars::S_FULL + 8 * (j & 1), (j >> 1) & 1)) { ok = false; break; }
       tc_fence_after();
       const uint32_t sa = lane_addr + (uint32_t)(j & 1) * 128u;
 #pragma unroll
       for (int c = 0; c < BN; c += 32) tmem_ld32(sa + c, s + c);
       tc_wait_ld();
-      const int kb = (t0 + j) * BN;
       // ---- scores (log2 domain) and masks
       float tmax = -INFINITY;
       if constexpr (FEAT) {
+        // logits in log2 units; alibi adds slope2 * (key - q), and key - q = d0 + c exactly in
+        // fp32.  Two tight loops (softcap or not) keep the unrolled code small.
+        const float d0 = (float)(kb - q);
+        if (cap_on) {
+#pragma unroll
+          for (int c = 0; c < BN; ++c) s[c] = fmaf(cap2, fa_tanh(s[c] * cap_in), slope2 * (d0 + (float)c));
+        } else {
+#pragma unroll
+          for (int c = 0; c < BN; ++c) s[c] = fmaf(s[c], scale2, slope2 * (d0 + (float)c));
+        }
+      }
+      const bool interior = full_rows && kb >= lo_last && kb + BN - 1 <= hi_first && kb + BN <= SK;
+      if (!interior) {
 #pragma unroll
         for (int c = 0; c < BN; ++c) {
           const int key = kb + c;
-          float v;
-          if (p.softcap > 0.f) v = p.softcap * tanhf(s[c] * p.scale / p.softcap) * FA_LOG2E;
-          else v = s[c] * scale2;
-          v += slope2 * (float)(key - q);
-          s[c] = (key < rlo || key > rhi) ? -INFINITY : v;
-          tmax = fmaxf(tmax, s[c]);
+          if (key < rlo || key > rhi) s[c] = -INFINITY;
         }
-      } else {
-        const bool interior = full_rows && kb >= lo_last && kb + BN - 1 <= hi_first && kb + BN <= SK;
-        if (!interior) {
-#pragma unroll
-          for (int c = 0; c < BN; ++c) {
-            const int key = kb + c;
-            if (key < rlo || key > rhi) s[c] = -INFINITY;
-          }
-        }
-#pragma unroll
-        for (int c = 0; c < BN; ++c) tmax = fmaxf(tmax, s[c]);
-        tmax = (tmax == -INFINITY) ? -INFINITY : tmax * scale2;
       }
+#pragma unroll
+      for (int c = 0; c < BN; ++c) tmax = fmaxf(tmax, s[c]);
+      if constexpr (!FEAT) tmax = (tmax == -INFINITY) ? -INFINITY : tmax * scale2;
       // ---- lazy online-softmax update: the reference max moves only when it grows by > 2^8
       const bool move = tmax > m_ref + LAZY_THRESH || (m_ref == -INFINITY && tmax != -INFINITY);
       float corr = 1.f;
@@ -304,10 +322,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           float a = ex2(fmaf(s[c0 + 2 * i], sc, -muse));
           float b = ex2(fmaf(s[c0 + 2 * i + 1], sc, -muse));
           lsum += a + b;
-          if (drop) {
-            const unsigned long long idx = ((unsigned long long)h * SQ + q) * SK + (kb + c0 + 2 * i);
-            a *= fa_dropout_mul(p.philox_seed, idx, p.dropout_p, inv_keep);
-            b *= fa_dropout_mul(p.philox_seed, idx + 1, p.dropout_p, inv_keep);
+          if (drop) {   // keys kb + c0 + 2i and +1 are bits 2i, 2i+1 of word c0/32
+            const unsigned int w = dw[c0 / 32] >> (2 * i);
+            a *= (w & 1u) ? inv_keep : 0.f;
+            b *= (w & 2u) ? inv_keep : 0.f;
           }
           if constexpr (BF16) {
             const __nv_bfloat162 t2 = __floats2bfloat162_rn(a, b);

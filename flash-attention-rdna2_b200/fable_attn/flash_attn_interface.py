@@ -122,10 +122,14 @@ class _AttnFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, scale, causal, wl, wr, softcap, alibi, dropout_p, chunk, out_buf):
         seed = random.getrandbits(63) if dropout_p > 0 else 0
+        # the keep mask is generated once (bits, no batch term) and read by forward and backward
+        bits = (_C.dropout_mask(q, int(seed), float(dropout_p), q.shape[1], q.shape[2], k.shape[2], bool(causal),
+                                int(wl), int(wr)) if dropout_p > 0 else None)
         out, lse = _C.fwd(q, k, v, float(scale), bool(causal), int(wl), int(wr), float(softcap), alibi,
-                          float(dropout_p), int(seed), int(chunk), out_buf)
+                          float(dropout_p), int(seed), int(chunk), out_buf, bits)
         ctx.save_for_backward(q, k, v, out, lse)
         ctx.mark_non_differentiable(lse)
+        ctx.bits = bits
         ctx.alibi = alibi
         ctx.cfg = (scale, causal, wl, wr, softcap, dropout_p, seed, chunk)
         return out, lse
@@ -139,7 +143,7 @@ class _AttnFn(torch.autograd.Function):
                 "run the chunked forward under torch.no_grad()")
         q, k, v, out, lse = ctx.saved_tensors
         dq, dk, dv = _C.bwd(_lastdim_contig(dout), q, k, v, out, lse, float(scale), bool(causal), int(wl),
-                            int(wr), float(softcap), ctx.alibi, float(dropout_p), int(seed))
+                            int(wr), float(softcap), ctx.alibi, float(dropout_p), int(seed), ctx.bits)
         return dq, dk, dv, None, None, None, None, None, None, None, None, None
 
 

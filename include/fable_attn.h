@@ -88,6 +88,8 @@ typedef struct FaFwdParams {
   const int* cu_q; const int* cu_k;    /* varlen: [batch+1] int32, or null */
   const int* seqused_q; const int* seqused_k;   /* varlen: [batch] int32, or null */
   long long lse_total_q;               /* varlen LSE row length (total tokens of q) */
+  const unsigned int* dropout_bits;    /* optional precomputed keep mask (fa_dropout_mask_launch,
+                                          dense only); null = Philox evaluated in the kernel */
 } FaFwdParams;
 
 FA_API int fa_forward_launch(const FaFwdParams* p, int dtype, void* stream);
@@ -118,9 +120,24 @@ typedef struct FaBwdParams {
   const int* cu_q; const int* cu_k;
   const int* seqused_q; const int* seqused_k;
   long long lse_total_q;
+  const unsigned int* dropout_bits;    /* optional precomputed keep mask, as in FaFwdParams */
 } FaBwdParams;
 
 FA_API int fable_attn_backward_launch(const FaBwdParams* p, int dtype, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Dropout keep mask as bits, computed once and read by the forward and backward kernels in place
+ * of evaluating Philox per score.  No counterpart in the reference (its kernels evaluate Philox
+ * per score, kernels/fa_forward.hip:255-259, kernels/backward.hip:171-173); the bits are exactly
+ * the reference's keep decisions: bit k%32 of word bits[(h*W + k/32)*SQ + q], W = ceil(SK/32),
+ * is 1 iff Philox(seed, (h*SQ + q)*SK + k) keeps (q, k) with drop probability p.  Words are
+ * query-row-minor so that 32 consecutive rows read one 128-byte line.  The mask has no batch
+ * term, like the reference's.  Only words holding a key that row q can see under (causal,
+ * win_left, win_right) are written; consumers read no others.  Dense layouts only.
+ * -------------------------------------------------------------------------------------------*/
+FA_API long long fa_dropout_mask_words(int NH, int SQ, int SK);
+FA_API int fa_dropout_mask_launch(unsigned long long seed, float p, int NH, int SQ, int SK, int causal, int win_left,
+                                  int win_right, unsigned int* bits, void* stream);
 
 /* ------------------------------------------------------------------------------------------
  * Paged-KV decode (one or several new tokens per sequence).  Replaces DecParams /

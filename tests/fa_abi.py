@@ -27,7 +27,7 @@ class FaFwdParams(C.Structure):
                 ("causal", C.c_int), ("win_left", C.c_int), ("win_right", C.c_int), ("attn_chunk", C.c_int),
                 ("alibi_slopes", C.c_void_p), ("dropout_p", C.c_float), ("philox_seed", C.c_ulonglong),
                 ("cu_q", C.c_void_p), ("cu_k", C.c_void_p), ("seqused_q", C.c_void_p), ("seqused_k", C.c_void_p),
-                ("lse_total_q", C.c_longlong)]
+                ("lse_total_q", C.c_longlong), ("dropout_bits", C.c_void_p)]
 
 
 class FaBwdParams(C.Structure):
@@ -38,7 +38,8 @@ class FaBwdParams(C.Structure):
         ("scale", C.c_float), ("softcap", C.c_float), ("alibi", C.c_void_p), ("causal", C.c_int),
         ("win_left", C.c_int), ("win_right", C.c_int), ("dropout", C.c_int), ("drop_seed", C.c_ulonglong),
         ("dropout_p", C.c_float), ("keep_scale", C.c_float), ("cu_q", C.c_void_p), ("cu_k", C.c_void_p),
-        ("seqused_q", C.c_void_p), ("seqused_k", C.c_void_p), ("lse_total_q", C.c_longlong)]
+        ("seqused_q", C.c_void_p), ("seqused_k", C.c_void_p), ("lse_total_q", C.c_longlong),
+        ("dropout_bits", C.c_void_p)]
 
 
 class FaDecParams(C.Structure):
@@ -71,6 +72,9 @@ def lib():
         L.fa_decode_scratch_floats.restype = C.c_longlong
         L.fa_decode_scratch_floats.argtypes = [C.c_int] * 5
         L.fa_combine_launch.argtypes = [C.POINTER(FaCombineParams), C.c_void_p]
+        L.fa_dropout_mask_words.restype = C.c_longlong
+        L.fa_dropout_mask_words.argtypes = [C.c_int] * 3
+        L.fa_dropout_mask_launch.argtypes = [C.c_ulonglong, C.c_float] + [C.c_int] * 6 + [C.c_void_p, C.c_void_p]
         L.fa_last_error.restype = C.c_char_p
         L.fa_kernel_launch_count.restype = C.c_ulonglong
         _LIB = L

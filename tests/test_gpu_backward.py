@@ -148,3 +148,22 @@ def test_backward_varlen_native(dt):
         rq, rk, rv = O.backward(qn[a:b][None], kn[a:b][None], vn[a:b][None], don[a:b][None], D ** -0.5, True)
         for g, r in ((dq, rq), (dk, rk), (dv, rv)):
             assert O.rel_rms(to_np(g)[a:b], r[0]) < TOL[dt]
+
+
+@pytest.mark.parametrize("dt", ["fp16", "bf16", "fp32"])
+@pytest.mark.parametrize("name", ["dropout0.2", "d128_causal_dropout_gqa"])
+def test_backward_with_bitmask_equals_inkernel_philox(dt, name):
+    """Backward reading the precomputed keep bits gives bitwise the same gradients as Philox in-kernel."""
+    case = next(c for c in CASES if c[0] == name)
+    p, got, _ = _run_case(case, dt)
+    first = [g.clone() for g in got]
+    bits = torch.zeros(A.lib().fa_dropout_mask_words(p.Hq, p.SQ, p.SK), dtype=torch.int32, device="cuda")
+    A.check(A.lib().fa_dropout_mask_launch(p.drop_seed, p.dropout_p, p.Hq, p.SQ, p.SK, p.causal, p.win_left,
+                                           p.win_right, A.ptr(bits), stream()))
+    p.dropout_bits = A.ptr(bits)
+    for g in got:
+        g.zero_()
+    A.check(A.lib().fable_attn_backward_launch(C.byref(p), A.DT[dt], stream()))
+    torch.cuda.synchronize()
+    for nm, a, b in zip(("dQ", "dK", "dV"), first, got):
+        assert torch.equal(a, b), nm

@@ -209,3 +209,58 @@ def test_forward_deterministic(dt):
         run_fwd(fwd_params(q, k, v, o, lse, scale=128 ** -0.5, causal=True), dt)
         outs.append((o, lse))
     assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+
+
+@pytest.mark.parametrize("causal,wl,wr", [(False, -1, -1), (True, -1, -1), (False, 40, 8)])
+def test_dropout_bitmask_matches_oracle(causal, wl, wr):
+    """fa_dropout_mask_launch writes exactly the oracle's keep bits for every word a row can see."""
+    import ctypes as C
+    NH, SQ, SK, p_drop, seed = 3, 77, 150, 0.3, 0xABCDEF0123
+    W = (SK + 31) // 32
+    words = A.lib().fa_dropout_mask_words(NH, SQ, SK)
+    assert words == NH * SQ * W
+    bits = torch.zeros(words, dtype=torch.int32, device="cuda")
+    A.check(A.lib().fa_dropout_mask_launch(seed, p_drop, NH, SQ, SK, int(causal), wl, wr, A.ptr(bits),
+                                           C.c_void_p(torch.cuda.current_stream().cuda_stream)))
+    torch.cuda.synchronize()
+    got = bits.cpu().numpy().view(np.uint32).reshape(NH, W, SQ)   # [h][key word][query row]
+    for h in range(NH):
+        ref = O.dropout_mask(seed, h, SQ, SK, p_drop)
+        for q in range(SQ):
+            diag = q + SK - SQ
+            lo = max(0, diag - wl) if wl >= 0 else 0
+            hi = min(SK - 1, diag if causal else SK - 1, diag + wr if wr >= 0 else SK - 1)
+            for w in range(W):
+                if hi < w * 32 or lo > w * 32 + 31 or lo > hi:
+                    continue            # words no row reads are not written
+                want = 0
+                for b in range(32):
+                    k = w * 32 + b
+                    if k < SK and ref[q, k]:
+                        want |= 1 << b
+                assert int(got[h, w, q]) == want, (h, q, w)
+
+
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+@pytest.mark.parametrize("D", [64, 128])
+def test_forward_with_bitmask_equals_inkernel_philox(dt, D):
+    import ctypes as C
+    rng = np.random.default_rng(33)
+    B, S, NH = 2, 320, 4
+    _, q = randn(rng, (B, S, NH, D), dt)
+    _, k = randn(rng, (B, S, NH, D), dt)
+    _, v = randn(rng, (B, S, NH, D), dt)
+    seed, pd = 4242, 0.15
+    outs = []
+    for use_bits in (False, True):
+        o = torch.empty_like(q)
+        lse = torch.empty((B, NH, S), device="cuda", dtype=torch.float32)
+        p = fwd_params(q, k, v, o, lse, scale=D ** -0.5, causal=True, dropout_p=pd, seed=seed)
+        if use_bits:
+            bits = torch.zeros(A.lib().fa_dropout_mask_words(NH, S, S), dtype=torch.int32, device="cuda")
+            A.check(A.lib().fa_dropout_mask_launch(seed, pd, NH, S, S, 1, -1, 0, A.ptr(bits),
+                                                   C.c_void_p(torch.cuda.current_stream().cuda_stream)))
+            p.dropout_bits = A.ptr(bits)
+        run_fwd(p, dt)
+        outs.append((o, lse))
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
