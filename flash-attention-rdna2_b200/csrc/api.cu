@@ -1,5 +1,6 @@
 // api.cu — the extern "C" entry points declared in include/fable_attn.h: argument validation,
 // error reporting (status codes + thread-local message, never abort), kernel selection.
+#include <algorithm>
 #include <stdarg.h>
 #include <stdio.h>
 #include <atomic>
@@ -137,10 +138,14 @@ extern "C" int fa_decode_num_splits(int batch, int nq, int nheads_kv, long long 
   if (num_splits > 0) {
     n = num_splits;
   } else {
-    // enough CTAs to cover every SM ~8 times over; each split keeps >= 256 positions
+    // enough work items to cover every SM ~8 times over, and splits of at most ~1024 positions
+    // so that the persistent tensor-core decode can balance them; each split keeps >= 256
+    // positions
     const long long groups = (long long)(batch > 0 ? batch : 1) * (nq > 0 ? nq : 1) * (nheads_kv > 0 ? nheads_kv : 1);
     const long long target = 8LL * fa::num_sms();
     n = (int)((target + groups - 1) / groups);
+    const long long by_len = (ctx_bound + 1023) / 1024;
+    if (by_len > n) n = (int)std::min<long long>(by_len, 512);
     long long maxn = (ctx_bound + 255) / 256;
     if (maxn < 1) maxn = 1;
     if (n > maxn) n = (int)maxn;

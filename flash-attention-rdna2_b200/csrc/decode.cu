@@ -17,8 +17,12 @@
 #include "fa_common.cuh"
 #include "fa_launch.h"
 #include "sm100_ptx.cuh"
+#include "decode_common.cuh"
 
 namespace {
+
+using fa_dec::page_of;
+using fa_dec::rotate_row;
 
 constexpr int DEC_THREADS = 256;
 
@@ -45,36 +49,6 @@ template <> struct Vec8<float> {
     f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
   }
 };
-
-__device__ __forceinline__ void rotate_row(float* v, int rdim, int mode, const float* c, const float* s) {
-  const int half = rdim / 2;
-  for (int d = 0; d < half; ++d) {
-    if (mode == 1) {
-      const float x = v[d], y = v[d + half];
-      v[d] = x * c[d] - y * s[d];
-      v[d + half] = y * c[d] + x * s[d];
-    } else {
-      const float x = v[2 * d], y = v[2 * d + 1];
-      v[2 * d] = x * c[d] - y * s[d];
-      v[2 * d + 1] = y * c[d] + x * s[d];
-    }
-  }
-}
-
-// Page lookup with a bounds check; an invalid page index marks the position invisible and
-// raises the caller's error flag (the cache is never read out of bounds).
-__device__ __forceinline__ long long page_of(const FaDecParams& p, int b, int pos, int shift, bool& ok) {
-  const int slot = pos >> shift;
-  if (pos < 0 || slot >= p.max_blocks) {   // position past the block table's row
-    ok = false;
-    if (p.err_flag) atomicExch(p.err_flag, 1);
-    return 0;
-  }
-  const int blk = p.block_table[(long long)b * p.max_blocks + slot];
-  ok = blk >= 0 && (p.num_blocks <= 0 || blk < p.num_blocks);
-  if (!ok && p.err_flag) atomicExch(p.err_flag, 1);
-  return ok ? (long long)blk : 0;
-}
 
 // ---------------------------------------------------------------- append (new k/v -> cache)
 template <typename T>
@@ -635,8 +609,13 @@ int launch_t(const FaDecParams& p, cudaStream_t st, const void* nk, const void* 
     fa::count_launch();
     if (int rc = fa::cuda_status(cudaGetLastError(), "decode append launch")) return rc;
   }
-  int rc;
-  switch (p.HD) {
+  int rc = FA_OK;
+  bool tc = false;
+  if constexpr (!std::is_same<T, float>::value) {
+    rc = fa::dec_tc_partial(p, std::is_same<T, __half>::value ? FA_DTYPE_F16 : FA_DTYPE_BF16, st, &tc);
+    if (rc) return rc;
+  }
+  if (!tc) switch (p.HD) {
     case 16: rc = launch_partial<T, 16>(p, st); break;
     case 32: rc = launch_partial<T, 32>(p, st); break;
     case 48: rc = launch_partial<T, 48>(p, st); break;
@@ -711,7 +690,7 @@ int dec_device_error(int clear) {
     const int zero = 0;
     cudaMemcpyToSymbol(g_dec_error, &zero, sizeof(int));
   }
-  return v;
+  return v | (dec_tc_device_error(clear) ? 1 : 0);
 }
 int dec_run(const FaDecParams& p, int dtype, cudaStream_t st, const void* nk, const void* nv) {
   if (dtype == FA_DTYPE_F16) return launch_t<__half>(p, st, nk, nv);

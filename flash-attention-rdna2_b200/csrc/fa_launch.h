@@ -14,6 +14,10 @@ int bwd_device_error(int clear);   // bits of the tensor-core backward's timed-o
 int dec_run(const FaDecParams& p, int dtype, cudaStream_t st, const void* new_k, const void* new_v);
 int combine_run(const FaCombineParams& p, cudaStream_t st);
 int dec_device_error(int clear);   // bit 0: a decode pipeline wait timed out
+// tensor-core split-K decode partials; *taken = false when the call is outside its envelope
+int dec_tc_partial(const FaDecParams& p, int dtype, cudaStream_t st, bool* taken);
+int dec_tc_device_error(int clear);
+int num_sms();
 
 int current_device();
 // Raise the dynamic shared-memory limit of `func` to `bytes` once per device.

@@ -58,11 +58,16 @@ CASES = [
 PAGE = 16
 
 
-def _setup(case, dt, nsplit=0, batch=2):
+def _setup(case, dt, nsplit=0, batch=2, page=None, ctxs=None):
     name, HD, NH, gqa, ctx, window, rotary, append, leftpad, nq, sc, al = case
+    PAGE = page or globals()["PAGE"]
     rng = np.random.default_rng(zlib.crc32(name.encode()))
     NKV = NH // gqa
-    ctxs = np.array([ctx, max(ctx // 2 + 7, 1)][:batch], dtype=np.int32)
+    if ctxs is None:
+        ctxs = np.array([ctx, max(ctx // 2 + 7, 1)][:batch], dtype=np.int32)
+    else:
+        ctxs = np.asarray(ctxs, dtype=np.int32)
+        batch = len(ctxs)
     total = ctxs + (nq if append else 0)
     max_blocks = int((total.max() + PAGE - 1) // PAGE)
     nblocks = batch * max_blocks + 3
@@ -184,3 +189,43 @@ def test_combine_kernel(in_dt, out_dt):
     got_l = lse.cpu().numpy()
     assert np.array_equal(np.isfinite(got_l), np.isfinite(rl))
     assert np.abs(got_l[np.isfinite(rl)] - rl[np.isfinite(rl)]).max() < 1e-4
+
+
+# The tensor-core decode (one new token, 16-bit cache, head_dim 128, gqa <= 16): page sizes from
+# one swizzle atom (8 rows) to two tiles, several work items per sequence (long contexts), a
+# sequence with an empty context, and query-head groups that fill 1..16 of its 16 MMA rows.
+TC_CASES = [
+    # (name, page, ctxs, NH, gqa, window, leftpad, append, rotary, softcap, alibi)
+    ("p256_long", 256, [5000, 3100, 129], 32, 4, -1, 0, False, 0, 0.0, False),
+    ("p8_gqa8", 8, [1500, 700], 32, 8, -1, 0, False, 0, 0.0, False),
+    ("p64_gqa16", 64, [2300, 1100], 32, 16, -1, 0, True, 1, 0.0, False),
+    ("p128_gqa2_window", 128, [4000, 260], 16, 2, 700, 0, False, 0, 0.0, False),
+    ("p32_gqa3_leftpad", 32, [3000, 900], 12, 3, -1, 130, False, 0, 30.0, True),
+    ("p256_empty_seq", 256, [2000, 0, 777], 16, 4, -1, 0, False, 0, 0.0, False),
+]
+
+
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+@pytest.mark.parametrize("tc", TC_CASES, ids=[c[0] for c in TC_CASES])
+def test_decode_tensor_core_envelope(tc, dt):
+    name, page, ctxs, NH, gqa, window, leftpad, append, rotary, sc, al = tc
+    case = (name, 128, NH, gqa, max(ctxs), window, rotary, append, leftpad, 1, sc, al)
+    s = _setup(case, dt, page=page, ctxs=ctxs)
+    _launch(s, dt)
+    ro, rl = s["ref"]
+    e = O.rel_rms(to_np(s["o"]), ro)
+    assert e < TOL[dt], f"O rel_rms {e:.3e}"
+    lse = s["lse"].cpu().numpy()
+    fin = np.isfinite(rl)
+    assert np.array_equal(np.isfinite(lse), fin)   # empty contexts: LSE -inf, O 0
+    assert O.rel_rms(lse[fin], rl[fin]) < TOL[dt]
+    assert int(s["err"].item()) == 0
+
+
+@pytest.mark.parametrize("nsplit", [1, 3, 64])
+def test_decode_tensor_core_split_invariance(nsplit):
+    tc = TC_CASES[0]
+    case = (tc[0], 128, tc[3], tc[4], max(tc[2]), -1, 0, False, 0, 1, 0.0, False)
+    s = _setup(case, "bf16", nsplit=nsplit, page=tc[1], ctxs=tc[2])
+    _launch(s, "bf16")
+    assert O.rel_rms(to_np(s["o"]), s["ref"][0]) < TOL["bf16"]
