@@ -245,6 +245,18 @@ __global__ void __launch_bounds__(DEC_THREADS) dec_partial_kernel(const FaDecPar
 template <typename T>
 __global__ void dec_merge_kernel(const FaDecParams p) {
   const int row = blockIdx.x, h = blockIdx.y, HD = p.HD;
+  {   // an empty context has no partials to read: O = 0, LSE = -inf
+    const int b = row / p.nq, tk = row % p.nq, ctx0 = p.ctx_len[b];
+    const int ctx = ctx0 + (p.append ? tk + 1 : 0);
+    int lo = p.leftpad ? p.leftpad[b] : 0;
+    if (p.window >= 0) lo = max(lo, ctx0 + tk - p.window + 1);
+    if (ctx <= max(lo, 0)) {
+      T* o = (T*)p.o + ((long long)row * p.NH + h) * HD;
+      for (int d = threadIdx.x; d < HD; d += blockDim.x) o[d] = Elem<T>::from_f(0.f);
+      if (p.lse_out && threadIdx.x == 0) p.lse_out[(long long)row * p.NH + h] = -INFINITY;
+      return;
+    }
+  }
   const float* base = p.scratch + ((long long)row * p.NH + h) * (long long)p.nsplit * (HD + 2);
   float M = -INFINITY;
   for (int s = 0; s < p.nsplit; ++s) M = fmaxf(M, base[(long long)s * (HD + 2)]);

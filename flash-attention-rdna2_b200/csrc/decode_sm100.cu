@@ -4,29 +4,33 @@
 // Decode streams every K/V byte of a sequence's context once per kv head; with GQA 4 that is
 // two multiply-adds per streamed byte, more than the CUDA cores sustain next to HBM3e.  Both
 // contractions therefore run on tcgen05, transposed so that the long dimension is M:
-//   S^T = K Q^T    M = 128 positions (TMEM lanes), N = 16 query rows, K = head dim
-//   O^T = V^T P^T  M = 128 head dims (TMEM lanes), N = 16 query rows, K = 128 positions
+//   S^T = K Q^T    M = 128 positions (TMEM lanes), N = query rows, K = head dim
+//   O^T = V^T P^T  M = 128 head dims (TMEM lanes), N = query rows, K = 128 positions
 // K and V tiles arrive by TMA (128-byte swizzle; one box per page slice and 64-column chunk)
-// in a 3-stage ring; Q and P^T sit in shared memory; S^T and O^T are double-buffered in TMEM.
-// Q and P enter the MMAs as 16-bit hi + lo pairs (rows r and NRV + r of the N dimension, summed
-// when S^T / O^T are read), so the contractions keep ~22 bits of q and p as the reference's fp32
-// arithmetic does; K and V are used exactly as stored.
+// in separate rings (K: 2 stages, freed as soon as S^T is computed; V: 4 stages, 3 for 16 query
+// rows, held until P.V completes), each fed by its own producer warp; Q and P^T sit in shared
+// memory; S^T and O^T are double-buffered in TMEM.  Q and P enter the MMAs as 16-bit hi + lo
+// pairs (rows r and NRV + r of the N dimension, summed when S^T / O^T are read), so the
+// contractions keep ~22 bits of q and p as the reference's fp32 arithmetic does; K and V are
+// used exactly as stored.
 // The 128 softmax threads own one position each for S^T and one head dim each for O^T.  Each
 // tile's O^T is folded into register accumulators with the tile's max change, so TMEM is never
 // rescaled.  The row max is lazy: a tile triggers a CTA-wide max only when a score exceeds the
 // running reference by more than 2^8, otherwise probabilities are taken against the reference.
 //
-// Work split: the context [lo, ctx) of every (sequence, kv head) is cut at absolute 128-position
-// tile boundaries into items of TPI tiles, TPI the same for all sequences (from the longest
-// context and nsplit), so items have equal cost.  A persistent grid of one CTA per SM takes items
-// round-robin and streams them through one continuous pipeline; item (b, kvh, sp) writes split
-// slot sp of each of its query heads (m in log2 units, l, acc[128]), and slots a sequence does
-// not reach are written neutral (m = -inf) for the merge kernel.  Semantics follow the
-// FaDecParams contract of fable_attn.h (kernels/fa_decode.hip:57-252 of the reference).
+// Work split (stream-K): the contexts [lo, ctx) of all (sequence, kv head) groups, cut at
+// absolute 128-position tile boundaries, form one sequence of tiles (sequence-major).  CTA c of
+// the persistent grid (one per SM) takes tiles [c*Q, (c+1)*Q), Q = ceil(total / grid) (raised so
+// that no group spans more than nsplit CTAs), so every CTA streams the same number of bytes.
+// Each piece of a group a CTA covers is a segment; it writes split slot c - first CTA of the
+// group (m in log2 units, l, acc[128]) for every query head of the group, and the CTA holding
+// the group's last segment writes the remaining slots neutral (m = -inf) for the merge kernel,
+// which handles empty contexts itself.  Semantics follow the FaDecParams contract of
+// fable_attn.h (kernels/fa_decode.hip:57-252 of the reference).
 //
-// Warp roles (192 threads): 0-3 softmax / accumulate, 4 TMA producer, 5 MMA issuer.  Every
-// wait is bounded (a timeout records an error and unwinds), and the softmax warps break out
-// of their loops only together (bar.red.and), so no named barrier is left waiting.
+// Warp roles (224 threads): 0-3 softmax / accumulate, 4 K producer, 5 MMA issuer, 6 V producer.
+// Every wait is bounded (a timeout records an error and unwinds), and the softmax warps break
+// out of their loops only together (bar.red.and), so no named barrier is left waiting.
 #include <cudaTypedefs.h>
 #include <algorithm>
 #include <cstdlib>
@@ -40,12 +44,11 @@ namespace {
 
 using namespace sm100;
 using fa_dec::page_of;
-using fa_dec::rotate_row;
 
 constexpr int TT = 128;            // positions per tile (M of S^T)
 constexpr int HD = 128;            // head dim (M of O^T)
-constexpr int NS = 3;              // K/V ring stages
-constexpr int NTH = 192;
+constexpr int NK = 2;              // K ring stages (a K tile is free once S^T is computed)
+constexpr int NTH = 224;
 constexpr int TILE_B = TT * HD * 2;             // one K or V tile, 32 KB
 constexpr int CHUNK_B = TT * 128;               // one 64-column chunk of a tile
 constexpr float LAZY = 8.f;                     // log2 headroom of the lazy row max
@@ -54,24 +57,24 @@ constexpr float LAZY = 8.f;                     // log2 headroom of the lazy row
 // [NRV, 2 NRV) and zeros above
 template <int NRV>
 struct Lay {
+  static constexpr int NV = NRV >= 16 ? 3 : 4;        // V ring stages (held until P.V completes)
   static constexpr int NQ = 2 * NRV < 16 ? 16 : 2 * NRV;
   static constexpr uint32_t S_COL = 0, O_COL = 2 * NQ, TMEM_COLS = 4 * NQ <= 64 ? 64 : 128;
-  static constexpr int K = 0;                         // [NS][2 chunks][128 rows][128 B]
-  static constexpr int V = NS * TILE_B;
-  static constexpr int Q = 2 * NS * TILE_B;           // [2][2 chunks][NQ rows][128 B]
+  static constexpr int K = 0;                         // [NK][2 chunks][128 rows][128 B]
+  static constexpr int V = NK * TILE_B;               // [NV][2 chunks][128 rows][128 B]
+  static constexpr int Q = (NK + NV) * TILE_B;        // [2][2 chunks][NQ rows][128 B]
   static constexpr int QB = NQ * HD * 2;
-  static constexpr int P = Q + 2 * QB;                // [2][2 chunks][NQ rows][128 B]; also the
-  static constexpr int PB = NQ * TT * 2;              //   fp32 q staging [NRV][HD] at item start
+  static constexpr int P = Q + 2 * QB;                // [2][2 chunks][NQ rows][128 B]
+  static constexpr int PB = NQ * TT * 2;
   static constexpr int RED = P + 2 * PB;              // cross-warp reductions [4][NRV] fp32
   static constexpr int BAR = RED + 4 * NRV * 4;
-  // barriers: KF[NS] VF[NS] EMPTY[NS] SF[2] PF[2] OF[2] QF[2] QE[2] DRAIN
-  static constexpr int KF = 0, VF = NS, EMPTY = 2 * NS, SF = 3 * NS, PF = SF + 2, OF = PF + 2, QFULL = OF + 2,
-                       QE = QFULL + 2, DRAIN = QE + 2, NBAR = DRAIN + 1;
+  // barriers: KF[NK] KE[NK] VF[NV] VE[NV] SF[2] PF[2] OF[2] QF[2] QE[2] DRAIN
+  static constexpr int KF = 0, KE = NK, VF = 2 * NK, VE = VF + NV, SF = VE + NV, PF = SF + 2, OF = PF + 2,
+                       QFULL = OF + 2, QE = QFULL + 2, DRAIN = QE + 2, NBAR = DRAIN + 1;
   static constexpr int SMEM = BAR + 8 * NBAR + 1024;  // + 1 KB to align the base for SW128
   static_assert(Q % 1024 == 0 && P % 1024 == 0 && QB % 1024 == 0 && PB % 1024 == 0,
                 "swizzled operand tiles must be 1 KB aligned");
-  static_assert(2 * PB >= NRV * HD * 4, "q staging must fit in the P^T buffers");
-  static_assert(SMEM <= 232448 - 64, "shared memory per CTA");
+  static_assert(SMEM <= 232448 - 2048, "shared memory per CTA");
 };
 
 __device__ int g_dectc_error = 0;
@@ -105,41 +108,6 @@ __device__ __forceinline__ uint32_t swz_off(int rows, int r, int c) {
   return (uint32_t)((c / 64) * rows * 128 + r * 128 + ((((c % 64) >> 3) ^ (r & 7)) << 4) + (c % 8) * 2);
 }
 
-// context of sequence b for its single new token: keys [lo, ctx)
-__device__ __forceinline__ void seq_range(const FaDecParams& p, int b, int& lo, int& ctx) {
-  const int ctx0 = p.ctx_len[b];
-  ctx = ctx0 + (p.append ? 1 : 0);
-  int l = p.leftpad ? p.leftpad[b] : 0;
-  if (p.window >= 0 && ctx0 - p.window + 1 > l) l = ctx0 - p.window + 1;
-  lo = l > 0 ? l : 0;
-}
-
-struct Item {
-  int b, kvh, sp, lo, ctx, t0, t1;   // absolute tiles [t0, t1), positions [lo, ctx)
-};
-__device__ __forceinline__ bool item_of(const FaDecParams& p, int i, int NKV, int TPI, Item& it) {
-  it.kvh = i % NKV;
-  const int r = i / NKV;
-  it.b = r % p.batch;
-  it.sp = r / p.batch;
-  seq_range(p, it.b, it.lo, it.ctx);
-  if (it.ctx <= it.lo) return false;
-  const int T0 = it.lo / TT, T1 = (it.ctx - 1) / TT + 1;
-  it.t0 = T0 + it.sp * TPI;
-  it.t1 = min(it.t0 + TPI, T1);
-  return it.t0 < it.t1;
-}
-
-template <typename T>
-__device__ __forceinline__ uint32_t pack2(float a, float b) {
-  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-    const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
-    return *reinterpret_cast<const uint32_t*>(&v);
-  } else {
-    const __half2 v = __floats2half2_rn(a, b);
-    return *reinterpret_cast<const uint32_t*>(&v);
-  }
-}
 template <typename T>
 __device__ __forceinline__ float round16(float a) {
   if constexpr (std::is_same<T, __nv_bfloat16>::value) return __bfloat162float(__float2bfloat16_rn(a));
@@ -151,6 +119,50 @@ __device__ __forceinline__ unsigned short bits16(float a) {
   else return __half_as_ushort(__float2half_rn(a));
 }
 
+// context of sequence b for its single new token: keys [lo, ctx); returns its tile count
+// (tiles lo/TT .. (ctx-1)/TT)
+__device__ __forceinline__ int seq_tiles(const FaDecParams& p, int b, int& lo, int& ctx) {
+  const int ctx0 = p.ctx_len[b];
+  ctx = ctx0 + (p.append ? 1 : 0);
+  int l = p.leftpad ? p.leftpad[b] : 0;
+  if (p.window >= 0 && ctx0 - p.window + 1 > l) l = ctx0 - p.window + 1;
+  lo = l > 0 ? l : 0;
+  return ctx > lo ? (ctx - 1) / TT + 1 - lo / TT : 0;
+}
+
+// One CTA's walk over its tile range [start, end) of the global tile sequence
+struct Seg {
+  int b, kvh, slot, lo, ctx;
+  int t0, t1;      // absolute tile indices [t0, t1)
+  bool last;       // the group's last segment
+};
+struct Walk {
+  long long start, end, Q, off;   // off: global tile offset of group (b, kvh)
+  int b, kvh, c;
+  __device__ bool next(const FaDecParams& p, int NKV, Seg& s) {
+    while (b < p.batch) {
+      int lo, ctx;
+      const int n = seq_tiles(p, b, lo, ctx);
+      if (n == 0) {   // empty context: no tiles, the merge handles it
+        ++b;
+        kvh = 0;
+        continue;
+      }
+      if (off >= end) return false;
+      const long long a0 = start > off ? start : off, a1 = end < off + n ? end : off + n;
+      s.b = b; s.kvh = kvh; s.lo = lo; s.ctx = ctx;
+      s.t0 = lo / TT + (int)(a0 - off);
+      s.t1 = lo / TT + (int)(a1 - off);
+      s.slot = c - (int)(off / Q);
+      s.last = off + n <= end;
+      off += n;
+      if (++kvh == NKV) { kvh = 0; ++b; }
+      return true;
+    }
+    return false;
+  }
+};
+
 // NRV: query rows handled (a power of two >= gqa, <= 16)
 template <typename T, int NRV>
 __global__ void __launch_bounds__(NTH, 1)
@@ -160,7 +172,9 @@ __global__ void __launch_bounds__(NTH, 1)
   constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
   extern __shared__ uint8_t smraw[];
   __shared__ uint32_t s_tmem;
-  __shared__ int s_maxt;
+  __shared__ long long s_part[NTH];   // per-thread tile sums, then their exclusive prefix
+  __shared__ int s_maxn, s_b0;
+  __shared__ long long s_total, s_off0;
   const uint32_t sb = (smem_u32(smraw) + 1023u) & ~1023u;
   uint8_t* sg = smraw + (sb - smem_u32(smraw));
   auto bar = [&](int i) { return sb + (uint32_t)L::BAR + 8u * (uint32_t)i; };
@@ -169,13 +183,28 @@ __global__ void __launch_bounds__(NTH, 1)
   const int NKV = p.NH / p.gqa, nh = p.gqa;
   const int shift = __ffs(p.page) - 1, pmask = p.page - 1;
   const int R = p.page < TT ? p.page : TT;   // rows of one page-slice box
+  const int c = blockIdx.x;
 
-  if (t == 0) s_maxt = 0;
-  __syncthreads();
-  for (int b = t; b < p.batch; b += NTH) {
-    int lo, ctx;
-    seq_range(p, b, lo, ctx);
-    if (ctx > lo) atomicMax(&s_maxt, (ctx - 1) / TT + 1 - lo / TT);
+  // ---- schedule: per-sequence tile counts (each thread a chunk of sequences), their prefix
+  const int CB = (p.batch + NTH - 1) / NTH;
+  {
+    long long sum = 0;
+    int mx = 0;
+    for (int b = t * CB; b < min(p.batch, (t + 1) * CB); ++b) {
+      int lo, ctx;
+      const int n = seq_tiles(p, b, lo, ctx);
+      sum += n;
+      mx = max(mx, n);
+    }
+    if (t == 0) { s_maxn = 0; s_b0 = p.batch; s_off0 = 0; }
+    s_part[t] = sum;
+    __syncthreads();
+    atomicMax(&s_maxn, mx);
+    if (t == 0) {
+      long long a = 0;
+      for (int i = 0; i < NTH; ++i) { const long long v = s_part[i]; s_part[i] = a; a += v; }
+      s_total = a * NKV;
+    }
   }
   if (t == 0) {
     for (int i = 0; i < L::NBAR; ++i) {
@@ -189,58 +218,100 @@ __global__ void __launch_bounds__(NTH, 1)
     tmem_alloc(smem_u32(&s_tmem), L::TMEM_COLS);
     tmem_relinquish();
   }
+  // Q and P^T rows >= 2 NRV stay zero for the whole kernel (16-byte units of the 4 buffers)
+  for (int e = t; e < 2 * (L::QB + L::PB) / 16; e += NTH) {
+    const int byte = e * 16, pair = L::QB + L::PB, bufi = byte / pair, in = byte % pair;
+    const bool isq = in < L::QB;
+    const int off = isq ? in : in - L::QB, row = (off % (NQ * 128)) / 128;
+    if (row >= 2 * NRV)
+      *reinterpret_cast<uint4*>(sg + (isq ? L::Q + bufi * L::QB : L::P + bufi * L::PB) + off) = make_uint4(0, 0, 0, 0);
+  }
+  __syncthreads();
+  const long long total = s_total;
+  const int G = gridDim.x;
+  long long Qt = (total + G - 1) / G;
+  if (Qt < (long long)((s_maxn + p.nsplit - 2) / (p.nsplit - 1))) Qt = (s_maxn + p.nsplit - 2) / (p.nsplit - 1);
+  if (Qt < 1) Qt = 1;
+  const long long start = (long long)c * Qt, end = (c == G - 1) ? (1ll << 62) : start + Qt;
+  // the thread whose chunk of sequences holds tile `start` finds the first sequence
+  if (start < total) {
+    const long long lo_t = s_part[t] * NKV;
+    const long long hi_t = (t + 1 < NTH ? s_part[t + 1] * NKV : total);
+    if (start >= lo_t && start < hi_t) {
+      long long off = lo_t;
+      for (int b = t * CB; b < min(p.batch, (t + 1) * CB); ++b) {
+        int lo, ctx;
+        const int n = seq_tiles(p, b, lo, ctx);
+        if (start < off + (long long)n * NKV) {
+          s_b0 = b;
+          s_off0 = off;
+          break;
+        }
+        off += (long long)n * NKV;
+      }
+    }
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s_tmem;
-  const int TPI = max(1, (s_maxt + p.nsplit - 1) / p.nsplit);
-  const int nitems = p.nsplit * p.batch * NKV;
+  auto walk0 = [&]() {
+    Walk w;
+    w.start = start; w.end = end; w.Q = Qt; w.c = c;
+    w.b = s_b0; w.kvh = 0; w.off = s_off0;
+    if (w.b < p.batch) {   // the group of sequence b0 that holds tile `start`
+      int lo, ctx;
+      const int n = seq_tiles(p, w.b, lo, ctx);
+      w.kvh = (int)((start - w.off) / n);
+      w.off += (long long)w.kvh * n;
+    }
+    return w;
+  };
 
-  if (warp == 4) {
-    // ============================================================ TMA producer
+  if (warp == 4 || warp == 6) {
+    // ============================================================ TMA producers: warp 4 K, warp 6 V
     if (lane == 0) {
+      const bool isk = warp == 4;
+      const int NR = isk ? NK : L::NV;
+      const int FULL = isk ? L::KF : L::VF, FREE = isk ? L::KE : L::VE;
+      const CUtensorMap* map = isk ? &tmK : &tmV;
+      const uint32_t ring = sb + (isk ? L::K : L::V);
+      Walk w = walk0();
+      Seg sgm;
       int g = 0;
       bool ok = true;
-      for (int i = blockIdx.x; ok && i < nitems; i += gridDim.x) {
-        Item it;
-        if (!item_of(p, i, NKV, TPI, it)) continue;
-        for (int tile = it.t0; tile < it.t1; ++tile, ++g) {
-          const int s = g % NS;
-          if (g >= NS && !mbar_wait(bar(L::EMPTY + s), ((g / NS) - 1) & 1)) { ok = false; break; }
+      while (ok && w.next(p, NKV, sgm)) {
+        for (int tile = sgm.t0; tile < sgm.t1; ++tile, ++g) {
+          const int s = g % NR;
+          if (g >= NR && !mbar_wait(bar(FREE + s), ((g / NR) - 1) & 1)) { ok = false; break; }
           const int base = tile * TT;
           uint32_t bytes = 0;
           for (int k = 0; k < TT / R; ++k) {
             const int pos0 = base + k * R;
-            if (pos0 + R <= it.lo || pos0 >= it.ctx) continue;
+            if (pos0 + R <= sgm.lo || pos0 >= sgm.ctx) continue;
             bool okp;
-            page_of(p, it.b, pos0, shift, okp);
+            page_of(p, sgm.b, pos0, shift, okp);
             if (okp) bytes += (uint32_t)(R * HD * 2);
           }
-          mbar_expect_tx(bar(L::KF + s), bytes);
-          mbar_expect_tx(bar(L::VF + s), bytes);
-          const uint32_t kd = sb + L::K + s * TILE_B, vd = sb + L::V + s * TILE_B;
+          mbar_expect_tx(bar(FULL + s), bytes);
+          const uint32_t dst = ring + s * TILE_B;
           for (int k = 0; k < TT / R; ++k) {
             const int pos0 = base + k * R;
-            if (pos0 + R <= it.lo || pos0 >= it.ctx) continue;
+            if (pos0 + R <= sgm.lo || pos0 >= sgm.ctx) continue;
             bool okp;
-            const long long blk = page_of(p, it.b, pos0, shift, okp);
+            const long long blk = page_of(p, sgm.b, pos0, shift, okp);
             if (!okp) continue;
             const int row = (int)(blk * p.page + (pos0 & pmask));
 #pragma unroll
-            for (int c = 0; c < HD / 64; ++c) {
-              tma_load_3d(kd + c * CHUNK_B + k * R * 128, &tmK, 64 * c, it.kvh, row, bar(L::KF + s));
-              tma_load_3d(vd + c * CHUNK_B + k * R * 128, &tmV, 64 * c, it.kvh, row, bar(L::VF + s));
-            }
+            for (int ch = 0; ch < HD / 64; ++ch)
+              tma_load_3d(dst + ch * CHUNK_B + k * R * 128, map, 64 * ch, sgm.kvh, row, bar(FULL + s));
           }
         }
       }
       if (!ok) {
         record_error(1);
         // copies still in flight must land before the CTA's shared memory is released
-        for (int j = max(0, g - NS); j < g; ++j) {
-          mbar_wait(bar(L::KF + j % NS), (j / NS) & 1, 1000000000ull);
-          mbar_wait(bar(L::VF + j % NS), (j / NS) & 1, 1000000000ull);
-        }
+        for (int j = max(0, g - NR); j < g; ++j) mbar_wait(bar(FULL + j % NR), (j / NR) & 1, 1000000000ull);
       }
     }
   } else if (warp == 5) {
@@ -250,9 +321,9 @@ __global__ void __launch_bounds__(NTH, 1)
     int g = 0, qi = 0;
     bool ok = true;
     auto issue_pv = [&](int gg) -> bool {
-      const int s = gg % NS;
+      const int s = gg % L::NV;
       if (!mbar_wait_warp(bar(L::PF + (gg & 1)), (gg >> 1) & 1)) return false;
-      if (!mbar_wait_warp(bar(L::VF + s), (gg / NS) & 1)) return false;
+      if (!mbar_wait_warp(bar(L::VF + s), (gg / L::NV) & 1)) return false;
       tc_fence_after();
       if (lane == 0) {
         const uint32_t vt = sb + L::V + s * TILE_B, pt = sb + L::P + (gg & 1) * L::PB;
@@ -260,18 +331,18 @@ __global__ void __launch_bounds__(NTH, 1)
         for (int kk = 0; kk < TT / 16; ++kk)
           mma_ss(tmem + L::O_COL + (gg & 1) * NQ, desc_mnmajor(vt, TT, kk), desc_kmajor(pt, NQ, kk), ID_O, kk > 0);
         mma_commit(bar(L::OF + (gg & 1)));
-        mma_commit(bar(L::EMPTY + s));
+        mma_commit(bar(L::VE + s));
       }
       __syncwarp();
       return true;
     };
-    for (int i = blockIdx.x; ok && i < nitems; i += gridDim.x) {
-      Item it;
-      if (!item_of(p, i, NKV, TPI, it)) continue;
+    Walk w = walk0();
+    Seg sgm;
+    while (ok && w.next(p, NKV, sgm)) {
       if (!mbar_wait_warp(bar(L::QFULL + (qi & 1)), (qi >> 1) & 1)) { ok = false; break; }
-      for (int tile = it.t0; tile < it.t1; ++tile, ++g) {
-        const int s = g % NS;
-        if (!mbar_wait_warp(bar(L::KF + s), (g / NS) & 1)) { ok = false; break; }
+      for (int tile = sgm.t0; tile < sgm.t1; ++tile, ++g) {
+        const int s = g % NK;
+        if (!mbar_wait_warp(bar(L::KF + s), (g / NK) & 1)) { ok = false; break; }
         tc_fence_after();
         if (lane == 0) {
           const uint32_t kt = sb + L::K + s * TILE_B, qt = sb + L::Q + (qi & 1) * L::QB;
@@ -279,14 +350,14 @@ __global__ void __launch_bounds__(NTH, 1)
           for (int kk = 0; kk < HD / 16; ++kk)
             mma_ss(tmem + L::S_COL + (g & 1) * NQ, desc_kmajor(kt, TT, kk), desc_kmajor(qt, NQ, kk), ID_S, kk > 0);
           mma_commit(bar(L::SF + (g & 1)));
-          if (tile == it.t1 - 1) mma_commit(bar(L::QE + (qi & 1)));
+          mma_commit(bar(L::KE + s));
+          if (tile == sgm.t1 - 1) mma_commit(bar(L::QE + (qi & 1)));
         }
         __syncwarp();
-        // P.V of the previous tile of this item overlaps the softmax of this one
-        if (tile > it.t0 && !issue_pv(g - 1)) { ok = false; break; }
+        // P.V of the previous tile of this segment overlaps the softmax of this one
+        if (tile > sgm.t0 && !issue_pv(g - 1)) { ok = false; break; }
       }
-      // the item's last P.V goes out before the next item's q is awaited (the softmax warps
-      // write that q only after consuming this O)
+      // the segment's last P.V goes out before the next segment's q is awaited
       if (ok && !issue_pv(g - 1)) ok = false;
       ++qi;
     }
@@ -301,7 +372,6 @@ __global__ void __launch_bounds__(NTH, 1)
     const bool cap_on = p.softcap > 0.f;
     const float cap_in = cap_on ? p.scale / p.softcap : 0.f, cap2 = p.softcap * FA_LOG2E;
     float* red = reinterpret_cast<float*>(sg + L::RED);
-    float* qf = reinterpret_cast<float*>(sg + L::P);   // q staging aliases the (idle) P^T buffers
     float acc[NRV], mref[NRV], lt[NRV], cprev[NRV], slope2[NRV];
     int g = 0, qi = 0;
     bool ok = true;
@@ -309,61 +379,64 @@ __global__ void __launch_bounds__(NTH, 1)
       tmem_ld16(addr, v);
       if constexpr (NQ == 32) tmem_ld16(addr + 16, v + 16);
     };
-    for (int i = blockIdx.x; ok && i < nitems; i += gridDim.x) {
-      Item it;
-      const bool live = item_of(p, i, NKV, TPI, it);
-      const int hbase = it.kvh * p.gqa;
-      if (!live) {   // a split this sequence does not reach: neutral slot for the merge
-        if (t < nh) {
-          float* o = p.scratch + ((long long)(it.b * p.NH + hbase + t) * p.nsplit + it.sp) * (HD + 2);
-          o[0] = -INFINITY;
-          o[1] = 0.f;
+    // q rows of a segment's group into Q buffer `buf`: rotary in fp32, then 16-bit hi / lo rows
+    // (one job = one pair of dims that rotate together)
+    auto write_q = [&](const Seg& sq, int buf) {
+      const int hb = sq.kvh * p.gqa;
+      const T* qg = (const T*)p.q + ((long long)sq.b * p.NH + hb) * HD;
+      const int mode = p.rotary, rdim = p.rotary_dim > 0 ? p.rotary_dim : HD, half = rdim / 2;
+      const int rp = p.rotary_pos ? p.rotary_pos[sq.b] : p.ctx_len[sq.b];
+      uint8_t* qs = sg + L::Q + buf * L::QB;
+      for (int j = t; j < NRV * (HD / 2); j += 128) {
+        const int r = j / (HD / 2), jj = j % (HD / 2);
+        int d1, d2;
+        bool rot = false;
+        if (mode == 1) {
+          if (jj < half) { d1 = jj; d2 = jj + half; rot = true; }
+          else { d1 = rdim + 2 * (jj - half); d2 = d1 + 1; }
+        } else {
+          d1 = 2 * jj; d2 = d1 + 1;
+          rot = mode == 2 && jj < half;
         }
-        continue;
-      }
-      // ---- q of this item: fp32 staging (+ rotary), then 16-bit hi / lo rows, swizzled K-major.
-      // Every P.V of earlier items has completed (their O^T were consumed), so the P^T buffers
-      // are free for the staging; they are re-zeroed afterwards.
-      const bool qfree = (qi < 2) ? true : mbar_wait_warp(bar(L::QE + (qi & 1)), ((qi >> 1) - 1) & 1);
-      if (!bar_and_128(qfree)) { ok = false; break; }
-      const T* qg = (const T*)p.q + ((long long)it.b * p.NH + hbase) * HD;
-      for (int e = t; e < NRV * HD; e += 128) qf[e] = (e / HD < nh) ? Elem<T>::to_f(qg[e]) : 0.f;
-      bar_sync_128();
-      if (p.rotary && t < nh && t < NRV) {
-        const int rdim = p.rotary_dim > 0 ? p.rotary_dim : HD;
-        const int rp = p.rotary_pos ? p.rotary_pos[it.b] : p.ctx_len[it.b];
-        rotate_row(qf + t * HD, rdim, p.rotary, p.cos + (long long)rp * (rdim / 2), p.sin + (long long)rp * (rdim / 2));
-      }
-      bar_sync_128();
-      {
-        uint8_t* qs = sg + L::Q + (qi & 1) * L::QB;
-        for (int v = t; v < NQ * HD / 8; v += 128) {
-          const int r = v / (HD / 8), c0 = (v % (HD / 8)) * 8;
-          uint4 w = make_uint4(0, 0, 0, 0);
-          if (r < 2 * NRV) {
-            const bool lo = r >= NRV;
-            const float* src = qf + (lo ? r - NRV : r) * HD + c0;
-            float x[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const float hi = round16<T>(src[j]);
-              x[j] = lo ? src[j] - hi : hi;
-            }
-            w = make_uint4(pack2<T>(x[0], x[1]), pack2<T>(x[2], x[3]), pack2<T>(x[4], x[5]), pack2<T>(x[6], x[7]));
+        float x1 = 0.f, x2 = 0.f;
+        if (r < nh) {
+          x1 = Elem<T>::to_f(qg[r * HD + d1]);
+          x2 = Elem<T>::to_f(qg[r * HD + d2]);
+          if (rot) {
+            const float cs = p.cos[(long long)rp * half + jj], sn = p.sin[(long long)rp * half + jj];
+            const float y1 = x1 * cs - x2 * sn, y2 = x2 * cs + x1 * sn;
+            x1 = y1; x2 = y2;
           }
-          *reinterpret_cast<uint4*>(qs + swz_off(NQ, r, c0)) = w;
         }
+        const float h1 = round16<T>(x1), h2 = round16<T>(x2);
+        *reinterpret_cast<unsigned short*>(qs + swz_off(NQ, r, d1)) = bits16<T>(h1);
+        *reinterpret_cast<unsigned short*>(qs + swz_off(NQ, r, d2)) = bits16<T>(h2);
+        *reinterpret_cast<unsigned short*>(qs + swz_off(NQ, NRV + r, d1)) = bits16<T>(x1 - h1);
+        *reinterpret_cast<unsigned short*>(qs + swz_off(NQ, NRV + r, d2)) = bits16<T>(x2 - h2);
       }
-      bar_sync_128();   // staging reads done before the P^T buffers are cleared
-      for (int e = t; e < 2 * L::PB / 16; e += 128) *reinterpret_cast<uint4*>(sg + L::P + e * 16) = make_uint4(0, 0, 0, 0);
       fence_proxy_async_smem();
-      mbar_arrive(bar(L::QFULL + (qi & 1)));
+      mbar_arrive(bar(L::QFULL + buf));
+    };
+    Walk w = walk0();
+    Seg cur, nxt;
+    bool have = w.next(p, NKV, cur);
+    if (have) write_q(cur, 0);
+    while (ok && have) {
+      // the next segment's q goes out now, so the MMAs can start it as soon as this one ends
+      const bool have_n = w.next(p, NKV, nxt);
+      if (have_n) {
+        const int nb = (qi + 1) & 1;
+        const bool qfree = (qi + 1 < 2) ? true : mbar_wait_warp(bar(L::QE + nb), (((qi + 1) >> 1) - 1) & 1);
+        if (!bar_and_128(qfree)) { ok = false; break; }
+        write_q(nxt, nb);
+      }
+      const int hbase = cur.kvh * p.gqa;
 #pragma unroll
       for (int r = 0; r < NRV; ++r) {
         acc[r] = 0.f; mref[r] = -INFINITY; lt[r] = 0.f; cprev[r] = 1.f;
         slope2[r] = (p.alibi && r < nh) ? p.alibi[hbase + r] * FA_LOG2E : 0.f;
       }
-      const int qpos = p.ctx_len[it.b];
+      const int qpos = p.ctx_len[cur.b];
       // O^T of tile gg into the accumulators (thread = head dim), scaled by that tile's change
       auto consume = [&](int gg) -> bool {
         const bool got = mbar_wait_warp(bar(L::OF + (gg & 1)), (gg >> 1) & 1);
@@ -376,20 +449,22 @@ __global__ void __launch_bounds__(NTH, 1)
         for (int r = 0; r < NRV; ++r) acc[r] = fmaf(acc[r], cprev[r], o[r] + o[NRV + r]);
         return true;
       };
-      for (int tile = it.t0; tile < it.t1; ++tile, ++g) {
+      for (int tile = cur.t0; tile < cur.t1; ++tile, ++g) {
+        // this thread's position and its page check, issued before the wait so that the
+        // block-table load overlaps the S^T MMA
+        const int pos = tile * TT + t;
+        bool valid = pos >= cur.lo && pos < cur.ctx;
+        if (valid) {
+          bool okp;
+          page_of(p, cur.b, pos, shift, okp);
+          valid = okp;
+        }
         const bool got = mbar_wait_warp(bar(L::SF + (g & 1)), (g >> 1) & 1);
         if (!bar_and_128(got)) { ok = false; break; }
         tc_fence_after();
         float s[NQ];
         ld_cols(la + L::S_COL + (g & 1) * NQ, s);
         tc_wait_ld();
-        const int pos = tile * TT + t;
-        bool valid = pos >= it.lo && pos < it.ctx;
-        if (valid) {
-          bool okp;
-          page_of(p, it.b, pos, shift, okp);
-          valid = okp;
-        }
         float v[NRV];
         bool need = false;
         const float dpos = (float)(pos - qpos);
@@ -435,26 +510,27 @@ __global__ void __launch_bounds__(NTH, 1)
         if (!valid) {
           // this position's V row may hold stale or unloaded bytes: P is 0 there, but 0 * NaN is
           // not, so the row is zeroed once its copy (if any) has landed
-          const int s = g % NS;
-          if (!mbar_wait(bar(L::VF + s), (g / NS) & 1)) record_error(8);
+          const int s = g % L::NV;
+          if (!mbar_wait(bar(L::VF + s), (g / L::NV) & 1)) record_error(8);
           uint8_t* vr = sg + L::V + s * TILE_B + t * 128;
 #pragma unroll
-          for (int c = 0; c < HD / 64; ++c)
+          for (int ch = 0; ch < HD / 64; ++ch)
 #pragma unroll
-            for (int u = 0; u < 8; ++u) *reinterpret_cast<uint4*>(vr + c * CHUNK_B + u * 16) = make_uint4(0, 0, 0, 0);
+            for (int u = 0; u < 8; ++u) *reinterpret_cast<uint4*>(vr + ch * CHUNK_B + u * 16) = make_uint4(0, 0, 0, 0);
         }
         // P^T / zeroed V rows visible to the tensor core; S^T (and the last O^T read) ordered
         // before the MMAs that will overwrite those TMEM columns
         fence_proxy_async_smem();
         tc_fence_before();
         mbar_arrive(bar(L::PF + (g & 1)));
-        if (tile > it.t0 && !consume(g - 1)) { ok = false; break; }
+        if (tile > cur.t0 && !consume(g - 1)) { ok = false; break; }
 #pragma unroll
         for (int r = 0; r < NRV; ++r) cprev[r] = corr[r];
       }
       if (ok && !consume(g - 1)) ok = false;
       if (!ok) break;
-      // ---- finalize: row sums over the 128 positions, then the split slot of each head
+      // ---- finalize: row sums over the 128 positions, then this segment's split slot of each
+      // head; the group's last segment also clears the slots no CTA reaches
       float lsum[NRV];
 #pragma unroll
       for (int r = 0; r < NRV; ++r) {
@@ -466,14 +542,25 @@ __global__ void __launch_bounds__(NTH, 1)
       bar_sync_128();
 #pragma unroll
       for (int r = 0; r < NRV; ++r) lsum[r] = (red[r] + red[NRV + r]) + (red[2 * NRV + r] + red[3 * NRV + r]);
+      const long long row0 = ((long long)cur.b * p.NH + hbase) * p.nsplit;
 #pragma unroll
       for (int r = 0; r < NRV; ++r) {
         if (r < nh) {
-          float* o = p.scratch + ((long long)(it.b * p.NH + hbase + r) * p.nsplit + it.sp) * (HD + 2);
+          float* o = p.scratch + (row0 + (long long)r * p.nsplit + cur.slot) * (HD + 2);
           o[2 + t] = acc[r];
           if (t == 0) { o[0] = mref[r]; o[1] = lsum[r]; }
         }
       }
+      if (cur.last) {
+        const int rest = p.nsplit - 1 - cur.slot;
+        for (int e = t; e < nh * rest; e += 128) {
+          float* o = p.scratch + (row0 + (long long)(e / rest) * p.nsplit + cur.slot + 1 + e % rest) * (HD + 2);
+          o[0] = -INFINITY;
+          o[1] = 0.f;
+        }
+      }
+      cur = nxt;
+      have = have_n;
       ++qi;
     }
     if (!ok) record_error(16);
@@ -516,9 +603,7 @@ template <typename T, int NRV>
 int launch(const FaDecParams& p, const CUtensorMap& mk, const CUtensorMap& mv, cudaStream_t st) {
   static unsigned long long done = 0;
   if (int rc = fa::ensure_smem((const void*)dec_tc_kernel<T, NRV>, Lay<NRV>::SMEM, &done)) return rc;
-  const long long items = (long long)p.nsplit * p.batch * (p.NH / p.gqa);
-  const int grid = (int)std::min<long long>(items, (long long)fa::num_sms());
-  dec_tc_kernel<T, NRV><<<grid, NTH, Lay<NRV>::SMEM, st>>>(mk, mv, p);
+  dec_tc_kernel<T, NRV><<<fa::num_sms(), NTH, Lay<NRV>::SMEM, st>>>(mk, mv, p);
   fa::count_launch();
   return fa::cuda_status(cudaGetLastError(), "decode partial (tcgen05) launch");
 }
@@ -531,10 +616,10 @@ namespace fa {
 int dec_tc_partial(const FaDecParams& p, int dtype, cudaStream_t st, bool* taken) {
   *taken = false;
   if (dtype != FA_DTYPE_F16 && dtype != FA_DTYPE_BF16) return FA_OK;
-  if (p.HD != HD || p.nq != 1 || p.gqa > 16 || p.page < 8 || p.num_blocks <= 0) return FA_OK;
+  if (p.HD != HD || p.nq != 1 || p.gqa > 16 || p.page < 8 || p.num_blocks <= 0 || p.nsplit < 2) return FA_OK;
   if (getenv("FABLE_ATTN_DECODE_NO_TC")) return FA_OK;
   const long long rows = p.num_blocks * (long long)p.page;
-  if (rows >= (1ll << 31) || (long long)p.nsplit * p.batch * (p.NH / p.gqa) >= (1ll << 31)) return FA_OK;
+  if (rows >= (1ll << 31)) return FA_OK;
   const int NKV = p.NH / p.gqa;
   const bool bf16 = dtype == FA_DTYPE_BF16;
   const int R = p.page < TT ? p.page : TT;
