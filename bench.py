@@ -330,6 +330,56 @@ def bench_decode(dev, steps=20, warmup=5):
             "GBps": round(nbytes / ms / 1e6, 1), "bytes": nbytes}
 
 
+def bench_varlen_swa(dev, steps=10, warmup=3):
+    """Config 5: 16 packed sequences, lengths ~ U[256, 8192] (seeded), cu_seqlens_q = cu_seqlens_k,
+    Hq 64, Hk 8, D 128 bf16, causal window (512, 0), softcap 30, NeoX rotary rd 64 (base 10000,
+    positions restart per sequence) on q and k.  Reports the attention kernel alone and the
+    public path (rotary as torch ops, then flash_attn_varlen_func)."""
+    import fable_attn as fa
+    from fable_attn import _C
+    from fable_attn.layers.rotary import apply_rotary_emb
+    rng = np.random.default_rng(5)
+    lens = rng.integers(256, 8193, size=16)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32, device=dev)
+    tot, Hq, Hk, D, rd = int(lens.sum()), 64, 8, 128, 64
+    g = torch.Generator(device=dev).manual_seed(5)
+    q = torch.randn(tot, Hq, D, device=dev, dtype=torch.bfloat16, generator=g)
+    k = torch.randn(tot, Hk, D, device=dev, dtype=torch.bfloat16, generator=g)
+    v = torch.randn(tot, Hk, D, device=dev, dtype=torch.bfloat16, generator=g)
+    inv = 10000.0 ** (-torch.arange(0, rd, 2, device=dev, dtype=torch.float32) / rd)
+    ang = torch.arange(int(lens.max()), device=dev, dtype=torch.float32)[:, None] * inv[None]
+    cos, sin = ang.cos(), ang.sin()
+    mx, sc = int(lens.max()), D ** -0.5
+    pairs = sum(min(i + 1, 513) for L in lens for i in range(L))
+    flops = 4.0 * D * Hq * pairs
+
+    def kernel():
+        _C.fwd_varlen(q, k, v, cu, cu, mx, mx, sc, True, 512, 0, 30.0, None, 0.0, 0)
+
+    def public():
+        qr = apply_rotary_emb(q, cos, sin, cu_seqlens=cu, max_seqlen=mx)
+        kr = apply_rotary_emb(k, cos, sin, cu_seqlens=cu, max_seqlen=mx)
+        fa.flash_attn_varlen_func(qr, kr, v, cu, cu, mx, mx, softmax_scale=sc, causal=True, window_size=(512, 0),
+                                  softcap=30.0)
+
+    out = {"config": "varlen SWA prefill 16 seqs U[256,8192] Hq64 Hk8 D128 bf16 window(512,0) softcap30 rotary64",
+           "tokens": tot, "flops": flops}
+    for name, fn in (("kernel", kernel), ("with_rotary", public)):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        a, b = _events()
+        a.record()
+        for _ in range(steps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / steps
+        out[name + "_ms"] = round(ms, 4)
+        out[name + "_tflops"] = round(flops / (ms * 1e-3) / 1e12, 1)
+    return out
+
+
 def _barrier(ws):
     if ws > 1:
         torch.distributed.barrier()
@@ -419,6 +469,10 @@ def main():
             extra["decode_paged"] = bench_decode(dev)
         except Exception as e:
             extra["decode_paged"] = {"error": f"{type(e).__name__}: {e}"[:200]}
+        try:
+            extra["varlen_swa_prefill"] = bench_varlen_swa(dev)
+        except Exception as e:
+            extra["varlen_swa_prefill"] = {"error": f"{type(e).__name__}: {e}"[:200]}
     cpu = None
     if rank == 0 and ws == 1:
         val, cores, kind, desc = cpu_reference_sample(seconds=args.cpu_seconds)

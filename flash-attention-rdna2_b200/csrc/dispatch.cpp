@@ -148,6 +148,7 @@ py::object fwd_varlen(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::
   p.cu_q = opt_i32(cu_q); p.cu_k = opt_i32(cu_k);
   p.seqused_q = opt_i32(seqused_q); p.seqused_k = opt_i32(seqused_k);
   p.lse_total_q = q.size(0);
+  p.total_k = k.size(0);
   check(fa_forward_launch(&p, dt_of(q), cur_stream(q)), "forward (varlen)");
   if (return_lse) return py::make_tuple(out, lse);
   return py::cast(out);
@@ -213,6 +214,7 @@ std::vector<torch::Tensor> bwd_varlen(torch::Tensor dout, torch::Tensor q, torch
   p.cu_q = opt_i32(cu_q); p.cu_k = opt_i32(cu_k);
   p.seqused_q = opt_i32(seqused_q); p.seqused_k = opt_i32(seqused_k);
   p.lse_total_q = q.size(0);
+  p.total_k = k.size(0);
   check(fable_attn_backward_launch(&p, dt_of(q), cur_stream(q)), "backward (varlen)");
   return {dq, dk, dv};
 }

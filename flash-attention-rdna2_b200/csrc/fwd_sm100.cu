@@ -478,12 +478,14 @@ int fwd_sm100(const FaFwdParams& p, int dtype, cudaStream_t st, bool* taken) {
   if (major != 10 || minor != 0) return FA_OK;
   const bool bf16 = dtype == FA_DTYPE_BF16;
   const bool varlen = p.cu_q != nullptr;
-  // varlen tensors are (total, H, D): a 4-D map with one batch entry, rows = tokens; the row
-  // extent is taken from the largest token index any sequence can address
+  // varlen tensors are (total, H, D): a 4-D map with one batch entry whose rows are the packed
+  // tokens, bounded by the tensors' true row counts so that no box reads past them (rows of the
+  // next sequence are loaded but masked, rows past the last token read as zeros)
   long long rows_q, rows_k;
   if (varlen) {
-    rows_q = rows_k = (1ll << 31) - 1;   // bounded by the allocation, see below
-    return FA_OK;                        // varlen on the tensor cores: not yet enabled
+    if (p.lse_total_q <= 0 || p.total_k <= 0) return FA_OK;
+    rows_q = p.lse_total_q;
+    rows_k = p.total_k;
   } else {
     rows_q = p.SQ;
     rows_k = p.SK;

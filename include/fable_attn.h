@@ -90,6 +90,9 @@ typedef struct FaFwdParams {
   long long lse_total_q;               /* varlen LSE row length (total tokens of q) */
   const unsigned int* dropout_bits;    /* optional precomputed keep mask (fa_dropout_mask_launch,
                                           dense only); null = Philox evaluated in the kernel */
+  long long total_k;                   /* varlen: rows of K and V (total key tokens).  The tensor-core
+                                          kernel needs it (with lse_total_q as the rows of Q and O) to
+                                          bound its TMA boxes; 0 = unknown, the CUDA-core kernel runs */
 } FaFwdParams;
 
 FA_API int fa_forward_launch(const FaFwdParams* p, int dtype, void* stream);
@@ -121,6 +124,7 @@ typedef struct FaBwdParams {
   const int* seqused_q; const int* seqused_k;
   long long lse_total_q;
   const unsigned int* dropout_bits;    /* optional precomputed keep mask, as in FaFwdParams */
+  long long total_k;                   /* varlen: rows of K and V, as in FaFwdParams */
 } FaBwdParams;
 
 FA_API int fable_attn_backward_launch(const FaBwdParams* p, int dtype, void* stream);

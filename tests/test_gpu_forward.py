@@ -126,7 +126,7 @@ def test_forward_varlen(dt, seqused):
     p.cu_q = p.cu_k = A.ptr(cu_t)
     if seqused:
         p.seqused_q, p.seqused_k = A.ptr(uq), A.ptr(uk)
-    p.lse_total_q = tot
+    p.lse_total_q = p.total_k = tot
     run_fwd(p, dt)
     ref_o = np.zeros_like(qn)
     ref_l = np.full((NH, tot), -np.inf, dtype=np.float32)
@@ -264,3 +264,47 @@ def test_forward_with_bitmask_equals_inkernel_philox(dt, D):
         run_fwd(p, dt)
         outs.append((o, lse))
     assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+
+
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+@pytest.mark.parametrize("total_k_known", [True, False])
+def test_forward_varlen_swa_softcap_gqa8(dt, total_k_known):
+    """Config-5 shape in miniature: packed sequences, GQA 8, causal sliding window (512, 0),
+    softcap 30, keys longer than queries (cu_seqlens_k != cu_seqlens_q).  With total_k the
+    tensor-core kernel runs; without it (an older caller) the CUDA-core kernel does."""
+    import ctypes as C
+    rng = np.random.default_rng(41)
+    lq, lk = [700, 130, 1000, 257, 1], [900, 130, 1000, 300, 1]
+    NH, Hk, D = 16, 2, 128
+    cq = np.concatenate([[0], np.cumsum(lq)]).astype(np.int32)
+    ck = np.concatenate([[0], np.cumsum(lk)]).astype(np.int32)
+    tq, tk = int(cq[-1]), int(ck[-1])
+    qn, q = randn(rng, (tq, NH, D), dt)
+    kn, k = randn(rng, (tk, Hk, D), dt)
+    vn, v = randn(rng, (tk, Hk, D), dt)
+    o = torch.zeros_like(q)
+    lse = torch.full((NH, tq), -np.inf, device="cuda", dtype=torch.float32)
+    cq_t, ck_t = torch.from_numpy(cq).cuda(), torch.from_numpy(ck).cuda()
+    p = A.FaFwdParams()
+    p.struct_size = C.sizeof(A.FaFwdParams)
+    p.Q, p.K, p.V, p.O, p.LSE = A.ptr(q), A.ptr(k), A.ptr(v), A.ptr(o), A.ptr(lse)
+    p.sQ = A.FaStrides(0, q.stride(1), q.stride(0))
+    p.sK = A.FaStrides(0, k.stride(1), k.stride(0))
+    p.sV = A.FaStrides(0, v.stride(1), v.stride(0))
+    p.sO = A.FaStrides(0, o.stride(1), o.stride(0))
+    p.batch, p.SQ, p.SK, p.HD, p.NH, p.gqa = len(lq), max(lq), max(lk), D, NH, NH // Hk
+    p.scale, p.causal, p.win_left, p.win_right, p.softcap = D ** -0.5, 1, 512, 0, 30.0
+    p.cu_q, p.cu_k = A.ptr(cq_t), A.ptr(ck_t)
+    p.lse_total_q = tq
+    p.total_k = tk if total_k_known else 0
+    run_fwd(p, dt)
+    ref_o = np.zeros_like(qn)
+    ref_l = np.full((NH, tq), -np.inf, dtype=np.float32)
+    for i in range(len(lq)):
+        a, b = int(cq[i]), int(ck[i])
+        oo, ll = O.forward(qn[a:a + lq[i]][None], kn[b:b + lk[i]][None], vn[b:b + lk[i]][None], D ** -0.5, True,
+                           512, 0, 30.0)
+        ref_o[a:a + lq[i]] = oo[0]
+        ref_l[:, a:a + lq[i]] = ll[0]
+    assert O.rel_rms(to_np(o), ref_o) < TOL[dt]
+    assert lse_close(lse.cpu().numpy(), ref_l, TOL[dt])[0]
