@@ -291,6 +291,57 @@ std::vector<torch::Tensor> combine(torch::Tensor out_partial, torch::Tensor lse_
 
 }  // namespace
 
+// ------------------------------------------------------------------ rotary (q / k, one pass)
+// x (batch, seqlen, heads, dim) or, with cu_seqlens, (total, heads, dim); dim contiguous.
+// offsets: int or per-sequence int32 tensor.  Returns the rotated tensor (x itself if inplace).
+torch::Tensor rotary(torch::Tensor x, torch::Tensor cos, torch::Tensor sin, bool interleaved, bool inplace,
+                     py::object offsets, c10::optional<torch::Tensor> cu_seqlens) {
+  TORCH_CHECK_VALUE(x.is_cuda(), "fable_attn: rotary expects a CUDA tensor");
+  TORCH_CHECK_VALUE(x.stride(-1) == 1, "fable_attn: rotary needs a contiguous last dim");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const bool varlen = cu_seqlens.has_value() && cu_seqlens->defined();
+  TORCH_CHECK_VALUE(x.dim() == (varlen ? 3 : 4), "fable_attn: rotary expects ", varlen ? "(total, heads, dim)" :
+                    "(batch, seqlen, heads, dim)");
+  // rows must be one strided dimension: (batch, seqlen) merge when batch stride = seqlen * row stride
+  torch::Tensor src = x;
+  if (!varlen && x.size(0) > 1 && x.stride(0) != x.size(1) * x.stride(1)) src = x.contiguous();
+  auto c = cos.to(torch::kFloat32).contiguous(), s = sin.to(torch::kFloat32).contiguous();
+  TORCH_CHECK_VALUE(c.dim() == 2 && s.sizes() == c.sizes(), "fable_attn: cos/sin must be (seqlen_ro, rotary_dim/2)");
+  torch::Tensor out = (inplace && src.is_same(x)) ? x : torch::empty_like(src);
+  FaRotaryParams p{};
+  p.struct_size = sizeof(FaRotaryParams);
+  p.x = src.data_ptr(); p.out = out.data_ptr();
+  const int hd = varlen ? 1 : 2;
+  p.rows = varlen ? src.size(0) : src.size(0) * src.size(1);
+  p.heads = (int)src.size(hd); p.dim = (int)src.size(hd + 1); p.rotary_dim = (int)c.size(1) * 2;
+  p.x_row_stride = src.stride(hd - 1); p.x_head_stride = src.stride(hd);
+  p.out_row_stride = out.stride(hd - 1); p.out_head_stride = out.stride(hd);
+  torch::Tensor cu, offs;
+  if (varlen) {
+    cu = cu_seqlens->to(torch::kInt32).contiguous();
+    p.cu_seqlens = cu.data_ptr<int>();
+    p.batch = (int)cu.numel() - 1;
+  } else {
+    p.seqlen = (int)src.size(1);
+    p.batch = (int)src.size(0);
+  }
+  if (py::isinstance<py::int_>(offsets)) {
+    p.offset = offsets.cast<int>();
+  } else {
+    offs = offsets.cast<torch::Tensor>().to(x.device(), torch::kInt32).contiguous();
+    TORCH_CHECK_VALUE(offs.numel() == p.batch, "fable_attn: seqlen_offsets needs one entry per sequence");
+    p.offsets = offs.data_ptr<int>();
+  }
+  p.cos = c.data_ptr<float>(); p.sin = s.data_ptr<float>(); p.seqlen_ro = (int)c.size(0);
+  p.interleaved = interleaved ? 1 : 0;
+  check(fa_rotary_launch(&p, dt_of(src), cur_stream(src)), "rotary");
+  if (inplace && !out.is_same(x)) {
+    x.copy_(out);
+    return x;
+  }
+  return out;
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "fable_attn sm_100a attention kernels (binds the C ABI of include/fable_attn.h)";
   m.def("fwd", &fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("scale"), py::arg("causal"),
@@ -300,6 +351,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("bwd", &bwd, py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"), py::arg("out"), py::arg("lse"),
         py::arg("scale"), py::arg("causal"), py::arg("win_left"), py::arg("win_right"), py::arg("softcap"),
         py::arg("alibi"), py::arg("dropout_p"), py::arg("seed"), py::arg("dropout_bits") = c10::optional<torch::Tensor>());
+  m.def("rotary", &rotary, py::arg("x"), py::arg("cos"), py::arg("sin"), py::arg("interleaved"), py::arg("inplace"),
+        py::arg("offsets"), py::arg("cu_seqlens") = c10::optional<torch::Tensor>());
   m.def("dropout_mask", &dropout_mask, py::arg("like"), py::arg("seed"), py::arg("dropout_p"), py::arg("nheads"),
         py::arg("seqlen_q"), py::arg("seqlen_k"), py::arg("causal"), py::arg("win_left"), py::arg("win_right"));
   m.def("fwd_varlen", &fwd_varlen, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("cu_q"), py::arg("cu_k"),

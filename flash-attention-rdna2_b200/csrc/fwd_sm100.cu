@@ -511,5 +511,6 @@ extern "C" FA_API int fa_device_error(int clear) {
     const int zero = 0;
     cudaMemcpyToSymbol(g_fwd_error, &zero, sizeof(int));
   }
-  return v | (fa::dec_device_error(clear) ? 64 : 0) | (fa::bwd_device_error(clear) ? 128 : 0);
+  return v | (fa::dec_device_error(clear) ? 64 : 0) | (fa::bwd_device_error(clear) ? 128 : 0) |
+         (fa::rot_device_error(clear) ? 256 : 0);
 }

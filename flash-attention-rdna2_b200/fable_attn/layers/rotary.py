@@ -43,7 +43,17 @@ def _positions_varlen(cu_seqlens, total, offsets, device):
 def apply_rotary_emb(x, cos, sin, interleaved=False, inplace=False, seqlen_offsets=0, cu_seqlens=None,
                      max_seqlen=None):
     """x: (batch, seqlen, nheads, headdim), or (total, nheads, headdim) with cu_seqlens.
-    cos/sin: (seqlen_ro, rotary_dim/2).  seqlen_offsets: int or (batch,) tensor."""
+    cos/sin: (seqlen_ro, rotary_dim/2).  seqlen_offsets: int or (batch,) tensor.
+    Device tensors are rotated by one native kernel (fa_rotary_launch) with the roundings of the
+    torch arithmetic below, which host tensors use."""
+    if x.is_cuda:
+        from .. import _C
+        if cu_seqlens is None and x.dim() != 4:
+            raise ValueError(f"apply_rotary_emb expects (batch, seqlen, nheads, headdim), got {tuple(x.shape)}")
+        if cu_seqlens is not None and x.dim() != 3:
+            raise ValueError("apply_rotary_emb with cu_seqlens expects (total, nheads, headdim)")
+        offs = seqlen_offsets if isinstance(seqlen_offsets, int) else seqlen_offsets
+        return _C.rotary(x, cos, sin, bool(interleaved), bool(inplace), offs, cu_seqlens)
     if cu_seqlens is None:
         if x.dim() != 4:
             raise ValueError(f"apply_rotary_emb expects (batch, seqlen, nheads, headdim), got {tuple(x.shape)}")

@@ -144,6 +144,38 @@ FA_API int fa_dropout_mask_launch(unsigned long long seed, float p, int NH, int 
                                   int win_right, unsigned int* bits, void* stream);
 
 /* ------------------------------------------------------------------------------------------
+ * Rotary position embedding of q or k, one HBM pass.  Replaces the torch arithmetic of
+ * apply_rotary_emb (package/fable_attn/layers/rotary.py:20-68) for device tensors, with the same
+ * roundings (cos/sin cast to x's dtype, each product and sum rounded to it), so the result is
+ * bit-identical to the reference's.  x / out are [rows][heads][dim] with element strides
+ * (dim contiguous); out == x rotates in place, otherwise dims past rotary_dim are copied.
+ *   dense:  rows = batch * seqlen, row b*seqlen + s sits at position s + offset(b)
+ *   varlen: cu_seqlens [batch+1] int32, row t of sequence i sits at t - cu[i] + offset(i)
+ * offset(b) = offsets ? offsets[b] : offset.  cos/sin [seqlen_ro][rotary_dim/2] fp32.
+ * interleaved: pairs (2j, 2j+1) (GPT-J); else (j, j + rotary_dim/2) (NeoX).  A position outside
+ * the table leaves its row unrotated and raises fa_device_error bit 256.  No counterpart in
+ * the reference's C++ (its rotary is torch code).
+ * -------------------------------------------------------------------------------------------*/
+typedef struct FaRotaryParams {
+  unsigned int struct_size;
+  const void* x;
+  void* out;
+  long long rows;
+  int heads, dim, rotary_dim;
+  long long x_row_stride, x_head_stride, out_row_stride, out_head_stride;
+  int seqlen;                          /* dense rows per sequence */
+  const int* cu_seqlens;               /* varlen [batch+1] or null */
+  int batch;
+  int offset;                          /* position offset for every sequence ... */
+  const int* offsets;                  /* ... or per sequence [batch] */
+  const float* cos; const float* sin;
+  int seqlen_ro;                       /* rows of the cos / sin tables */
+  int interleaved;
+} FaRotaryParams;
+
+FA_API int fa_rotary_launch(const FaRotaryParams* p, int dtype, void* stream);
+
+/* ------------------------------------------------------------------------------------------
  * Paged-KV decode (one or several new tokens per sequence).  Replaces DecParams /
  * fa_decode_launch (kernels/fa_decode.hip:343-362).
  *   q         [batch, nq, NH, HD] contiguous (nq new tokens per sequence)
