@@ -1,13 +1,18 @@
 // fwd_sm100.cu — exact attention forward on the Blackwell tensor cores (tcgen05 + TMEM + TMA).
 //
-// One CTA = one 128-row query tile of one head of one sequence.  Warp roles (192 threads):
-//   warps 0-3  softmax: thread t owns query row t (= TMEM lane t).  Reads its S row from TMEM,
-//              applies masks / softcap / alibi / Philox dropout, keeps the online-softmax state
-//              (lazy rescale: the reference max only moves when it grows by > 2^8), writes P as
-//              packed 16-bit pairs back into the same TMEM columns, and finally normalises O
-//              and writes O and LSE.
-//   warp 4     TMA producer: Q once, then K and V tiles (128 keys x D) into an NS-stage ring.
-//   warp 5     MMA issuer: owns the TMEM allocation; S_j = Q K_j^T into one of two S buffers
+// One CTA = one 128-row query tile of one head of one sequence.  Warp roles (320 threads):
+//   warps 0-7  softmax: warps w and w+4 share query rows 32 (w%4) .. +31 (their TMEM lane
+//              quadrant); w / 4 picks the half of each S row (64 keys) and of each O row (D/2
+//              columns) the thread owns.  Each thread reads its half row of S from TMEM, applies
+//              masks / softcap / alibi / dropout, agrees on the row max with its partner through
+//              shared memory (a 64-thread named barrier per quadrant), keeps the online-softmax
+//              state (lazy rescale: the reference max only moves when it grows by > 2^8), writes
+//              P as packed 16-bit pairs into the first 32 columns of its own half, and finally
+//              normalises its half of O and writes O and LSE.  Two softmax warps per scheduler
+//              double the issue rate of the exponentials, and one pair in four is computed on the
+//              FMA pipe (ex2_poly) instead of the SFU.
+//   warp 8     TMA producer: Q once, then K and V tiles (128 keys x D) into separate rings.
+//   warp 9     MMA issuer: owns the TMEM allocation; S_j = Q K_j^T into one of two S buffers
 //              (SS form), then O += P_j V_j with P read from TMEM (TS form).
 // TMEM columns: S0 [0,128), S1 [128,256), O [256, 256+D).  K/V tiles are 128-byte swizzled
 // (TMA SWIZZLE_128B, one 64-column box per 128-byte row chunk); S uses K-major Q and K operands,
@@ -27,8 +32,39 @@ namespace {
 
 using namespace sm100;
 
-constexpr int BM = 128, BN = 128, NTHREADS = 192;
+constexpr int BM = 128, BN = 128;
+constexpr int NSOFT = 256;                         // softmax threads: 8 warps, two per TMEM quadrant
+constexpr int WARP_TMA = 8, WARP_MMA = 9, NTHREADS = 320;
 constexpr float LAZY_THRESH = 8.0f;   // log2 units: rescale O only when the max grows by > 2^8
+constexpr int POLY_EVERY = 4;         // one score pair in 4 takes 2^x on the FMA pipe
+
+// 2^x on the FMA pipe, for x <= 2^7: 2^x = 2^n * 2^f with n = round(x) (the 1.5 * 2^23 shift
+// leaves n in the low mantissa bits) and f = x - n in [-1/2, 1/2]; 2^f by a degree-4 polynomial
+// fitted here by a Remez exchange on the relative error over [-1/2, 1/2] (max 2.7e-6 in fp32,
+// far below the 16-bit rounding P receives); n is added to the exponent field.  x < -126 gives 0,
+// as the SFU's flush-to-zero ex2 does.
+__device__ __forceinline__ float ex2_poly(float x) {
+  const float xc = fmaxf(x, -127.f);
+  const float t = xc + 12582912.f;
+  const float f = xc - (t - 12582912.f);
+  float pz = fmaf(0.009570102207362652f, f, 0.05591785907745361f);
+  pz = fmaf(pz, f, 0.240247443318367f);
+  pz = fmaf(pz, f, 0.6931217908859253f);
+  pz = fmaf(pz, f, 0.9999992847442627f);
+  const int n = __float_as_int(t) - 0x4B400000;
+  return x < -126.f ? 0.f : __int_as_float(__float_as_int(pz) + n * (1 << 23));
+}
+
+// named barrier `id` over the two softmax warps of one TMEM quadrant: AND of a predicate
+// (uniform loop exits) and a plain sync (the row-max exchange)
+__device__ __forceinline__ bool bar_and_pair(uint32_t id, bool v) {
+  uint32_t r;
+  asm volatile("{\n\t.reg .pred pi, po;\n\tsetp.ne.u32 pi, %2, 0;\n\tbar.red.and.pred po, %1, 64, pi;\n\t"
+               "selp.u32 %0, 1, 0, po;\n\t}"
+               : "=r"(r) : "r"(id), "r"((uint32_t)v) : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ void bar_sync_pair(uint32_t id) { asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory"); }
 
 __device__ int g_fwd_error = 0;       // non-zero after a pipeline wait timed out
 
@@ -44,7 +80,8 @@ struct Cfg {
   static constexpr int OFF_K = Q_BYTES;
   static constexpr int OFF_V = OFF_K + NSK * KV_BYTES;
   static constexpr int OFF_BAR = OFF_V + NSV * KV_BYTES;
-  static constexpr int SMEM = OFF_BAR + 256 + 1024;            // barriers + alignment slack
+  static constexpr int OFF_X = OFF_BAR + 256;                  // row-max / row-sum exchange
+  static constexpr int SMEM = OFF_X + 6 * BM * 4 + 1024;       // + alignment slack
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t O_COL = 256;
 };
@@ -61,12 +98,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                   const __grid_constant__ CUtensorMap tmV, const FaFwdParams p) {
   using C = Cfg<D>;
+  constexpr int HB = BN / 2;            // S columns (keys) per softmax thread
+  constexpr int HD2 = D / 2;            // O columns per softmax thread
   extern __shared__ uint8_t smem_raw[];
   const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
   uint8_t* sgen = smem_raw + (sbase - smem_u32(smem_raw));
   const uint32_t sQ = sbase + C::OFF_Q, sK = sbase + C::OFF_K, sV = sbase + C::OFF_V;
   const uint32_t bar = sbase + C::OFF_BAR;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sgen + C::OFF_BAR + Bars::TMEM_ADDR);
+  float* xch = reinterpret_cast<float*>(sgen + C::OFF_X);   // [2 parity][2 halves][BM] row maxima, then l
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int z = blockIdx.z, h = blockIdx.y, kvh = h / p.gqa;
@@ -96,7 +136,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const int t0 = klo / BN;
   const int ntiles = (khi >= klo) ? (khi / BN - t0 + 1) : 0;
 
-  // ---- set-up: barriers (thread 0), TMEM (warp 5)
+  // ---- set-up: barriers (thread 0), TMEM (MMA warp)
   if (tid == 0) {
     mbar_init(bar + Bars::Q_FULL, 1);
     for (int s = 0; s < C::NSK; ++s) {
@@ -109,17 +149,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(bar + Bars::S_FULL + 8 * s, 1);
-      mbar_init(bar + Bars::P_FULL + 8 * s, BM);
+      mbar_init(bar + Bars::P_FULL + 8 * s, NSOFT);
     }
     mbar_init(bar + Bars::O_DONE, 1);
     mbar_init(bar + Bars::MMA_DRAIN, 1);
     fence_barrier_init();
   }
-  if (warp == 5) {
+  if (warp == WARP_MMA) {
     tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
     tmem_relinquish();
   }
-  if (warp == 4 && lane == 0) {
+  if (warp == WARP_TMA && lane == 0) {
     prefetch_tmap(&tmQ);
     prefetch_tmap(&tmK);
     prefetch_tmap(&tmV);
@@ -129,7 +169,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == WARP_TMA) {
     // ======================= TMA producer
     if (lane == 0 && ntiles > 0) {
       mbar_expect_tx(bar + Bars::Q_FULL, C::Q_BYTES);
@@ -162,7 +202,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         mbar_wait(bar + Bars::V_FULL + 8 * (j % C::NSV), (j / C::NSV) & 1);
     }
     __syncwarp();
-  } else if (warp == 5) {
+  } else if (warp == WARP_MMA) {
     // ======================= MMA issuer (whole warp follows; lane 0 issues)
     constexpr uint32_t IDESC_S = idesc_f16(BF16 ? 1 : 0, BM, BN, 0, 0);
     constexpr uint32_t IDESC_O = idesc_f16(BF16 ? 1 : 0, BM, D, 0, 1);
@@ -192,9 +232,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const uint32_t pt = tmem + (uint32_t)(i & 1) * 128u;
         const uint32_t vbase = sV + s * C::KV_BYTES;
         for (int kk = 0; kk < BN / 16; ++kk) {
+          // A = P from TMEM: keys [64 hf, 64 hf + 64) sit packed in columns [64 hf, 64 hf + 32)
           // B = V tile, MN-major: 16 keys = 16 rows of 128 B; D spans NCH swizzle atoms (LBO apart)
+          const uint32_t pa = pt + (uint32_t)((kk * 16) / HB) * 64u + (uint32_t)(((kk * 16) % HB) / 2);
           const uint64_t bd = sdesc_sw128(vbase + kk * 16 * 128, C::CH_BYTES, 1024);
-          mma_ts(tmem + C::O_COL, pt + kk * 8, bd, IDESC_O, (i > 0 || kk > 0) ? 1u : 0u);
+          mma_ts(tmem + C::O_COL, pa, bd, IDESC_O, (i > 0 || kk > 0) ? 1u : 0u);
         }
         mma_commit(bar + Bars::V_EMPTY + 8 * s);
         mma_commit(bar + Bars::O_DONE);
@@ -228,9 +270,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     __syncwarp();
     if (!mbar_wait_warp(bar + Bars::MMA_DRAIN, 0)) record_error(32);
   } else {
-    // ======================= softmax + epilogue (warps 0-3, thread = query row)
-    const int r = tid, q = qb + r;
-    const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+    // ======================= softmax + epilogue (warps 0-7).  Warps w and w + 4 share TMEM lane
+    // quadrant w % 4 (query rows 32 (w%4) .. + 31); half hf = w / 4 takes S columns (keys)
+    // [64 hf, 64 hf + 64) and O columns [D/2 hf, D/2 hf + D/2).  The two halves of a row agree on
+    // the row max through shared memory and a 64-thread named barrier per quadrant.
+    const int qd = warp & 3, hf = warp >> 2;
+    const int r = qd * 32 + lane, q = qb + r;
+    const uint32_t pair_bar = 1 + qd;
+    const uint32_t lane_addr = tmem + ((uint32_t)(qd * 32) << 16);
     int rlo, rhi;
     fa_key_range(q, SQ, SK, p.causal, p.win_left, p.win_right, p.attn_chunk, rlo, rhi);
     if (q >= SQ) { rlo = 1; rhi = 0; }
@@ -248,59 +295,67 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const float inv_keep = drop ? 1.0f / (1.0f - p.dropout_p) : 1.f;
     float m_ref = -INFINITY, l = 0.f;
     bool ok = true;
-    float s[BN];
+    float s[HB];
     const bool use_bits = drop && p.dropout_bits != nullptr;
     const int mask_w = (SK + 31) / 32;
     const uint32_t thresh = fa_drop_thresh(p.dropout_p);
     const bool cap_on = FEAT && p.softcap > 0.f;
     const float cap_in = cap_on ? p.scale / p.softcap : 0.f, cap2 = p.softcap * FA_LOG2E;
     for (int j = 0; j < ntiles; ++j) {
-      const int kb = (t0 + j) * BN;
-      // this tile's keep bits, one word per 32 keys (bit b <-> key kb + 32i + b), prepared before
+      const int kb = (t0 + j) * BN, kh = kb + hf * HB;   // first key of this thread's half
+      // this half's keep bits, one word per 32 keys (bit b <-> key kh + 32i + b), prepared before
       // the wait so that they overlap it: loaded from the mask (its layout puts the warp's 32 rows
       // on one line) or evaluated with Philox.  Mask words past the row's visible keys may be
       // unwritten: they only multiply probabilities that are already 0.
-      uint32_t dw[BN / 32];
+      uint32_t dw[HB / 32];
 #pragma unroll
-      for (int i = 0; i < BN / 32; ++i) {
-        const int kw = kb / 32 + i;
+      for (int i = 0; i < HB / 32; ++i) {
+        const int kw = kh / 32 + i;
         dw[i] = 0u;
         if (drop && q < SQ && kw < mask_w)
           dw[i] = use_bits ? __ldg(p.dropout_bits + fa_mask_word(h, SQ, SK, q, kw))
                            : fa_keep_word(p.philox_seed, ((uint64_t)h * SQ + q) * SK + 32 * kw, 1, thresh,
                                           SK - 32 * kw);
       }
-      if (!mbar_wait_warp(bar + Bars::S_FULL + 8 * (j & 1), (j >> 1) & 1)) { ok = false; break; }
+      // both warps of the pair leave together (the exchange below is a barrier without timeout)
+      const bool got = mbar_wait_warp(bar + Bars::S_FULL + 8 * (j & 1), (j >> 1) & 1);
+      if (!bar_and_pair(pair_bar, got && ok)) { ok = false; break; }
       tc_fence_after();
-      const uint32_t sa = lane_addr + (uint32_t)(j & 1) * 128u;
+      const uint32_t sa = lane_addr + (uint32_t)(j & 1) * 128u + (uint32_t)(hf * HB);
 #pragma unroll
-      for (int c = 0; c < BN; c += 32) tmem_ld32(sa + c, s + c);
+      for (int c = 0; c < HB; c += 32) tmem_ld32(sa + c, s + c);
       tc_wait_ld();
       // ---- scores (log2 domain) and masks
       float tmax = -INFINITY;
       if constexpr (FEAT) {
         // logits in log2 units; alibi adds slope2 * (key - q), and key - q = d0 + c exactly in
         // fp32.  Two tight loops (softcap or not) keep the unrolled code small.
-        const float d0 = (float)(kb - q);
+        const float d0 = (float)(kh - q);
         if (cap_on) {
 #pragma unroll
-          for (int c = 0; c < BN; ++c) s[c] = fmaf(cap2, fa_tanh(s[c] * cap_in), slope2 * (d0 + (float)c));
+          for (int c = 0; c < HB; ++c) s[c] = fmaf(cap2, fa_tanh(s[c] * cap_in), slope2 * (d0 + (float)c));
         } else {
 #pragma unroll
-          for (int c = 0; c < BN; ++c) s[c] = fmaf(s[c], scale2, slope2 * (d0 + (float)c));
+          for (int c = 0; c < HB; ++c) s[c] = fmaf(s[c], scale2, slope2 * (d0 + (float)c));
         }
       }
       const bool interior = full_rows && kb >= lo_last && kb + BN - 1 <= hi_first && kb + BN <= SK;
       if (!interior) {
 #pragma unroll
-        for (int c = 0; c < BN; ++c) {
-          const int key = kb + c;
+        for (int c = 0; c < HB; ++c) {
+          const int key = kh + c;
           if (key < rlo || key > rhi) s[c] = -INFINITY;
         }
       }
 #pragma unroll
-      for (int c = 0; c < BN; ++c) tmax = fmaxf(tmax, s[c]);
+      for (int c = 0; c < HB; ++c) tmax = fmaxf(tmax, s[c]);
       if constexpr (!FEAT) tmax = (tmax == -INFINITY) ? -INFINITY : tmax * scale2;
+      // ---- row max over both halves (slots alternate by tile parity, so a slot is rewritten only
+      //      after the partner has passed the next exchange)
+      float* xs = xch + (j & 1) * (2 * BM);
+      xs[hf * BM + r] = tmax;
+      bar_sync_pair(pair_bar);
+      tmax = fmaxf(tmax, xs[(1 - hf) * BM + r]);
       // ---- lazy online-softmax update: the reference max moves only when it grows by > 2^8
       const bool move = tmax > m_ref + LAZY_THRESH || (m_ref == -INFINITY && tmax != -INFINITY);
       float corr = 1.f;
@@ -311,18 +366,26 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
       const float muse = (m_ref == -INFINITY) ? 0.f : m_ref;
       const float sc = FEAT ? 1.f : scale2;
-      // ---- P = 2^(s - m): row sum (before dropout), dropout, 16-bit pairs into the first
-      //      BN/2 columns of the same S buffer (chunk c overwrites S columns already consumed)
+      // ---- P = 2^(s - m): row sum (before dropout), dropout, 16-bit pairs into the first HB/2
+      //      columns of this half's S range (already read into registers).  One pair in
+      //      POLY_EVERY takes 2^x on the FMA pipe (ex2_poly) to relieve the SFU.
       float lsum = 0.f;
 #pragma unroll
-      for (int c0 = 0; c0 < BN; c0 += 32) {
+      for (int c0 = 0; c0 < HB; c0 += 32) {
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          float a = ex2(fmaf(s[c0 + 2 * i], sc, -muse));
-          float b = ex2(fmaf(s[c0 + 2 * i + 1], sc, -muse));
+          const float xa = fmaf(s[c0 + 2 * i], sc, -muse), xb = fmaf(s[c0 + 2 * i + 1], sc, -muse);
+          float a, b;
+          if (i % POLY_EVERY == POLY_EVERY - 1) {
+            a = ex2_poly(xa);
+            b = ex2_poly(xb);
+          } else {
+            a = ex2(xa);
+            b = ex2(xb);
+          }
           lsum += a + b;
-          if (drop) {   // keys kb + c0 + 2i and +1 are bits 2i, 2i+1 of word c0/32
+          if (drop) {   // keys kh + c0 + 2i and +1 are bits 2i, 2i+1 of word c0/32
             const unsigned int w = dw[c0 / 32] >> (2 * i);
             a *= (w & 1u) ? inv_keep : 0.f;
             b *= (w & 2u) ? inv_keep : 0.f;
@@ -337,21 +400,21 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         tmem_st16(sa + c0 / 2, pk);
       }
-      // ---- O rescale.  Every tile j >= 1 waits exactly once for PV_{j-1} (so the parity wait
-      //      can never alias an older phase); PV_{j-1} normally finished while P_j was computed.
-      //      tcgen05.ld/st are warp-collective: rows that did not move scale by 1.
+      // ---- O rescale of this half's columns.  Every tile j >= 1 waits exactly once for PV_{j-1}
+      //      (so the parity wait can never alias an older phase); PV_{j-1} normally finished while
+      //      P_j was computed.  tcgen05.ld/st are warp-collective: rows that did not move scale by 1.
       if (j > 0) {
-        if (!mbar_wait_warp(bar + Bars::O_DONE, (j - 1) & 1)) { ok = false; break; }
-        if (__any_sync(0xffffffffu, corr != 1.f)) {
+        if (!mbar_wait_warp(bar + Bars::O_DONE, (j - 1) & 1)) ok = false;   // leaves at the next exchange
+        if (ok && __any_sync(0xffffffffu, corr != 1.f)) {
           tc_fence_after();
 #pragma unroll
-          for (int c = 0; c < D; c += 32) {
+          for (int c = 0; c < HD2; c += 32) {
             float o[32];
-            tmem_ld32(lane_addr + C::O_COL + c, o);
+            tmem_ld32(lane_addr + C::O_COL + hf * HD2 + c, o);
             tc_wait_ld();
 #pragma unroll
             for (int i = 0; i < 32; ++i) o[i] *= corr;
-            tmem_st32(lane_addr + C::O_COL + c, reinterpret_cast<const uint32_t*>(o));
+            tmem_st32(lane_addr + C::O_COL + hf * HD2 + c, reinterpret_cast<const uint32_t*>(o));
           }
         }
       }
@@ -361,19 +424,23 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       mbar_arrive(bar + Bars::P_FULL + 8 * (j & 1));
     }
     if (!ok) record_error(8);
-    // ---- epilogue: O / l, LSE (TMEM reads by whole warps; stores only for real rows)
+    // ---- epilogue: row sum over both halves, this half's O columns / l, LSE (first half)
     const bool have_o = ok && ntiles > 0;
     if (have_o && !mbar_wait_warp(bar + Bars::O_DONE, (ntiles - 1) & 1)) record_error(16);
     tc_fence_after();
+    float* xl = xch + 4 * BM;
+    xl[hf * BM + r] = l;
+    bar_sync_pair(pair_bar);
+    l += xl[(1 - hf) * BM + r];
     const float inv = l > 0.f ? 1.f / l : 0.f;
     using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
     T* orow = (T*)p.O + (varlen ? (long long)qtok0 * p.sO.s : (long long)z * p.sO.b) + (long long)h * p.sO.h +
-              (long long)q * p.sO.s;
+              (long long)q * p.sO.s + hf * HD2;
 #pragma unroll
-    for (int c = 0; c < D; c += 32) {
+    for (int c = 0; c < HD2; c += 32) {
       float o[32];
       if (have_o) {
-        tmem_ld32(lane_addr + C::O_COL + c, o);
+        tmem_ld32(lane_addr + C::O_COL + hf * HD2 + c, o);
         tc_wait_ld();
       } else {
 #pragma unroll
@@ -396,14 +463,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
       }
     }
-    if (q < SQ && p.LSE) {
+    if (hf == 0 && q < SQ && p.LSE) {
       const long long li = fa_lse_index(varlen, z, h, p.NH, p.SQ, qtok0, p.lse_total_q, q);
       p.LSE[li] = l > 0.f ? m_ref * FA_LN2 + logf(l) : -INFINITY;
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == WARP_MMA) {
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
   }
