@@ -9,8 +9,8 @@
 //              state (lazy rescale: the reference max only moves when it grows by > 2^8), writes
 //              P as packed 16-bit pairs into the first 32 columns of its own half, and finally
 //              normalises its half of O and writes O and LSE.  Two softmax warps per scheduler
-//              double the issue rate of the exponentials, and one pair in four is computed on the
-//              FMA pipe (ex2_poly) instead of the SFU.
+//              keep the exponentials of two half rows in flight; the scale / subtract and the
+//              row sums run as packed fp32x2 operations.
 //   warp 8     TMA producer: Q once, then K and V tiles (128 keys x D) into separate rings.
 //   warp 9     MMA issuer: owns the TMEM allocation; S_j = Q K_j^T into one of two S buffers
 //              (SS form), then O += P_j V_j with P read from TMEM (TS form).
@@ -36,25 +36,6 @@ constexpr int BM = 128, BN = 128;
 constexpr int NSOFT = 256;                         // softmax threads: 8 warps, two per TMEM quadrant
 constexpr int WARP_TMA = 8, WARP_MMA = 9, NTHREADS = 320;
 constexpr float LAZY_THRESH = 8.0f;   // log2 units: rescale O only when the max grows by > 2^8
-constexpr int POLY_EVERY = 4;         // one score pair in 4 takes 2^x on the FMA pipe
-
-// 2^x on the FMA pipe, for x <= 2^7: 2^x = 2^n * 2^f with n = round(x) (the 1.5 * 2^23 shift
-// leaves n in the low mantissa bits) and f = x - n in [-1/2, 1/2]; 2^f by a degree-4 polynomial
-// fitted here by a Remez exchange on the relative error over [-1/2, 1/2] (max 2.7e-6 in fp32,
-// far below the 16-bit rounding P receives); n is added to the exponent field.  x < -126 gives 0,
-// as the SFU's flush-to-zero ex2 does.
-__device__ __forceinline__ float ex2_poly(float x) {
-  const float xc = fmaxf(x, -127.f);
-  const float t = xc + 12582912.f;
-  const float f = xc - (t - 12582912.f);
-  float pz = fmaf(0.009570102207362652f, f, 0.05591785907745361f);
-  pz = fmaf(pz, f, 0.240247443318367f);
-  pz = fmaf(pz, f, 0.6931217908859253f);
-  pz = fmaf(pz, f, 0.9999992847442627f);
-  const int n = __float_as_int(t) - 0x4B400000;
-  return x < -126.f ? 0.f : __int_as_float(__float_as_int(pz) + n * (1 << 23));
-}
-
 // named barrier `id` over the two softmax warps of one TMEM quadrant: AND of a predicate
 // (uniform loop exits) and a plain sync (the row-max exchange)
 __device__ __forceinline__ bool bar_and_pair(uint32_t id, bool v) {
@@ -367,24 +348,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const float muse = (m_ref == -INFINITY) ? 0.f : m_ref;
       const float sc = FEAT ? 1.f : scale2;
       // ---- P = 2^(s - m): row sum (before dropout), dropout, 16-bit pairs into the first HB/2
-      //      columns of this half's S range (already read into registers).  One pair in
-      //      POLY_EVERY takes 2^x on the FMA pipe (ex2_poly) to relieve the SFU.
-      float lsum = 0.f;
+      //      columns of this half's S range (already read into registers).
+      float2 lsum2 = make_float2(0.f, 0.f);
 #pragma unroll
       for (int c0 = 0; c0 < HB; c0 += 32) {
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float xa = fmaf(s[c0 + 2 * i], sc, -muse), xb = fmaf(s[c0 + 2 * i + 1], sc, -muse);
-          float a, b;
-          if (i % POLY_EVERY == POLY_EVERY - 1) {
-            a = ex2_poly(xa);
-            b = ex2_poly(xb);
-          } else {
-            a = ex2(xa);
-            b = ex2(xb);
-          }
-          lsum += a + b;
+          // packed fp32x2 arithmetic (one FFMA2 / FADD2 per pair) around the two SFU exponentials
+          const float2 x2 = __ffma2_rn(make_float2(s[c0 + 2 * i], s[c0 + 2 * i + 1]), make_float2(sc, sc),
+                                       make_float2(-muse, -muse));
+          float a = ex2(x2.x), b = ex2(x2.y);
+          lsum2 = __fadd2_rn(lsum2, make_float2(a, b));
           if (drop) {   // keys kh + c0 + 2i and +1 are bits 2i, 2i+1 of word c0/32
             const unsigned int w = dw[c0 / 32] >> (2 * i);
             a *= (w & 1u) ? inv_keep : 0.f;
@@ -418,7 +393,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           }
         }
       }
-      l += lsum;
+      l += lsum2.x + lsum2.y;
       tc_wait_st();
       tc_fence_before();
       mbar_arrive(bar + Bars::P_FULL + 8 * (j & 1));
