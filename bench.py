@@ -330,6 +330,46 @@ def bench_decode(dev, steps=20, warmup=5):
             "GBps": round(nbytes / ms / 1e6, 1), "bytes": nbytes}
 
 
+def bench_decode_split(dev, ws, rank, steps=20, warmup=5):
+    """Config 4 across ranks: each sequence's context (lengths ~ U[16K, 32K], seeded) is cut into
+    ws contiguous chunks; rank r holds the pages of its chunks (bf16, page 256, permuted block
+    table) and decodes against them, then one NCCL all-gather of the (out, lse) partials and the
+    LSE merge (fable_attn.multigpu.decode_kv_split).  Every rank runs this (collectives); the
+    time is the max over ranks, GB/s counts the K/V bytes of the whole job."""
+    from fable_attn import multigpu as M
+    B, Hq, Hk, D, page = 16, 32, 8, 128, 256
+    rng = np.random.default_rng(11)
+    lens = rng.integers(16384, 32769, size=B).astype(np.int64)
+    starts, ends = M.plan_kv_split(torch.from_numpy(lens), ws)
+    local = (ends[rank] - starts[rank]).to(torch.int32)
+    nper = int((int(local.max()) + page - 1) // page)
+    g = torch.Generator(device=dev).manual_seed(100 + rank)
+    kc = torch.randn(B * nper, page, Hk, D, device=dev, dtype=torch.bfloat16, generator=g)
+    vc = torch.randn(B * nper, page, Hk, D, device=dev, dtype=torch.bfloat16, generator=g)
+    bt = torch.from_numpy(np.random.default_rng(200 + rank).permutation(B * nper).astype(np.int32).reshape(B, nper)).to(dev)
+    q = torch.randn(B, 1, Hq, D, device=dev, dtype=torch.bfloat16, generator=torch.Generator(device=dev).manual_seed(7))
+    lc = local.to(dev)
+
+    def call():
+        return M.decode_kv_split(q, kc, vc, bt, lc, softmax_scale=D ** -0.5)
+
+    for _ in range(warmup):
+        call()
+    torch.cuda.synchronize()
+    _barrier(ws)
+    a, b = _events()
+    a.record()
+    for _ in range(steps):
+        call()
+    b.record()
+    torch.cuda.synchronize()
+    ms = _max_over_ranks(a.elapsed_time(b) / steps, ws, dev)
+    nbytes = float(lens.sum()) * Hk * D * 2 * 2
+    return {"config": f"paged decode B16 Hq32 Hk8 D128 bf16 page256 L~U[16K,32K], KV range split over {ws} GPUs "
+                      "+ NCCL all-gather + LSE merge", "ms": round(ms, 4), "GBps": round(nbytes / ms / 1e6, 1),
+            "bytes": nbytes}
+
+
 def bench_varlen_swa(dev, steps=10, warmup=3):
     """Config 5: 16 packed sequences, lengths ~ U[256, 8192] (seeded), cu_seqlens_q = cu_seqlens_k,
     Hq 64, Hk 8, D 128 bf16, causal window (512, 0), softcap 30, NeoX rotary rd 64 (base 10000,
@@ -456,6 +496,11 @@ def main():
 
     r = bench_fwd_dense(args, ws, rank, dev)
     extra = {}
+    if ws > 1 and not args.no_extra:   # every rank takes part (collectives)
+        try:
+            extra["decode_kv_split"] = bench_decode_split(dev, ws, rank)
+        except Exception as e:
+            extra["decode_kv_split"] = {"error": f"{type(e).__name__}: {e}"[:200]}
     if not args.no_extra and rank == 0:
         try:
             extra["fwd_bwd_causal"] = bench_fwd_bwd_causal(dev)

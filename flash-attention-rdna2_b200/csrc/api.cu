@@ -99,6 +99,11 @@ extern "C" int fa_forward_launch(const FaFwdParams* pp, int dtype, void* stream)
   }
   if (p.cu_q && p.LSE) FA_CHECK_ARG(p.lse_total_q > 0, "forward: varlen LSE needs lse_total_q");
   FA_CHECK_ARG(!(p.dropout_bits && p.cu_q), "forward: dropout_bits is for dense layouts only");
+  if (p.block_table) {
+    FA_CHECK_ARG(p.cu_q != nullptr, "forward: a block table needs the varlen layout (cu_q / cu_k)");
+    FA_CHECK_ARG(p.page > 0 && p.max_blocks > 0 && p.num_blocks > 0, "forward: paged K/V needs page=%d > 0, "
+                 "max_blocks=%d > 0, num_blocks=%lld > 0", p.page, p.max_blocks, p.num_blocks);
+  }
   if (p.batch == 0 || p.SQ == 0) return FA_OK;
   cudaStream_t st = (cudaStream_t)stream;
   bool taken = false;

@@ -13,6 +13,9 @@
 // dS feeds its MMAs as a pair of 16-bit numbers hi + lo (lo = dS - hi), two MMAs each, so the
 // 16-bit rounding of dS does not reach dQ/dK; P~ goes in as one 16-bit number.  The preprocess
 // dsum = rowsum(O*dO) is the CUDA-core kernel of bwd_simt.cu.  Every mbarrier wait is bounded.
+// Warp roles (320 threads): warps 0-7 elementwise, two per TMEM lane quadrant (w and w + 4 share
+// the quadrant's 32 rows; w / 4 takes half of each 64-wide tile and D/2 output columns, and
+// writes its packed P~ / dS into its own TMEM columns), warp 8 TMA, warp 9 MMA.
 #include <cudaTypedefs.h>
 #include <type_traits>
 #include "fa_common.cuh"
@@ -23,17 +26,18 @@ namespace {
 
 using namespace sm100;
 
-constexpr int NTHREADS = 192;        // warps 0-3 elementwise, 4 TMA, 5 MMA
+constexpr int NTHREADS = 320;        // warps 0-7 elementwise (two per TMEM quadrant), 8 TMA, 9 MMA
+constexpr int WARP_TMA = 8, WARP_MMA = 9, NELEM = 256;
 __device__ int g_bwd_error = 0;
 __device__ __forceinline__ void record_error(int code) { atomicOr(&g_bwd_error, code); }
 
-// named barrier 1 over the 128 elementwise threads, AND-reducing a predicate (uniform break)
-__device__ __forceinline__ bool bar_and_128(bool v) {
+// named barrier 1 over the 256 elementwise threads, AND-reducing a predicate (uniform break)
+__device__ __forceinline__ bool bar_and_elem(bool v) {
   uint32_t r;
   asm volatile(
       "{\n\t.reg .pred pi, po;\n\t"
       "setp.ne.u32 pi, %1, 0;\n\t"
-      "bar.red.and.pred po, 1, 128, pi;\n\t"
+      "bar.red.and.pred po, 1, 256, pi;\n\t"
       "selp.u32 %0, 1, 0, po;\n\t}"
       : "=r"(r)
       : "r"((uint32_t)v)
@@ -52,10 +56,26 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
     return *reinterpret_cast<const uint32_t*>(&t);
   }
 }
+// the two floats a packed 16-bit pair holds (exact)
 template <bool BF16>
-__device__ __forceinline__ float round16(float a) {
-  if constexpr (BF16) return __bfloat162float(__float2bfloat16_rn(a));
-  else return __half2float(__float2half_rn(a));
+__device__ __forceinline__ void unpack2(uint32_t w, float& a, float& b) {
+  if constexpr (BF16) {
+    a = __uint_as_float(w << 16);
+    b = __uint_as_float(w & 0xffff0000u);
+  } else {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w));
+    a = f.x;
+    b = f.y;
+  }
+}
+// dS as hi + lo 16-bit pairs: hi = dS rounded, lo = the rounding remainder rounded (one packing
+// conversion per pair for each; hi is read back from its packed bits)
+template <bool BF16>
+__device__ __forceinline__ void split2(float d0, float d1, uint32_t& hi, uint32_t& lo) {
+  hi = pack2<BF16>(d0, d1);
+  float h0, h1;
+  unpack2<BF16>(hi, h0, h1);
+  lo = pack2<BF16>(d0 - h0, d1 - h1);
 }
 
 // K-major / MN-major descriptors of a [rows][D] tile stored as D/64 chunks of rows x 128 B
@@ -126,13 +146,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(bar + Bz::SP_FULL + 8 * s, 1);
-      mbar_init(bar + Bz::DS_FULL + 8 * s, BM);
+      mbar_init(bar + Bz::DS_FULL + 8 * s, NELEM);
     }
     mbar_init(bar + Bz::DQ_DONE, 1);
     mbar_init(bar + Bz::DRAIN, 1);
     fence_barrier_init();
   }
-  if (warp == 5) {
+  if (warp == WARP_MMA) {
     tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
   }
@@ -141,7 +161,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == WARP_TMA) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0 && ntiles > 0) {
       mbar_expect_tx(bar + Bz::Q_FULL, 2 * C::Q_BYTES);
@@ -166,7 +186,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
     }
     __syncwarp();
-  } else if (warp == 5) {
+  } else if (warp == WARP_MMA) {
     // ------------------------------------------------------------ MMA issuer
     constexpr uint32_t ID_S = idesc_f16(BF16 ? 1 : 0, BM, BN, 0, 0);   // S, dP: 128 x 64
     constexpr uint32_t ID_Q = idesc_f16(BF16 ? 1 : 0, BM, D, 0, 1);    // dQ += dS K: 128 x D, K MN-major
@@ -176,11 +196,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       tc_fence_after();
       if (lane == 0) {
         const uint32_t kt = sK + (i % C::NS) * C::KV_BYTES;
+        // dS of keys [32 hf, 32 hf + 32) sits packed in the first 16 columns of half hf's own
+        // S (hi) and dP (lo) columns
         const uint32_t hi = tmem + C::S_COL + (i & 1) * 64, lo = tmem + C::DP_COL + (i & 1) * 64;
         for (int kk = 0; kk < BN / 16; ++kk) {
           const uint64_t bd = desc_mnmajor(kt, BN, kk);
-          mma_ts(tmem + C::DQ_COL, hi + kk * 8, bd, ID_Q, (i > 0 || kk > 0) ? 1u : 0u);
-          mma_ts(tmem + C::DQ_COL, lo + kk * 8, bd, ID_Q, 1u);
+          const uint32_t off = (uint32_t)(32 * (kk / 2) + 8 * (kk % 2));
+          mma_ts(tmem + C::DQ_COL, hi + off, bd, ID_Q, (i > 0 || kk > 0) ? 1u : 0u);
+          mma_ts(tmem + C::DQ_COL, lo + off, bd, ID_Q, 1u);
         }
         mma_commit(bar + Bz::K_EMPTY + 8 * (i % C::NS));
       }
@@ -211,8 +234,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (!mbar_wait_warp(bar + Bz::DRAIN, 0)) record_error(4);
   } else {
     // ------------------------------------------------------------ elementwise (thread = query row)
-    const int q = qb + tid;
-    const uint32_t la = tmem + ((uint32_t)(warp * 32) << 16);
+    // warps w and w + 4 share query rows 32 (w%4) .. + 31; w / 4 picks the half of the 64-key tile
+    // (32 keys) and of the dQ row (D/2 columns) the thread owns
+    const int qd = warp & 3, hf = warp >> 2;
+    const int q = qb + qd * 32 + lane;
+    const uint32_t la = tmem + ((uint32_t)(qd * 32) << 16);
     int rlo, rhi;
     fa_key_range(q, SQ, SK, p.causal, p.win_left, p.win_right, 0, rlo, rhi);
     float lse2 = 0.f, dsum = 0.f;
@@ -233,34 +259,31 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const float cap_in = cap_on ? p.scale / p.softcap : 0.f;
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
-      const int kb = (t0 + j) * BN;
-      // keep bits of this row for the tile (bit b of word i <-> key kb + 32i + b), prepared ahead
-      // of the wait: loaded from the mask (coalesced over rows) or evaluated with Philox
-      uint32_t dw[BN / 32];
-#pragma unroll
-      for (int i = 0; i < BN / 32; ++i) {
-        const int kw = kb / 32 + i;
-        dw[i] = 0u;
+      const int kb = (t0 + j) * BN + 32 * hf;   // first key of this thread's half
+      // keep bits of this row for the half (bit b <-> key kb + b), prepared ahead of the wait:
+      // loaded from the mask (coalesced over rows) or evaluated with Philox
+      uint32_t dw[1];
+      {
+        const int kw = kb / 32;
+        dw[0] = 0u;
         if (drop && q < SQ && kw < mask_w)
-          dw[i] = use_bits ? __ldg(p.dropout_bits + fa_mask_word(h, SQ, SK, q, kw))
+          dw[0] = use_bits ? __ldg(p.dropout_bits + fa_mask_word(h, SQ, SK, q, kw))
                            : fa_keep_word(p.drop_seed, ((uint64_t)h * SQ + q) * SK + 32 * kw, 1, thresh,
                                           SK - 32 * kw);
       }
       if (!mbar_wait_warp(bar + Bz::SP_FULL + 8 * (j & 1), (j >> 1) & 1)) { ok = false; break; }
       tc_fence_after();
-      float s[BN], dp[BN];
-      tmem_ld32(la + C::S_COL + (j & 1) * 64, s);
-      tmem_ld32(la + C::S_COL + (j & 1) * 64 + 32, s + 32);
-      tmem_ld32(la + C::DP_COL + (j & 1) * 64, dp);
-      tmem_ld32(la + C::DP_COL + (j & 1) * 64 + 32, dp + 32);
+      float s[32], dp[32];
+      tmem_ld32(la + C::S_COL + (j & 1) * 64 + 32 * hf, s);
+      tmem_ld32(la + C::DP_COL + (j & 1) * 64 + 32 * hf, dp);
       tc_wait_ld();
       const float d0 = (float)(kb - q);   // key - q = d0 + cc, exact in fp32
       // dS = P o (Z dP - dsum) o dlogit/ds, with Z the keep multiplier; one unrolled body per
       // softcap setting so that neither carries the other's code
       auto body = [&](auto cap_tag) {
         constexpr bool kCap = decltype(cap_tag)::value;
-#pragma unroll
-        for (int h32 = 0; h32 < BN; h32 += 32) {   // 16 packed columns per chunk; inputs in registers
+        {   // the half's 32 keys -> 16 packed columns of hi and of lo; inputs in registers
+          constexpr int h32 = 0;
           uint32_t hi[16], lo[16];
 #pragma unroll
           for (int c = 0; c < 32; c += 2) {
@@ -282,12 +305,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               const float zm = drop ? (((dw[cc / 32] >> (cc % 32)) & 1u) ? p.keep_scale : 0.f) : 1.f;
               dsv[u] = pr * (zm * dp[cc] - dsum) * deriv;
             }
-            const float h0 = round16<BF16>(dsv[0]), h1 = round16<BF16>(dsv[1]);
-            hi[c / 2] = pack2<BF16>(h0, h1);
-            lo[c / 2] = pack2<BF16>(dsv[0] - h0, dsv[1] - h1);
+            split2<BF16>(dsv[0], dsv[1], hi[c / 2], lo[c / 2]);
           }
-          tmem_st16(la + C::S_COL + (j & 1) * 64 + h32 / 2, hi);
-          tmem_st16(la + C::DP_COL + (j & 1) * 64 + h32 / 2, lo);
+          tmem_st16(la + C::S_COL + (j & 1) * 64 + 32 * hf, hi);
+          tmem_st16(la + C::DP_COL + (j & 1) * 64 + 32 * hf, lo);
         }
       };
       if constexpr (FEAT) {
@@ -305,12 +326,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (have && !mbar_wait_warp(bar + Bz::DQ_DONE, 0)) record_error(16);
     tc_fence_after();
     using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-    T* qrow = (T*)p.dQ + (long long)z * p.dqs.b + (long long)h * p.dqs.h + (long long)q * p.dqs.s;
+    T* qrow = (T*)p.dQ + (long long)z * p.dqs.b + (long long)h * p.dqs.h + (long long)q * p.dqs.s + hf * (D / 2);
 #pragma unroll
-    for (int c = 0; c < D; c += 32) {
+    for (int c = 0; c < D / 2; c += 32) {
       float o[32];
       if (have) {
-        tmem_ld32(la + C::DQ_COL + c, o);
+        tmem_ld32(la + C::DQ_COL + hf * (D / 2) + c, o);
         tc_wait_ld();
       } else {
 #pragma unroll
@@ -328,7 +349,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == WARP_MMA) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -393,13 +414,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(bar + Bz::SP_FULL + 8 * s, 1);
-      mbar_init(bar + Bz::DS_FULL + 8 * s, BK);
+      mbar_init(bar + Bz::DS_FULL + 8 * s, NELEM);
     }
     mbar_init(bar + Bz::DONE, 1);
     mbar_init(bar + Bz::DRAIN, 1);
     fence_barrier_init();
   }
-  if (warp == 5) {
+  if (warp == WARP_MMA) {
     tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
   }
@@ -408,7 +429,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == WARP_TMA) {
     if (lane == 0 && niter > 0) {
       mbar_expect_tx(bar + Bz::KV_FULL, 2 * C::KV_BYTES);
       for (int c = 0; c < C::NCH; ++c) {
@@ -427,7 +448,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       for (int i = max(0, niter - C::NS); i < niter; ++i) mbar_wait(bar + Bz::Q_FULL + 8 * (i % C::NS), (i / C::NS) & 1);
     }
     __syncwarp();
-  } else if (warp == 5) {
+  } else if (warp == WARP_MMA) {
     constexpr uint32_t ID_S = idesc_f16(BF16 ? 1 : 0, BK, BQ, 0, 0);   // S^T, dP^T: 128 x 64
     constexpr uint32_t ID_O = idesc_f16(BF16 ? 1 : 0, BK, D, 0, 1);    // dV, dK: 128 x D, B MN-major
     bool ok = niter == 0 || mbar_wait_warp(bar + Bz::KV_FULL, 0);
@@ -437,12 +458,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       if (lane == 0) {
         const int s = i % C::NS;
         const uint32_t qt = sQ + s * C::QT_BYTES, dot = sDO + s * C::QT_BYTES;
-        const uint32_t pb = tmem + C::S_COL + (i & 1) * 64;        // P~^T at [0,32), dS^T hi at [32,64)
-        const uint32_t lo = tmem + C::DP_COL + (i & 1) * 64;       // dS^T lo at [0,32)
+        // half hf (query rows [32 hf, 32 hf + 32)) keeps, in its own 32 S^T columns, P~^T packed at
+        // [0,16) and dS^T hi at [16,32), and dS^T lo in the first 16 of its dP^T columns
+        const uint32_t pb = tmem + C::S_COL + (i & 1) * 64, lo = tmem + C::DP_COL + (i & 1) * 64;
         for (int kk = 0; kk < BQ / 16; ++kk) {
-          mma_ts(tmem + C::DV_COL, pb + kk * 8, desc_mnmajor(dot, BQ, kk), ID_O, (i > 0 || kk > 0) ? 1u : 0u);
-          mma_ts(tmem + C::DK_COL, pb + 32 + kk * 8, desc_mnmajor(qt, BQ, kk), ID_O, (i > 0 || kk > 0) ? 1u : 0u);
-          mma_ts(tmem + C::DK_COL, lo + kk * 8, desc_mnmajor(qt, BQ, kk), ID_O, 1u);
+          const uint32_t off = (uint32_t)(32 * (kk / 2) + 8 * (kk % 2));
+          mma_ts(tmem + C::DV_COL, pb + off, desc_mnmajor(dot, BQ, kk), ID_O, (i > 0 || kk > 0) ? 1u : 0u);
+          mma_ts(tmem + C::DK_COL, pb + 16 + off, desc_mnmajor(qt, BQ, kk), ID_O, (i > 0 || kk > 0) ? 1u : 0u);
+          mma_ts(tmem + C::DK_COL, lo + off, desc_mnmajor(qt, BQ, kk), ID_O, 1u);
         }
         mma_commit(bar + Bz::Q_EMPTY + 8 * s);
       }
@@ -471,15 +494,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (!mbar_wait_warp(bar + Bz::DRAIN, 0)) record_error(64);
   } else {
     // ------------------------------------------------------------ elementwise (thread = key row)
-    const int key = kb + tid;
-    const uint32_t la = tmem + ((uint32_t)(warp * 32) << 16);
+    // warps w and w + 4 share keys kb + 32 (w%4) .. + 31; w / 4 picks the half of the 64-row query
+    // tile (32 rows) and of the dK / dV rows (D/2 columns) the thread owns
+    const int qd = warp & 3, hf = warp >> 2;
+    const int key = kb + qd * 32 + lane;
+    const uint32_t la = tmem + ((uint32_t)(qd * 32) << 16);
     const bool drop = FEAT && p.dropout;
     const bool use_bits = drop && p.dropout_bits != nullptr;
     const uint32_t thresh = fa_drop_thresh(p.dropout_p);
     const bool cap_on = FEAT && p.softcap > 0.f;
     const float cap_in = cap_on ? p.scale / p.softcap : 0.f;
     // the warp's 32 keys are one mask word column (kb is a multiple of 128)
-    const int kw = kb / 32 + warp;
+    const int kw = kb / 32 + qd;
     const bool kw_ok = kw < (SK + 31) / 32;
     // query rows that see this key (empty for keys past SK)
     int qlo, qhi;
@@ -488,14 +514,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     bool ok = true;
     for (int i = 0; i < niter; ++i) {
       const int h = kvh * p.gqa + i / nqt, qbase = (qt0 + i % nqt) * BQ;
-      // keep bits of this key over the tile's query rows: cw[hq] bit r <-> row qbase + 32hq + r.
-      // From the mask, lane l loads the word of row qbase + 32hq + l (one line per warp) and a
+      // keep bits of this key over the half's query rows: cw[0] bit r <-> row qbase + 32hf + r.
+      // From the mask, lane l loads the word of row qbase + 32hf + l (one line per warp) and a
       // ballot transpose after the wait turns rows-of-keys into keys-of-rows; without a mask,
       // Philox is evaluated here, down the key's column (counter stride SK).
-      uint32_t cw[BQ / 32];
-#pragma unroll
-      for (int hq = 0; hq < BQ / 32; ++hq) {
-        const int q0 = qbase + 32 * hq;
+      uint32_t cw[1];
+      {
+        constexpr int hq = 0;
+        const int q0 = qbase + 32 * hf;
         cw[hq] = 0u;
         if (use_bits) {
           if (kw_ok && q0 + lane < SQ) cw[hq] = __ldg(p.dropout_bits + fa_mask_word(h, SQ, SK, q0 + lane, kw));
@@ -505,8 +531,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
       float* stb = st + (i & 1) * 128;
       // this tile's lse2 / dsum (threads 0-63 and 64-127); the named barrier publishes them to the
-      // 4 warps and AND-reduces the wait outcome, so a timeout ends every warp at the same point
-      {
+      // 8 warps and AND-reduces the wait outcome, so a timeout ends every warp at the same point
+      if (tid < 128) {
         const int qi = tid & 63, q = qbase + qi;
         float v = 0.f;
         if (q < SQ) {
@@ -518,17 +544,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         stb[(tid < 64 ? 0 : 64) + qi] = v;
       }
       const bool got = mbar_wait_warp(bar + Bz::SP_FULL + 8 * (i & 1), (i >> 1) & 1);
-      if (!bar_and_128(got)) { ok = false; break; }
+      if (!bar_and_elem(got)) { ok = false; break; }
       tc_fence_after();
-      float s[BQ], dp[BQ];
-      tmem_ld32(la + C::S_COL + (i & 1) * 64, s);
-      tmem_ld32(la + C::S_COL + (i & 1) * 64 + 32, s + 32);
-      tmem_ld32(la + C::DP_COL + (i & 1) * 64, dp);
-      tmem_ld32(la + C::DP_COL + (i & 1) * 64 + 32, dp + 32);
+      float s[32], dp[32];
+      tmem_ld32(la + C::S_COL + (i & 1) * 64 + 32 * hf, s);
+      tmem_ld32(la + C::DP_COL + (i & 1) * 64 + 32 * hf, dp);
       tc_wait_ld();
       if (use_bits) {   // warp-uniform: every lane takes part in the ballots
-#pragma unroll
-        for (int hq = 0; hq < BQ / 32; ++hq) {
+        {
+          constexpr int hq = 0;
           uint32_t t = 0u;
 #pragma unroll
           for (int b = 0; b < 32; ++b) {
@@ -539,19 +563,20 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
       }
       const float slope = (FEAT && p.alibi) ? p.alibi[h] : 0.f;
-      const float d0 = (float)(key - qbase);   // key - q = d0 - cc, exact in fp32
+      const int qh = qbase + 32 * hf;          // first query row of this thread's half
+      const float d0 = (float)(key - qh);      // key - q = d0 - cc, exact in fp32
       auto body = [&](auto cap_tag) {
         constexpr bool kCap = decltype(cap_tag)::value;
-#pragma unroll
-        for (int h32 = 0; h32 < BQ; h32 += 32) {   // inputs are all in registers: in-place outputs are safe
+        {   // the half's 32 query rows; inputs are all in registers: in-place outputs are safe
+          constexpr int h32 = 0;
           uint32_t pk[16], hi[16], lo[16];
 #pragma unroll
           for (int c = 0; c < 32; c += 2) {
             float pv[2], dsv[2];
 #pragma unroll
             for (int u = 0; u < 2; ++u) {
-              const int cc = h32 + c + u, q = qbase + cc;
-              const float l2 = stb[cc];
+              const int cc = h32 + c + u, q = qh + cc;
+              const float l2 = stb[32 * hf + cc];
               const bool vis = q >= qlo && q <= qhi && l2 > -INFINITY;
               float logit, deriv = 1.f;
               if constexpr (kCap) {
@@ -566,16 +591,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               const float pr = vis ? ex2(fmaf(logit, FA_LOG2E, -l2)) : 0.f;
               const float zm = drop ? (((cw[h32 / 32] >> (c + u)) & 1u) ? p.keep_scale : 0.f) : 1.f;
               pv[u] = zm * pr;
-              dsv[u] = pr * (zm * dp[cc] - stb[64 + cc]) * deriv;
+              dsv[u] = pr * (zm * dp[cc] - stb[64 + 32 * hf + cc]) * deriv;
             }
             pk[c / 2] = pack2<BF16>(pv[0], pv[1]);
-            const float h0 = round16<BF16>(dsv[0]), h1 = round16<BF16>(dsv[1]);
-            hi[c / 2] = pack2<BF16>(h0, h1);
-            lo[c / 2] = pack2<BF16>(dsv[0] - h0, dsv[1] - h1);
+            split2<BF16>(dsv[0], dsv[1], hi[c / 2], lo[c / 2]);
           }
-          tmem_st16(la + C::S_COL + (i & 1) * 64 + h32 / 2, pk);
-          tmem_st16(la + C::S_COL + (i & 1) * 64 + 32 + h32 / 2, hi);
-          tmem_st16(la + C::DP_COL + (i & 1) * 64 + h32 / 2, lo);
+          tmem_st16(la + C::S_COL + (i & 1) * 64 + 32 * hf, pk);
+          tmem_st16(la + C::S_COL + (i & 1) * 64 + 32 * hf + 16, hi);
+          tmem_st16(la + C::DP_COL + (i & 1) * 64 + 32 * hf, lo);
         }
       };
       if constexpr (FEAT) {
@@ -593,15 +616,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (have && !mbar_wait_warp(bar + Bz::DONE, 0)) record_error(256);
     tc_fence_after();
     using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-    T* vrow = (T*)p.dV + (long long)z * p.dvs.b + (long long)kvh * p.dvs.h + (long long)key * p.dvs.s;
-    T* krow = (T*)p.dK + (long long)z * p.dks.b + (long long)kvh * p.dks.h + (long long)key * p.dks.s;
+    T* vrow = (T*)p.dV + (long long)z * p.dvs.b + (long long)kvh * p.dvs.h + (long long)key * p.dvs.s + hf * (D / 2);
+    T* krow = (T*)p.dK + (long long)z * p.dks.b + (long long)kvh * p.dks.h + (long long)key * p.dks.s + hf * (D / 2);
 #pragma unroll
     for (int part = 0; part < 2; ++part) {
-      const uint32_t col = part == 0 ? C::DV_COL : C::DK_COL;
+      const uint32_t col = (part == 0 ? C::DV_COL : C::DK_COL) + hf * (D / 2);
       const float mul = part == 0 ? 1.f : p.scale;
       T* row = part == 0 ? vrow : krow;
 #pragma unroll
-      for (int c = 0; c < D; c += 32) {
+      for (int c = 0; c < D / 2; c += 32) {
         float o[32];
         if (have) {
           tmem_ld32(la + col + c, o);
@@ -623,7 +646,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == WARP_MMA) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }

@@ -124,11 +124,19 @@ py::object fwd_varlen(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::
                       int64_t max_sq, int64_t max_sk, double scale, bool causal, int64_t win_left,
                       int64_t win_right, double softcap, c10::optional<torch::Tensor> alibi, double dropout_p,
                       int64_t seed, int64_t attn_chunk, c10::optional<torch::Tensor> seqused_q,
-                      c10::optional<torch::Tensor> seqused_k, bool return_lse) {
+                      c10::optional<torch::Tensor> seqused_k, bool return_lse,
+                      c10::optional<torch::Tensor> block_table) {
   need_cuda_lastdim(q, "q"); need_cuda_lastdim(k, "k"); need_cuda_lastdim(v, "v");
-  TORCH_CHECK_VALUE(q.dim() == 3 && k.dim() == 3 && v.dim() == 3, "fable_attn: varlen expects (total, H, D)");
+  const bool paged = block_table.has_value() && block_table->defined();
+  if (paged) {
+    TORCH_CHECK_VALUE(q.dim() == 3 && k.dim() == 4 && v.dim() == 4 && k.is_contiguous() && v.is_contiguous() &&
+                          k.sizes() == v.sizes(),
+                      "fable_attn: paged varlen expects q (total, H, D) and contiguous k/v (num_blocks, page, Hk, D)");
+  } else {
+    TORCH_CHECK_VALUE(q.dim() == 3 && k.dim() == 3 && v.dim() == 3, "fable_attn: varlen expects (total, H, D)");
+  }
   const c10::cuda::CUDAGuard guard(q.device());
-  const int Hq = q.size(1), D = q.size(2), Hk = k.size(1);
+  const int Hq = q.size(1), D = q.size(2), Hk = paged ? k.size(2) : k.size(1);
   TORCH_CHECK_VALUE(Hq % Hk == 0, "fable_attn: Hq must be a multiple of Hk (GQA)");
   const int batch = (int)cu_q.numel() - 1;
   // rows past seqused_q are not written by the kernel: zero them so nothing uninitialised leaks
@@ -148,7 +156,16 @@ py::object fwd_varlen(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::
   p.cu_q = opt_i32(cu_q); p.cu_k = opt_i32(cu_k);
   p.seqused_q = opt_i32(seqused_q); p.seqused_k = opt_i32(seqused_k);
   p.lse_total_q = q.size(0);
-  p.total_k = k.size(0);
+  p.total_k = paged ? 0 : k.size(0);
+  torch::Tensor bt;
+  if (paged) {
+    bt = block_table->to(torch::kInt32).contiguous();
+    TORCH_CHECK_VALUE(bt.dim() == 2 && bt.size(0) == batch, "fable_attn: block_table must be (batch, max_blocks)");
+    p.block_table = bt.data_ptr<int>();
+    p.page = (int)k.size(1);
+    p.max_blocks = (int)bt.size(1);
+    p.num_blocks = k.size(0);
+  }
   check(fa_forward_launch(&p, dt_of(q), cur_stream(q)), "forward (varlen)");
   if (return_lse) return py::make_tuple(out, lse);
   return py::cast(out);
@@ -359,7 +376,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("max_sq"), py::arg("max_sk"), py::arg("scale"), py::arg("causal"), py::arg("win_left"),
         py::arg("win_right"), py::arg("softcap"), py::arg("alibi"), py::arg("dropout_p"), py::arg("seed"),
         py::arg("attn_chunk") = 0, py::arg("seqused_q") = c10::optional<torch::Tensor>(),
-        py::arg("seqused_k") = c10::optional<torch::Tensor>(), py::arg("return_lse") = false);
+        py::arg("seqused_k") = c10::optional<torch::Tensor>(), py::arg("return_lse") = false,
+        py::arg("block_table") = c10::optional<torch::Tensor>());
   m.def("bwd_varlen", &bwd_varlen, py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"), py::arg("out"),
         py::arg("lse"), py::arg("cu_q"), py::arg("cu_k"), py::arg("max_sq"), py::arg("max_sk"), py::arg("scale"),
         py::arg("causal"), py::arg("win_left"), py::arg("win_right"), py::arg("softcap"), py::arg("alibi"),

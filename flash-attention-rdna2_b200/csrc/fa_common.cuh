@@ -131,6 +131,23 @@ __device__ __forceinline__ SeqGeom fa_seq_geom(int z, int SQd, int SKd, const in
   return g;
 }
 
+// Cache row of key position k of sequence z in a paged K/V (FaFwdParams block_table): page
+// block_table[z][k / page], slot k % page.  Positions past the table's row and invalid entries
+// give row k % page of page 0; `bad` is set for an invalid entry of a real key (k < SK).
+__device__ __forceinline__ long long fa_paged_row(const FaFwdParams& p, int z, int k, int SK, bool& bad) {
+  const int pi = k / p.page;
+  long long blk = 0;
+  bad = false;
+  if (pi < p.max_blocks) {
+    blk = p.block_table[(long long)z * p.max_blocks + pi];
+    if (blk < 0 || blk >= p.num_blocks) {
+      bad = k < SK;
+      blk = 0;
+    }
+  }
+  return blk * p.page + k % p.page;
+}
+
 // LSE / dsum row address: dense [batch, NH, SQ]; varlen [NH, total_q]
 __device__ __forceinline__ long long fa_lse_index(bool varlen, int z, int h, int NH, int SQd,
                                                   long long tok_q, long long total_q, int q) {

@@ -17,7 +17,8 @@ int dec_device_error(int clear);   // bit 0: a decode pipeline wait timed out
 // tensor-core split-K decode partials; *taken = false when the call is outside its envelope
 int dec_tc_partial(const FaDecParams& p, int dtype, cudaStream_t st, bool* taken);
 int dec_tc_device_error(int clear);
-int rot_device_error(int clear);   // bit 0: a rotary position outside the cos/sin table
+int rot_device_error(int clear);
+int fwd_simt_device_error(int clear);   // bit 0: an invalid block-table entry (paged forward)   // bit 0: a rotary position outside the cos/sin table
 int num_sms();
 
 int current_device();

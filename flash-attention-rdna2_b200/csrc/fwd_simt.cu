@@ -11,6 +11,7 @@
 namespace {
 
 constexpr int BR = 32, BC = 32;
+__device__ int g_simt_error = 0;   // bit 0: an invalid block-table entry of a real key
 
 template <typename T, int HD>
 __global__ void __launch_bounds__(256) fwd_simt_kernel(const FaFwdParams p) {
@@ -70,8 +71,17 @@ __global__ void __launch_bounds__(256) fwd_simt_kernel(const FaFwdParams p) {
     for (int e = t; e < BC * HD; e += 256) {
       const int r = e / HD, d = e % HD, k = kb + r;
       const bool ok = k < SK;
-      Ks[r * LDQ + d] = ok ? Elem<T>::to_f(Kg[(long long)k * p.sK.s + d]) : 0.f;
-      Vs[r * HD + d] = ok ? Elem<T>::to_f(Vg[(long long)k * p.sV.s + d]) : 0.f;
+      if (p.block_table) {   // paged cache [num_blocks * page rows][NKV][HD]
+        bool bad = false;
+        const long long row = ok ? fa_paged_row(p, z, k, SK, bad) : 0;
+        if (bad && d == 0) atomicOr(&g_simt_error, 1);
+        const long long off = (row * (p.NH / p.gqa) + kvh) * HD + d;
+        Ks[r * LDQ + d] = ok ? Elem<T>::to_f(((const T*)p.K)[off]) : 0.f;
+        Vs[r * HD + d] = ok ? Elem<T>::to_f(((const T*)p.V)[off]) : 0.f;
+      } else {
+        Ks[r * LDQ + d] = ok ? Elem<T>::to_f(Kg[(long long)k * p.sK.s + d]) : 0.f;
+        Vs[r * HD + d] = ok ? Elem<T>::to_f(Vg[(long long)k * p.sV.s + d]) : 0.f;
+      }
     }
     __syncthreads();
 
@@ -194,6 +204,15 @@ int launch_t(const FaFwdParams& p, cudaStream_t st) {
 }  // namespace
 
 namespace fa {
+int fwd_simt_device_error(int clear) {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_simt_error, sizeof(int));
+  if (clear && v) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_simt_error, &zero, sizeof(int));
+  }
+  return v;
+}
 int fwd_simt(const FaFwdParams& p, int dtype, cudaStream_t st) {
   if (dtype == FA_DTYPE_F16) return launch_t<__half>(p, st);
   if (dtype == FA_DTYPE_BF16) return launch_t<__nv_bfloat16>(p, st);

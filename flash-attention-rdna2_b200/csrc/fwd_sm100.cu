@@ -24,6 +24,7 @@
 // alibi without diagonal offset, Philox dropout keyed (h*SQ+q)*SK+key, LSE in natural log,
 // empty rows -> O = 0 and LSE = -inf.
 #include <cudaTypedefs.h>
+#include <algorithm>
 #include "fa_common.cuh"
 #include "fa_launch.h"
 #include "sm100_ptx.cuh"
@@ -156,25 +157,49 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       mbar_expect_tx(bar + Bars::Q_FULL, C::Q_BYTES);
       for (int c = 0; c < C::NCH; ++c)
         tma_load_4d(sQ + c * (BM * 128), &tmQ, c * 64, qtok0 + qb, h, bcoord, bar + Bars::Q_FULL);
+      // paged K/V: a tile is loaded as page slices of R rows (3-D maps over the cache rows);
+      // positions past the block table's row, and invalid entries, read page 0 (an invalid entry
+      // for a real key also raises the error flag), so every slice lands and expect_tx is fixed
+      const bool paged = p.block_table != nullptr;
+      const int R = paged ? min(p.page, BN) : BN;
+      auto page_row = [&](int pos) -> int {
+        const int pi = pos / p.page;
+        long long blk = 0;
+        if (pi < p.max_blocks) {
+          blk = p.block_table[(long long)z * p.max_blocks + pi];
+          if (blk < 0 || blk >= p.num_blocks) {
+            if (pos < SK) record_error(1024);
+            blk = 0;
+          }
+        }
+        return (int)(blk * p.page + pos % p.page);
+      };
+      auto load_tile = [&](uint32_t dst, const CUtensorMap* map, int kpos, uint32_t fb) {
+        if (!paged) {
+          for (int c = 0; c < C::NCH; ++c)
+            tma_load_4d(dst + c * C::CH_BYTES, map, c * 64, ktok0 + kpos, kvh, bcoord, fb);
+          return;
+        }
+        for (int sl = 0; sl < BN / R; ++sl) {
+          const int row = page_row(kpos + sl * R);
+          for (int c = 0; c < C::NCH; ++c) tma_load_3d(dst + c * C::CH_BYTES + sl * R * 128, map, c * 64, kvh, row, fb);
+        }
+      };
       for (int j = 0; j < ntiles; ++j) {
-        const int krow = ktok0 + (t0 + j) * BN;
+        const int kpos = (t0 + j) * BN;
         const int sk = j % C::NSK, sv = j % C::NSV;
         if (j >= C::NSK && !mbar_wait(bar + Bars::K_EMPTY + 8 * sk, ((j / C::NSK) - 1) & 1)) {
           record_error(1);
           break;
         }
         mbar_expect_tx(bar + Bars::K_FULL + 8 * sk, C::KV_BYTES);
-        for (int c = 0; c < C::NCH; ++c)
-          tma_load_4d(sK + sk * C::KV_BYTES + c * C::CH_BYTES, &tmK, c * 64, krow, kvh, bcoord,
-                      bar + Bars::K_FULL + 8 * sk);
+        load_tile(sK + sk * C::KV_BYTES, &tmK, kpos, bar + Bars::K_FULL + 8 * sk);
         if (j >= C::NSV && !mbar_wait(bar + Bars::V_EMPTY + 8 * sv, ((j / C::NSV) - 1) & 1)) {
           record_error(1);
           break;
         }
         mbar_expect_tx(bar + Bars::V_FULL + 8 * sv, C::KV_BYTES);
-        for (int c = 0; c < C::NCH; ++c)
-          tma_load_4d(sV + sv * C::KV_BYTES + c * C::CH_BYTES, &tmV, c * 64, krow, kvh, bcoord,
-                      bar + Bars::V_FULL + 8 * sv);
+        load_tile(sV + sv * C::KV_BYTES, &tmV, kpos, bar + Bars::V_FULL + 8 * sv);
       }
       // do not leave while copies of this CTA are still landing in shared memory
       for (int j = max(0, ntiles - C::NSK); j < ntiles; ++j)
@@ -485,6 +510,19 @@ bool make_map(CUtensorMap* m, const void* base, bool bf16, long long D, long lon
   return r == CUDA_SUCCESS;
 }
 
+// paged cache rows [rows][H][D] as 3-D (D, H, rows) with 128-byte swizzled boxes of 64 x 1 x R
+bool make_map3(CUtensorMap* m, const void* base, bool bf16, long long D, long long H, long long rows, int R) {
+  auto enc = encode_fn();
+  if (!enc || ((uintptr_t)base) % 16 != 0) return false;
+  const cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)rows};
+  const cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)(H * D) * 2};
+  const cuuint32_t box[3] = {64, 1, (cuuint32_t)R};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base),
+             dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int D, bool BF16, bool FEAT>
 int launch(const FaFwdParams& p, cudaStream_t st, const CUtensorMap& mq, const CUtensorMap& mk,
            const CUtensorMap& mv) {
@@ -525,7 +563,7 @@ int fwd_sm100(const FaFwdParams& p, int dtype, cudaStream_t st, bool* taken) {
   // next sequence are loaded but masked, rows past the last token read as zeros)
   long long rows_q, rows_k;
   if (varlen) {
-    if (p.lse_total_q <= 0 || p.total_k <= 0) return FA_OK;
+    if (p.lse_total_q <= 0 || (p.total_k <= 0 && !p.block_table)) return FA_OK;
     rows_q = p.lse_total_q;
     rows_k = p.total_k;
   } else {
@@ -535,8 +573,17 @@ int fwd_sm100(const FaFwdParams& p, int dtype, cudaStream_t st, bool* taken) {
   const int NKV = p.NH / p.gqa;
   CUtensorMap mq, mk, mv;
   if (!make_map(&mq, p.Q, bf16, p.HD, rows_q, p.NH, varlen ? 1 : p.batch, p.sQ, BM)) return FA_OK;
-  if (!make_map(&mk, p.K, bf16, p.HD, rows_k, NKV, varlen ? 1 : p.batch, p.sK, BN)) return FA_OK;
-  if (!make_map(&mv, p.V, bf16, p.HD, rows_k, NKV, varlen ? 1 : p.batch, p.sV, BN)) return FA_OK;
+  if (p.block_table) {
+    // paged cache [num_blocks * page rows][NKV][HD]: boxes of one page slice (a power of two of at
+    // least 8 rows, so each slice starts on a 1 KB swizzle atom)
+    if (p.page < 8 || (p.page & (p.page - 1)) || p.num_blocks * (long long)p.page >= (1ll << 31)) return FA_OK;
+    if (!make_map3(&mk, p.K, bf16, p.HD, NKV, p.num_blocks * (long long)p.page, std::min(p.page, BN)) ||
+        !make_map3(&mv, p.V, bf16, p.HD, NKV, p.num_blocks * (long long)p.page, std::min(p.page, BN)))
+      return FA_OK;
+  } else {
+    if (!make_map(&mk, p.K, bf16, p.HD, rows_k, NKV, varlen ? 1 : p.batch, p.sK, BN)) return FA_OK;
+    if (!make_map(&mv, p.V, bf16, p.HD, rows_k, NKV, varlen ? 1 : p.batch, p.sV, BN)) return FA_OK;
+  }
   if (((uintptr_t)p.O) % 16 || (p.sO.s % 8) || (p.sO.h % 8) || (!varlen && p.sO.b % 8)) return FA_OK;
   *taken = true;
   const bool feat = p.softcap > 0.f || p.alibi_slopes != nullptr || p.dropout_p > 0.f;
@@ -554,5 +601,5 @@ extern "C" FA_API int fa_device_error(int clear) {
     cudaMemcpyToSymbol(g_fwd_error, &zero, sizeof(int));
   }
   return v | (fa::dec_device_error(clear) ? 64 : 0) | (fa::bwd_device_error(clear) ? 128 : 0) |
-         (fa::rot_device_error(clear) ? 256 : 0);
+         (fa::rot_device_error(clear) ? 256 : 0) | (fa::fwd_simt_device_error(clear) ? 1024 : 0);
 }

@@ -282,8 +282,7 @@ def flash_attn_kvpacked_func(q, kv, dropout_p=0.0, softmax_scale=None, causal=Fa
                      v_descale, num_splits, pack_gqa, sm_margin)
 
 
-def _unpage(k, v, block_table, cu_seqlens_k, seqused_k):
-    """Paged (num_blocks, page, nheads_k, d) K/V + block_table -> packed varlen K/V."""
+def _check_paged(k, v, block_table, cu_seqlens_k):
     if k.dim() != 4 or v.dim() != 4:
         raise ValueError(
             "fable_attn: with block_table, k and v must be paged (num_blocks, page_block_size, nheads_k, "
@@ -293,6 +292,13 @@ def _unpage(k, v, block_table, cu_seqlens_k, seqused_k):
     if bt.dim() != 2 or bt.shape[0] != nseq:
         raise ValueError(f"fable_attn: block_table must be (batch, max_blocks), got {tuple(bt.shape)} for "
                          f"batch={nseq}")
+    return bt
+
+
+def _unpage(k, v, block_table, cu_seqlens_k, seqused_k):
+    """Paged (num_blocks, page, nheads_k, d) K/V + block_table -> packed varlen K/V (the autograd
+    path: the backward reads packed K/V)."""
+    bt = _check_paged(k, v, block_table, cu_seqlens_k)
     page = k.shape[1]
     lens = (seqused_k if seqused_k is not None else cu_seqlens_k[1:] - cu_seqlens_k[:-1]).tolist()
     ks, vs = [], []
@@ -315,9 +321,15 @@ def flash_attn_varlen_func(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, ma
     _reject_fp8(q_descale, k_descale, v_descale)
     _accept_hints(num_splits, pack_gqa, sm_margin)
     chunk = _check_chunk(attention_chunk)
+    paged_bt = None
     if block_table is not None:
-        k, v, cu_seqlens_k = _unpage(k, v, block_table, cu_seqlens_k, seqused_k)
-        seqused_k = None
+        grad = torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad)
+        if (grad or return_attn_probs or qv is not None or _pad_dim(q.shape[-1]) != q.shape[-1]
+                or not k.is_cuda or not k.is_contiguous() or not v.is_contiguous()):
+            k, v, cu_seqlens_k = _unpage(k, v, block_table, cu_seqlens_k, seqused_k)
+            seqused_k = None
+        else:   # the forward kernel reads the pages in place (no gather, no host sync)
+            paged_bt = _check_paged(k, v, block_table, cu_seqlens_k).contiguous()
     keep_cols = None
     if _needs_qv(q, v, qv):
         if softmax_scale is None:
@@ -340,8 +352,14 @@ def flash_attn_varlen_func(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, ma
     su_q = seqused_q.to(torch.int32).contiguous() if seqused_q is not None else None
     su_k = seqused_k.to(torch.int32).contiguous() if seqused_k is not None else None
     q, k, v = _lastdim_contig(q), _lastdim_contig(k), _lastdim_contig(v)
-    out, lse = _VarlenAttnFn.apply(q, k, v, cu_q, cu_k, max_seqlen_q, max_seqlen_k, softmax_scale, cflag, wl, wr,
-                                   softcap, al, dropout_p, chunk, su_q, su_k)
+    if paged_bt is not None:
+        seed = random.getrandbits(63) if dropout_p > 0 else 0
+        out, lse = _C.fwd_varlen(q, k, v, cu_q, cu_k, int(max_seqlen_q), int(max_seqlen_k), float(softmax_scale),
+                                 bool(cflag), int(wl), int(wr), float(softcap), al, float(dropout_p), int(seed),
+                                 int(chunk), su_q, su_k, True, block_table=paged_bt)
+    else:
+        out, lse = _VarlenAttnFn.apply(q, k, v, cu_q, cu_k, max_seqlen_q, max_seqlen_k, softmax_scale, cflag, wl,
+                                       wr, softcap, al, dropout_p, chunk, su_q, su_k)
     if keep_cols is not None:
         out = out[..., :keep_cols]
     if return_attn_probs:

@@ -93,6 +93,15 @@ typedef struct FaFwdParams {
   long long total_k;                   /* varlen: rows of K and V (total key tokens).  The tensor-core
                                           kernel needs it (with lse_total_q as the rows of Q and O) to
                                           bound its TMA boxes; 0 = unknown, the CUDA-core kernel runs */
+  /* paged K/V (varlen only; flash_attn_varlen_func's block_table): K and V are caches
+   * [num_blocks, page, NH/gqa, HD] contiguous, key position k of sequence z sits in page
+   * block_table[z * max_blocks + k / page], slot k % page; cu_k (or seqused_k) gives the key
+   * counts and sK / sV are ignored.  An entry outside [0, num_blocks) reads page 0 and raises
+   * fa_device_error bit 1024.  Replaces the reference's page unrolling before the forward
+   * (package/fable_attn/flash_attn_interface.py:438-472).  block_table null = not paged. */
+  const int* block_table;
+  int page, max_blocks;
+  long long num_blocks;
 } FaFwdParams;
 
 FA_API int fa_forward_launch(const FaFwdParams* p, int dtype, void* stream);

@@ -27,7 +27,8 @@ class FaFwdParams(C.Structure):
                 ("causal", C.c_int), ("win_left", C.c_int), ("win_right", C.c_int), ("attn_chunk", C.c_int),
                 ("alibi_slopes", C.c_void_p), ("dropout_p", C.c_float), ("philox_seed", C.c_ulonglong),
                 ("cu_q", C.c_void_p), ("cu_k", C.c_void_p), ("seqused_q", C.c_void_p), ("seqused_k", C.c_void_p),
-                ("lse_total_q", C.c_longlong), ("dropout_bits", C.c_void_p), ("total_k", C.c_longlong)]
+                ("lse_total_q", C.c_longlong), ("dropout_bits", C.c_void_p), ("total_k", C.c_longlong),
+                ("block_table", C.c_void_p), ("page", C.c_int), ("max_blocks", C.c_int), ("num_blocks", C.c_longlong)]
 
 
 class FaBwdParams(C.Structure):

@@ -1,0 +1,78 @@
+"""Multi-GPU decode (fable_attn.multigpu.decode_kv_split) on 2 GPUs over NCCL: each rank holds
+its contiguous chunk of every sequence's context and decodes against it; the all-gathered
+partials merged by flash_attn_combine equal single-GPU decode over the whole context within the
+bf16 tolerance.  Skipped when fewer than 2 GPUs are visible."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, ret):
+    import datetime
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        import fable_attn as fa
+        from fable_attn import multigpu as M
+        dev = torch.device("cuda", rank)
+        B, H, Hk, D, page = 4, 16, 4, 128, 64
+        rng = np.random.default_rng(0)              # the same global cache on every rank
+        lens = np.array([3000, 640, 1999, 129])
+        nper = int((lens.max() + page - 1) // page)
+        kc = torch.from_numpy(rng.standard_normal((B * nper, page, Hk, D)).astype(np.float32)).to(dev, torch.bfloat16)
+        vc = torch.from_numpy(rng.standard_normal((B * nper, page, Hk, D)).astype(np.float32)).to(dev, torch.bfloat16)
+        bt = torch.from_numpy(rng.permutation(B * nper).astype(np.int32).reshape(B, nper)).to(dev)
+        q = torch.from_numpy(rng.standard_normal((B, 1, H, D)).astype(np.float32)).to(dev, torch.bfloat16)
+        ref = fa.flash_attn_with_kvcache(q, kc, vc, cache_seqlens=torch.from_numpy(lens.astype(np.int32)).to(dev),
+                                         block_table=bt)
+        # this rank's chunk, copied into its own dense pages (page-aligned local positions)
+        starts, ends = M.plan_kv_split(torch.from_numpy(lens), world)
+        s, e = starts[rank], ends[rank]
+        loc = (e - s).to(torch.int32)
+        lp = int((int(loc.max()) + page - 1) // page)
+        kl = torch.zeros(B * lp, page, Hk, D, device=dev, dtype=torch.bfloat16)
+        vl = torch.zeros_like(kl)
+        for b in range(B):
+            fk = kc[bt[b].long()].reshape(-1, Hk, D)[int(s[b]):int(e[b])]
+            fv = vc[bt[b].long()].reshape(-1, Hk, D)[int(s[b]):int(e[b])]
+            kl.view(B, lp * page, Hk, D)[b, :fk.shape[0]] = fk
+            vl.view(B, lp * page, Hk, D)[b, :fv.shape[0]] = fv
+        btl = torch.arange(B * lp, device=dev, dtype=torch.int32).view(B, lp)
+        out = M.decode_kv_split(q, kl, vl, btl, loc.to(dev))
+        err = ((out.float() - ref.float()).norm() / ref.float().norm()).item()
+        ret[rank] = err
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_decode_kv_split_nccl_two_gpus():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    ret = ctx.Manager().dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, ret)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(180)
+        assert p.exitcode == 0
+    assert len(ret) == 2 and max(ret.values()) < 2.5e-3
