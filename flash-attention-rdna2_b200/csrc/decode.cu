@@ -251,8 +251,10 @@ __global__ void dec_merge_kernel(const FaDecParams p) {
     int lo = p.leftpad ? p.leftpad[b] : 0;
     if (p.window >= 0) lo = max(lo, ctx0 + tk - p.window + 1);
     if (ctx <= max(lo, 0)) {
-      T* o = (T*)p.o + ((long long)row * p.NH + h) * HD;
-      for (int d = threadIdx.x; d < HD; d += blockDim.x) o[d] = Elem<T>::from_f(0.f);
+      for (int d = threadIdx.x; d < HD; d += blockDim.x) {
+        if (p.o_f32) ((float*)p.o)[((long long)row * p.NH + h) * HD + d] = 0.f;
+        else ((T*)p.o)[((long long)row * p.NH + h) * HD + d] = Elem<T>::from_f(0.f);
+      }
       if (p.lse_out && threadIdx.x == 0) p.lse_out[(long long)row * p.NH + h] = -INFINITY;
       return;
     }
@@ -267,7 +269,7 @@ __global__ void dec_merge_kernel(const FaDecParams p) {
       if (ms != -INFINITY) L += base[(long long)s * (HD + 2) + 1] * exp2f(ms - M);
     }
   const float invL = L > 0.f ? 1.f / L : 0.f;
-  T* o = (T*)p.o + ((long long)row * p.NH + h) * HD;
+  const long long obase = ((long long)row * p.NH + h) * HD;
   for (int d = threadIdx.x; d < HD; d += blockDim.x) {
     float a = 0.f;
     if (M != -INFINITY)
@@ -275,7 +277,8 @@ __global__ void dec_merge_kernel(const FaDecParams p) {
         const float ms = base[(long long)s * (HD + 2)];
         if (ms != -INFINITY) a += base[(long long)s * (HD + 2) + 2 + d] * exp2f(ms - M);
       }
-    o[d] = Elem<T>::from_f(a * invL);
+    if (p.o_f32) ((float*)p.o)[obase + d] = a * invL;
+    else ((T*)p.o)[obase + d] = Elem<T>::from_f(a * invL);
   }
   if (p.lse_out && threadIdx.x == 0)
     p.lse_out[(long long)row * p.NH + h] = L > 0.f ? M * FA_LN2 + logf(L) : -INFINITY;

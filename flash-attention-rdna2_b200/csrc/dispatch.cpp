@@ -243,7 +243,7 @@ std::vector<torch::Tensor> dec(torch::Tensor q, torch::Tensor k_cache, torch::Te
                                c10::optional<torch::Tensor> rotary_sin, bool rotary_interleaved, double scale,
                                int64_t window, int64_t num_splits, c10::optional<torch::Tensor> cache_leftpad,
                                bool return_lse, double softcap, c10::optional<torch::Tensor> alibi,
-                               int64_t rotary_dim, c10::optional<torch::Tensor> rotary_pos) {
+                               int64_t rotary_dim, c10::optional<torch::Tensor> rotary_pos, bool out_fp32) {
   TORCH_CHECK_VALUE(q.is_cuda() && k_cache.is_cuda() && v_cache.is_cuda(), "fable_attn: decode needs CUDA tensors");
   TORCH_CHECK_VALUE(q.dim() == 4 && q.is_contiguous(), "fable_attn: decode q must be contiguous [B,nq,Hq,D]");
   TORCH_CHECK_VALUE(k_cache.dim() == 4 && k_cache.is_contiguous() && v_cache.is_contiguous(),
@@ -256,7 +256,7 @@ std::vector<torch::Tensor> dec(torch::Tensor q, torch::Tensor k_cache, torch::Te
   // split count from shapes only (no .item(): no host sync)
   const long long ctx_bound = (long long)block_table.size(1) * page;
   const int nsplit = fa_decode_num_splits(B, NQ, Hk, ctx_bound, (int)num_splits);
-  auto out = torch::empty({B, NQ, Hq, D}, q.options());
+  auto out = torch::empty({B, NQ, Hq, D}, out_fp32 ? q.options().dtype(torch::kFloat32) : q.options());
   auto scratch = torch::empty({fa_decode_scratch_floats(B, NQ, Hq, D, nsplit)}, q.options().dtype(torch::kFloat32));
   auto lse = return_lse ? torch::empty({B, NQ, Hq}, q.options().dtype(torch::kFloat32))
                         : torch::empty({0}, q.options().dtype(torch::kFloat32));
@@ -274,6 +274,7 @@ std::vector<torch::Tensor> dec(torch::Tensor q, torch::Tensor k_cache, torch::Te
   p.softcap = (float)softcap; p.alibi = opt_f32(alibi); p.nq = NQ;
   p.rotary_dim = (int)rotary_dim; p.rotary_pos = opt_i32(rotary_pos);
   p.num_blocks = k_cache.size(0);
+  p.o_f32 = out_fp32 ? 1 : 0;
   const void* nk = nullptr; const void* nv = nullptr;
   if (new_k.has_value()) {
     TORCH_CHECK_VALUE(new_v.has_value() && new_k->is_contiguous() && new_v->is_contiguous(),
@@ -388,7 +389,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("rotary_interleaved"), py::arg("scale"), py::arg("window"), py::arg("num_splits"),
         py::arg("cache_leftpad") = c10::optional<torch::Tensor>(), py::arg("return_lse") = false,
         py::arg("softcap") = 0.0, py::arg("alibi") = c10::optional<torch::Tensor>(), py::arg("rotary_dim") = 0,
-        py::arg("rotary_pos") = c10::optional<torch::Tensor>());
+        py::arg("rotary_pos") = c10::optional<torch::Tensor>(), py::arg("out_fp32") = false);
   m.def("combine", &combine, py::arg("out_partial"), py::arg("lse_partial"), py::arg("out_dtype"),
         py::arg("return_lse") = false);
   m.def("kernel_launch_count", []() { return fa_kernel_launch_count(); });

@@ -1,5 +1,5 @@
 // sm100_ptx.cuh — thin inline-PTX wrappers for the Blackwell (sm_100a) primitives the tensor-core
-// kernels use: mbarriers (with bounded waits), TMA tensor loads (no multicast), tcgen05 TMEM
+// kernels use: mbarriers (with bounded waits), TMA tensor loads (each into this CTA only), tcgen05 TMEM
 // allocation / MMA / commit / load / store / fences, and the UMMA shared-memory and instruction
 // descriptors.  Descriptor bit layouts follow the PTX ISA description of tcgen05 matrix
 // descriptors (also documented in CUTLASS's cute/arch/mma_sm100_desc.hpp).
@@ -52,7 +52,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint64_
   }
 }
 
-// ---------------------------------------------------------------- TMA (tiled, no multicast)
+// ---------------------------------------------------------------- TMA (tiled, this CTA only)
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
                                             uint32_t bar) {
   asm volatile(

@@ -65,10 +65,14 @@ def decode_kv_split(q, k_cache_local, v_cache_local, block_table_local, local_le
     """Decode against a context split across ranks (no rotary / alibi / window: those depend on
     the global query position and are served by the single-GPU flash_attn_with_kvcache).
     Each rank passes its local paged cache and local lengths; every rank returns the full
-    output (B, nq, H, D) in q's dtype."""
-    from .flash_attn_interface import flash_attn_combine, flash_attn_with_kvcache
-    out_r, lse_r = flash_attn_with_kvcache(q, k_cache_local, v_cache_local, cache_seqlens=local_lengths,
-                                           block_table=block_table_local, softmax_scale=softmax_scale,
-                                           num_splits=num_splits, return_softmax_lse=True)
-    out_all, lse_all = gather_partials(out_r.float(), lse_r.float(), group)
+    output (B, nq, H, D) in q's dtype.  The rank's partial stays fp32 until the LSE merge (its
+    16-bit rounding would otherwise add to the final one)."""
+    from . import _C
+    from .flash_attn_interface import flash_attn_combine
+    scale = softmax_scale if softmax_scale is not None else q.shape[-1] ** -0.5
+    lens = local_lengths.to(device=q.device, dtype=torch.int32).contiguous()
+    out_r, lse_r = _C.dec(q.contiguous(), k_cache_local, v_cache_local, block_table_local.to(torch.int32).contiguous(),
+                          lens, None, None, None, None, False, float(scale), -1, int(num_splits), None, True,
+                          out_fp32=True)
+    out_all, lse_all = gather_partials(out_r, lse_r.transpose(1, 2).contiguous(), group)
     return flash_attn_combine(out_all, lse_all, out_dtype=q.dtype)

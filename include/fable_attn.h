@@ -227,6 +227,8 @@ typedef struct FaDecParams {
                                           against it on the device; out-of-range pages read as
                                           empty and set the error flag) */
   int* err_flag;                       /* optional device int set non-zero on a bad page index */
+  int o_f32;                           /* 1: o is fp32 (for callers that merge partial results further,
+                                          e.g. a KV range split across GPUs); 0: o has q's dtype */
 } FaDecParams;
 
 FA_API int fa_decode_launch(const FaDecParams* p, int dtype, void* stream,

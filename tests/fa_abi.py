@@ -50,7 +50,7 @@ class FaDecParams(C.Structure):
         (n, C.c_int) for n in ("batch", "NH", "gqa", "HD", "page", "max_blocks", "nsplit", "window", "rotary")] + [
         ("scale", C.c_float), ("leftpad", C.c_void_p), ("lse_out", C.c_void_p), ("softcap", C.c_float),
         ("alibi", C.c_void_p), ("nq", C.c_int), ("append", C.c_int), ("rotary_dim", C.c_int),
-        ("rotary_pos", C.c_void_p), ("num_blocks", C.c_longlong), ("err_flag", C.c_void_p)]
+        ("rotary_pos", C.c_void_p), ("num_blocks", C.c_longlong), ("err_flag", C.c_void_p), ("o_f32", C.c_int)]
 
 
 class FaCombineParams(C.Structure):
