@@ -52,8 +52,8 @@ __device__ int g_fwd_error = 0;       // non-zero after a pipeline wait timed ou
 
 template <int D>
 struct Cfg {
-  static constexpr int NSK = (D <= 64) ? 4 : 3;                // K ring depth (freed after S)
-  static constexpr int NSV = (D <= 64) ? 4 : 2;                // V ring depth (freed after PV)
+  static constexpr int NSK = (D <= 64) ? 4 : 2;                // K ring depth (freed after S)
+  static constexpr int NSV = (D <= 64) ? 4 : 3;                // V ring depth (freed after PV)
   static constexpr int NCH = D / 64;                           // 64-column (128-byte) chunks per row
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int KV_BYTES = BN * D * 2;                  // one K (or V) tile
