@@ -476,6 +476,367 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   }
 }
 
+// =====================================================================================
+// Two query tiles per CTA ("ping-pong"), dense inputs without softcap / alibi / dropout.
+//
+// One CTA = rows [qb, qb + 256) of one head: tile A = the first 128 rows, tile B = the next 128.
+// The MMA warp alternates the tiles, so the tensor cores run one tile's S = Q K^T and O += P V
+// while the other tile's softmax is in flight:
+//   S_A(0) S_B(0) | PV_A(0) S_A(1) PV_B(0) S_B(1) | PV_A(1) S_A(2) PV_B(1) S_B(2) | ...
+// Warp roles (384 threads, three warpgroups):
+//   warps 0-3   softmax of tile A, warps 4-7 softmax of tile B: thread = query row (TMEM lane
+//               32 (w % 4) + lane), the whole 128-key S row read into registers in one pass
+//               (max, lazy online-softmax update, 2^(s - m), row sum, P as packed 16-bit pairs into
+//               the first 64 columns of the same S buffer), then the O row of its tile.
+//   warp 8      TMA producer (Q tiles once, K and V tiles into rings);
+//   warp 9      MMA issuer (owns TMEM); warps 10-11 idle (they complete warpgroup 2).
+// Registers: the kernel is compiled for 384 x 168; warpgroup 2 lowers itself to 56 per thread
+// (setmaxnreg.dec) and the two softmax warpgroups raise themselves to 224, which holds a full S row.
+// 2 * 224 + 56 = 3 * 168, so the raises are always satisfiable; the host launches this kernel only
+// after checking that it really was built with 168 registers per thread.
+// TMEM: S_A [0,128), S_B [128,256), O_A [256, 384), O_B [384, 512).
+// Semantics are those of the single-tile kernel above (masks, lazy rescale, LSE, empty rows).
+constexpr int PP_THREADS = 384, PP_REGS = 168, PP_REGS_SOFTMAX = 224, PP_REGS_OTHER = 56;
+static_assert(2 * PP_REGS_SOFTMAX + PP_REGS_OTHER == 3 * PP_REGS, "register split must use the launch total");
+
+struct PpCfg {   // D = 128
+  static constexpr int D = 128, NSK = 2, NSV = 3, NCH = 2;
+  static constexpr int Q_BYTES = BM * D * 2, KV_BYTES = BN * D * 2, CH_BYTES = BN * 128;
+  static constexpr int OFF_Q = 0, OFF_K = 2 * Q_BYTES, OFF_V = OFF_K + NSK * KV_BYTES;
+  static constexpr int OFF_BAR = OFF_V + NSV * KV_BYTES;
+  static constexpr int SMEM = OFF_BAR + 256 + 1024;
+  static constexpr uint32_t O_COL = 256;
+  static_assert(SMEM <= 232448, "shared memory per CTA");
+};
+struct PpBars {   // S_FULL / P_FULL / O_DONE: [tile A, tile B]
+  static constexpr int Q_FULL = 0, K_FULL = 8, K_EMPTY = 24, V_FULL = 40, V_EMPTY = 64, S_FULL = 88,
+                       P_FULL = 104, O_DONE = 120, MMA_DRAIN = 136, TMEM_ADDR = 144;
+};
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+template <bool BF16>
+__global__ void __launch_bounds__(PP_THREADS, 1)
+    fwd_pp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                  const __grid_constant__ CUtensorMap tmV, const FaFwdParams p) {
+  using C = PpCfg;
+  using Bz = PpBars;
+  constexpr int D = C::D;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  uint8_t* sgen = smem_raw + (sbase - smem_u32(smem_raw));
+  const uint32_t sQ = sbase + C::OFF_Q, sK = sbase + C::OFF_K, sV = sbase + C::OFF_V;
+  const uint32_t bar = sbase + C::OFF_BAR;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sgen + C::OFF_BAR + Bz::TMEM_ADDR);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int z = blockIdx.z, h = blockIdx.y, kvh = h / p.gqa;
+  const int SQ = p.SQ, SK = p.SK;
+  const int qb = (gridDim.x - 1 - blockIdx.x) * (2 * BM);   // heavy (late, causal) tiles first
+  if (qb >= SQ) return;
+
+  // key tiles: the union of what the CTA's 256 rows can see
+  int klo, khi, dmy;
+  fa_key_range(qb, SQ, SK, p.causal, p.win_left, p.win_right, p.attn_chunk, klo, dmy);
+  fa_key_range(min(qb + 2 * BM, SQ) - 1, SQ, SK, p.causal, p.win_left, p.win_right, p.attn_chunk, dmy, khi);
+  klo = max(klo, 0);
+  khi = min(khi, SK - 1);
+  const int t0 = klo / BN;
+  const int ntiles = (khi >= klo) ? (khi / BN - t0 + 1) : 0;
+
+  if (tid == 0) {
+    mbar_init(bar + Bz::Q_FULL, 1);
+    for (int s = 0; s < C::NSK; ++s) {
+      mbar_init(bar + Bz::K_FULL + 8 * s, 1);
+      mbar_init(bar + Bz::K_EMPTY + 8 * s, 1);
+    }
+    for (int s = 0; s < C::NSV; ++s) {
+      mbar_init(bar + Bz::V_FULL + 8 * s, 1);
+      mbar_init(bar + Bz::V_EMPTY + 8 * s, 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(bar + Bz::S_FULL + 8 * t, 1);
+      mbar_init(bar + Bz::P_FULL + 8 * t, BM);
+      mbar_init(bar + Bz::O_DONE + 8 * t, 1);
+    }
+    mbar_init(bar + Bz::MMA_DRAIN, 1);
+    fence_barrier_init();
+  }
+  if (warp == WARP_MMA) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  if (warp == WARP_TMA && lane == 0) {
+    prefetch_tmap(&tmQ);
+    prefetch_tmap(&tmK);
+    prefetch_tmap(&tmV);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp >= 8) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(PP_REGS_OTHER));
+    if (warp == WARP_TMA) {
+      // ======================= TMA producer
+      if (lane == 0 && ntiles > 0) {
+        mbar_expect_tx(bar + Bz::Q_FULL, 2 * C::Q_BYTES);
+        for (int t = 0; t < 2; ++t)
+          for (int c = 0; c < C::NCH; ++c)
+            tma_load_4d(sQ + t * C::Q_BYTES + c * (BM * 128), &tmQ, c * 64, qb + t * BM, h, z, bar + Bz::Q_FULL);
+        for (int j = 0; j < ntiles; ++j) {
+          const int kpos = (t0 + j) * BN;
+          const int sk = j % C::NSK, sv = j % C::NSV;
+          if (j >= C::NSK && !mbar_wait(bar + Bz::K_EMPTY + 8 * sk, ((j / C::NSK) - 1) & 1)) {
+            record_error(1);
+            break;
+          }
+          mbar_expect_tx(bar + Bz::K_FULL + 8 * sk, C::KV_BYTES);
+          for (int c = 0; c < C::NCH; ++c)
+            tma_load_4d(sK + sk * C::KV_BYTES + c * C::CH_BYTES, &tmK, c * 64, kpos, kvh, z, bar + Bz::K_FULL + 8 * sk);
+          if (j >= C::NSV && !mbar_wait(bar + Bz::V_EMPTY + 8 * sv, ((j / C::NSV) - 1) & 1)) {
+            record_error(1);
+            break;
+          }
+          mbar_expect_tx(bar + Bz::V_FULL + 8 * sv, C::KV_BYTES);
+          for (int c = 0; c < C::NCH; ++c)
+            tma_load_4d(sV + sv * C::KV_BYTES + c * C::CH_BYTES, &tmV, c * 64, kpos, kvh, z, bar + Bz::V_FULL + 8 * sv);
+        }
+        // do not leave while copies of this CTA are still landing in shared memory
+        for (int j = max(0, ntiles - C::NSK); j < ntiles; ++j)
+          mbar_wait(bar + Bz::K_FULL + 8 * (j % C::NSK), (j / C::NSK) & 1);
+        for (int j = max(0, ntiles - C::NSV); j < ntiles; ++j)
+          mbar_wait(bar + Bz::V_FULL + 8 * (j % C::NSV), (j / C::NSV) & 1);
+      }
+      __syncwarp();
+    } else if (warp == WARP_MMA) {
+      // ======================= MMA issuer (whole warp follows; lane 0 issues).  S_X(j+1) reuses
+      // the TMEM columns PV_X(j) reads P_X(j) from; the tensor core executes one thread's MMAs in
+      // issue order, so the overwrite follows the read.
+      constexpr uint32_t IDESC_S = idesc_f16(BF16 ? 1 : 0, BM, BN, 0, 0);
+      constexpr uint32_t IDESC_O = idesc_f16(BF16 ? 1 : 0, BM, D, 0, 1);
+      bool ok = ntiles == 0 || mbar_wait_warp(bar + Bz::Q_FULL, 0);
+      if (!ok) record_error(2);
+      auto issue_s = [&](int j, int t) {   // lane 0; K tile j has landed
+        const uint32_t kbase = sK + (j % C::NSK) * C::KV_BYTES, qbase = sQ + t * C::Q_BYTES;
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const int c = kk / 4, off = (kk % 4) * 32;   // 16 columns = 32 bytes inside a 128-byte chunk
+          const uint64_t ad = sdesc_sw128(qbase + c * (BM * 128) + off, 16, 1024);
+          const uint64_t bd = sdesc_sw128(kbase + c * C::CH_BYTES + off, 16, 1024);
+          mma_ss(tmem + (uint32_t)(t * BN), ad, bd, IDESC_S, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(bar + Bz::S_FULL + 8 * t);
+      };
+      auto wait_k = [&](int j) -> bool {
+        if (!mbar_wait_warp(bar + Bz::K_FULL + 8 * (j % C::NSK), (j / C::NSK) & 1)) return false;
+        tc_fence_after();
+        return true;
+      };
+      auto issue_pv = [&](int j, int t) -> bool {
+        const int s = j % C::NSV;
+        if (!mbar_wait_warp(bar + Bz::P_FULL + 8 * t, j & 1)) return false;
+        if (t == 0 && !mbar_wait_warp(bar + Bz::V_FULL + 8 * s, (j / C::NSV) & 1)) return false;
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t pt = tmem + (uint32_t)(t * BN);
+          const uint32_t vbase = sV + s * C::KV_BYTES;
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            // A = P from TMEM (keys packed two per column); B = V tile, MN-major
+            const uint64_t bd = sdesc_sw128(vbase + kk * 16 * 128, C::CH_BYTES, 1024);
+            mma_ts(tmem + C::O_COL + (uint32_t)(t * D), pt + kk * 8, bd, IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(bar + Bz::O_DONE + 8 * t);
+          if (t == 1) mma_commit(bar + Bz::V_EMPTY + 8 * s);
+        }
+        __syncwarp();
+        return true;
+      };
+      if (ok && ntiles > 0) {
+        if (!wait_k(0)) ok = false;
+        if (ok && lane == 0) {
+          issue_s(0, 0);
+          issue_s(0, 1);
+          mma_commit(bar + Bz::K_EMPTY);
+        }
+        __syncwarp();
+      }
+      for (int j = 0; ok && j < ntiles; ++j) {
+        const bool more = j + 1 < ntiles;
+        if (!issue_pv(j, 0)) { ok = false; break; }
+        if (more) {
+          if (!wait_k(j + 1)) { ok = false; break; }
+          if (lane == 0) issue_s(j + 1, 0);
+          __syncwarp();
+        }
+        if (!issue_pv(j, 1)) { ok = false; break; }
+        if (more) {
+          if (lane == 0) {
+            issue_s(j + 1, 1);
+            mma_commit(bar + Bz::K_EMPTY + 8 * ((j + 1) % C::NSK));
+          }
+          __syncwarp();
+        }
+      }
+      if (!ok) record_error(4);
+      // every MMA this warp issued has completed before TMEM can be released (also on error paths)
+      if (lane == 0) mma_commit(bar + Bz::MMA_DRAIN);
+      __syncwarp();
+      if (!mbar_wait_warp(bar + Bz::MMA_DRAIN, 0)) record_error(32);
+    }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(PP_REGS_SOFTMAX));
+    // ======================= softmax + epilogue of tile tt
+    const int tt = warp >> 2;
+    const int r = (warp & 3) * 32 + lane, q = qb + tt * BM + r;
+    const int qt = qb + tt * BM;   // first row of this tile
+    const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    const uint32_t o_col = C::O_COL + (uint32_t)(tt * D);
+    int rlo, rhi;
+    fa_key_range(q, SQ, SK, p.causal, p.win_left, p.win_right, p.attn_chunk, rlo, rhi);
+    if (q >= SQ) { rlo = 1; rhi = 0; }
+    int lo_last = 1, hi_first = 0;   // tile-uniform bounds: key tiles every row sees in full
+    if (qt < SQ) {
+      int a, b;
+      fa_key_range(min(qt + BM, SQ) - 1, SQ, SK, p.causal, p.win_left, p.win_right, p.attn_chunk, lo_last, a);
+      fa_key_range(qt, SQ, SK, p.causal, p.win_left, p.win_right, p.attn_chunk, b, hi_first);
+    }
+    const bool full_rows = qt + BM <= SQ;
+    const float scale2 = p.scale * FA_LOG2E;
+    float m_ref = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < ntiles; ++j) {
+      const int kb = (t0 + j) * BN;
+      if (!mbar_wait_warp(bar + Bz::S_FULL + 8 * tt, j & 1)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t sa = lane_addr + (uint32_t)(tt * BN);
+      float s[BN];
+#pragma unroll
+      for (int c0 = 0; c0 < BN; c0 += 32) tmem_ld32(sa + c0, s + c0);
+      tc_wait_ld();
+      if (!(full_rows && kb >= lo_last && kb + BN - 1 <= hi_first && kb + BN <= SK)) {
+#pragma unroll
+        for (int c = 0; c < BN; ++c) {
+          const int key = kb + c;
+          if (key < rlo || key > rhi) s[c] = -INFINITY;
+        }
+      }
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int c = 0; c < BN; c += 8) {
+        mx[0] = fmax3(mx[0], s[c], s[c + 1]);
+        mx[1] = fmax3(mx[1], s[c + 2], s[c + 3]);
+        mx[2] = fmax3(mx[2], s[c + 4], s[c + 5]);
+        mx[3] = fmax3(mx[3], s[c + 6], s[c + 7]);
+      }
+      float tmax = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]);
+      tmax = (tmax == -INFINITY) ? -INFINITY : tmax * scale2;
+      // lazy online-softmax update: the reference max moves only when it grows by > 2^8
+      const bool move = tmax > m_ref + LAZY_THRESH || (m_ref == -INFINITY && tmax != -INFINITY);
+      float corr = 1.f;
+      if (move) {
+        corr = ex2(m_ref - tmax);   // 0 when the row had no visible key yet (its O row is 0)
+        l *= corr;
+        m_ref = tmax;
+      }
+      const float muse = (m_ref == -INFINITY) ? 0.f : m_ref;
+      // P = 2^(s - m): row sum, 16-bit pairs into the first BN/2 columns of the same S buffer
+      // (the whole row is already in registers)
+      float2 lsum2 = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float2 x2 = __ffma2_rn(make_float2(s[c0 + 2 * i], s[c0 + 2 * i + 1]), make_float2(scale2, scale2),
+                                       make_float2(-muse, -muse));
+          const float a = ex2(x2.x), b = ex2(x2.y);
+          lsum2 = __fadd2_rn(lsum2, make_float2(a, b));
+          if constexpr (BF16) {
+            const __nv_bfloat162 t2 = __floats2bfloat162_rn(a, b);
+            pk[i] = *reinterpret_cast<const uint32_t*>(&t2);
+          } else {
+            const __half2 t2 = __floats2half2_rn(a, b);
+            pk[i] = *reinterpret_cast<const uint32_t*>(&t2);
+          }
+        }
+        tmem_st16(sa + c0 / 2, pk);
+      }
+      // O rescale.  Every tile j >= 1 waits exactly once for PV_{j-1} of this tile (so the parity
+      // wait never aliases an older phase).  tcgen05.ld/st are warp-collective: rows that did not
+      // move scale by 1.
+      if (j > 0) {
+        if (!mbar_wait_warp(bar + Bz::O_DONE + 8 * tt, (j - 1) & 1)) { ok = false; break; }
+        if (__any_sync(0xffffffffu, corr != 1.f)) {
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < D; c += 32) {
+            float o[32];
+            tmem_ld32(lane_addr + o_col + c, o);
+            tc_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] *= corr;
+            tmem_st32(lane_addr + o_col + c, reinterpret_cast<const uint32_t*>(o));
+          }
+        }
+      }
+      l += lsum2.x + lsum2.y;
+      tc_wait_st();
+      tc_fence_before();
+      mbar_arrive(bar + Bz::P_FULL + 8 * tt);
+    }
+    if (!ok) record_error(8);
+    // epilogue: O / l, LSE (TMEM reads by whole warps; stores only for real rows)
+    const bool have_o = ok && ntiles > 0;
+    if (have_o && !mbar_wait_warp(bar + Bz::O_DONE + 8 * tt, (ntiles - 1) & 1)) record_error(16);
+    tc_fence_after();
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+    T* orow = (T*)p.O + (long long)z * p.sO.b + (long long)h * p.sO.h + (long long)q * p.sO.s;
+#pragma unroll
+    for (int c = 0; c < D; c += 32) {
+      float o[32];
+      if (have_o) {
+        tmem_ld32(lane_addr + o_col + c, o);
+        tc_wait_ld();
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] = 0.f;
+      }
+      if (q < SQ) {
+        uint32_t w[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          if constexpr (BF16) {
+            const __nv_bfloat162 t2 = __floats2bfloat162_rn(o[2 * i] * inv, o[2 * i + 1] * inv);
+            w[i] = *reinterpret_cast<const uint32_t*>(&t2);
+          } else {
+            const __half2 t2 = __floats2half2_rn(o[2 * i] * inv, o[2 * i + 1] * inv);
+            w[i] = *reinterpret_cast<const uint32_t*>(&t2);
+          }
+        }
+        uint4* dst = reinterpret_cast<uint4*>(orow + c);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+      }
+    }
+    if (q < SQ && p.LSE) {
+      const long long li = fa_lse_index(false, z, h, p.NH, p.SQ, 0, p.lse_total_q, q);
+      p.LSE[li] = l > 0.f ? m_ref * FA_LN2 + logf(l) : -INFINITY;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == WARP_MMA) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 // ---------------------------------------------------------------- host side
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -535,9 +896,43 @@ int launch(const FaFwdParams& p, cudaStream_t st, const CUtensorMap& mq, const C
   return fa::cuda_status(cudaGetLastError(), "fwd_sm100 launch");
 }
 
+// The two-tile kernel, when it applies: D = 128, dense, no softcap / alibi / dropout, and the build
+// gave it exactly the 168 registers per thread its register split is computed from (checked once;
+// otherwise every request stays on the single-tile kernel).  Returns -1 when not taken.
+template <bool BF16>
+bool pp_ready() {
+  static int regs = -1;
+  if (regs < 0) {
+    cudaFuncAttributes attr;
+    regs = cudaFuncGetAttributes(&attr, (const void*)fwd_pp_kernel<BF16>) == cudaSuccess ? attr.numRegs : 0;
+  }
+  return regs == PP_REGS;
+}
+
+template <bool BF16>
+int launch_pp(const FaFwdParams& p, cudaStream_t st, const CUtensorMap& mq, const CUtensorMap& mk,
+              const CUtensorMap& mv) {
+  if (!pp_ready<BF16>()) return -1;
+  static unsigned long long done = 0;
+  if (int rc = fa::ensure_smem((const void*)fwd_pp_kernel<BF16>, PpCfg::SMEM, &done)) return rc;
+  dim3 grid((p.SQ + 2 * BM - 1) / (2 * BM), p.NH, p.batch);
+  fwd_pp_kernel<BF16><<<grid, PP_THREADS, PpCfg::SMEM, st>>>(mq, mk, mv, p);
+  fa::count_launch();
+  return fa::cuda_status(cudaGetLastError(), "fwd_sm100 launch");
+}
+
 template <bool BF16, bool FEAT>
 int launch_d(const FaFwdParams& p, cudaStream_t st, const CUtensorMap& mq, const CUtensorMap& mk,
              const CUtensorMap& mv) {
+  // two query tiles per CTA pay off once there are enough rows to fill the GPU with 256-row CTAs;
+  // FABLE_ATTN_FWD_TILES=1 / =2 forces one or two tiles per CTA wherever the two-tile kernel applies
+  const bool eligible = !FEAT && p.HD == 128 && p.cu_q == nullptr && p.block_table == nullptr;
+  bool two = eligible && (long long)((p.SQ + 2 * BM - 1) / (2 * BM)) * p.NH * p.batch >= 2 * 148;
+  if (const char* force = getenv("FABLE_ATTN_FWD_TILES")) two = eligible && force[0] == '2';
+  if (two) {
+    const int rc = launch_pp<BF16>(p, st, mq, mk, mv);
+    if (rc >= 0) return rc;
+  }
   if (p.HD == 64) return launch<64, BF16, FEAT>(p, st, mq, mk, mv);
   return launch<128, BF16, FEAT>(p, st, mq, mk, mv);
 }
@@ -592,6 +987,15 @@ int fwd_sm100(const FaFwdParams& p, int dtype, cudaStream_t st, bool* taken) {
 }
 
 }  // namespace fa
+
+extern "C" FA_API int fa_forward_two_tile_ready(int bf16) {
+  int dev = fa::current_device(), major = 0, minor = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
+    return 0;
+  if (major != 10 || minor != 0) return 0;
+  return (bf16 ? pp_ready<true>() : pp_ready<false>()) ? 1 : 0;
+}
 
 extern "C" FA_API int fa_device_error(int clear) {
   int v = 0;

@@ -295,6 +295,10 @@ FA_API const char* fa_last_error(void);       /* message of the last failing cal
 FA_API int fa_device_error(int clear);
 /* Number of this library's kernels launched since load (all threads, all devices). */
 FA_API unsigned long long fa_kernel_launch_count(void);
+/* 1 when the forward's two-query-tile kernel (dense fp16/bf16, head_dim 128, no softcap / alibi /
+ * dropout) can run on the current device with this build, 0 otherwise (those requests then run on
+ * the one-tile kernel).  Needs a device; makes no launch. */
+FA_API int fa_forward_two_tile_ready(int bf16);
 
 #ifdef __cplusplus
 }

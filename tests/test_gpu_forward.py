@@ -308,3 +308,64 @@ def test_forward_varlen_swa_softcap_gqa8(dt, total_k_known):
         ref_l[:, a:a + lq[i]] = ll[0]
     assert O.rel_rms(to_np(o), ref_o) < TOL[dt]
     assert lse_close(lse.cpu().numpy(), ref_l, TOL[dt])[0]
+
+
+# cases the two-query-tile kernel takes (head_dim 128, no softcap / alibi / dropout), plus row
+# counts that leave the second tile of the last CTA partly or wholly past the sequence end
+TWO_TILE_CASES = [c for c in CASES if c[3] == 128 and c[10] == 0.0 and not c[7]] + [
+    ("d128_sq300_full", 300, 300, 128, 8, 2, False, False, -1, -1, 0.0, 0),
+    ("d128_sq100_causal", 100, 100, 128, 8, 1, True, False, -1, -1, 0.0, 0),
+    ("d128_sq640_sk200_causal", 640, 200, 128, 8, 4, True, False, -1, -1, 0.0, 0),
+    ("d128_sq384_win_100_20", 384, 384, 128, 8, 2, False, False, 100, 20, 0.0, 0),
+]
+
+
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+@pytest.mark.parametrize("case", TWO_TILE_CASES, ids=[c[0] for c in TWO_TILE_CASES])
+def test_forward_two_tile_kernel(case, dt, monkeypatch):
+    """The two-query-tile kernel (forced on small shapes with FABLE_ATTN_FWD_TILES=2) against the
+    oracle: masks, windows, chunks, empty rows, partial and empty second tiles."""
+    assert A.lib().fa_forward_two_tile_ready(int(dt == "bf16")) == 1, "two-tile kernel unavailable"
+    monkeypatch.setenv("FABLE_ATTN_FWD_TILES", "2")
+    name, SQ, SK, D, NH, g, causal, al, wl, wr, sc, ch = case
+    rng = np.random.default_rng(zlib.crc32(name.encode()) + 7)
+    B = 2
+    qn, q = randn(rng, (B, SQ, NH, D), dt)
+    kn, k = randn(rng, (B, SK, NH // g, D), dt)
+    vn, v = randn(rng, (B, SK, NH // g, D), dt)
+    o = torch.full_like(q, float("nan"))
+    lse = torch.full((B, NH, SQ), float("nan"), device="cuda", dtype=torch.float32)
+    run_fwd(fwd_params(q, k, v, o, lse, scale=D ** -0.5, causal=causal, wl=wl, wr=wr, chunk=ch), dt)
+    ro, rl = O.forward(qn, kn, vn, D ** -0.5, causal, wl, wr, 0.0, None, ch)
+    e = O.rel_rms(to_np(o), ro)
+    assert e < TOL[dt], f"O rel_rms {e:.3e}"
+    ok, el = lse_close(lse.cpu().numpy(), rl, TOL[dt])
+    assert ok, f"LSE {el}"
+    if causal and SQ > SK:
+        assert torch.all(o[:, : SQ - SK] == 0)
+
+
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+def test_forward_two_tile_matches_one_tile(dt, monkeypatch):
+    """Both forward kernels on the same dense causal input: equal within the dtype's tolerance, and
+    the two-tile kernel is the default at this size (enough 256-row CTAs to fill the GPU)."""
+    rng = np.random.default_rng(11)
+    B, S, H, D = 1, 4096, 32, 128
+    _, q = randn(rng, (B, S, H, D), dt)
+    _, k = randn(rng, (B, S, H, D), dt)
+    _, v = randn(rng, (B, S, H, D), dt)
+    outs = {}
+    for tiles in ("1", "2", None):
+        if tiles is None:
+            monkeypatch.delenv("FABLE_ATTN_FWD_TILES", raising=False)
+        else:
+            monkeypatch.setenv("FABLE_ATTN_FWD_TILES", tiles)
+        o = torch.empty_like(q)
+        lse = torch.empty((B, H, S), device="cuda", dtype=torch.float32)
+        run_fwd(fwd_params(q, k, v, o, lse, scale=D ** -0.5, causal=True), dt)
+        outs[tiles] = (o.float(), lse.clone())
+    o1, l1 = outs["1"]
+    o2, l2 = outs["2"]
+    assert ((o1 - o2).norm() / o1.norm()).item() < TOL[dt]
+    assert ((l1 - l2).abs().max()).item() < 1e-3
+    assert torch.equal(outs[None][0], o2), "the default at this size is the two-tile kernel"
