@@ -78,6 +78,20 @@ __device__ __forceinline__ void split2(float d0, float d1, uint32_t& hi, uint32_
   lo = pack2<BF16>(d0 - h0, d1 - h1);
 }
 
+// the same split for a pair held as float2: the remainder dS - hi (exact in fp32) by one FFMA2
+template <bool BF16>
+__device__ __forceinline__ void split2p(float2 d, uint32_t& hi, uint32_t& lo) {
+  hi = pack2<BF16>(d.x, d.y);
+  float h0, h1;
+  unpack2<BF16>(hi, h0, h1);
+  const float2 r = __ffma2_rn(make_float2(h0, h1), make_float2(-1.f, -1.f), d);
+  lo = pack2<BF16>(r.x, r.y);
+}
+// dropout multipliers of keys / rows b and b + 1 of a keep word: keep_scale where kept, else 0
+__device__ __forceinline__ float2 keep_mul2(uint32_t w, int b, float ks) {
+  return make_float2(((w >> b) & 1u) ? ks : 0.f, ((w >> (b + 1)) & 1u) ? ks : 0.f);
+}
+
 // K-major / MN-major descriptors of a [rows][D] tile stored as D/64 chunks of rows x 128 B
 // (TMA SWIZZLE_128B boxes).  kstep = 16-element step along the contracted dimension.
 __device__ __forceinline__ uint64_t desc_kmajor(uint32_t tile, int rows, int kstep) {
@@ -257,6 +271,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const uint32_t thresh = fa_drop_thresh(p.dropout_p);
     const bool cap_on = FEAT && p.softcap > 0.f;
     const float cap_in = cap_on ? p.scale / p.softcap : 0.f;
+    // packed path (no softcap, no alibi): x = s * scale*log2e + nl2 with nl2 = -lse2, or -inf for a
+    // row that saw no key (so its P is 0 without a test); key masks only on boundary tiles
+    const bool fast = !cap_on && slope == 0.f;
+    const float sl2 = p.scale * FA_LOG2E;
+    const float nl2 = (rlo <= rhi) ? -lse2 : -INFINITY, nds = -dsum;
+    int lo_last = 1, hi_first = 0;   // key tiles every row of the CTA sees in full
+    {
+      int a, b;
+      fa_key_range(min(qb + BM, SQ) - 1, SQ, SK, p.causal, p.win_left, p.win_right, 0, lo_last, a);
+      fa_key_range(qb, SQ, SK, p.causal, p.win_left, p.win_right, 0, b, hi_first);
+    }
+    const bool full_rows = qb + BM <= SQ;
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
       const int kb = (t0 + j) * BN + 32 * hf;   // first key of this thread's half
@@ -311,11 +337,28 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           tmem_st16(la + C::DP_COL + (j & 1) * 64 + 32 * hf, lo);
         }
       };
-      if constexpr (FEAT) {
+      if (fast) {
+        const int kt = (t0 + j) * BN;
+        const bool interior = full_rows && kt >= lo_last && kt + BN - 1 <= hi_first && kt + BN <= SK;
+        uint32_t hi[16], lo[16];
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) {
+          const float2 x = __ffma2_rn(make_float2(s[c], s[c + 1]), make_float2(sl2, sl2), make_float2(nl2, nl2));
+          float a = ex2(x.x), b = ex2(x.y);
+          if (!interior) {
+            a = (kb + c >= rlo && kb + c <= rhi) ? a : 0.f;
+            b = (kb + c + 1 >= rlo && kb + c + 1 <= rhi) ? b : 0.f;
+          }
+          const float2 dp2 = make_float2(dp[c], dp[c + 1]);
+          const float2 dd = drop ? __ffma2_rn(keep_mul2(dw[0], c, p.keep_scale), dp2, make_float2(nds, nds))
+                                 : __fadd2_rn(dp2, make_float2(nds, nds));
+          split2p<BF16>(__fmul2_rn(make_float2(a, b), dd), hi[c / 2], lo[c / 2]);
+        }
+        tmem_st16(la + C::S_COL + (j & 1) * 64 + 32 * hf, hi);
+        tmem_st16(la + C::DP_COL + (j & 1) * 64 + 32 * hf, lo);
+      } else if constexpr (FEAT) {
         if (cap_on) body(std::true_type{});
         else body(std::false_type{});
-      } else {
-        body(std::false_type{});
       }
       tc_wait_st();
       tc_fence_before();
@@ -511,6 +554,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     int qlo, qhi;
     fa_query_range(key, SQ, SK, p.causal, p.win_left, p.win_right, qlo, qhi);
     if (key >= SK) { qlo = 1; qhi = 0; }
+    // query tiles every key of the CTA sees in full (the ranges grow with the key)
+    int qlo_last, qhi_first, qd0, qd1;
+    fa_query_range(min(kb + BK, SK) - 1, SQ, SK, p.causal, p.win_left, p.win_right, qlo_last, qd0);
+    fa_query_range(kb, SQ, SK, p.causal, p.win_left, p.win_right, qd1, qhi_first);
+    const bool full_keys = kb + BK <= SK;
+    const float sl2 = p.scale * FA_LOG2E;
     bool ok = true;
     for (int i = 0; i < niter; ++i) {
       const int h = kvh * p.gqa + i / nqt, qbase = (qt0 + i % nqt) * BQ;
@@ -537,11 +586,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         float v = 0.f;
         if (q < SQ) {
           const long long li = fa_lse_index(false, z, h, p.Hq, SQ, 0, 0, q);
-          v = (tid < 64) ? p.lse[li] * FA_LOG2E : p.dsum[li];
+          if (tid < 64) {
+            const float l = p.lse[li];
+            v = (l > -INFINITY) ? -l * FA_LOG2E : -INFINITY;
+          } else {
+            v = -p.dsum[li];
+          }
         } else if (tid < 64) {
           v = -INFINITY;
         }
-        stb[(tid < 64 ? 0 : 64) + qi] = v;
+        stb[(tid < 64 ? 0 : 64) + qi] = v;   // [nl2 = -lse2 or -inf | nds = -dsum]
       }
       const bool got = mbar_wait_warp(bar + Bz::SP_FULL + 8 * (i & 1), (i >> 1) & 1);
       if (!bar_and_elem(got)) { ok = false; break; }
@@ -576,8 +630,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
             for (int u = 0; u < 2; ++u) {
               const int cc = h32 + c + u, q = qh + cc;
-              const float l2 = stb[32 * hf + cc];
-              const bool vis = q >= qlo && q <= qhi && l2 > -INFINITY;
+              const float nl2 = stb[32 * hf + cc];
+              const bool vis = q >= qlo && q <= qhi && nl2 > -INFINITY;
               float logit, deriv = 1.f;
               if constexpr (kCap) {
                 const float tn = fa_tanh(s[cc] * cap_in);
@@ -588,10 +642,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               } else {
                 logit = s[cc] * p.scale;
               }
-              const float pr = vis ? ex2(fmaf(logit, FA_LOG2E, -l2)) : 0.f;
+              const float pr = vis ? ex2(fmaf(logit, FA_LOG2E, nl2)) : 0.f;
               const float zm = drop ? (((cw[h32 / 32] >> (c + u)) & 1u) ? p.keep_scale : 0.f) : 1.f;
               pv[u] = zm * pr;
-              dsv[u] = pr * (zm * dp[cc] - stb[64 + 32 * hf + cc]) * deriv;
+              dsv[u] = pr * (zm * dp[cc] + stb[64 + 32 * hf + cc]) * deriv;
             }
             pk[c / 2] = pack2<BF16>(pv[0], pv[1]);
             split2<BF16>(dsv[0], dsv[1], hi[c / 2], lo[c / 2]);
@@ -601,11 +655,38 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           tmem_st16(la + C::DP_COL + (i & 1) * 64 + 32 * hf, lo);
         }
       };
-      if constexpr (FEAT) {
+      if (!cap_on && slope == 0.f) {
+        // packed path: nl2 = -inf for rows that saw no key, query masks only on boundary tiles
+        const bool interior = full_keys && qbase >= qlo_last && qbase + BQ - 1 <= qhi_first && qbase + BQ <= SQ;
+        uint32_t pk[16], hi[16], lo[16];
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) {
+          const float2 nl2 = *reinterpret_cast<const float2*>(stb + 32 * hf + c);
+          const float2 nds = *reinterpret_cast<const float2*>(stb + 64 + 32 * hf + c);
+          const float2 x = __ffma2_rn(make_float2(s[c], s[c + 1]), make_float2(sl2, sl2), nl2);
+          float a = ex2(x.x), b = ex2(x.y);
+          if (!interior) {
+            a = (qh + c >= qlo && qh + c <= qhi) ? a : 0.f;
+            b = (qh + c + 1 >= qlo && qh + c + 1 <= qhi) ? b : 0.f;
+          }
+          const float2 pr = make_float2(a, b), dp2 = make_float2(dp[c], dp[c + 1]);
+          float2 pv = pr, dd;
+          if (drop) {
+            const float2 z2 = keep_mul2(cw[0], c, p.keep_scale);
+            pv = __fmul2_rn(z2, pr);
+            dd = __ffma2_rn(z2, dp2, nds);
+          } else {
+            dd = __fadd2_rn(dp2, nds);
+          }
+          pk[c / 2] = pack2<BF16>(pv.x, pv.y);
+          split2p<BF16>(__fmul2_rn(pr, dd), hi[c / 2], lo[c / 2]);
+        }
+        tmem_st16(la + C::S_COL + (i & 1) * 64 + 32 * hf, pk);
+        tmem_st16(la + C::S_COL + (i & 1) * 64 + 32 * hf + 16, hi);
+        tmem_st16(la + C::DP_COL + (i & 1) * 64 + 32 * hf, lo);
+      } else if constexpr (FEAT) {
         if (cap_on) body(std::true_type{});
         else body(std::false_type{});
-      } else {
-        body(std::false_type{});
       }
       tc_wait_st();
       tc_fence_before();
