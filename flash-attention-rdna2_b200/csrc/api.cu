@@ -131,6 +131,7 @@ extern "C" int fable_attn_backward_launch(const FaBwdParams* pp, int dtype, void
   }
   if (p.cu_q) FA_CHECK_ARG(p.lse_total_q > 0, "backward: varlen needs lse_total_q");
   FA_CHECK_ARG(!(p.dropout_bits && p.cu_q), "backward: dropout_bits is for dense layouts only");
+  FA_CHECK_ARG(!(p.dropout_bits_t && !p.dropout_bits), "backward: dropout_bits_t is the workspace of dropout_bits");
   if (p.B == 0 || p.SQ == 0 || p.SK == 0) return FA_OK;
   bool taken = false;
   const int rc = fa::bwd_sm100(p, dtype, (cudaStream_t)stream, &taken);

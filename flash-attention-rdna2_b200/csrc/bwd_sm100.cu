@@ -544,6 +544,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const uint32_t la = tmem + ((uint32_t)(qd * 32) << 16);
     const bool drop = FEAT && p.dropout;
     const bool use_bits = drop && p.dropout_bits != nullptr;
+    const bool use_bits_t = use_bits && p.dropout_bits_t != nullptr;   // key-major copy, no transpose
     const uint32_t thresh = fa_drop_thresh(p.dropout_p);
     const bool cap_on = FEAT && p.softcap > 0.f;
     const float cap_in = cap_on ? p.scale / p.softcap : 0.f;
@@ -572,7 +573,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         constexpr int hq = 0;
         const int q0 = qbase + 32 * hf;
         cw[hq] = 0u;
-        if (use_bits) {
+        if (use_bits_t) {   // this key's word over the half's 32 rows (q0 is a multiple of 32)
+          if (key < SK && q0 < SQ)
+            cw[hq] = __ldg(p.dropout_bits_t + ((long long)h * ((SQ + 31) / 32) + q0 / 32) * SK + key);
+        } else if (use_bits) {
           if (kw_ok && q0 + lane < SQ) cw[hq] = __ldg(p.dropout_bits + fa_mask_word(h, SQ, SK, q0 + lane, kw));
         } else if (drop && key < SK && q0 < SQ) {
           cw[hq] = fa_keep_word(p.drop_seed, ((uint64_t)h * SQ + q0) * SK + key, (uint64_t)SK, thresh, SQ - q0);
@@ -604,7 +608,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       tmem_ld32(la + C::S_COL + (i & 1) * 64 + 32 * hf, s);
       tmem_ld32(la + C::DP_COL + (i & 1) * 64 + 32 * hf, dp);
       tc_wait_ld();
-      if (use_bits) {   // warp-uniform: every lane takes part in the ballots
+      if (use_bits && !use_bits_t) {   // warp-uniform: every lane takes part in the ballots
         {
           constexpr int hq = 0;
           uint32_t t = 0u;
@@ -811,6 +815,8 @@ int bwd_sm100(const FaBwdParams& p, int dtype, cudaStream_t st, bool* taken) {
   if (!out_ok(p.dQ, p.dqs, p.B) || !out_ok(p.dK, p.dks, p.B) || !out_ok(p.dV, p.dvs, p.B)) return FA_OK;
   *taken = true;
   if (int rc = bwd_dsum(p, dtype, st)) return rc;
+  if (p.dropout && p.dropout_bits && p.dropout_bits_t)
+    if (int rc = dropout_mask_transpose(p.dropout_bits, p.dropout_bits_t, p.Hq, p.SQ, p.SK, st)) return rc;
   const bool feat = p.softcap > 0.f || p.alibi != nullptr || p.dropout;
   if (bf16) return feat ? launch_all<true, true>(p, st, maps) : launch_all<true, false>(p, st, maps);
   return feat ? launch_all<false, true>(p, st, maps) : launch_all<false, false>(p, st, maps);

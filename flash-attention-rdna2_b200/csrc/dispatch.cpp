@@ -206,6 +206,11 @@ std::vector<torch::Tensor> bwd(torch::Tensor dout, torch::Tensor q, torch::Tenso
   if (dropout_p > 0 && !mask_ptr(bits, Hq, SQ, SK))
     bits = make_mask(q, seed, dropout_p, Hq, SQ, SK, causal, win_left, win_right);
   p.dropout_bits = mask_ptr(bits, Hq, SQ, SK);
+  torch::Tensor bits_t;   // key-major copy of the mask for the dK/dV kernel (filled by the backward)
+  if (p.dropout_bits) {
+    bits_t = torch::empty({fa_dropout_mask_words(Hq, SK, SQ)}, q.options().dtype(torch::kInt32));
+    p.dropout_bits_t = reinterpret_cast<unsigned int*>(bits_t.data_ptr<int32_t>());
+  }
   check(fable_attn_backward_launch(&p, dt_of(q), cur_stream(q)), "backward");
   return {dq, dk, dv};
 }

@@ -29,7 +29,50 @@ __global__ void __launch_bounds__(256) dropout_mask_kernel(unsigned long long se
   bits[gid] = fa_keep_word(seed, ((uint64_t)h * SQ + q) * SK + k0, 1, thresh, SK - k0);
 }
 
+// One warp per 32 x 32 block (32 query rows x 32 keys): lane l reads the row-major word of row
+// 32 qw + l, 32 ballots turn rows-of-keys into keys-of-rows, lane b writes the word of key 32 kw + b.
+// Warps run query blocks fastest, so reads and writes are 128-byte lines.  Words the mask kernel
+// skipped (no row can see their keys) transpose to words of the same unseen (row, key) pairs.
+__global__ void __launch_bounds__(256) dropout_mask_t_kernel(const unsigned int* __restrict__ bits,
+                                                             unsigned int* __restrict__ bits_t, int NH, int SQ,
+                                                             int SK) {
+  const int W = (SK + 31) / 32, QW = (SQ + 31) / 32;
+  const long long wid = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (wid >= (long long)NH * W * QW) return;   // whole warps
+  const int qw = (int)(wid % QW);
+  const long long hk = wid / QW;
+  const int kw = (int)(hk % W), h = (int)(hk / W);
+  const int q = qw * 32 + lane;
+  const unsigned int w = q < SQ ? bits[((long long)h * W + kw) * SQ + q] : 0u;
+  unsigned int t = 0u;
+#pragma unroll
+  for (int b = 0; b < 32; ++b) {
+    const unsigned int m = __ballot_sync(0xffffffffu, (w >> b) & 1u);
+    t = (lane == b) ? m : t;
+  }
+  const int k = kw * 32 + lane;
+  if (k < SK) bits_t[((long long)h * QW + qw) * SK + k] = t;
+}
+
 }  // namespace
+
+namespace fa {
+
+int dropout_mask_transpose(const unsigned int* bits, unsigned int* bits_t, int NH, int SQ, int SK, cudaStream_t st) {
+  const long long warps = (long long)NH * ((SK + 31) / 32) * ((SQ + 31) / 32);
+  if (warps == 0) return FA_OK;
+  const long long blocks = (warps + 7) / 8;
+  if (blocks >= (1ll << 31)) {
+    set_error("dropout mask transpose: %lld blocks is too large", blocks);
+    return FA_ERR_SIZE;
+  }
+  dropout_mask_t_kernel<<<(unsigned)blocks, 256, 0, st>>>(bits, bits_t, NH, SQ, SK);
+  count_launch();
+  return cuda_status(cudaGetLastError(), "dropout mask transpose launch");
+}
+
+}  // namespace fa
 
 extern "C" FA_API long long fa_dropout_mask_words(int NH, int SQ, int SK) {
   if (NH <= 0 || SQ <= 0 || SK <= 0) return 0;

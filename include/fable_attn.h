@@ -134,6 +134,11 @@ typedef struct FaBwdParams {
   long long lse_total_q;
   const unsigned int* dropout_bits;    /* optional precomputed keep mask, as in FaFwdParams */
   long long total_k;                   /* varlen: rows of K and V, as in FaFwdParams */
+  /* optional workspace of fa_dropout_mask_words(Hq, SK, SQ) words (dense, with dropout_bits): the
+   * backward writes the key-major copy of dropout_bits there, layout [Hq][ceil(SQ/32)][SK] with bit
+   * r of word (h, qw, k) = keep decision of (query row 32 qw + r, key k), and its dK/dV kernel reads
+   * it instead of transposing the row-major words itself.  NULL: the transpose stays in the kernel. */
+  unsigned int* dropout_bits_t;
 } FaBwdParams;
 
 FA_API int fable_attn_backward_launch(const FaBwdParams* p, int dtype, void* stream);

@@ -40,7 +40,7 @@ class FaBwdParams(C.Structure):
         ("win_left", C.c_int), ("win_right", C.c_int), ("dropout", C.c_int), ("drop_seed", C.c_ulonglong),
         ("dropout_p", C.c_float), ("keep_scale", C.c_float), ("cu_q", C.c_void_p), ("cu_k", C.c_void_p),
         ("seqused_q", C.c_void_p), ("seqused_k", C.c_void_p), ("lse_total_q", C.c_longlong),
-        ("dropout_bits", C.c_void_p), ("total_k", C.c_longlong)]
+        ("dropout_bits", C.c_void_p), ("total_k", C.c_longlong), ("dropout_bits_t", C.c_void_p)]
 
 
 class FaDecParams(C.Structure):

@@ -167,3 +167,24 @@ def test_backward_with_bitmask_equals_inkernel_philox(dt, name):
     torch.cuda.synchronize()
     for nm, a, b in zip(("dQ", "dK", "dV"), first, got):
         assert torch.equal(a, b), nm
+    # with the key-major workspace (pre-filled with all-ones words, so a word the backward failed
+    # to write would show up as kept scores)
+    bits_t = torch.full((A.lib().fa_dropout_mask_words(p.Hq, p.SK, p.SQ),), -1, dtype=torch.int32, device="cuda")
+    p.dropout_bits_t = A.ptr(bits_t)
+    for g in got:
+        g.zero_()
+    A.check(A.lib().fable_attn_backward_launch(C.byref(p), A.DT[dt], stream()))
+    torch.cuda.synchronize()
+    for nm, a, b in zip(("dQ", "dK", "dV"), first, got):
+        assert torch.equal(a, b), nm + " (key-major mask copy)"
+    if dt != "fp32" and p.D == 128:   # the tensor-core backward wrote the copy: check its layout
+        QW = (p.SQ + 31) // 32
+        row = bits.view(p.Hq, (p.SK + 31) // 32, p.SQ).cpu().numpy().view(np.uint32)
+        col = bits_t.view(p.Hq, QW, p.SK).cpu().numpy().view(np.uint32)
+        for h, q, k in [(0, 0, 0), (1, 37, 5), (p.Hq - 1, p.SQ - 1, p.SK - 1), (2, 100, 64)]:
+            diag = q + p.SK - p.SQ
+            hi = min(p.SK - 1, diag) if p.causal else p.SK - 1
+            lo = max(0, diag - p.win_left) if p.win_left >= 0 else 0
+            hi = min(hi, diag + p.win_right) if p.win_right >= 0 else hi
+            if lo <= k <= hi:   # words of keys the row cannot see are never read
+                assert (row[h, k // 32, q] >> (k % 32)) & 1 == (col[h, q // 32, k] >> (q % 32)) & 1
