@@ -87,10 +87,6 @@ __device__ __forceinline__ void split2p(float2 d, uint32_t& hi, uint32_t& lo) {
   const float2 r = __ffma2_rn(make_float2(h0, h1), make_float2(-1.f, -1.f), d);
   lo = pack2<BF16>(r.x, r.y);
 }
-// dropout multipliers of keys / rows b and b + 1 of a keep word: keep_scale where kept, else 0
-__device__ __forceinline__ float2 keep_mul2(uint32_t w, int b, float ks) {
-  return make_float2(((w >> b) & 1u) ? ks : 0.f, ((w >> (b + 1)) & 1u) ? ks : 0.f);
-}
 
 // K-major / MN-major descriptors of a [rows][D] tile stored as D/64 chunks of rows x 128 B
 // (TMA SWIZZLE_128B boxes).  kstep = 16-element step along the contracted dimension.
@@ -337,25 +333,45 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           tmem_st16(la + C::DP_COL + (j & 1) * 64 + 32 * hf, lo);
         }
       };
-      if (fast) {
-        const int kt = (t0 + j) * BN;
-        const bool interior = full_rows && kt >= lo_last && kt + BN - 1 <= hi_first && kt + BN <= SK;
+      // packed body, one straight-line instantiation per (dropout, boundary tile) pair
+      auto fast_body = [&](auto drop_tag, auto mask_tag) {
+        constexpr bool kDrop = decltype(drop_tag)::value, kMask = decltype(mask_tag)::value;
         uint32_t hi[16], lo[16];
 #pragma unroll
         for (int c = 0; c < 32; c += 2) {
           const float2 x = __ffma2_rn(make_float2(s[c], s[c + 1]), make_float2(sl2, sl2), make_float2(nl2, nl2));
           float a = ex2(x.x), b = ex2(x.y);
-          if (!interior) {
+          if constexpr (kMask) {
             a = (kb + c >= rlo && kb + c <= rhi) ? a : 0.f;
             b = (kb + c + 1 >= rlo && kb + c + 1 <= rhi) ? b : 0.f;
           }
           const float2 dp2 = make_float2(dp[c], dp[c + 1]);
-          const float2 dd = drop ? __ffma2_rn(keep_mul2(dw[0], c, p.keep_scale), dp2, make_float2(nds, nds))
-                                 : __fadd2_rn(dp2, make_float2(nds, nds));
-          split2p<BF16>(__fmul2_rn(make_float2(a, b), dd), hi[c / 2], lo[c / 2]);
+          float2 dsv;
+          if constexpr (kDrop) {   // dS = P (Z dP - D) = (Z P) dP - P D, Z P by a sign-extended keep bit
+            const uint32_t m0 = (uint32_t)((int32_t)(dw[0] << (31 - c)) >> 31);
+            const uint32_t m1 = (uint32_t)((int32_t)(dw[0] << (30 - c)) >> 31);
+            const float2 zp = __fmul2_rn(make_float2(__uint_as_float(__float_as_uint(a) & m0),
+                                                     __uint_as_float(__float_as_uint(b) & m1)),
+                                         make_float2(p.keep_scale, p.keep_scale));
+            dsv = __ffma2_rn(make_float2(a, b), make_float2(nds, nds), __fmul2_rn(zp, dp2));
+          } else {
+            dsv = __fmul2_rn(make_float2(a, b), __fadd2_rn(dp2, make_float2(nds, nds)));
+          }
+          split2p<BF16>(dsv, hi[c / 2], lo[c / 2]);
         }
         tmem_st16(la + C::S_COL + (j & 1) * 64 + 32 * hf, hi);
         tmem_st16(la + C::DP_COL + (j & 1) * 64 + 32 * hf, lo);
+      };
+      if (fast) {
+        const int kt = (t0 + j) * BN;
+        const bool interior = full_rows && kt >= lo_last && kt + BN - 1 <= hi_first && kt + BN <= SK;
+        if (drop) {
+          if (interior) fast_body(std::true_type{}, std::false_type{});
+          else fast_body(std::true_type{}, std::true_type{});
+        } else {
+          if (interior) fast_body(std::false_type{}, std::false_type{});
+          else fast_body(std::false_type{}, std::true_type{});
+        }
       } else if constexpr (FEAT) {
         if (cap_on) body(std::true_type{});
         else body(std::false_type{});
@@ -659,9 +675,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           tmem_st16(la + C::DP_COL + (i & 1) * 64 + 32 * hf, lo);
         }
       };
-      if (!cap_on && slope == 0.f) {
-        // packed path: nl2 = -inf for rows that saw no key, query masks only on boundary tiles
-        const bool interior = full_keys && qbase >= qlo_last && qbase + BQ - 1 <= qhi_first && qbase + BQ <= SQ;
+      // packed path: nl2 = -inf for rows that saw no key, query masks only on boundary tiles; one
+      // straight-line instantiation per (dropout, boundary tile) pair
+      auto fast_body = [&](auto drop_tag, auto mask_tag) {
+        constexpr bool kDrop = decltype(drop_tag)::value, kMask = decltype(mask_tag)::value;
         uint32_t pk[16], hi[16], lo[16];
 #pragma unroll
         for (int c = 0; c < 32; c += 2) {
@@ -669,25 +686,37 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           const float2 nds = *reinterpret_cast<const float2*>(stb + 64 + 32 * hf + c);
           const float2 x = __ffma2_rn(make_float2(s[c], s[c + 1]), make_float2(sl2, sl2), nl2);
           float a = ex2(x.x), b = ex2(x.y);
-          if (!interior) {
+          if constexpr (kMask) {
             a = (qh + c >= qlo && qh + c <= qhi) ? a : 0.f;
             b = (qh + c + 1 >= qlo && qh + c + 1 <= qhi) ? b : 0.f;
           }
           const float2 pr = make_float2(a, b), dp2 = make_float2(dp[c], dp[c + 1]);
-          float2 pv = pr, dd;
-          if (drop) {
-            const float2 z2 = keep_mul2(cw[0], c, p.keep_scale);
-            pv = __fmul2_rn(z2, pr);
-            dd = __ffma2_rn(z2, dp2, nds);
+          float2 pv = pr, dsv;
+          if constexpr (kDrop) {   // P~ = Z P by a sign-extended keep bit; dS = P~ dP - P D
+            const uint32_t m0 = (uint32_t)((int32_t)(cw[0] << (31 - c)) >> 31);
+            const uint32_t m1 = (uint32_t)((int32_t)(cw[0] << (30 - c)) >> 31);
+            pv = __fmul2_rn(make_float2(__uint_as_float(__float_as_uint(a) & m0), __uint_as_float(__float_as_uint(b) & m1)),
+                            make_float2(p.keep_scale, p.keep_scale));
+            dsv = __ffma2_rn(pr, nds, __fmul2_rn(pv, dp2));
           } else {
-            dd = __fadd2_rn(dp2, nds);
+            dsv = __fmul2_rn(pr, __fadd2_rn(dp2, nds));
           }
           pk[c / 2] = pack2<BF16>(pv.x, pv.y);
-          split2p<BF16>(__fmul2_rn(pr, dd), hi[c / 2], lo[c / 2]);
+          split2p<BF16>(dsv, hi[c / 2], lo[c / 2]);
         }
         tmem_st16(la + C::S_COL + (i & 1) * 64 + 32 * hf, pk);
         tmem_st16(la + C::S_COL + (i & 1) * 64 + 32 * hf + 16, hi);
         tmem_st16(la + C::DP_COL + (i & 1) * 64 + 32 * hf, lo);
+      };
+      if (!cap_on && slope == 0.f) {
+        const bool interior = full_keys && qbase >= qlo_last && qbase + BQ - 1 <= qhi_first && qbase + BQ <= SQ;
+        if (drop) {
+          if (interior) fast_body(std::true_type{}, std::false_type{});
+          else fast_body(std::true_type{}, std::true_type{});
+        } else {
+          if (interior) fast_body(std::false_type{}, std::false_type{});
+          else fast_body(std::false_type{}, std::true_type{});
+        }
       } else if constexpr (FEAT) {
         if (cap_on) body(std::true_type{});
         else body(std::false_type{});
