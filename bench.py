@@ -297,10 +297,12 @@ def bench_fwd_bwd_causal(dev, steps=5, warmup=3, dropout_p=0.1):
     torch.cuda.synchronize()
     f0, f1 = _events()
     b0, b1 = _events()
-    tf, tb = 0.0, 0.0
+    m1 = torch.cuda.Event(enable_timing=True)
+    tf, tb, tm = 0.0, 0.0, 0.0
     for _ in range(steps):
         f0.record()
         bits = mask()
+        m1.record()
         _, lse = _C.fwd(qh, kh, vh, sc, True, -1, 0, 0.0, None, pd, 777, 0, out, bits)
         f1.record()
         b0.record()
@@ -308,12 +310,17 @@ def bench_fwd_bwd_causal(dev, steps=5, warmup=3, dropout_p=0.1):
         b1.record()
         torch.cuda.synchronize()
         tf += f0.elapsed_time(f1)
+        tm += f0.elapsed_time(m1)
         tb += b0.elapsed_time(b1)
     fwd_flops = 4.0 * D * B * H * S * (S + 1) / 2
-    fms, bms = tf / steps, tb / steps
-    return {"config": f"causal fwd+bwd B2 S4096 H32 D128 fp16 dropout{pd:g}", "fwd_ms": round(fms, 3),
-            "fwd_tflops": round(fwd_flops / fms / 1e9, 1), "bwd_ms": round(bms, 3),
-            "bwd_tflops": round(2.5 * fwd_flops / bms / 1e9, 1)}
+    fms, bms, mms = tf / steps, tb / steps, tm / steps
+    r = {"config": f"causal fwd+bwd B2 S4096 H32 D128 fp16 dropout{pd:g}", "fwd_ms": round(fms, 3),
+         "fwd_tflops": round(fwd_flops / fms / 1e9, 1), "bwd_ms": round(bms, 3),
+         "bwd_tflops": round(2.5 * fwd_flops / bms / 1e9, 1)}
+    if pd > 0:   # the keep mask (one Philox4x32-10 per visible score, as the reference draws it)
+        r["mask_ms"] = round(mms, 3)
+        r["fwd_attention_ms"] = round(fms - mms, 3)
+    return r
 
 
 def bench_decode(dev, steps=20, warmup=5):

@@ -477,7 +477,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 }
 
 // =====================================================================================
-// Two query tiles per CTA ("ping-pong"), dense inputs without softcap / alibi / dropout.
+// Two query tiles per CTA ("ping-pong"), dense inputs without softcap / alibi; dropout only from a
+// precomputed keep mask (DROP).
 //
 // One CTA = rows [qb, qb + 256) of one head: tile A = the first 128 rows, tile B = the next 128.
 // The MMA warp alternates the tiles, so the tensor cores run one tile's S = Q K^T and O += P V
@@ -519,7 +520,7 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return r;
 }
 
-template <bool BF16>
+template <bool BF16, bool DROP>
 __global__ void __launch_bounds__(PP_THREADS, 1)
     fwd_pp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                   const __grid_constant__ CUtensorMap tmV, const FaFwdParams p) {
@@ -707,10 +708,19 @@ __global__ void __launch_bounds__(PP_THREADS, 1)
     }
     const bool full_rows = qt + BM <= SQ;
     const float scale2 = p.scale * FA_LOG2E;
+    const float inv_keep = DROP ? 1.0f / (1.0f - p.dropout_p) : 1.f;
+    const int mask_w = (SK + 31) / 32;
     float m_ref = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
       const int kb = (t0 + j) * BN;
+      // keep bits of this row for the tile (bit b of word i <-> key kb + 32 i + b), loaded ahead of
+      // the wait; the mask layout puts the warp's 32 rows on one line.  Words past the row's visible
+      // keys may be unwritten: they only meet probabilities that are already 0.
+      uint32_t dw[BN / 32];
+#pragma unroll
+      for (int i = 0; i < BN / 32; ++i)
+        dw[i] = (DROP && q < SQ && kb / 32 + i < mask_w) ? __ldg(p.dropout_bits + fa_mask_word(h, SQ, SK, q, kb / 32 + i)) : 0u;
       if (!mbar_wait_warp(bar + Bz::S_FULL + 8 * tt, j & 1)) { ok = false; break; }
       tc_fence_after();
       const uint32_t sa = lane_addr + (uint32_t)(tt * BN);
@@ -754,8 +764,18 @@ __global__ void __launch_bounds__(PP_THREADS, 1)
         for (int i = 0; i < 16; ++i) {
           const float2 x2 = __ffma2_rn(make_float2(s[c0 + 2 * i], s[c0 + 2 * i + 1]), make_float2(scale2, scale2),
                                        make_float2(-muse, -muse));
-          const float a = ex2(x2.x), b = ex2(x2.y);
-          lsum2 = __fadd2_rn(lsum2, make_float2(a, b));
+          float a = ex2(x2.x), b = ex2(x2.y);
+          lsum2 = __fadd2_rn(lsum2, make_float2(a, b));   // the row sum is taken before dropout
+          if constexpr (DROP) {   // keys kb + c0 + 2i, +1: bits 2i, 2i + 1 of word c0 / 32, sign-extended
+            const uint32_t w = dw[c0 / 32];
+            const uint32_t m0 = (uint32_t)((int32_t)(w << (31 - 2 * i)) >> 31);
+            const uint32_t m1 = (uint32_t)((int32_t)(w << (30 - 2 * i)) >> 31);
+            const float2 z = __fmul2_rn(make_float2(__uint_as_float(__float_as_uint(a) & m0),
+                                                    __uint_as_float(__float_as_uint(b) & m1)),
+                                        make_float2(inv_keep, inv_keep));
+            a = z.x;
+            b = z.y;
+          }
           if constexpr (BF16) {
             const __nv_bfloat162 t2 = __floats2bfloat162_rn(a, b);
             pk[i] = *reinterpret_cast<const uint32_t*>(&t2);
@@ -899,24 +919,24 @@ int launch(const FaFwdParams& p, cudaStream_t st, const CUtensorMap& mq, const C
 // The two-tile kernel, when it applies: D = 128, dense, no softcap / alibi / dropout, and the build
 // gave it exactly the 168 registers per thread its register split is computed from (checked once;
 // otherwise every request stays on the single-tile kernel).  Returns -1 when not taken.
-template <bool BF16>
+template <bool BF16, bool DROP>
 bool pp_ready() {
   static int regs = -1;
   if (regs < 0) {
     cudaFuncAttributes attr;
-    regs = cudaFuncGetAttributes(&attr, (const void*)fwd_pp_kernel<BF16>) == cudaSuccess ? attr.numRegs : 0;
+    regs = cudaFuncGetAttributes(&attr, (const void*)fwd_pp_kernel<BF16, DROP>) == cudaSuccess ? attr.numRegs : 0;
   }
   return regs == PP_REGS;
 }
 
-template <bool BF16>
+template <bool BF16, bool DROP>
 int launch_pp(const FaFwdParams& p, cudaStream_t st, const CUtensorMap& mq, const CUtensorMap& mk,
               const CUtensorMap& mv) {
-  if (!pp_ready<BF16>()) return -1;
+  if (!pp_ready<BF16, DROP>()) return -1;
   static unsigned long long done = 0;
-  if (int rc = fa::ensure_smem((const void*)fwd_pp_kernel<BF16>, PpCfg::SMEM, &done)) return rc;
+  if (int rc = fa::ensure_smem((const void*)fwd_pp_kernel<BF16, DROP>, PpCfg::SMEM, &done)) return rc;
   dim3 grid((p.SQ + 2 * BM - 1) / (2 * BM), p.NH, p.batch);
-  fwd_pp_kernel<BF16><<<grid, PP_THREADS, PpCfg::SMEM, st>>>(mq, mk, mv, p);
+  fwd_pp_kernel<BF16, DROP><<<grid, PP_THREADS, PpCfg::SMEM, st>>>(mq, mk, mv, p);
   fa::count_launch();
   return fa::cuda_status(cudaGetLastError(), "fwd_sm100 launch");
 }
@@ -926,11 +946,14 @@ int launch_d(const FaFwdParams& p, cudaStream_t st, const CUtensorMap& mq, const
              const CUtensorMap& mv) {
   // two query tiles per CTA pay off once there are enough rows to fill the GPU with 256-row CTAs;
   // FABLE_ATTN_FWD_TILES=1 / =2 forces one or two tiles per CTA wherever the two-tile kernel applies
-  const bool eligible = !FEAT && p.HD == 128 && p.cu_q == nullptr && p.block_table == nullptr;
+  // (dropout qualifies when its keep mask is precomputed; softcap and alibi do not)
+  const bool drop = p.dropout_p > 0.f;
+  const bool eligible = p.HD == 128 && p.cu_q == nullptr && p.block_table == nullptr && p.softcap <= 0.f &&
+                        p.alibi_slopes == nullptr && (!drop || p.dropout_bits != nullptr);
   bool two = eligible && (long long)((p.SQ + 2 * BM - 1) / (2 * BM)) * p.NH * p.batch >= 2 * 148;
   if (const char* force = getenv("FABLE_ATTN_FWD_TILES")) two = eligible && force[0] == '2';
   if (two) {
-    const int rc = launch_pp<BF16>(p, st, mq, mk, mv);
+    const int rc = drop ? launch_pp<BF16, true>(p, st, mq, mk, mv) : launch_pp<BF16, false>(p, st, mq, mk, mv);
     if (rc >= 0) return rc;
   }
   if (p.HD == 64) return launch<64, BF16, FEAT>(p, st, mq, mk, mv);
@@ -994,7 +1017,8 @@ extern "C" FA_API int fa_forward_two_tile_ready(int bf16) {
       cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
     return 0;
   if (major != 10 || minor != 0) return 0;
-  return (bf16 ? pp_ready<true>() : pp_ready<false>()) ? 1 : 0;
+  return (bf16 ? (pp_ready<true, false>() && pp_ready<true, true>())
+               : (pp_ready<false, false>() && pp_ready<false, true>())) ? 1 : 0;
 }
 
 extern "C" FA_API int fa_device_error(int clear) {

@@ -369,3 +369,32 @@ def test_forward_two_tile_matches_one_tile(dt, monkeypatch):
     assert ((o1 - o2).norm() / o1.norm()).item() < TOL[dt]
     assert ((l1 - l2).abs().max()).item() < 1e-3
     assert torch.equal(outs[None][0], o2), "the default at this size is the two-tile kernel"
+
+
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+@pytest.mark.parametrize("causal,wl,wr,SQ", [(True, -1, -1, 300), (False, -1, -1, 256), (False, 70, 10, 384)])
+def test_forward_two_tile_dropout_bits(dt, causal, wl, wr, SQ, monkeypatch):
+    """The two-query-tile kernel with a precomputed keep mask against the oracle's dropout forward,
+    and bitwise equal to itself run twice."""
+    import ctypes as C
+    monkeypatch.setenv("FABLE_ATTN_FWD_TILES", "2")
+    rng = np.random.default_rng(SQ + 5)
+    B, NH, D, seed, pd = 2, 4, 128, 9090, 0.2
+    qn, q = randn(rng, (B, SQ, NH, D), dt)
+    kn, k = randn(rng, (B, SQ, NH, D), dt)
+    vn, v = randn(rng, (B, SQ, NH, D), dt)
+    bits = torch.zeros(A.lib().fa_dropout_mask_words(NH, SQ, SQ), dtype=torch.int32, device="cuda")
+    A.check(A.lib().fa_dropout_mask_launch(seed, pd, NH, SQ, SQ, int(causal), wl, wr, A.ptr(bits),
+                                           C.c_void_p(torch.cuda.current_stream().cuda_stream)))
+    outs = []
+    for _ in range(2):
+        o = torch.empty_like(q)
+        lse = torch.empty((B, NH, SQ), device="cuda", dtype=torch.float32)
+        p = fwd_params(q, k, v, o, lse, scale=D ** -0.5, causal=causal, wl=wl, wr=wr, dropout_p=pd, seed=seed)
+        p.dropout_bits = A.ptr(bits)
+        run_fwd(p, dt)
+        outs.append((o, lse))
+    ro, rl = O.forward(qn, kn, vn, D ** -0.5, causal, wl, wr, dropout_p=pd, seed=seed)
+    assert O.rel_rms(to_np(outs[0][0]), ro) < TOL[dt]
+    assert lse_close(outs[0][1].cpu().numpy(), rl, TOL[dt])[0]
+    assert torch.equal(outs[0][0], outs[1][0])
