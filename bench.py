@@ -399,8 +399,9 @@ def bench_decode_split(dev, ws, rank, steps=20, warmup=5):
 def bench_varlen_swa(dev, steps=10, warmup=3):
     """Config 5: 16 packed sequences, lengths ~ U[256, 8192] (seeded), cu_seqlens_q = cu_seqlens_k,
     Hq 64, Hk 8, D 128 bf16, causal window (512, 0), softcap 30, NeoX rotary rd 64 (base 10000,
-    positions restart per sequence) on q and k.  Reports the attention kernel alone and the
-    public path (rotary as torch ops, then flash_attn_varlen_func)."""
+    positions restart per sequence) on q and k.  Reports the attention kernel alone, the public
+    path as the reference runs it (apply_rotary_emb on q and k, then flash_attn_varlen_func), and
+    the same call with rotary_cos / rotary_sin (q rotated inside the forward kernel)."""
     import fable_attn as fa
     from fable_attn import _C
     from fable_attn.layers.rotary import apply_rotary_emb
@@ -428,9 +429,13 @@ def bench_varlen_swa(dev, steps=10, warmup=3):
         fa.flash_attn_varlen_func(qr, kr, v, cu, cu, mx, mx, softmax_scale=sc, causal=True, window_size=(512, 0),
                                   softcap=30.0)
 
+    def fused():
+        fa.flash_attn_varlen_func(q, k, v, cu, cu, mx, mx, softmax_scale=sc, causal=True, window_size=(512, 0),
+                                  softcap=30.0, rotary_cos=cos, rotary_sin=sin)
+
     out = {"config": "varlen SWA prefill 16 seqs U[256,8192] Hq64 Hk8 D128 bf16 window(512,0) softcap30 rotary64",
            "tokens": tot, "flops": flops}
-    for name, fn in (("kernel", kernel), ("with_rotary", public)):
+    for name, fn in (("kernel", kernel), ("with_rotary", public), ("fused_rotary", fused)):
         for _ in range(warmup):
             fn()
         torch.cuda.synchronize()

@@ -104,12 +104,23 @@ extern "C" int fa_forward_launch(const FaFwdParams* pp, int dtype, void* stream)
     FA_CHECK_ARG(p.page > 0 && p.max_blocks > 0 && p.num_blocks > 0, "forward: paged K/V needs page=%d > 0, "
                  "max_blocks=%d > 0, num_blocks=%lld > 0", p.page, p.max_blocks, p.num_blocks);
   }
+  if (p.rot_cos) {
+    FA_CHECK_ARG(p.rot_sin != nullptr && p.rot_dim > 0 && p.rot_dim % 2 == 0 && p.rot_dim <= p.HD &&
+                     p.rot_seqlen_ro > 0,
+                 "forward: rotary needs rot_sin, an even rot_dim=%d in (0, head_dim], rot_seqlen_ro=%d > 0",
+                 p.rot_dim, p.rot_seqlen_ro);
+  }
   if (p.batch == 0 || p.SQ == 0) return FA_OK;
   cudaStream_t st = (cudaStream_t)stream;
   bool taken = false;
   if (dtype != FA_DTYPE_F32) {
     const int rc = fa::fwd_sm100(p, dtype, st, &taken);
     if (taken || rc) return rc;
+  }
+  if (p.rot_cos) {
+    set_error("forward: in-kernel rotary needs the tensor-core path (fp16/bf16, head_dim 64 or 128, 16-byte "
+              "aligned rows); rotate q with fa_rotary_launch instead");
+    return FA_ERR_UNSUPPORTED;
   }
   return fa::fwd_simt(p, dtype, st);
 }

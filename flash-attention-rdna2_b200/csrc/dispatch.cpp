@@ -85,14 +85,70 @@ const unsigned int* mask_ptr(const c10::optional<torch::Tensor>& m, int NH, int 
 }
 
 // ------------------------------------------------------------------ forward (dense)
+// In-kernel rotary of q (fa_forward_launch rotates each Q tile as it lands) and a one-pass rotary
+// of k into a new tensor (k is read by many CTAs, so it is rotated once).  rows of k: dense
+// (B, Hk, SK, D) view -> B*SK rows at positions 0..SK-1 per batch entry; varlen (total, Hk, D) with
+// cu_k -> positions restart per sequence.  Returns the rotated k; fills p's rot_* fields.
+struct RotaryArgs {
+  torch::Tensor cos, sin;
+  bool interleaved = false;
+  bool on() const { return cos.defined(); }
+};
+RotaryArgs rotary_args(const c10::optional<torch::Tensor>& cos, const c10::optional<torch::Tensor>& sin,
+                       bool interleaved, int D) {
+  RotaryArgs r;
+  const bool has_c = cos.has_value() && cos->defined(), has_s = sin.has_value() && sin->defined();
+  TORCH_CHECK_VALUE(has_c == has_s, "fable_attn: rotary_cos and rotary_sin go together");
+  if (!has_c) return r;
+  r.cos = cos->to(torch::kFloat32).contiguous();
+  r.sin = sin->to(torch::kFloat32).contiguous();
+  TORCH_CHECK_VALUE(r.cos.dim() == 2 && r.sin.sizes() == r.cos.sizes() && 2 * r.cos.size(1) <= D,
+                    "fable_attn: rotary_cos / rotary_sin must be (seqlen_ro, rotary_dim / 2) with rotary_dim <= head_dim");
+  r.interleaved = interleaved;
+  return r;
+}
+torch::Tensor rotate_k_rows(const torch::Tensor& k, const RotaryArgs& r, const int* cu_k, int batch, bool varlen) {
+  torch::Tensor src = k;
+  // dense rows (b, s) must form one strided dimension: batch stride = SK * row stride
+  if (!varlen && k.size(0) > 1 && k.stride(0) != k.size(2) * k.stride(2)) src = k.contiguous();
+  auto out = torch::empty_like(src);
+  FaRotaryParams rp{};
+  rp.struct_size = sizeof(FaRotaryParams);
+  rp.x = src.data_ptr(); rp.out = out.data_ptr();
+  if (varlen) {
+    rp.rows = src.size(0); rp.heads = (int)src.size(1); rp.dim = (int)src.size(2);
+    rp.x_row_stride = src.stride(0); rp.x_head_stride = src.stride(1);
+    rp.out_row_stride = out.stride(0); rp.out_head_stride = out.stride(1);
+    rp.cu_seqlens = cu_k; rp.batch = batch;
+  } else {   // (B, Hk, SK, D) view
+    rp.rows = src.size(0) * src.size(2); rp.heads = (int)src.size(1); rp.dim = (int)src.size(3);
+    rp.x_row_stride = src.stride(2); rp.x_head_stride = src.stride(1);
+    rp.out_row_stride = out.stride(2); rp.out_head_stride = out.stride(1);
+    rp.seqlen = (int)src.size(2); rp.batch = (int)src.size(0);
+  }
+  rp.rotary_dim = (int)r.cos.size(1) * 2;
+  rp.cos = r.cos.data_ptr<float>(); rp.sin = r.sin.data_ptr<float>(); rp.seqlen_ro = (int)r.cos.size(0);
+  rp.interleaved = r.interleaved ? 1 : 0;
+  check(fa_rotary_launch(&rp, dt_of(src), cur_stream(src)), "rotary (k)");
+  return out;
+}
+void set_q_rotary(FaFwdParams& p, const RotaryArgs& r) {
+  p.rot_cos = r.cos.data_ptr<float>(); p.rot_sin = r.sin.data_ptr<float>();
+  p.rot_dim = (int)r.cos.size(1) * 2; p.rot_seqlen_ro = (int)r.cos.size(0);
+  p.rot_interleaved = r.interleaved ? 1 : 0;
+}
+
 std::vector<torch::Tensor> fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, double scale, bool causal,
                                int64_t win_left, int64_t win_right, double softcap,
                                c10::optional<torch::Tensor> alibi, double dropout_p, int64_t seed,
                                int64_t attn_chunk, c10::optional<torch::Tensor> out_opt,
-                               c10::optional<torch::Tensor> dropout_bits) {
+                               c10::optional<torch::Tensor> dropout_bits, c10::optional<torch::Tensor> rotary_cos,
+                               c10::optional<torch::Tensor> rotary_sin, bool rotary_interleaved) {
   need_cuda_lastdim(q, "q"); need_cuda_lastdim(k, "k"); need_cuda_lastdim(v, "v");
   TORCH_CHECK_VALUE(q.dim() == 4 && k.dim() == 4 && v.dim() == 4, "fable_attn: fwd expects [B,H,S,D]");
   const c10::cuda::CUDAGuard guard(q.device());
+  const RotaryArgs rot = rotary_args(rotary_cos, rotary_sin, rotary_interleaved, (int)q.size(3));
+  if (rot.on()) k = rotate_k_rows(k, rot, nullptr, 0, false);
   const int B = q.size(0), Hq = q.size(1), SQ = q.size(2), D = q.size(3), Hk = k.size(1), SK = k.size(2);
   TORCH_CHECK_VALUE(Hq % Hk == 0, "fable_attn: Hq must be a multiple of Hk (GQA)");
   TORCH_CHECK_VALUE(k.scalar_type() == q.scalar_type() && v.scalar_type() == q.scalar_type(), "fable_attn: q/k/v dtypes differ");
@@ -115,6 +171,7 @@ std::vector<torch::Tensor> fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v
   if (dropout_p > 0 && !mask_ptr(bits, Hq, SQ, SK))
     bits = make_mask(q, seed, dropout_p, Hq, SQ, SK, causal, win_left, win_right);
   p.dropout_bits = mask_ptr(bits, Hq, SQ, SK);
+  if (rot.on()) set_q_rotary(p, rot);
   check(fa_forward_launch(&p, dt_of(q), cur_stream(q)), "forward");
   return {out, lse};
 }
@@ -125,7 +182,8 @@ py::object fwd_varlen(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::
                       int64_t win_right, double softcap, c10::optional<torch::Tensor> alibi, double dropout_p,
                       int64_t seed, int64_t attn_chunk, c10::optional<torch::Tensor> seqused_q,
                       c10::optional<torch::Tensor> seqused_k, bool return_lse,
-                      c10::optional<torch::Tensor> block_table) {
+                      c10::optional<torch::Tensor> block_table, c10::optional<torch::Tensor> rotary_cos,
+                      c10::optional<torch::Tensor> rotary_sin, bool rotary_interleaved) {
   need_cuda_lastdim(q, "q"); need_cuda_lastdim(k, "k"); need_cuda_lastdim(v, "v");
   const bool paged = block_table.has_value() && block_table->defined();
   if (paged) {
@@ -136,6 +194,9 @@ py::object fwd_varlen(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::
     TORCH_CHECK_VALUE(q.dim() == 3 && k.dim() == 3 && v.dim() == 3, "fable_attn: varlen expects (total, H, D)");
   }
   const c10::cuda::CUDAGuard guard(q.device());
+  const RotaryArgs rot = rotary_args(rotary_cos, rotary_sin, rotary_interleaved, (int)q.size(2));
+  TORCH_CHECK_VALUE(!(rot.on() && paged), "fable_attn: in-kernel rotary takes packed k/v, not a paged cache");
+  if (rot.on()) k = rotate_k_rows(k, rot, opt_i32(cu_k), (int)cu_k.numel() - 1, true);
   const int Hq = q.size(1), D = q.size(2), Hk = paged ? k.size(2) : k.size(1);
   TORCH_CHECK_VALUE(Hq % Hk == 0, "fable_attn: Hq must be a multiple of Hk (GQA)");
   const int batch = (int)cu_q.numel() - 1;
@@ -166,6 +227,7 @@ py::object fwd_varlen(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::
     p.max_blocks = (int)bt.size(1);
     p.num_blocks = k.size(0);
   }
+  if (rot.on()) set_q_rotary(p, rot);
   check(fa_forward_launch(&p, dt_of(q), cur_stream(q)), "forward (varlen)");
   if (return_lse) return py::make_tuple(out, lse);
   return py::cast(out);
@@ -370,7 +432,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fwd", &fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("scale"), py::arg("causal"),
         py::arg("win_left"), py::arg("win_right"), py::arg("softcap"), py::arg("alibi"), py::arg("dropout_p"),
         py::arg("seed"), py::arg("attn_chunk") = 0, py::arg("out") = c10::optional<torch::Tensor>(),
-        py::arg("dropout_bits") = c10::optional<torch::Tensor>());
+        py::arg("dropout_bits") = c10::optional<torch::Tensor>(), py::arg("rotary_cos") = c10::optional<torch::Tensor>(),
+        py::arg("rotary_sin") = c10::optional<torch::Tensor>(), py::arg("rotary_interleaved") = false);
   m.def("bwd", &bwd, py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"), py::arg("out"), py::arg("lse"),
         py::arg("scale"), py::arg("causal"), py::arg("win_left"), py::arg("win_right"), py::arg("softcap"),
         py::arg("alibi"), py::arg("dropout_p"), py::arg("seed"), py::arg("dropout_bits") = c10::optional<torch::Tensor>());
@@ -383,7 +446,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("win_right"), py::arg("softcap"), py::arg("alibi"), py::arg("dropout_p"), py::arg("seed"),
         py::arg("attn_chunk") = 0, py::arg("seqused_q") = c10::optional<torch::Tensor>(),
         py::arg("seqused_k") = c10::optional<torch::Tensor>(), py::arg("return_lse") = false,
-        py::arg("block_table") = c10::optional<torch::Tensor>());
+        py::arg("block_table") = c10::optional<torch::Tensor>(), py::arg("rotary_cos") = c10::optional<torch::Tensor>(),
+        py::arg("rotary_sin") = c10::optional<torch::Tensor>(), py::arg("rotary_interleaved") = false);
   m.def("bwd_varlen", &bwd_varlen, py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"), py::arg("out"),
         py::arg("lse"), py::arg("cu_q"), py::arg("cu_k"), py::arg("max_sq"), py::arg("max_sk"), py::arg("scale"),
         py::arg("causal"), py::arg("win_left"), py::arg("win_right"), py::arg("softcap"), py::arg("alibi"),

@@ -70,7 +70,8 @@ struct Cfg {
 
 struct Bars {   // mbarrier offsets inside the barrier block (8 bytes each; rings of up to 4)
   static constexpr int Q_FULL = 0, K_FULL = 8, K_EMPTY = 40, V_FULL = 72, V_EMPTY = 104, S_FULL = 136,
-                       P_FULL = 152, O_DONE = 168, MMA_DRAIN = 176, TMEM_ADDR = 184;
+                       P_FULL = 152, O_DONE = 168, MMA_DRAIN = 176, TMEM_ADDR = 184,
+                       Q_ROT = 192;   // Q rotated in shared memory (rotary requests only)
 };
 
 __device__ __forceinline__ void record_error(int code) { atomicOr(&g_fwd_error, code); }
@@ -121,6 +122,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   // ---- set-up: barriers (thread 0), TMEM (MMA warp)
   if (tid == 0) {
     mbar_init(bar + Bars::Q_FULL, 1);
+    mbar_init(bar + Bars::Q_ROT, NSOFT);
     for (int s = 0; s < C::NSK; ++s) {
       mbar_init(bar + Bars::K_FULL + 8 * s, 1);
       mbar_init(bar + Bars::K_EMPTY + 8 * s, 1);
@@ -212,7 +214,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     // ======================= MMA issuer (whole warp follows; lane 0 issues)
     constexpr uint32_t IDESC_S = idesc_f16(BF16 ? 1 : 0, BM, BN, 0, 0);
     constexpr uint32_t IDESC_O = idesc_f16(BF16 ? 1 : 0, BM, D, 0, 1);
-    bool ok = ntiles == 0 || mbar_wait_warp(bar + Bars::Q_FULL, 0);
+    const bool rot = p.rot_cos != nullptr;   // then the softmax warps rotate Q before the first MMA
+    bool ok = ntiles == 0 || mbar_wait_warp(bar + (rot ? Bars::Q_ROT : Bars::Q_FULL), 0);
     if (!ok) record_error(2);
     auto issue_pv = [&](int i) -> bool {
       const int s = i % C::NSV;
@@ -283,6 +286,105 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int qd = warp & 3, hf = warp >> 2;
     const int r = qd * 32 + lane, q = qb + r;
     const uint32_t pair_bar = 1 + qd;
+    if (p.rot_cos != nullptr && ntiles > 0) {
+      // rotary embedding of the Q tile in shared memory (before any MMA reads it): thread pair
+      // (2 rr, 2 rr + 1) takes row rr, alternate rotary pairs; the roundings are the reference's
+      // (cos / sin cast to the dtype, each product and the sum rounded, no fused multiply-add).
+      // Element d of row rr sits in 64-column chunk d / 64 at 16-byte unit (d % 64) / 8 XOR rr % 8
+      // (the TMA 128-byte swizzle).
+      using RT = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+      auto rnd = [](float x) { return Elem<RT>::to_f(Elem<RT>::from_f(x)); };
+      auto qel = [&](int rr, int d) -> RT* {
+        const int e = d & 63;
+        return reinterpret_cast<RT*>(sgen + C::OFF_Q + (d >> 6) * (BM * 128) + rr * 128 + (((e >> 3) ^ (rr & 7)) << 4) +
+                                     ((e & 7) << 1));
+      };
+      // 16-byte unit of row rr holding elements d .. d + 7 (d a multiple of 8)
+      auto qunit = [&](int rr, int d) -> uint4* {
+        const int e = d & 63;
+        return reinterpret_cast<uint4*>(sgen + C::OFF_Q + (d >> 6) * (BM * 128) + rr * 128 + (((e >> 3) ^ (rr & 7)) << 4));
+      };
+      auto rot1 = [&](float a, float b, float c, float sn, float& o1, float& o2) {
+        c = rnd(c);
+        sn = rnd(sn);
+        o1 = Elem<RT>::to_f(Elem<RT>::from_f(__fsub_rn(rnd(__fmul_rn(a, c)), rnd(__fmul_rn(b, sn)))));
+        o2 = Elem<RT>::to_f(Elem<RT>::from_f(__fadd_rn(rnd(__fmul_rn(b, c)), rnd(__fmul_rn(a, sn)))));
+      };
+      const int rr = tid >> 1, pos = qb + rr, half = p.rot_dim / 2;
+      // cos / sin of this thread's pairs are loaded before the wait for Q: thread (2 rr + t) owns the
+      // contiguous pairs [t * half/2, (t + 1) * half/2) of row rr, whole 16-byte units when
+      // half/2 is a multiple of 8 (rot_dim 32, 64, 96, 128)
+      const int per = half / 2, j0 = (tid & 1) * per;
+      const bool vec = per % 8 == 0 && per <= 32 && ((uintptr_t)p.rot_cos | (uintptr_t)p.rot_sin) % 16 == 0;
+      const bool row_ok = pos < SQ && pos < p.rot_seqlen_ro;
+      float4 c4[8], s4[8];
+#pragma unroll
+      for (int g = 0; g < 8; ++g) {
+        c4[g] = s4[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (vec && row_ok && 4 * g < per) {
+          c4[g] = __ldg(reinterpret_cast<const float4*>(p.rot_cos + (long long)pos * half + j0) + g);
+          s4[g] = __ldg(reinterpret_cast<const float4*>(p.rot_sin + (long long)pos * half + j0) + g);
+        }
+      }
+      const bool got = mbar_wait(bar + Bars::Q_FULL, 0);
+      if (got && pos < SQ && pos >= p.rot_seqlen_ro) record_error(4096);
+      if (got && row_ok && vec) {
+        const float* cf = reinterpret_cast<const float*>(c4);
+        const float* sf = reinterpret_cast<const float*>(s4);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (8 * u >= per) break;
+          if (!p.rot_interleaved) {   // pairs (j, j + half): one unit of each side
+            uint4* pa = qunit(rr, j0 + 8 * u);
+            uint4* pb = qunit(rr, j0 + half + 8 * u);
+            uint4 ua = *pa, ub = *pb;
+            RT* xa = reinterpret_cast<RT*>(&ua);
+            RT* xb = reinterpret_cast<RT*>(&ub);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              float o1, o2;
+              rot1(Elem<RT>::to_f(xa[e]), Elem<RT>::to_f(xb[e]), cf[8 * u + e], sf[8 * u + e], o1, o2);
+              xa[e] = Elem<RT>::from_f(o1);
+              xb[e] = Elem<RT>::from_f(o2);
+            }
+            *pa = ua;
+            *pb = ub;
+          } else {   // pairs (2j, 2j + 1): 8 pairs = two units
+            uint4* pa = qunit(rr, 2 * (j0 + 8 * u));
+            uint4* pb = qunit(rr, 2 * (j0 + 8 * u) + 8);
+            uint4 ua = *pa, ub = *pb;
+            RT* x = reinterpret_cast<RT*>(&ua);
+            RT* y = reinterpret_cast<RT*>(&ub);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              RT* w = e < 4 ? x : y;
+              const int o = 2 * (e & 3);
+              float o1, o2;
+              rot1(Elem<RT>::to_f(w[o]), Elem<RT>::to_f(w[o + 1]), cf[8 * u + e], sf[8 * u + e], o1, o2);
+              w[o] = Elem<RT>::from_f(o1);
+              w[o + 1] = Elem<RT>::from_f(o2);
+            }
+            *pa = ua;
+            *pb = ub;
+          }
+        }
+      } else if (got && row_ok) {
+        {
+          for (int j = tid & 1; j < half; j += 2) {
+            const int d1 = p.rot_interleaved ? 2 * j : j, d2 = p.rot_interleaved ? 2 * j + 1 : j + half;
+            RT* x1 = qel(rr, d1);
+            RT* x2 = qel(rr, d2);
+            const float a = Elem<RT>::to_f(*x1), b = Elem<RT>::to_f(*x2);
+            const float c = rnd(p.rot_cos[(long long)pos * half + j]), sn = rnd(p.rot_sin[(long long)pos * half + j]);
+            *x1 = Elem<RT>::from_f(__fsub_rn(rnd(__fmul_rn(a, c)), rnd(__fmul_rn(b, sn))));
+            *x2 = Elem<RT>::from_f(__fadd_rn(rnd(__fmul_rn(b, c)), rnd(__fmul_rn(a, sn))));
+          }
+        }
+      }
+      if (!got) record_error(8);
+      fence_proxy_async_smem();   // generic-proxy stores, read next by the tensor core
+      mbar_arrive(bar + Bars::Q_ROT);
+    }
     const uint32_t lane_addr = tmem + ((uint32_t)(qd * 32) << 16);
     int rlo, rhi;
     fa_key_range(q, SQ, SK, p.causal, p.win_left, p.win_right, p.attn_chunk, rlo, rhi);
@@ -949,7 +1051,7 @@ int launch_d(const FaFwdParams& p, cudaStream_t st, const CUtensorMap& mq, const
   // (dropout qualifies when its keep mask is precomputed; softcap and alibi do not)
   const bool drop = p.dropout_p > 0.f;
   const bool eligible = p.HD == 128 && p.cu_q == nullptr && p.block_table == nullptr && p.softcap <= 0.f &&
-                        p.alibi_slopes == nullptr && (!drop || p.dropout_bits != nullptr);
+                        p.alibi_slopes == nullptr && (!drop || p.dropout_bits != nullptr) && p.rot_cos == nullptr;
   bool two = eligible && (long long)((p.SQ + 2 * BM - 1) / (2 * BM)) * p.NH * p.batch >= 2 * 148;
   if (const char* force = getenv("FABLE_ATTN_FWD_TILES")) two = eligible && force[0] == '2';
   if (two) {

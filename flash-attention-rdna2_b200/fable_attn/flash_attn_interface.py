@@ -116,6 +116,27 @@ def _lastdim_contig(t):
     return t if t.stride(-1) == 1 else t.contiguous()
 
 
+def _rotary_plan(q, k, v, rotary_cos, rotary_sin, rotary_interleaved, return_attn_probs, qv, cu_q=None, cu_k=None,
+                 paged=False):
+    """Rotary embedding of q and k requested with the attention call (keyword-only extension;
+    equivalent to layers.rotary.apply_rotary_emb on q and k first, positions restarting per
+    sequence).  Inference calls on fp16/bf16 with head_dim 64 or 128 rotate q inside the forward
+    kernel and k in one pass (returns the cos/sin/interleaved triple to hand to _C); anything else
+    rotates both here, differentiably, and returns (q, k, None)."""
+    if rotary_cos is None and rotary_sin is None:
+        return q, k, None
+    if (rotary_cos is None) != (rotary_sin is None):
+        raise ValueError("fable_attn: rotary_cos and rotary_sin go together")
+    grad = torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad)
+    if (not grad and not return_attn_probs and qv is None and not paged and q.is_cuda
+            and q.dtype in (torch.float16, torch.bfloat16) and q.shape[-1] in (64, 128)):
+        return q, k, (rotary_cos, rotary_sin, bool(rotary_interleaved))
+    from .layers.rotary import apply_rotary_emb
+    q = apply_rotary_emb(q, rotary_cos, rotary_sin, rotary_interleaved, cu_seqlens=cu_q)
+    k = apply_rotary_emb(k, rotary_cos, rotary_sin, rotary_interleaved, cu_seqlens=cu_k)
+    return q, k, None
+
+
 class _AttnFn(torch.autograd.Function):
     """Dense attention with autograd; q/k/v are [B,H,S,D] views (any strides, last dim 1)."""
 
@@ -215,11 +236,12 @@ def _attn_probs(q, k, lse, scale, causal, wl, wr, softcap, alibi, chunk):
 
 def _fwd_bshd(q, k, v, dropout_p, softmax_scale, causal, window_size, softcap, alibi_slopes, deterministic,
               return_attn_probs, qv, attention_chunk, q_descale, k_descale, v_descale, num_splits, pack_gqa,
-              sm_margin):
+              sm_margin, rotary_cos=None, rotary_sin=None, rotary_interleaved=False):
     """Shared body of flash_attn_func and the packed variants; inputs (B, S, H, D)."""
     _reject_fp8(q_descale, k_descale, v_descale)
     _accept_hints(num_splits, pack_gqa, sm_margin)
     chunk = _check_chunk(attention_chunk)
+    q, k, rot = _rotary_plan(q, k, v, rotary_cos, rotary_sin, rotary_interleaved, return_attn_probs, qv)
     keep_cols = None
     if _needs_qv(q, v, qv):
         if softmax_scale is None:
@@ -240,7 +262,15 @@ def _fwd_bshd(q, k, v, dropout_p, softmax_scale, causal, window_size, softcap, a
     out_buf = torch.empty((B, SQ, Hq, D), dtype=q.dtype, device=q.device).transpose(1, 2)
     al = alibi_slopes.float().contiguous() if alibi_slopes is not None else None
     qh, kh, vh = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
-    out, lse = _AttnFn.apply(qh, kh, vh, softmax_scale, cflag, wl, wr, softcap, al, dropout_p, chunk, out_buf)
+    if rot is not None:   # inference with in-kernel rotary of q (k rotated once by the glue)
+        seed = random.getrandbits(63) if dropout_p > 0 else 0
+        bits = (_C.dropout_mask(qh, int(seed), float(dropout_p), Hq, SQ, kh.shape[2], bool(cflag), int(wl), int(wr))
+                if dropout_p > 0 else None)
+        out, lse = _C.fwd(qh, kh, vh, float(softmax_scale), bool(cflag), int(wl), int(wr), float(softcap), al,
+                          float(dropout_p), int(seed), int(chunk), out_buf, bits, rotary_cos=rot[0],
+                          rotary_sin=rot[1], rotary_interleaved=rot[2])
+    else:
+        out, lse = _AttnFn.apply(qh, kh, vh, softmax_scale, cflag, wl, wr, softcap, al, dropout_p, chunk, out_buf)
     res = out.transpose(1, 2)
     if keep_cols is not None:
         res = res[..., :keep_cols].contiguous()
@@ -253,13 +283,16 @@ def _fwd_bshd(q, k, v, dropout_p, softmax_scale, causal, window_size, softcap, a
 def flash_attn_func(q, k, v, dropout_p=0.0, softmax_scale=None, causal=False, window_size=(-1, -1),
                     softcap=0.0, alibi_slopes=None, deterministic=False, return_attn_probs=False, *,
                     qv=None, attention_chunk=0, q_descale=None, k_descale=None, v_descale=None,
-                    num_splits=1, pack_gqa=None, sm_margin=0):
+                    num_splits=1, pack_gqa=None, sm_margin=0, rotary_cos=None, rotary_sin=None,
+                    rotary_interleaved=False):
     """q: (batch, seqlen_q, nheads, headdim); k, v: (batch, seqlen_k, nheads_k, headdim).
     Returns out (batch, seqlen_q, nheads, headdim), or (out, softmax_lse, S_dmask) when
-    return_attn_probs.  deterministic is accepted; the backward is always deterministic."""
+    return_attn_probs.  deterministic is accepted; the backward is always deterministic.
+    rotary_cos / rotary_sin (seqlen_ro, rotary_dim/2), keyword-only: rotate q and k first, as
+    layers.rotary.apply_rotary_emb does (positions 0..seqlen-1), inside the kernel for inference."""
     return _fwd_bshd(q, k, v, dropout_p, softmax_scale, causal, window_size, softcap, alibi_slopes, deterministic,
                      return_attn_probs, qv, attention_chunk, q_descale, k_descale, v_descale, num_splits, pack_gqa,
-                     sm_margin)
+                     sm_margin, rotary_cos, rotary_sin, rotary_interleaved)
 
 
 def flash_attn_qkvpacked_func(qkv, dropout_p=0.0, softmax_scale=None, causal=False, window_size=(-1, -1),
@@ -314,13 +347,19 @@ def flash_attn_varlen_func(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, ma
                            softmax_scale=None, causal=False, window_size=(-1, -1), softcap=0.0, alibi_slopes=None,
                            deterministic=False, return_attn_probs=False, *, seqused_q=None, seqused_k=None,
                            qv=None, attention_chunk=0, q_descale=None, k_descale=None, v_descale=None,
-                           num_splits=1, pack_gqa=None, sm_margin=0, block_table=None):
+                           num_splits=1, pack_gqa=None, sm_margin=0, block_table=None, rotary_cos=None,
+                           rotary_sin=None, rotary_interleaved=False):
     """Packed variable-length attention: q (total_q, nheads, d), k/v (total_k, nheads_k, d) with
     cu_seqlens_* int32 (batch+1).  seqused_q/seqused_k clip each sequence.  With block_table, k/v
-    are paged (num_blocks, page, nheads_k, d).  Forward and backward are single native launches."""
+    are paged (num_blocks, page, nheads_k, d).  Forward and backward are single native launches.
+    rotary_cos / rotary_sin (seqlen_ro, rotary_dim/2), keyword-only: rotate q and k first, as
+    layers.rotary.apply_rotary_emb(..., cu_seqlens=...) does (positions restart per sequence),
+    inside the kernel for inference."""
     _reject_fp8(q_descale, k_descale, v_descale)
     _accept_hints(num_splits, pack_gqa, sm_margin)
     chunk = _check_chunk(attention_chunk)
+    q, k, rot = _rotary_plan(q, k, v, rotary_cos, rotary_sin, rotary_interleaved, return_attn_probs, qv,
+                             cu_q=cu_seqlens_q, cu_k=cu_seqlens_k, paged=block_table is not None)
     paged_bt = None
     if block_table is not None:
         grad = torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad)
@@ -357,6 +396,12 @@ def flash_attn_varlen_func(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, ma
         out, lse = _C.fwd_varlen(q, k, v, cu_q, cu_k, int(max_seqlen_q), int(max_seqlen_k), float(softmax_scale),
                                  bool(cflag), int(wl), int(wr), float(softcap), al, float(dropout_p), int(seed),
                                  int(chunk), su_q, su_k, True, block_table=paged_bt)
+    elif rot is not None:   # inference with in-kernel rotary of q (k rotated once by the glue)
+        seed = random.getrandbits(63) if dropout_p > 0 else 0
+        out, lse = _C.fwd_varlen(q, k, v, cu_q, cu_k, int(max_seqlen_q), int(max_seqlen_k), float(softmax_scale),
+                                 bool(cflag), int(wl), int(wr), float(softcap), al, float(dropout_p), int(seed),
+                                 int(chunk), su_q, su_k, True, rotary_cos=rot[0], rotary_sin=rot[1],
+                                 rotary_interleaved=rot[2])
     else:
         out, lse = _VarlenAttnFn.apply(q, k, v, cu_q, cu_k, max_seqlen_q, max_seqlen_k, softmax_scale, cflag, wl,
                                        wr, softcap, al, dropout_p, chunk, su_q, su_k)

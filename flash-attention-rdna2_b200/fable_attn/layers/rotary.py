@@ -40,6 +40,27 @@ def _positions_varlen(cu_seqlens, total, offsets, device):
     return pos + offsets.to(device=device, dtype=torch.long)[seq_of]
 
 
+class _RotaryFn(torch.autograd.Function):
+    """Rotary on device tensors with autograd.  The gradient of a rotation by theta is the rotation
+    of the incoming gradient by -theta; with sin negated the native kernel performs exactly the
+    roundings torch autograd applies to the elementwise ops of the host path (each product and the
+    sum rounded to the dtype), so both paths give the same gradient bits."""
+
+    @staticmethod
+    def forward(ctx, x, cos, sin, interleaved, offs, cu_seqlens):
+        from .. import _C
+        ctx.save_for_backward(cos, sin)
+        ctx.interleaved, ctx.offs, ctx.cu = interleaved, offs, cu_seqlens
+        return _C.rotary(x, cos, sin, interleaved, False, offs, cu_seqlens)
+
+    @staticmethod
+    def backward(ctx, grad):
+        from .. import _C
+        cos, sin = ctx.saved_tensors
+        dx = _C.rotary(grad.contiguous(), cos, -sin, ctx.interleaved, False, ctx.offs, ctx.cu)
+        return dx, None, None, None, None, None
+
+
 def apply_rotary_emb(x, cos, sin, interleaved=False, inplace=False, seqlen_offsets=0, cu_seqlens=None,
                      max_seqlen=None):
     """x: (batch, seqlen, nheads, headdim), or (total, nheads, headdim) with cu_seqlens.
@@ -47,12 +68,16 @@ def apply_rotary_emb(x, cos, sin, interleaved=False, inplace=False, seqlen_offse
     Device tensors are rotated by one native kernel (fa_rotary_launch) with the roundings of the
     torch arithmetic below, which host tensors use."""
     if x.is_cuda:
-        from .. import _C
         if cu_seqlens is None and x.dim() != 4:
             raise ValueError(f"apply_rotary_emb expects (batch, seqlen, nheads, headdim), got {tuple(x.shape)}")
         if cu_seqlens is not None and x.dim() != 3:
             raise ValueError("apply_rotary_emb with cu_seqlens expects (total, nheads, headdim)")
         offs = seqlen_offsets if isinstance(seqlen_offsets, int) else seqlen_offsets
+        if torch.is_grad_enabled() and x.requires_grad:
+            if inplace:
+                raise RuntimeError("apply_rotary_emb: inplace rotation of a tensor that requires grad")
+            return _RotaryFn.apply(x, cos, sin, bool(interleaved), offs, cu_seqlens)
+        from .. import _C
         return _C.rotary(x, cos, sin, bool(interleaved), bool(inplace), offs, cu_seqlens)
     if cu_seqlens is None:
         if x.dim() != 4:

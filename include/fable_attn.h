@@ -102,6 +102,16 @@ typedef struct FaFwdParams {
   const int* block_table;
   int page, max_blocks;
   long long num_blocks;
+  /* Optional rotary embedding of Q inside the kernel (rot_cos null = none): each Q row is rotated
+   * as it lands in shared memory, with the roundings of fa_rotary_launch (the reference's torch
+   * arithmetic, layers/rotary.py:20-68); position = the row's index in its sequence, rot_cos /
+   * rot_sin fp32 [rot_seqlen_ro, rot_dim / 2], NeoX pairs (j, j + rot_dim/2) or interleaved
+   * (2j, 2j + 1).  K is not rotated here: rotate it once beforehand (fa_rotary_launch); it is read
+   * by many CTAs.  fp16/bf16 with head_dim 64 or 128 only (FA_ERR_UNSUPPORTED otherwise).  A
+   * position past the table leaves its row unrotated and raises fa_device_error bit 4096. */
+  const float* rot_cos;
+  const float* rot_sin;
+  int rot_dim, rot_seqlen_ro, rot_interleaved;
 } FaFwdParams;
 
 FA_API int fa_forward_launch(const FaFwdParams* p, int dtype, void* stream);

@@ -28,7 +28,9 @@ class FaFwdParams(C.Structure):
                 ("alibi_slopes", C.c_void_p), ("dropout_p", C.c_float), ("philox_seed", C.c_ulonglong),
                 ("cu_q", C.c_void_p), ("cu_k", C.c_void_p), ("seqused_q", C.c_void_p), ("seqused_k", C.c_void_p),
                 ("lse_total_q", C.c_longlong), ("dropout_bits", C.c_void_p), ("total_k", C.c_longlong),
-                ("block_table", C.c_void_p), ("page", C.c_int), ("max_blocks", C.c_int), ("num_blocks", C.c_longlong)]
+                ("block_table", C.c_void_p), ("page", C.c_int), ("max_blocks", C.c_int), ("num_blocks", C.c_longlong),
+                ("rot_cos", C.c_void_p), ("rot_sin", C.c_void_p), ("rot_dim", C.c_int), ("rot_seqlen_ro", C.c_int),
+                ("rot_interleaved", C.c_int)]
 
 
 class FaBwdParams(C.Structure):
