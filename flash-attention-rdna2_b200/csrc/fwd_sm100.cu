@@ -1046,13 +1046,18 @@ int launch_pp(const FaFwdParams& p, cudaStream_t st, const CUtensorMap& mq, cons
 template <bool BF16, bool FEAT>
 int launch_d(const FaFwdParams& p, cudaStream_t st, const CUtensorMap& mq, const CUtensorMap& mk,
              const CUtensorMap& mv) {
-  // two query tiles per CTA pay off once there are enough rows to fill the GPU with 256-row CTAs;
-  // FABLE_ATTN_FWD_TILES=1 / =2 forces one or two tiles per CTA wherever the two-tile kernel applies
-  // (dropout qualifies when its keep mask is precomputed; softcap and alibi do not)
+  // Two query tiles per CTA: ~1.1x the rows per second of the one-tile kernel, but half as many
+  // CTAs, so the choice compares whole waves: two tiles when ceil(n2 / SMs) * 2 / 1.1 <=
+  // ceil(n1 / SMs) (n1, n2 = CTAs of each kernel; a two-tile CTA takes ~2 / 1.1 one-tile CTAs).
+  // FABLE_ATTN_FWD_TILES=1 / =2 forces one or two tiles per CTA wherever the two-tile kernel
+  // applies (dropout qualifies when its keep mask is precomputed; softcap and alibi do not).
   const bool drop = p.dropout_p > 0.f;
   const bool eligible = p.HD == 128 && p.cu_q == nullptr && p.block_table == nullptr && p.softcap <= 0.f &&
                         p.alibi_slopes == nullptr && (!drop || p.dropout_bits != nullptr) && p.rot_cos == nullptr;
-  bool two = eligible && (long long)((p.SQ + 2 * BM - 1) / (2 * BM)) * p.NH * p.batch >= 2 * 148;
+  const long long sms = fa::num_sms();
+  const long long n2 = (long long)((p.SQ + 2 * BM - 1) / (2 * BM)) * p.NH * p.batch;
+  const long long n1 = (long long)((p.SQ + BM - 1) / BM) * p.NH * p.batch;
+  bool two = eligible && (double)((n2 + sms - 1) / sms) * (2.0 / 1.1) <= (double)((n1 + sms - 1) / sms);
   if (const char* force = getenv("FABLE_ATTN_FWD_TILES")) two = eligible && force[0] == '2';
   if (two) {
     const int rc = drop ? launch_pp<BF16, true>(p, st, mq, mk, mv) : launch_pp<BF16, false>(p, st, mq, mk, mv);
