@@ -135,7 +135,7 @@ class ClockSampler:
 def cpu_reference_sample(seconds=10.0, threads=None):
     """Time the reference's fp64 CPU oracle (oracle/_ref; the restated oracle if absent) on rows of
     the config-2 workload (one head, all 16384 keys; non-causal, so rows are independent), across
-    the host threads.  Returns (TFLOP/s, threads, kind, sample description)."""
+    the host threads.  Returns (TFLOP/s, threads, kind, sample description, wall seconds)."""
     from concurrent.futures import ThreadPoolExecutor
     from oracle import oracle as O
     S, D = CFG2["S"], CFG2["D"]
@@ -170,7 +170,7 @@ def cpu_reference_sample(seconds=10.0, threads=None):
     flops = 4.0 * rows * S * D
     desc = (f"{rows} query rows x {S} keys x D={D} of config 2 (1 head, non-causal), "
             f"{threads} threads, {wall:.1f} s wall")
-    return flops / wall / 1e12, threads, kind, desc
+    return flops / wall / 1e12, threads, kind, desc, wall
 
 
 # ----------------------------------------------------------------------------- GPU arms
@@ -510,13 +510,16 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
-        vals = []
+        vals, walls = [], []
         for _ in range(args.warmup + args.steps):
-            val, cores, kind, desc = cpu_reference_sample(seconds=max(1.0, args.cpu_seconds / 4))
+            val, cores, kind, desc, wall = cpu_reference_sample(seconds=max(1.0, args.cpu_seconds / 4))
             vals.append(val)
+            walls.append(wall)
         v = statistics.mean(vals[args.warmup:])
+        # a step is one bounded sample of the workload (see cpu_baseline.sample): its wall time
+        ms = 1e3 * statistics.mean(walls[args.warmup:])
         line = {"metric": METRIC, "value": round(v, 6), "unit": "TFLOP/s", "n_gpus": ws, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True, "impl": "reference",
+                "warmup": args.warmup, "ms_per_step": round(ms, 1), "higher_is_better": True, "impl": "reference",
                 "dtype": "f64", "data": "synthetic N(0,1), seeded", "config": config, "vs_baseline": None,
                 "cpu_baseline": {"value": round(v, 6), "unit": "TFLOP/s", "cores": cores, "kind": kind,
                                  "sample": desc},
@@ -556,7 +559,7 @@ def main():
             extra["varlen_swa_prefill"] = {"error": f"{type(e).__name__}: {e}"[:200]}
     cpu = None
     if rank == 0 and ws == 1:
-        val, cores, kind, desc = cpu_reference_sample(seconds=args.cpu_seconds)
+        val, cores, kind, desc, _ = cpu_reference_sample(seconds=args.cpu_seconds)
         cpu = {"value": round(val, 6), "unit": "TFLOP/s", "cores": cores, "kind": kind, "sample": desc}
     peaks = _peaks()
     if peaks and peaks.get("bf16_tflops"):
