@@ -127,6 +127,14 @@ def _rotary_plan(q, k, v, rotary_cos, rotary_sin, rotary_interleaved, return_att
         return q, k, None
     if (rotary_cos is None) != (rotary_sin is None):
         raise ValueError("fable_attn: rotary_cos and rotary_sin go together")
+    # every position must have a table row (the reference's apply_rotary_emb indexes cos[pos])
+    if cu_q is not None:
+        longest = max(int((cu_q[1:] - cu_q[:-1]).max()), int((cu_k[1:] - cu_k[:-1]).max()))
+    else:
+        longest = max(q.shape[1], k.shape[1])
+    if rotary_cos.shape[0] < longest or rotary_sin.shape != rotary_cos.shape:
+        raise ValueError(f"fable_attn: rotary_cos / rotary_sin {tuple(rotary_cos.shape)} must be (seqlen_ro, "
+                         f"rotary_dim / 2) with seqlen_ro >= the longest sequence ({longest})")
     grad = torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad)
     if (not grad and not return_attn_probs and qv is None and not paged and q.is_cuda
             and q.dtype in (torch.float16, torch.bfloat16) and q.shape[-1] in (64, 128)):

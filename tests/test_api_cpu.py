@@ -111,3 +111,17 @@ def test_torch_op_returns_empty_on_unsupported():
     q = torch.randn(1, 2, 8, 64)
     assert fa.torch_op._forward(q, q, q, 0.125, True).numel() == 0          # CPU tensor
     assert fa.torch_op.REGISTERED
+
+
+def test_rotary_arguments_validated_before_any_device_work():
+    """rotary_cos / rotary_sin (keyword-only extension) must come together and cover every position
+    (the reference's apply_rotary_emb indexes cos[pos]); both errors are raised on the host."""
+    import torch
+    import fable_attn
+    q = torch.zeros(2, 50, 4, 64, dtype=torch.bfloat16)
+    k = torch.zeros(2, 50, 2, 64, dtype=torch.bfloat16)
+    cos = torch.zeros(49, 16)
+    with pytest.raises(ValueError, match="seqlen_ro"):
+        fable_attn.flash_attn_func(q, k, k, rotary_cos=cos, rotary_sin=cos)
+    with pytest.raises(ValueError, match="go together"):
+        fable_attn.flash_attn_func(q, k, k, rotary_cos=cos)

@@ -142,3 +142,11 @@ def test_attention_rotary_with_grad_is_differentiable():
         grads.append((qq.grad, kk.grad, vv.grad))
     for a, b in zip(*grads):
         assert torch.equal(a, b)
+
+
+def test_attention_rotary_table_too_short():
+    import fable_attn
+    q, k, v, cu, mx = _attn_inputs(torch.bfloat16, True, 128)
+    cos, sin = (t.cuda() for t in _tables(64, n=mx - 1))
+    with pytest.raises(ValueError, match="seqlen_ro"):
+        fable_attn.flash_attn_varlen_func(q, k, v, cu, cu, mx, mx, causal=True, rotary_cos=cos, rotary_sin=sin)
