@@ -277,11 +277,12 @@ def bench_fwd_dense(args, ws, rank, dev):
                 launches=launches, clocks=clk.summary(), e2e=e2e)
 
 
-def bench_fwd_bwd_causal(dev, steps=5, warmup=3, dropout_p=0.1):
+def bench_fwd_bwd_causal(dev, steps=5, warmup=3, dropout_p=0.1, heads=32):
     """Config 3: B2 S4096 H32 D128 fp16 causal, dropout 0.1, fixed seed: fwd and bwd times (the
-    keep mask is generated once per step, as the autograd path does, and its time is included)."""
+    keep mask is generated once per step, as the autograd path does, and its time is included).
+    `heads` < 32: one rank's share of the (batch, head) units."""
     from fable_attn import _C
-    B, S, H, D = 2, 4096, 32, 128
+    B, S, H, D = 2, 4096, heads, 128
     g = torch.Generator(device=dev).manual_seed(7)
     q, k, v, do = (torch.randn(B, S, H, D, device=dev, dtype=torch.float16, generator=g) for _ in range(4))
     qh, kh, vh, doh = (t.transpose(1, 2) for t in (q, k, v, do))
@@ -398,7 +399,7 @@ def bench_decode_split(dev, ws, rank, steps=20, warmup=5):
             "bytes": nbytes}
 
 
-def bench_varlen_swa(dev, steps=10, warmup=3):
+def bench_varlen_swa(dev, steps=10, warmup=3, kv_groups=8):
     """Config 5: 16 packed sequences, lengths ~ U[256, 8192] (seeded), cu_seqlens_q = cu_seqlens_k,
     Hq 64, Hk 8, D 128 bf16, causal window (512, 0), softcap 30, NeoX rotary rd 64 (base 10000,
     positions restart per sequence) on q and k.  Reports the attention kernel alone, the public
@@ -410,7 +411,7 @@ def bench_varlen_swa(dev, steps=10, warmup=3):
     rng = np.random.default_rng(5)
     lens = rng.integers(256, 8193, size=16)
     cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32, device=dev)
-    tot, Hq, Hk, D, rd = int(lens.sum()), 64, 8, 128, 64
+    tot, Hq, Hk, D, rd = int(lens.sum()), 8 * kv_groups, kv_groups, 128, 64
     g = torch.Generator(device=dev).manual_seed(5)
     q = torch.randn(tot, Hq, D, device=dev, dtype=torch.bfloat16, generator=g)
     k = torch.randn(tot, Hk, D, device=dev, dtype=torch.bfloat16, generator=g)
@@ -540,6 +541,33 @@ def main():
             extra["decode_kv_split"] = bench_decode_split(dev, ws, rank)
         except Exception as e:
             extra["decode_kv_split"] = {"error": f"{type(e).__name__}: {e}"[:200]}
+        # independent shards, no data-path collective: config 3 by (batch, head) units (heads/ws
+        # per rank), config 5 by kv-head groups (8/ws per rank); whole-job throughput from the
+        # slowest rank's time
+        try:
+            _barrier(ws)
+            r3 = bench_fwd_bwd_causal(dev, heads=32 // ws)
+            f_ms, b_ms = _max_over_ranks(r3["fwd_ms"], ws, dev), _max_over_ranks(r3["bwd_ms"], ws, dev)
+            fl3 = 4.0 * 128 * 2 * 32 * 4096 * 4097 / 2
+            extra["fwd_bwd_causal_sharded"] = {
+                "config": f"causal fwd+bwd B2 S4096 H32 D128 fp16 dropout0.1, heads/{ws} per GPU",
+                "fwd_ms": round(f_ms, 3), "fwd_tflops": round(fl3 / f_ms / 1e9, 1),
+                "bwd_ms": round(b_ms, 3), "bwd_tflops": round(2.5 * fl3 / b_ms / 1e9, 1)}
+        except Exception as e:
+            extra["fwd_bwd_causal_sharded"] = {"error": f"{type(e).__name__}: {e}"[:200]}
+        if 8 % ws == 0:
+            try:
+                _barrier(ws)
+                r5 = bench_varlen_swa(dev, kv_groups=8 // ws)
+                k_ms = _max_over_ranks(r5["kernel_ms"], ws, dev)
+                f_ms = _max_over_ranks(r5["fused_rotary_ms"], ws, dev)
+                fl5 = r5["flops"] * ws
+                extra["varlen_swa_prefill_sharded"] = {
+                    "config": f"varlen SWA prefill (config 5), kv-head groups/{ws} per GPU",
+                    "kernel_ms": round(k_ms, 4), "kernel_tflops": round(fl5 / (k_ms * 1e-3) / 1e12, 1),
+                    "fused_rotary_ms": round(f_ms, 4), "fused_rotary_tflops": round(fl5 / (f_ms * 1e-3) / 1e12, 1)}
+            except Exception as e:
+                extra["varlen_swa_prefill_sharded"] = {"error": f"{type(e).__name__}: {e}"[:200]}
     if not args.no_extra and rank == 0:
         try:
             extra["fwd_bwd_causal"] = bench_fwd_bwd_causal(dev)
