@@ -1,6 +1,13 @@
 // fwd_sm100.cu — exact attention forward on the Blackwell tensor cores (tcgen05 + TMEM + TMA).
 //
-// One CTA = one 128-row query tile of one head of one sequence.  Warp roles (320 threads):
+// Two kernels.  fwd_tc_kernel (below) takes one 128-row query tile per CTA and every feature
+// (softcap, alibi, dropout, varlen, paged K/V, in-kernel rotary of Q, head_dim 64 or 128);
+// fwd_pp_kernel (further down) takes two query tiles per CTA for dense head_dim-128 requests
+// without softcap / alibi (dropout from a precomputed mask), and is chosen when its half-as-many
+// CTAs do not cost whole waves (launch_d).
+//
+// fwd_tc_kernel: one CTA = one 128-row query tile of one head of one sequence.  With rotary,
+// the softmax warps first rotate the Q tile in shared memory.  Warp roles (320 threads):
 //   warps 0-7  softmax: warps w and w+4 share query rows 32 (w%4) .. +31 (their TMEM lane
 //              quadrant); w / 4 picks the half of each S row (64 keys) and of each O row (D/2
 //              columns) the thread owns.  Each thread reads its half row of S from TMEM, applies
