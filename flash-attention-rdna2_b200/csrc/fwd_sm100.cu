@@ -32,6 +32,7 @@
 // empty rows -> O = 0 and LSE = -inf.
 #include <cudaTypedefs.h>
 #include <algorithm>
+#include <type_traits>
 #include "fa_common.cuh"
 #include "fa_launch.h"
 #include "sm100_ptx.cuh"
@@ -483,31 +484,48 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const float sc = FEAT ? 1.f : scale2;
       // ---- P = 2^(s - m): row sum (before dropout), dropout, 16-bit pairs into the first HB/2
       //      columns of this half's S range (already read into registers).
-      float2 lsum2 = make_float2(0.f, 0.f);
+      // one straight-line instantiation per dropout setting (a runtime test inside the unrolled
+      // pair loop would be compiled as predicated code that runs both sides)
+      auto p_pass = [&](auto drop_tag) -> float2 {
+        constexpr bool kDrop = decltype(drop_tag)::value;
+        float2 lsum2 = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int c0 = 0; c0 < HB; c0 += 32) {
-        uint32_t pk[16];
+        for (int c0 = 0; c0 < HB; c0 += 32) {
+          uint32_t pk[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          // packed fp32x2 arithmetic (one FFMA2 / FADD2 per pair) around the two SFU exponentials
-          const float2 x2 = __ffma2_rn(make_float2(s[c0 + 2 * i], s[c0 + 2 * i + 1]), make_float2(sc, sc),
-                                       make_float2(-muse, -muse));
-          float a = ex2(x2.x), b = ex2(x2.y);
-          lsum2 = __fadd2_rn(lsum2, make_float2(a, b));
-          if (drop) {   // keys kh + c0 + 2i and +1 are bits 2i, 2i+1 of word c0/32
-            const unsigned int w = dw[c0 / 32] >> (2 * i);
-            a *= (w & 1u) ? inv_keep : 0.f;
-            b *= (w & 2u) ? inv_keep : 0.f;
+          for (int i = 0; i < 16; ++i) {
+            // packed fp32x2 arithmetic (one FFMA2 / FADD2 per pair) around the two SFU exponentials
+            const float2 x2 = __ffma2_rn(make_float2(s[c0 + 2 * i], s[c0 + 2 * i + 1]), make_float2(sc, sc),
+                                         make_float2(-muse, -muse));
+            float a = ex2(x2.x), b = ex2(x2.y);
+            lsum2 = __fadd2_rn(lsum2, make_float2(a, b));
+            if constexpr (kDrop) {   // keys kh + c0 + 2i, +1: bits 2i, 2i + 1 of word c0/32, sign-extended
+              const uint32_t w = dw[c0 / 32];
+              const uint32_t m0 = (uint32_t)((int32_t)(w << (31 - 2 * i)) >> 31);
+              const uint32_t m1 = (uint32_t)((int32_t)(w << (30 - 2 * i)) >> 31);
+              const float2 z = __fmul2_rn(make_float2(__uint_as_float(__float_as_uint(a) & m0),
+                                                      __uint_as_float(__float_as_uint(b) & m1)),
+                                          make_float2(inv_keep, inv_keep));
+              a = z.x;
+              b = z.y;
+            }
+            if constexpr (BF16) {
+              const __nv_bfloat162 t2 = __floats2bfloat162_rn(a, b);
+              pk[i] = *reinterpret_cast<const uint32_t*>(&t2);
+            } else {
+              const __half2 t2 = __floats2half2_rn(a, b);
+              pk[i] = *reinterpret_cast<const uint32_t*>(&t2);
+            }
           }
-          if constexpr (BF16) {
-            const __nv_bfloat162 t2 = __floats2bfloat162_rn(a, b);
-            pk[i] = *reinterpret_cast<const uint32_t*>(&t2);
-          } else {
-            const __half2 t2 = __floats2half2_rn(a, b);
-            pk[i] = *reinterpret_cast<const uint32_t*>(&t2);
-          }
+          tmem_st16(sa + c0 / 2, pk);
         }
-        tmem_st16(sa + c0 / 2, pk);
+        return lsum2;
+      };
+      float2 lsum2;
+      if constexpr (FEAT) {
+        lsum2 = drop ? p_pass(std::true_type{}) : p_pass(std::false_type{});
+      } else {
+        lsum2 = p_pass(std::false_type{});
       }
       // ---- O rescale of this half's columns.  Every tile j >= 1 waits exactly once for PV_{j-1}
       //      (so the parity wait can never alias an older phase); PV_{j-1} normally finished while
