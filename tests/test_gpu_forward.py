@@ -317,6 +317,10 @@ TWO_TILE_CASES = [c for c in CASES if c[3] == 128 and c[10] == 0.0 and not c[7]]
     ("d128_sq100_causal", 100, 100, 128, 8, 1, True, False, -1, -1, 0.0, 0),
     ("d128_sq640_sk200_causal", 640, 200, 128, 8, 4, True, False, -1, -1, 0.0, 0),
     ("d128_sq384_win_100_20", 384, 384, 128, 8, 2, False, False, 100, 20, 0.0, 0),
+    ("d128_gqa8_sq1000_causal", 1000, 1000, 128, 16, 8, True, False, -1, -1, 0.0, 0),
+    ("d128_sq700_win_256_64", 700, 700, 128, 8, 4, False, False, 256, 64, 0.0, 0),
+    ("d128_chunk96_causal", 520, 520, 128, 8, 2, True, False, -1, -1, 0.0, 96),
+    ("d128_sq200_sk900_full", 200, 900, 128, 8, 1, False, False, -1, -1, 0.0, 0),
 ]
 
 
