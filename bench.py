@@ -113,9 +113,17 @@ class ClockSampler:
     def summary(self):
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ts, ln in self.lines:
-            if self.t_start is not None and not (self.t_start <= ts <= (self.t_stop or ts)):
-                continue
+        chosen = [(ts, ln) for ts, ln in self.lines
+                  if self.t_start is None or self.t_start <= ts <= (self.t_stop or ts)]
+        bracketing = False
+        if not chosen and self.t_start is not None and self.lines:
+            # a timed region shorter than the sampling period holds no sample: use the last sample
+            # before it and the first after it instead (marked in the summary)
+            before = [x for x in self.lines if x[0] < self.t_start]
+            after = [x for x in self.lines if x[0] > (self.t_stop or self.t_start)]
+            chosen = before[-1:] + after[:1]
+            bracketing = bool(chosen)
+        for ts, ln in chosen:
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
@@ -127,8 +135,11 @@ class ClockSampler:
             for n, v in zip(names, f[5:9]):
                 if v.lower() == "active":
                     reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        out = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+               "samples": len(sm)}
+        if bracketing:
+            out["samples_bracket_the_region"] = True
+        return out
 
 
 # ----------------------------------------------------------------------------- CPU baseline
