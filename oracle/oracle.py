@@ -6,7 +6,7 @@ as the checker or the timed CPU baseline; the product path never imports it.
   lib()      -> oracle/_build/libfa_oracle.so  (fa_oracle.c, plain-C fp64 restatement)
   ref_lib()  -> oracle/_ref/libfa_ref.so       (the reference's own fp64 oracle compiled from its
                 sources by oracle/Makefile), or None when it was not built
-Both are built by `make -C oracle` (and by __graft_entry__.build()).
+Both are built by `make -C oracle REF_DIR=<reference checkout>` (and by __graft_entry__.build()).
 """
 import ctypes as C
 import os

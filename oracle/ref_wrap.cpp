@@ -1,5 +1,5 @@
 // ref_wrap.cpp — exports the reference's OWN CPU oracle (kernels/fa_common.hpp:71-139, compiled
-// from /root/reference at build time, never copied) through a C ABI for the tests and for
+// from the reference sources at build time, never copied) through a C ABI for the tests and for
 // bench.py's reference arm.  Test infrastructure only.
 #include <hip/hip_runtime.h>
 #include FA_REF_COMMON

@@ -8,7 +8,7 @@ restated oracle (oracle/fa_oracle.c) and the GPU kernels can be checked against 
 numbers on machines where the reference is absent.  Also stores Philox known answers from the
 reference's `philox` (kernels/fa_common.hpp:71-82).
 
-Run from the repo root:  make -C oracle && python tests/golden/make_golden.py
+Run from the repo root:  make -C oracle REF_DIR=<reference checkout> && python tests/golden/make_golden.py
 """
 import os
 import sys
@@ -43,7 +43,7 @@ FWD_CASES = [
 
 def main():
     if O.ref_lib() is None:
-        raise SystemExit("oracle/_ref/libfa_ref.so is missing: run `make -C oracle` with the reference present")
+        raise SystemExit("oracle/_ref/libfa_ref.so is missing: run `make -C oracle REF_DIR=<reference checkout>`")
     arrays = {}
     for i, (name, SQ, SK, D, NH, g, causal, al, wl, wr, sc, ch) in enumerate(FWD_CASES):
         rng = np.random.default_rng(1000 + i)
