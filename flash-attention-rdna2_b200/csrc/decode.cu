@@ -723,7 +723,7 @@ int combine_run(const FaCombineParams& p, cudaStream_t st) {
 // Split-K scratch for fa_decode_launch_noalloc: a fixed device array (16 MiB) owned by the
 // library, so callers that cannot allocate device memory can still decode.  Device code could
 // name it directly; host code only holds a stand-in symbol, so the launcher passes the real
-// device address, looked up once per device with that device current.
+// device address, looked up with the call's device current.
 static __device__ __align__(256) float g_noalloc_scratch[FA_DECODE_NOALLOC_MAX_SCRATCH_FLOATS];
 
 extern "C" FA_API int fa_decode_launch_noalloc(const FaDecParams* pp, int dtype, void* stream, const void* new_k,
@@ -744,18 +744,11 @@ extern "C" FA_API int fa_decode_launch_noalloc(const FaDecParams* pp, int dtype,
                   (long long)FA_DECODE_NOALLOC_MAX_SCRATCH_FLOATS);
     return FA_ERR_SIZE;
   }
-  static float* dev_ptr[64] = {nullptr};
-  const int d = fa::current_device();
-  if (d < 0 || d >= 64) {
-    fa::set_error("decode (no-alloc): device ordinal %d out of range", d);
-    return FA_ERR_INVALID;
-  }
-  if (!dev_ptr[d]) {
-    void* ptr = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-    if (e != cudaSuccess) return fa::cuda_status(e, "decode (no-alloc): cudaGetSymbolAddress");
-    dev_ptr[d] = (float*)ptr;
-  }
-  p.scratch = dev_ptr[d];
+  // the array's address on the current device, looked up on every call: nothing cached can go
+  // stale after a context reset, and concurrent first calls from several threads share no state
+  void* ptr = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+  if (e != cudaSuccess) return fa::cuda_status(e, "decode (no-alloc): cudaGetSymbolAddress");
+  p.scratch = (float*)ptr;
   return fa_decode_launch(&p, dtype, stream, new_k, new_v);
 }

@@ -462,5 +462,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("combine", &combine, py::arg("out_partial"), py::arg("lse_partial"), py::arg("out_dtype"),
         py::arg("return_lse") = false);
   m.def("kernel_launch_count", []() { return fa_kernel_launch_count(); });
+  m.def("device_error", [](bool clear) { return fa_device_error(clear ? 1 : 0); }, py::arg("clear") = false);
+  m.def("wait_selftest", [](int64_t limit_ns) {
+    check(fa_wait_selftest((unsigned long long)limit_ns, (void*)at::cuda::getCurrentCUDAStream().stream()),
+          "wait self-test");
+  }, py::arg("limit_ns"));
   m.def("abi_version", []() { return fa_abi_version(); });
 }

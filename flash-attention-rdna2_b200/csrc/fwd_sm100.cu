@@ -1153,6 +1153,29 @@ extern "C" FA_API int fa_forward_two_tile_ready(int bf16) {
                : (pp_ready<false, false>() && pp_ready<false, true>())) ? 1 : 0;
 }
 
+// Self-test of the bounded mbarrier wait every pipeline uses: one thread waits on a barrier that
+// nothing ever arrives on (no copy or MMA is in flight), gives up after limit_ns and records
+// FA_DEVERR_WAIT_SELFTEST; the kernel then returns normally and the context stays usable.
+__global__ void wait_selftest_kernel(unsigned long long limit_ns) {
+  __shared__ __align__(8) unsigned long long slot;
+  const uint32_t b = smem_u32(&slot);
+  if (threadIdx.x == 0) {
+    mbar_init(b, 1);
+    fence_barrier_init();
+    if (!mbar_wait(b, 0, limit_ns)) record_error(FA_DEVERR_WAIT_SELFTEST);
+  }
+}
+
+extern "C" FA_API int fa_wait_selftest(unsigned long long limit_ns, void* stream) {
+  if (limit_ns == 0 || limit_ns > 10000000000ull) {
+    fa::set_error("wait self-test: limit_ns=%llu outside (0, 1e10]", limit_ns);
+    return FA_ERR_INVALID;
+  }
+  wait_selftest_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(limit_ns);
+  fa::count_launch();
+  return fa::cuda_status(cudaGetLastError(), "wait self-test launch");
+}
+
 extern "C" FA_API int fa_device_error(int clear) {
   int v = 0;
   cudaMemcpyFromSymbol(&v, g_fwd_error, sizeof(int));

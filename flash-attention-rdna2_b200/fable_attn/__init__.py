@@ -24,8 +24,18 @@ from . import torch_op
 
 torch_op.register()
 
+
+
+def device_error(clear=False):
+    """Error bits the kernels recorded on the current device (0 = none): a pipeline wait that gave
+    up (the kernel unwound and its outputs are not valid), a paged-K/V entry outside the cache, or
+    a rotary position outside its table.  Synchronises with the device; clear=True resets them."""
+    from . import _C
+    return int(_C.device_error(bool(clear)))
+
+
 __all__ = [
-    "flash_attn_func", "flash_attn_qkvpacked_func", "flash_attn_kvpacked_func", "flash_attn_varlen_func",
+    "device_error", "flash_attn_func", "flash_attn_qkvpacked_func", "flash_attn_kvpacked_func", "flash_attn_varlen_func",
     "flash_attn_varlen_qkvpacked_func", "flash_attn_varlen_kvpacked_func", "flash_attn_combine",
     "flash_attn_with_kvcache", "bert_padding", "install_as_flash_attn",
 ]

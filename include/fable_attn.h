@@ -264,8 +264,9 @@ FA_API int fa_decode_launch(const FaDecParams* p, int dtype, void* stream,
  *   - p->scratch is ignored (may be null).  Requests needing more scratch than the array holds
  *     (fa_decode_scratch_floats(batch, nq, NH, HD, nsplit) > the maximum) are refused with
  *     FA_ERR_SIZE before any work; lower nsplit to fit.
- *   - The first call on each device looks up the array's device address (cudaGetSymbolAddress,
- *     with that device current) and caches it; make that first call before any stream capture.
+ *   - Each call looks up the array's device address on the current device
+ *     (cudaGetSymbolAddress); the first call on a device also loads the library's kernels there,
+ *     so make that first call before any stream capture.
  *   - No allocation of any kind: no cudaMalloc/cudaFree, no library allocator.
  *   - All calls share the one array and it keeps the last call's contents.  Nothing in it needs
  *     to start at zero (every split writes its whole slot before the merge reads it), but calls
@@ -304,10 +305,20 @@ FA_API int fa_combine_launch(const FaCombineParams* p, void* stream);
 /* ---- introspection ---- */
 FA_API int fa_abi_version(void);
 FA_API const char* fa_last_error(void);       /* message of the last failing call on this thread */
-/* Error bits recorded by device-side pipeline waits that gave up (0 = none).  A bounded wait in
- * a tensor-core kernel that times out records a bit here and the kernel unwinds instead of
- * hanging.  Synchronous (device -> host copy); clear != 0 resets the bits. */
+/* Error bits recorded on the device (0 = none).  A bounded wait in a tensor-core kernel that
+ * times out records a bit here and the kernel unwinds instead of hanging (its outputs are then
+ * not valid); bits 1024 / 4096 / 256 flag a paged-K/V entry outside the cache and a rotary
+ * position outside the cos/sin table.  Synchronous (device -> host copy); clear != 0 resets the
+ * bits.  No counterpart in the reference (its kernels have no waits that can give up). */
 FA_API int fa_device_error(int clear);
+/* Bit of fa_device_error set by fa_wait_selftest. */
+#define FA_DEVERR_WAIT_SELFTEST 65536
+/* Launches one tiny kernel whose bounded wait can never be satisfied (nothing arrives on its
+ * mbarrier and nothing is in flight): after limit_ns (0 < limit_ns <= 1e10) the wait gives up,
+ * records FA_DEVERR_WAIT_SELFTEST in fa_device_error and the kernel returns.  Lets a host check
+ * the give-up path of the pipelines' waits without faulting or hanging a GPU.  No counterpart in
+ * the reference. */
+FA_API int fa_wait_selftest(unsigned long long limit_ns, void* stream);
 /* Number of this library's kernels launched since load (all threads, all devices). */
 FA_API unsigned long long fa_kernel_launch_count(void);
 /* 1 when the forward's two-query-tile kernel (dense fp16/bf16, head_dim 128, no softcap / alibi /

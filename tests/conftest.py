@@ -21,3 +21,21 @@ def pytest_collection_modifyitems(config, items):
     for it in items:
         if "gpu" in it.keywords:
             it.add_marker(skip)
+
+
+@pytest.fixture(autouse=True, scope="module")
+def _device_error_flags_clear(request):
+    """Every GPU test module must end with no device-side error recorded (a pipeline wait that
+    gave up, a bad page index, a rotary position past its table): such a kernel returns wrong
+    values without a host error, so the flag is read here after the module's tests."""
+    import torch
+    gpu_module = any("gpu" in it.keywords for it in request.session.items
+                     if it.module is request.module) if hasattr(request, "module") else False
+    if not (gpu_module and torch.cuda.is_available()):
+        yield
+        return
+    import fable_attn
+    fable_attn.device_error(clear=True)
+    yield
+    flags = fable_attn.device_error(clear=True)
+    assert flags == 0, f"device error bits 0x{flags:x} recorded during {request.module.__name__}"

@@ -19,11 +19,18 @@ from gpu_util import TOL, randn, stream, to_np
 pytestmark = pytest.mark.gpu
 
 
-def _decode_case(dt, nsplit):
+# (nq, page, ctx): nq = 2 runs the CUDA-core split-K partial; nq = 1 with head_dim 128 and a page
+# of at least 8 runs the tensor-core partial (stream-K work split; the 5-position context leaves
+# most of its split slots empty, which the merge must see as empty in the reused array)
+SHAPES = {"cuda_core": (2, 16, (700, 333, 1021)), "tensor_core": (1, 256, (700, 5, 3000))}
+
+
+def _decode_case(dt, nsplit, shape="cuda_core"):
     rng = np.random.default_rng(2024)
-    B, nq, NH, gqa, HD, page = 3, 2, 16, 4, 128, 16
+    nq, page, ctx = SHAPES[shape]
+    B, NH, gqa, HD = 3, 16, 4, 128
     NKV = NH // gqa
-    ctx = np.array([700, 333, 1021], np.int32)
+    ctx = np.array(ctx, np.int32)
     max_blocks = int((ctx.max() + nq + page - 1) // page)
     nblocks = B * max_blocks
     bt = rng.permutation(nblocks).astype(np.int32).reshape(B, max_blocks)
@@ -44,12 +51,13 @@ def _decode_case(dt, nsplit):
     return keep, params, (B, nq, NH, HD)
 
 
+@pytest.mark.parametrize("shape", ["cuda_core", "tensor_core"])
 @pytest.mark.parametrize("dt", ["bf16", "fp16"])
-def test_noalloc_matches_allocating_decode_twice(dt):
+def test_noalloc_matches_allocating_decode_twice(dt, shape):
     L = A.lib()
     L.fa_decode_launch_noalloc.argtypes = [C.POINTER(A.FaDecParams), C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]
     nsplit = 6
-    keep, params, (B, nq, NH, HD) = _decode_case(dt, nsplit)
+    keep, params, (B, nq, NH, HD) = _decode_case(dt, nsplit, shape)
     o_ref = torch.empty((B, nq, NH, HD), device="cuda", dtype=keep["q"].dtype)
     l_ref = torch.empty((B, nq, NH), device="cuda", dtype=torch.float32)
     scratch = torch.empty(L.fa_decode_scratch_floats(B, nq, NH, HD, nsplit), device="cuda")
