@@ -13,7 +13,10 @@ Also reported in the same line:
                peak (MEASURED_PEAKS.json), plus DRAM traffic from the committed ncu summary
   cpu_baseline the reference's own fp64 CPU oracle (oracle/_ref, kernels/fa_common.hpp:102-134)
                on a bounded sample of the same workload, all host threads
-  extra        config 3 (causal fwd+bwd fp16, dropout 0.1) and config 4 (paged decode) figures
+  extra        configs 1, 3, 4 and 5 (fp32 causal, causal fwd+bwd fp16 dropout 0.1, paged decode,
+               varlen sliding-window prefill), each with its own roofline / e2e / cpu_baseline
+               (reference oracle or restated oracle) / cpu_baseline_torch_fp32 block, and the
+               decode KV-range split (also at N=1) with per-phase times
   clocks       nvidia-smi samples taken during the timed region
 
 `--impl reference` times only the reference's CPU implementation on the host cores (rank 0).
@@ -337,18 +340,32 @@ def bench_fwd_bwd_causal(dev, steps=5, warmup=3, dropout_p=0.1, heads=32):
     return r
 
 
-def bench_decode(dev, steps=20, warmup=5):
-    """Config 4: B16 Hq32 Hk8 D128 bf16, page 256, cache_seqlens ~ U[16384, 32768], permuted pages."""
-    from fable_attn import _C
+def decode_lengths(B=16):
+    """Config 4's cache_seqlens ~ U[16384, 32768] (seeded): the same draw for the single-GPU decode
+    and for the KV-range split across GPUs, so the two curves compare like with like."""
+    return np.random.default_rng(11).integers(16384, 32769, size=B).astype(np.int32)
+
+
+def decode_setup(dev):
+    """Config 4 inputs: B16 Hq32 Hk8 D128 bf16, page 256, 2048 permuted pages, resident cache."""
     B, Hq, Hk, D, page, maxctx = 16, 32, 8, 128, 256, 32768
     nper = maxctx // page
     g = torch.Generator(device=dev).manual_seed(11)
-    rng = np.random.default_rng(11)
     kc = torch.randn(B * nper, page, Hk, D, device=dev, dtype=torch.bfloat16, generator=g)
     vc = torch.randn(B * nper, page, Hk, D, device=dev, dtype=torch.bfloat16, generator=g)
-    bt = torch.from_numpy(rng.permutation(B * nper).astype(np.int32).reshape(B, nper)).to(dev)
-    lens = rng.integers(16384, 32769, size=B).astype(np.int32)
-    cs = torch.from_numpy(lens).to(dev)
+    bt = torch.from_numpy(np.random.default_rng(12).permutation(B * nper).astype(np.int32).reshape(B, nper)).to(dev)
+    lens = decode_lengths(B)
+    q = torch.randn(B, 1, Hq, D, device=dev, dtype=torch.bfloat16, generator=g)
+    return dict(B=B, Hq=Hq, Hk=Hk, D=D, page=page, kc=kc, vc=vc, bt=bt, lens=lens, q=q,
+                cs=torch.from_numpy(lens).to(dev), nbytes=float(lens.sum()) * Hk * D * 2 * 2)
+
+
+def bench_decode(dev, steps=20, warmup=5):
+    """Config 4: B16 Hq32 Hk8 D128 bf16, page 256, cache_seqlens ~ U[16384, 32768], permuted pages."""
+    from fable_attn import _C
+    c = decode_setup(dev)
+    q, kc, vc, bt, cs, D, lens = c["q"], c["kc"], c["vc"], c["bt"], c["cs"], c["D"], c["lens"]
+    Hk = c["Hk"]
     q = torch.randn(B, 1, Hq, D, device=dev, dtype=torch.bfloat16, generator=g)
     sc = D ** -0.5
 
@@ -367,7 +384,7 @@ def bench_decode(dev, steps=20, warmup=5):
     ms = a.elapsed_time(b) / steps
     nbytes = float(lens.sum()) * Hk * D * 2 * 2
     return {"config": "paged decode B16 Hq32 Hk8 D128 bf16 page256 L~U[16K,32K]", "ms": round(ms, 4),
-            "GBps": round(nbytes / ms / 1e6, 1), "bytes": nbytes}
+            "GBps": round(nbytes / ms / 1e6, 1), "bytes": nbytes, "_setup": c}
 
 
 def bench_decode_split(dev, ws, rank, steps=20, warmup=5):
@@ -378,8 +395,7 @@ def bench_decode_split(dev, ws, rank, steps=20, warmup=5):
     time is the max over ranks, GB/s counts the K/V bytes of the whole job."""
     from fable_attn import multigpu as M
     B, Hq, Hk, D, page = 16, 32, 8, 128, 256
-    rng = np.random.default_rng(11)
-    lens = rng.integers(16384, 32769, size=B).astype(np.int64)
+    lens = decode_lengths(B).astype(np.int64)
     starts, ends = M.plan_kv_split(torch.from_numpy(lens), ws)
     local = (ends[rank] - starts[rank]).to(torch.int32)
     nper = int((int(local.max()) + page - 1) // page)
@@ -390,8 +406,10 @@ def bench_decode_split(dev, ws, rank, steps=20, warmup=5):
     q = torch.randn(B, 1, Hq, D, device=dev, dtype=torch.bfloat16, generator=torch.Generator(device=dev).manual_seed(7))
     lc = local.to(dev)
 
-    def call():
-        return M.decode_kv_split(q, kc, vc, bt, lc, softmax_scale=D ** -0.5)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
+
+    def call(e=None):
+        return M.decode_kv_split(q, kc, vc, bt, lc, softmax_scale=D ** -0.5, phase_events=e)
 
     for _ in range(warmup):
         call()
@@ -399,15 +417,23 @@ def bench_decode_split(dev, ws, rank, steps=20, warmup=5):
     _barrier(ws)
     a, b = _events()
     a.record()
-    for _ in range(steps):
+    for i in range(steps):
         call()
     b.record()
     torch.cuda.synchronize()
     ms = _max_over_ranks(a.elapsed_time(b) / steps, ws, dev)
+    # per-phase times (a separate pass: the events between the phases would otherwise be in the
+    # timed region): partial decode / all-gather / merge, mean over steps, max over ranks
+    for i in range(steps):
+        call(ev[i])
+    torch.cuda.synchronize()
+    ph = [statistics.mean(e[j].elapsed_time(e[j + 1]) for e in ev) for j in range(3)]
+    ph = [_max_over_ranks(x, ws, dev) for x in ph]
     nbytes = float(lens.sum()) * Hk * D * 2 * 2
-    return {"config": f"paged decode B16 Hq32 Hk8 D128 bf16 page256 L~U[16K,32K], KV range split over {ws} GPUs "
-                      "+ NCCL all-gather + LSE merge", "ms": round(ms, 4), "GBps": round(nbytes / ms / 1e6, 1),
-            "bytes": nbytes}
+    return {"config": f"paged decode B16 Hq32 Hk8 D128 bf16 page256 L~U[16K,32K] (same lengths as decode_paged), "
+                      f"KV range split over {ws} GPU(s) + one NCCL all-gather of packed fp32 partials + LSE merge",
+            "ms": round(ms, 4), "GBps": round(nbytes / ms / 1e6, 1), "bytes": nbytes,
+            "phase_ms": {"partial": round(ph[0], 4), "all_gather": round(ph[1], 4), "merge": round(ph[2], 4)}}
 
 
 def bench_varlen_swa(dev, steps=10, warmup=3, kv_groups=8):
@@ -463,6 +489,311 @@ def bench_varlen_swa(dev, steps=10, warmup=3, kv_groups=8):
         out[name + "_ms"] = round(ms, 4)
         out[name + "_tflops"] = round(flops / (ms * 1e-3) / 1e12, 1)
     return out
+
+
+# ----------------------------------------------------------------------------- per-config blocks
+# Configs 1, 3, 4 and 5 each get the measurement set of the headline: the kernel figure (CUDA
+# events, resident inputs), `roofline` against MEASURED_PEAKS.json, `e2e` through the public API
+# with pinned host buffers (the step's inputs copied in and its results copied out inside the
+# timed region), and two CPU baselines on the host cores: `cpu_baseline` = the reference's CPU
+# oracle (compiled from its sources where it builds alone, else the restated oracle in oracle/) and
+# `cpu_baseline_torch_fp32` = the reference's exact torch fp32 reference (oracle/torch_ref.py).
+def _gpu_ms(fn, steps, warmup):
+    """Mean ms per call of fn over `steps` calls on the current stream (CUDA events)."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    a, b = _events()
+    a.record()
+    for _ in range(steps):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / steps
+
+
+def _wall(fn):
+    t0 = time.perf_counter()
+    fn()
+    return time.perf_counter() - t0
+
+
+def _roofline(achieved, bound, peaks, traffic=None, note=None):
+    if bound == "hbm":
+        if peaks and peaks.get("hbm_gbs"):
+            peak, src = float(peaks["hbm_gbs"]), "MEASURED_PEAKS.json hbm_gbs (copy), of measured"
+        else:
+            peak, src = 6650.0, "fallback 6.65 TB/s, of fallback"
+        unit = "GB/s"
+    elif bound == "fp32":   # CUDA-core fp32: no measured figure exists; nominal FMA rate
+        mhz = float((peaks or {}).get("sm_max_mhz") or 1965.0)
+        sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+        peak, src, unit = sms * 128 * 2 * mhz * 1e6 / 1e12, f"nominal fp32 FMA rate ({sms} SMs x 128 x 2 x {mhz:.0f} MHz)", "TFLOP/s"
+    else:
+        if peaks and peaks.get("bf16_tflops"):
+            peak, src = float(peaks["bf16_tflops"]), "MEASURED_PEAKS.json bf16_tflops (burst), of measured"
+        else:
+            peak, src = 1590.0, "fallback 1.59 PFLOP/s, of fallback"
+        unit = "TFLOP/s"
+    r = {"bound": bound if bound != "fp32" else "fp32 CUDA cores", "achieved": round(achieved, 2), "peak": peak,
+         "unit": unit, "frac": round(achieved / peak, 4), "traffic": traffic, "peak_source": src}
+    if bound == "tensor" and peaks and peaks.get("bf16_tflops_sustained"):
+        r["frac_of_sustained"] = round(achieved / float(peaks["bf16_tflops_sustained"]), 4)
+    if note:
+        r["note"] = note
+    return r
+
+
+def _torch_cpu_threads():
+    n = os.cpu_count() or 1
+    torch.set_num_threads(n)
+    return n
+
+
+def measure_config1(dev, peaks, steps=20, warmup=5):
+    """Config 1: B1 S512 H8 D64 fp32 causal, scale 1/8 (the CPU-runnable case):
+    the fp32 forward on the GPU's CUDA cores, and both CPU paths on the whole config."""
+    import fable_attn as fa
+    from fable_attn import _C
+    from oracle import oracle as O, torch_ref
+    from concurrent.futures import ThreadPoolExecutor
+    B, S, H, D, scale = 1, 512, 8, 64, 0.125
+    flops = 4.0 * D * H * B * S * (S + 1) / 2
+    rng = np.random.default_rng(1)
+    host = [rng.standard_normal((B, S, H, D), dtype=np.float32) for _ in range(3)]
+    q, k, v = (torch.from_numpy(x).to(dev) for x in host)
+    qh, kh, vh = (t.transpose(1, 2) for t in (q, k, v))
+    out = torch.empty_like(q).transpose(1, 2)
+    ms = _gpu_ms(lambda: _C.fwd(qh, kh, vh, scale, True, -1, 0, 0.0, None, 0.0, 0, 0, out), steps, warmup)
+    pin = [torch.from_numpy(x).pin_memory() for x in host]
+    hout = torch.empty(B, S, H, D).pin_memory()
+    dbuf = [torch.empty_like(q) for _ in range(3)]
+
+    def e2e():
+        for d_, h_ in zip(dbuf, pin):
+            d_.copy_(h_, non_blocking=True)
+        hout.copy_(fa.flash_attn_func(*dbuf, softmax_scale=scale, causal=True), non_blocking=True)
+
+    e2e_ms = _gpu_ms(e2e, steps, warmup)
+    # CPU: the reference's ref_attention on the whole config, one head per thread
+    R = O.ref_lib()
+    n = os.cpu_count() or 1
+
+    def head(h):
+        sl = [np.ascontiguousarray(x[0][:, h:h + 1]) for x in host]
+        if R is not None:
+            O.ref_forward(sl[0], sl[1], sl[2], scale, True)
+        else:
+            O.forward(sl[0][None], sl[1][None], sl[2][None], scale, True)
+
+    with ThreadPoolExecutor(min(n, H)) as ex:
+        t_ref = _wall(lambda: list(ex.map(head, range(H))))
+    thr = _torch_cpu_threads()
+    tq, tk, tv = (torch.from_numpy(x) for x in host)
+    torch_ref.ref_attn(tq, tk, tv, scale, causal=True)   # warm-up
+    t_torch = _wall(lambda: torch_ref.ref_attn(tq, tk, tv, scale, causal=True))
+    return {"config": "B1 S512 H8 D64 fp32 causal scale 1/8 (BASELINE configs[0])", "dtype": "f32",
+            "kernel_ms": round(ms, 4), "value": round(flops / ms / 1e9, 3), "unit": "TFLOP/s",
+            "flops": flops,
+            "roofline": _roofline(flops / ms / 1e9, "fp32", peaks,
+                                  note="CUDA-core fp32 kernel; a 0.27 GFLOP problem is launch- and latency-bound"),
+            "e2e": {"value": round(flops / e2e_ms / 1e9, 3), "unit": "TFLOP/s", "ms_per_step": round(e2e_ms, 4),
+                    "h2d_bytes_per_step": 3 * B * S * H * D * 4, "d2h_bytes_per_step": B * S * H * D * 4},
+            "cpu_baseline": {"value": round(flops / t_ref / 1e12, 6), "unit": "TFLOP/s", "cores": min(n, H),
+                             "kind": "reference" if R is not None else "port",
+                             "sample": f"whole config 1 ({t_ref:.2f} s), one head per thread, fp64"},
+            "cpu_baseline_torch_fp32": {"value": round(flops / t_torch / 1e12, 6), "unit": "TFLOP/s", "cores": thr,
+                                        "kind": "port", "sample": f"whole config 1 ({t_torch:.3f} s), torch fp32 "
+                                        "exact reference (lab/parity_new_api.py:36-75) on the host cores"}}
+
+
+def measure_config3(dev, peaks, r3, steps=5, warmup=2):
+    """Config 3 blocks around bench_fwd_bwd_causal's kernel figures (r3): e2e of one training step
+    through flash_attn_func (+ backward) from pinned host buffers, roofline of the backward, CPU
+    baselines on one (batch, head) unit."""
+    import fable_attn as fa
+    from oracle import oracle as O, torch_ref
+    B, S, H, D, p = 2, 4096, 32, 128, 0.1
+    fwd_flops = 4.0 * D * B * H * S * (S + 1) / 2
+    g = torch.Generator(device=dev).manual_seed(7)
+    dev_in = [torch.randn(B, S, H, D, device=dev, dtype=torch.float16, generator=g) for _ in range(4)]
+    pin = [t.cpu().pin_memory() for t in dev_in]
+    hres = [torch.empty(B, S, H, D, dtype=torch.float16).pin_memory() for _ in range(4)]
+    dbuf = [torch.empty_like(t) for t in dev_in]
+
+    def e2e():
+        for d_, h_ in zip(dbuf, pin):
+            d_.copy_(h_, non_blocking=True)
+        q, k, v = (t.detach().requires_grad_() for t in dbuf[:3])
+        o = fa.flash_attn_func(q, k, v, dropout_p=p, causal=True, deterministic=True)
+        o.backward(dbuf[3])
+        for h_, t in zip(hres, (o.detach(), q.grad, k.grad, v.grad)):
+            h_.copy_(t, non_blocking=True)
+
+    e2e_ms = _gpu_ms(e2e, steps, warmup)
+    nb = B * S * H * D * 2
+    # CPU (one (batch, head) unit of 64, fwd + bwd with the Philox dropout): the restated oracle in
+    # fp64 (the reference's backward oracle lives inside its GPU gate and does not build alone)
+    rng = np.random.default_rng(3)
+    qn, kn, vn, don = (rng.standard_normal((S, D), dtype=np.float32) for _ in range(4))
+    unit_flops = 3.5 * 4.0 * D * S * (S + 1) / 2
+    t_port = _wall(lambda: O.attention_head(qn, kn, vn, D ** -0.5, causal=True, dropout_p=p, seed=777, h=0, do=don))
+    thr = _torch_cpu_threads()
+    tq, tk, tv = (torch.from_numpy(x).view(1, S, 1, D).requires_grad_() for x in (qn, kn, vn))
+    tdo = torch.from_numpy(don).view(1, S, 1, D)
+
+    def torch_unit():
+        o = torch_ref.ref_attn(tq, tk, tv, D ** -0.5, causal=True)
+        o.backward(tdo)
+
+    t_torch = _wall(torch_unit)
+    bwd_ach = 2.5 * fwd_flops / r3["bwd_ms"] / 1e9
+    return {"roofline": _roofline(bwd_ach, "tensor", peaks, _traffic("bwd_causal_fp16_b2_s4096_h32_d128_dropout"),
+                                  note="whole backward call (dsum, keep-mask transpose, dK/dV, dQ); FLOP = 2.5 x "
+                                       "the causal forward (lab/bench_e2e.py:164-165)"),
+            "roofline_fwd": _roofline(fwd_flops / r3["fwd_ms"] / 1e9, "tensor", peaks,
+                                      note="forward incl. the keep-mask kernel"),
+            "e2e": {"value": round(3.5 * fwd_flops / e2e_ms / 1e9, 1), "unit": "TFLOP/s (fwd+bwd)",
+                    "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": 4 * nb, "d2h_bytes_per_step": 4 * nb,
+                    "step": "flash_attn_func(dropout 0.1, causal) + backward, q/k/v/dO in, out/dQ/dK/dV out"},
+            "cpu_baseline": {"value": round(unit_flops / t_port / 1e12, 6), "unit": "TFLOP/s (fwd+bwd)",
+                             "cores": os.cpu_count() or 1, "kind": "port",
+                             "sample": f"1 of 64 (batch, head) units, fwd+bwd with dropout, fp64 numpy "
+                                       f"({t_port:.1f} s; rate extrapolates linearly in units)"},
+            "cpu_baseline_torch_fp32": {"value": round(unit_flops / t_torch / 1e12, 6), "unit": "TFLOP/s (fwd+bwd)",
+                                        "cores": thr, "kind": "port",
+                                        "sample": f"1 of 64 units, torch fp32 exact reference + autograd, no dropout "
+                                                  f"(the reference's torch reference has none) ({t_torch:.1f} s)"}}
+
+
+def measure_config4(dev, peaks, r4, steps=20, warmup=5):
+    """Config 4 blocks around bench_decode's figure (r4): e2e through flash_attn_with_kvcache with q
+    from pinned host memory and the output read back (the cache is resident: it is the model's
+    state), roofline against the measured HBM copy rate, CPU baselines on 2 of the 16 sequences."""
+    import fable_attn as fa
+    from oracle import oracle as O, torch_ref
+    from concurrent.futures import ThreadPoolExecutor
+    c = r4["_setup"]
+    hq = c["q"].cpu().pin_memory()
+    hout = torch.empty_like(hq).pin_memory()
+    dq = torch.empty_like(c["q"])
+
+    def e2e():
+        dq.copy_(hq, non_blocking=True)
+        hout.copy_(fa.flash_attn_with_kvcache(dq, c["kc"], c["vc"], cache_seqlens=c["cs"], block_table=c["bt"]),
+                   non_blocking=True)
+
+    e2e_ms = _gpu_ms(e2e, steps, warmup)
+    # CPU sample: sequences 0 and 1, every head; the oracle per (sequence, kv-head group) in threads
+    lens, page, Hk, D = c["lens"], c["page"], c["Hk"], c["D"]
+    qn = c["q"].float().cpu().numpy()
+    seqs = []
+    for b in (0, 1):
+        npg = (int(lens[b]) + page - 1) // page
+        pages = c["bt"][b, :npg].long()
+        seqs.append((b, c["kc"][pages].float().cpu().numpy(), c["vc"][pages].float().cpu().numpy(), npg))
+    gq = c["Hq"] // Hk
+
+    def task(arg):
+        (b, kp, vp, npg), gi = arg
+        O.decode(qn[b:b + 1, :, gi * gq:(gi + 1) * gq], np.ascontiguousarray(kp[:, :, gi:gi + 1]),
+                 np.ascontiguousarray(vp[:, :, gi:gi + 1]), np.arange(npg, dtype=np.int32)[None], lens[b:b + 1])
+
+    n = os.cpu_count() or 1
+    work = [(s, gi) for s in seqs for gi in range(Hk)]
+    with ThreadPoolExecutor(min(n, len(work))) as ex:
+        t_port = _wall(lambda: list(ex.map(task, work)))
+    sample_bytes = float(lens[0] + lens[1]) * Hk * D * 2 * 2
+    thr = _torch_cpu_threads()
+
+    def torch_path():
+        for b, kp, vp, npg in seqs:
+            L = int(lens[b])
+            kk = torch.from_numpy(kp).reshape(-1, Hk, D)[:L][None]
+            vv = torch.from_numpy(vp).reshape(-1, Hk, D)[:L][None]
+            torch_ref.ref_attn(torch.from_numpy(qn[b:b + 1]), kk, vv, D ** -0.5)
+
+    t_torch = _wall(torch_path)
+    nbytes = r4["bytes"]
+    return {"roofline": _roofline(nbytes / r4["ms"] / 1e6, "hbm", peaks, _traffic("decode_paged_bf16_b16_page256"),
+                                  note="whole decode call (tensor-core split-K partial + merge); algorithmic bytes "
+                                       "= cached K and V of every sequence"),
+            "e2e": {"value": round(nbytes / e2e_ms / 1e6, 1), "unit": "GB/s", "ms_per_step": round(e2e_ms, 4),
+                    "h2d_bytes_per_step": int(hq.numel() * 2), "d2h_bytes_per_step": int(hout.numel() * 2),
+                    "step": "flash_attn_with_kvcache(q from host, resident paged cache) -> out to host"},
+            "cpu_baseline": {"value": round(sample_bytes / t_port / 1e9, 3), "unit": "GB/s", "cores": min(n, len(work)),
+                             "kind": "port", "sample": f"sequences 0-1 of 16 (ctx {int(lens[0])}, {int(lens[1])}), all "
+                             f"heads, fp64 decode oracle per (sequence, kv head) in threads ({t_port:.1f} s)"},
+            "cpu_baseline_torch_fp32": {"value": round(sample_bytes / t_torch / 1e9, 3), "unit": "GB/s", "cores": thr,
+                                        "kind": "port", "sample": f"sequences 0-1 of 16, torch fp32 exact reference "
+                                                                  f"over the gathered pages ({t_torch:.2f} s)"}}
+
+
+def measure_config5(dev, peaks, r5, steps=5, warmup=2):
+    """Config 5 blocks around bench_varlen_swa's figures (r5): e2e of the fused-rotary call from
+    pinned host q/k/v/cu_seqlens (the cos/sin tables are resident model constants), roofline of the
+    forward kernel, CPU baselines on one query head over all 16 sequences."""
+    import fable_attn as fa
+    from oracle import oracle as O, torch_ref
+    rng = np.random.default_rng(5)
+    lens = rng.integers(256, 8193, size=16)
+    cu_np = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    tot, Hq, Hk, D, rd = int(lens.sum()), 64, 8, 128, 64
+    g = torch.Generator(device=dev).manual_seed(5)
+    dev_in = [torch.randn(tot, h, D, device=dev, dtype=torch.bfloat16, generator=g) for h in (Hq, Hk, Hk)]
+    pin = [t.cpu().pin_memory() for t in dev_in]
+    hcu = torch.from_numpy(cu_np).pin_memory()
+    inv = 10000.0 ** (-torch.arange(0, rd, 2, device=dev, dtype=torch.float32) / rd)
+    ang = torch.arange(int(lens.max()), device=dev, dtype=torch.float32)[:, None] * inv[None]
+    cos, sin = ang.cos(), ang.sin()
+    dbuf = [torch.empty_like(t) for t in dev_in]
+    dcu = torch.empty_like(hcu, device=dev)
+    hout = torch.empty(tot, Hq, D, dtype=torch.bfloat16).pin_memory()
+    mx = int(lens.max())
+
+    def e2e():
+        for d_, h_ in zip(dbuf + [dcu], pin + [hcu]):
+            d_.copy_(h_, non_blocking=True)
+        hout.copy_(fa.flash_attn_varlen_func(*dbuf, dcu, dcu, mx, mx, softmax_scale=D ** -0.5, causal=True,
+                                             window_size=(512, 0), softcap=30.0, rotary_cos=cos, rotary_sin=sin),
+                   non_blocking=True)
+
+    e2e_ms = _gpu_ms(e2e, steps, warmup)
+    flops = r5["flops"]
+    # CPU: one query head (and its kv head) over all 16 sequences
+    qn = rng.standard_normal((tot, D), dtype=np.float32)
+    kn = rng.standard_normal((tot, D), dtype=np.float32)
+    vn = rng.standard_normal((tot, D), dtype=np.float32)
+    head_flops = flops / Hq
+
+    def port():
+        for i in range(16):
+            a, b = int(cu_np[i]), int(cu_np[i + 1])
+            O.attention_head(qn[a:b], kn[a:b], vn[a:b], D ** -0.5, causal=True, wl=512, wr=0, softcap=30.0)
+
+    t_port = _wall(port)
+    thr = _torch_cpu_threads()
+
+    def torch_path():
+        for i in range(16):
+            a, b = int(cu_np[i]), int(cu_np[i + 1])
+            x = [torch.from_numpy(t[a:b]).view(1, b - a, 1, D) for t in (qn, kn, vn)]
+            torch_ref.ref_attn(*x, D ** -0.5, causal=True, wl=512, wr=0, softcap=30.0)
+
+    t_torch = _wall(torch_path)
+    nbytes_in = sum(t.numel() * 2 for t in dev_in) + hcu.numel() * 4
+    return {"roofline": _roofline(flops / r5["kernel_ms"] / 1e9, "tensor", peaks,
+                                  note="forward kernel alone (q, k already rotated); FLOP = 4 D Hq x visible pairs"),
+            "e2e": {"value": round(flops / e2e_ms / 1e9, 1), "unit": "TFLOP/s", "ms_per_step": round(e2e_ms, 3),
+                    "h2d_bytes_per_step": int(nbytes_in), "d2h_bytes_per_step": int(hout.numel() * 2),
+                    "step": "flash_attn_varlen_func(rotary_cos/sin fused, window (512,0), softcap 30) from host"},
+            "cpu_baseline": {"value": round(head_flops / t_port / 1e12, 6), "unit": "TFLOP/s",
+                             "cores": os.cpu_count() or 1, "kind": "port",
+                             "sample": f"1 of 64 query heads, all 16 sequences, fp64 banded oracle ({t_port:.1f} s; "
+                                       "rate extrapolates linearly in heads)"},
+            "cpu_baseline_torch_fp32": {"value": round(head_flops / t_torch / 1e12, 6), "unit": "TFLOP/s", "cores": thr,
+                                        "kind": "port", "sample": f"1 of 64 query heads, all 16 sequences, torch fp32 "
+                                                                  f"exact reference ({t_torch:.1f} s)"}}
 
 
 def _barrier(ws):
@@ -545,6 +876,7 @@ def main():
     dev = torch.device("cuda", local if ws > 1 else 0)
     torch.cuda.set_device(dev)
 
+    peaks = _peaks()
     r = bench_fwd_dense(args, ws, rank, dev)
     extra = {}
     if ws > 1 and not args.no_extra:   # every rank takes part (collectives)
@@ -580,27 +912,45 @@ def main():
             except Exception as e:
                 extra["varlen_swa_prefill_sharded"] = {"error": f"{type(e).__name__}: {e}"[:200]}
     if not args.no_extra and rank == 0:
+        def err(e):
+            return {"error": f"{type(e).__name__}: {e}"[:300]}
+        if ws == 1:   # the N=1 point of the decode split (same workload as decode_kv_split at N>1)
+            try:
+                extra["decode_kv_split"] = bench_decode_split(dev, 1, 0)
+            except Exception as e:
+                extra["decode_kv_split"] = err(e)
         try:
-            extra["fwd_bwd_causal"] = bench_fwd_bwd_causal(dev)
-        except Exception as e:  # keep the headline even if a secondary figure fails
-            extra["fwd_bwd_causal"] = {"error": f"{type(e).__name__}: {e}"[:200]}
+            extra["config1_fp32_causal"] = measure_config1(dev, peaks)
+        except Exception as e:
+            extra["config1_fp32_causal"] = err(e)
+        try:   # keep the headline even if a secondary figure fails
+            r3 = bench_fwd_bwd_causal(dev)
+            extra["fwd_bwd_causal"] = r3
+            r3.update(measure_config3(dev, peaks, r3))
+        except Exception as e:
+            extra.setdefault("fwd_bwd_causal", {}).update(err(e))
         try:
             extra["fwd_bwd_causal_no_dropout"] = bench_fwd_bwd_causal(dev, dropout_p=0.0)
         except Exception as e:
-            extra["fwd_bwd_causal_no_dropout"] = {"error": f"{type(e).__name__}: {e}"[:200]}
+            extra["fwd_bwd_causal_no_dropout"] = err(e)
         try:
-            extra["decode_paged"] = bench_decode(dev)
+            r4 = bench_decode(dev)
+            extra["decode_paged"] = r4
+            r4.update(measure_config4(dev, peaks, r4))
         except Exception as e:
-            extra["decode_paged"] = {"error": f"{type(e).__name__}: {e}"[:200]}
+            extra.setdefault("decode_paged", {}).update(err(e))
+        finally:
+            extra.get("decode_paged", {}).pop("_setup", None)
         try:
-            extra["varlen_swa_prefill"] = bench_varlen_swa(dev)
+            r5 = bench_varlen_swa(dev)
+            extra["varlen_swa_prefill"] = r5
+            r5.update(measure_config5(dev, peaks, r5))
         except Exception as e:
-            extra["varlen_swa_prefill"] = {"error": f"{type(e).__name__}: {e}"[:200]}
+            extra.setdefault("varlen_swa_prefill", {}).update(err(e))
     cpu = None
     if rank == 0 and ws == 1:
         val, cores, kind, desc, _ = cpu_reference_sample(seconds=args.cpu_seconds)
         cpu = {"value": round(val, 6), "unit": "TFLOP/s", "cores": cores, "kind": kind, "sample": desc}
-    peaks = _peaks()
     if peaks and peaks.get("bf16_tflops"):
         peak, peak_src = float(peaks["bf16_tflops"]), "MEASURED_PEAKS.json bf16_tflops (burst), of measured"
     else:

@@ -212,5 +212,8 @@ extern "C" int fa_combine_launch(const FaCombineParams* pp, void* stream) {
   FA_CHECK_ARG(p.nsplit >= 1 && p.B >= 0 && p.S >= 0 && p.H >= 0 && p.D > 0, "combine: bad sizes");
   if ((long long)p.B * p.S * p.H == 0) return FA_OK;
   FA_CHECK_ARG((long long)p.B * p.S * p.H < (1LL << 31), "combine: too many rows");
+  FA_CHECK_ARG(p.out_split_stride >= 0 && p.lse_split_stride >= 0 && (p.lse_bsh == 0 || p.lse_bsh == 1),
+               "combine: split strides %lld / %lld must be >= 0 and lse_bsh 0 or 1", p.out_split_stride,
+               p.lse_split_stride);
   return fa::combine_run(p, (cudaStream_t)stream);
 }

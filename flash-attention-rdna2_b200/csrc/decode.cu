@@ -664,19 +664,21 @@ __global__ void combine_kernel(const FaCombineParams p) {
   const int s = (int)(bs % p.S);
   const int b = (int)(bs / p.S);
   const long long rows = (long long)p.B * p.S * p.H;
+  const long long ostride = p.out_split_stride ? p.out_split_stride : rows * p.D;
+  const long long lstride = p.lse_split_stride ? p.lse_split_stride : rows;
+  const long long lrow = p.lse_bsh ? row : ((long long)b * p.H + h) * p.S + s;
   float M = -INFINITY;
-  for (int k = 0; k < p.nsplit; ++k)
-    M = fmaxf(M, p.lse_partial[(((long long)k * p.B + b) * p.H + h) * p.S + s]);
+  for (int k = 0; k < p.nsplit; ++k) M = fmaxf(M, p.lse_partial[k * lstride + lrow]);
   float W = 0.f;
   if (M != -INFINITY)
-    for (int k = 0; k < p.nsplit; ++k) W += expf(p.lse_partial[(((long long)k * p.B + b) * p.H + h) * p.S + s] - M);
+    for (int k = 0; k < p.nsplit; ++k) W += expf(p.lse_partial[k * lstride + lrow] - M);
   const float invW = W > 0.f ? 1.f / W : 0.f;
   for (int d = threadIdx.x; d < p.D; d += blockDim.x) {
     float a = 0.f;
     if (M != -INFINITY)
       for (int k = 0; k < p.nsplit; ++k) {
-        const float w = expf(p.lse_partial[(((long long)k * p.B + b) * p.H + h) * p.S + s] - M);
-        a += w * Elem<TI>::to_f(((const TI*)p.out_partial)[((long long)k * rows + row) * p.D + d]);
+        const float w = expf(p.lse_partial[k * lstride + lrow] - M);
+        a += w * Elem<TI>::to_f(((const TI*)p.out_partial)[k * ostride + row * p.D + d]);
       }
     ((TO*)p.out)[row * p.D + d] = Elem<TO>::from_f(a * invW);
   }

@@ -310,7 +310,8 @@ std::vector<torch::Tensor> dec(torch::Tensor q, torch::Tensor k_cache, torch::Te
                                c10::optional<torch::Tensor> rotary_sin, bool rotary_interleaved, double scale,
                                int64_t window, int64_t num_splits, c10::optional<torch::Tensor> cache_leftpad,
                                bool return_lse, double softcap, c10::optional<torch::Tensor> alibi,
-                               int64_t rotary_dim, c10::optional<torch::Tensor> rotary_pos, bool out_fp32) {
+                               int64_t rotary_dim, c10::optional<torch::Tensor> rotary_pos, bool out_fp32,
+                               c10::optional<torch::Tensor> out_opt, c10::optional<torch::Tensor> lse_opt) {
   TORCH_CHECK_VALUE(q.is_cuda() && k_cache.is_cuda() && v_cache.is_cuda(), "fable_attn: decode needs CUDA tensors");
   TORCH_CHECK_VALUE(q.dim() == 4 && q.is_contiguous(), "fable_attn: decode q must be contiguous [B,nq,Hq,D]");
   TORCH_CHECK_VALUE(k_cache.dim() == 4 && k_cache.is_contiguous() && v_cache.is_contiguous(),
@@ -323,10 +324,29 @@ std::vector<torch::Tensor> dec(torch::Tensor q, torch::Tensor k_cache, torch::Te
   // split count from shapes only (no .item(): no host sync)
   const long long ctx_bound = (long long)block_table.size(1) * page;
   const int nsplit = fa_decode_num_splits(B, NQ, Hk, ctx_bound, (int)num_splits);
-  auto out = torch::empty({B, NQ, Hq, D}, out_fp32 ? q.options().dtype(torch::kFloat32) : q.options());
+  // optional caller-owned destinations (e.g. views of one packed buffer that a single all-gather
+  // sends): out [B, NQ, Hq, D] and lse [B, NQ, Hq], contiguous
+  const auto odt = out_fp32 ? torch::kFloat32 : q.scalar_type();
+  torch::Tensor out;
+  if (out_opt.has_value() && out_opt->defined()) {
+    out = *out_opt;
+    TORCH_CHECK_VALUE(out.is_contiguous() && out.scalar_type() == odt && out.sizes() == q.sizes() &&
+                          out.device() == q.device(),
+                      "fable_attn: decode out must be a contiguous [B, nq, H, D] tensor of the output dtype");
+  } else {
+    out = torch::empty({B, NQ, Hq, D}, q.options().dtype(odt));
+  }
   auto scratch = torch::empty({fa_decode_scratch_floats(B, NQ, Hq, D, nsplit)}, q.options().dtype(torch::kFloat32));
-  auto lse = return_lse ? torch::empty({B, NQ, Hq}, q.options().dtype(torch::kFloat32))
-                        : torch::empty({0}, q.options().dtype(torch::kFloat32));
+  torch::Tensor lse;
+  if (lse_opt.has_value() && lse_opt->defined()) {
+    lse = *lse_opt;
+    TORCH_CHECK_VALUE(return_lse && lse.is_contiguous() && lse.scalar_type() == torch::kFloat32 &&
+                          lse.numel() == (int64_t)B * NQ * Hq && lse.device() == q.device(),
+                      "fable_attn: decode lse must be a contiguous fp32 [B, nq, H] tensor (with return_lse)");
+  } else {
+    lse = return_lse ? torch::empty({B, NQ, Hq}, q.options().dtype(torch::kFloat32))
+                     : torch::empty({0}, q.options().dtype(torch::kFloat32));
+  }
   FaDecParams p{};
   p.struct_size = sizeof(FaDecParams);
   p.q = q.data_ptr(); p.Kc = k_cache.data_ptr(); p.Vc = v_cache.data_ptr();
@@ -372,6 +392,28 @@ std::vector<torch::Tensor> combine(torch::Tensor out_partial, torch::Tensor lse_
   p.nsplit = ns; p.B = B; p.S = S; p.H = H; p.D = D;
   check(fa_combine_launch(&p, cur_stream(out_partial)), "combine");
   return {out, lse};
+}
+
+// LSE-merge of `nsplit` packed partials: buf holds, per split, rows = B*S*H output rows of D fp32
+// values followed by the rows' fp32 LSE in the same (b, s, h) order (one rank's decode partial, as
+// multigpu.decode_kv_split sends it); the merge reads that layout in place.  Returns out (B, S, H, D).
+torch::Tensor combine_packed(torch::Tensor buf, int64_t nsplit, int64_t B, int64_t S, int64_t H, int64_t D,
+                             c10::ScalarType out_dtype) {
+  TORCH_CHECK_VALUE(buf.is_cuda() && buf.is_contiguous() && buf.scalar_type() == torch::kFloat32,
+                    "fable_attn: packed partials must be a contiguous fp32 CUDA tensor");
+  const int64_t rows = B * S * H, per = rows * (D + 1);
+  TORCH_CHECK_VALUE(nsplit >= 1 && buf.numel() == nsplit * per, "fable_attn: packed partials hold ", buf.numel(),
+                    " floats, expected nsplit * B*S*H*(D+1) = ", nsplit * per);
+  const c10::cuda::CUDAGuard guard(buf.device());
+  auto out = torch::empty({B, S, H, D}, buf.options().dtype(out_dtype));
+  FaCombineParams p{};
+  p.struct_size = sizeof(FaCombineParams);
+  p.out_partial = buf.data_ptr(); p.in_dtype = FA_DTYPE_F32;
+  p.lse_partial = buf.data_ptr<float>() + rows * D; p.out = out.data_ptr(); p.out_dtype = dt_of(out);
+  p.nsplit = (int)nsplit; p.B = (int)B; p.S = (int)S; p.H = (int)H; p.D = (int)D;
+  p.out_split_stride = per; p.lse_split_stride = per; p.lse_bsh = 1;
+  check(fa_combine_launch(&p, cur_stream(buf)), "combine (packed)");
+  return out;
 }
 
 }  // namespace
@@ -458,9 +500,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("rotary_interleaved"), py::arg("scale"), py::arg("window"), py::arg("num_splits"),
         py::arg("cache_leftpad") = c10::optional<torch::Tensor>(), py::arg("return_lse") = false,
         py::arg("softcap") = 0.0, py::arg("alibi") = c10::optional<torch::Tensor>(), py::arg("rotary_dim") = 0,
-        py::arg("rotary_pos") = c10::optional<torch::Tensor>(), py::arg("out_fp32") = false);
+        py::arg("rotary_pos") = c10::optional<torch::Tensor>(), py::arg("out_fp32") = false,
+        py::arg("out") = c10::optional<torch::Tensor>(), py::arg("lse_out") = c10::optional<torch::Tensor>());
   m.def("combine", &combine, py::arg("out_partial"), py::arg("lse_partial"), py::arg("out_dtype"),
         py::arg("return_lse") = false);
+  m.def("combine_packed", &combine_packed, py::arg("buf"), py::arg("nsplit"), py::arg("B"), py::arg("S"),
+        py::arg("H"), py::arg("D"), py::arg("out_dtype"));
   m.def("kernel_launch_count", []() { return fa_kernel_launch_count(); });
   m.def("device_error", [](bool clear) { return fa_device_error(clear ? 1 : 0); }, py::arg("clear") = false);
   m.def("wait_selftest", [](int64_t limit_ns) {

@@ -6,9 +6,10 @@ Only two kinds of work are split, and only one of them communicates:
   groups (varlen prefill): `shard_range` gives each rank its contiguous slice; no collective.
 * long-context decode — every sequence's KV range [0, L_b) is cut into `world` contiguous
   chunks; rank r holds the pages of its chunk locally and attends to them, producing a
-  normalised partial output and its LSE.  One all-gather (NCCL over NVLink) brings every rank's
-  (out, lse) pair to every rank, and flash_attn_combine merges them with the LSE rule
-  out = sum_r exp(lse_r - M) out_r / sum_r exp(lse_r - M), M = max_r lse_r.
+  normalised partial output and its LSE, packed into one fp32 buffer.  One all-gather (NCCL over
+  NVLink) brings every rank's packed buffer to every rank, and the merge kernel applies the LSE
+  rule out = sum_r exp(lse_r - M) out_r / sum_r exp(lse_r - M), M = max_r lse_r, reading the
+  gathered buffer in place.
   The reference has no multi-GPU layer; the merge rule is its flash_attn_combine
   (package/fable_attn/flash_attn_interface.py:567-580).
 Remote partials always arrive through NCCL into local buffers: no kernel reads peer memory.
@@ -48,9 +49,14 @@ def local_block_table(block_table, start, end, page):
     return torch.stack(rows).contiguous()
 
 
+def _world(group):
+    return dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+
+
 def gather_partials(out_r, lse_r, group=None):
     """All-gather every rank's partial (out_r (B, nq, H, D), lse_r (B, H, nq) fp32) into
-    (world, B, nq, H, D) and (world, B, H, nq)."""
+    (world, B, nq, H, D) and (world, B, H, nq).  Two collectives; decode_kv_split sends one packed
+    buffer instead (pack_partials / unpack_partials)."""
     world = dist.get_world_size(group)
     # flat (world * dim0, ...) buffers: the layout both NCCL and gloo gather into
     out_all = out_r.new_empty((world * out_r.shape[0],) + tuple(out_r.shape[1:]))
@@ -60,19 +66,67 @@ def gather_partials(out_r, lse_r, group=None):
     return out_all.view((world,) + tuple(out_r.shape)), lse_all.view((world,) + tuple(lse_r.shape))
 
 
+def packed_partial_views(buf, B, nq, H, D):
+    """One rank's packed partial: B*nq*H output rows of D fp32 values, then the rows' fp32 LSE in
+    the same (b, t, h) order.  Returns the (out (B, nq, H, D), lse (B, nq, H)) views of buf."""
+    rows = B * nq * H
+    return buf[:rows * D].view(B, nq, H, D), buf[rows * D:rows * (D + 1)].view(B, nq, H)
+
+
+def pack_partials(out_r, lse_r):
+    """(out (B, nq, H, D), lse (B, nq, H)) fp32 -> one flat fp32 buffer of B*nq*H*(D+1) floats."""
+    return torch.cat([out_r.reshape(-1).float(), lse_r.reshape(-1).float()])
+
+
+def unpack_partials(recv, world, B, nq, H, D):
+    """Gathered packed buffers (world * B*nq*H*(D+1) floats) -> (out (world, B, nq, H, D),
+    lse (world, B, H, nq)): the layout flash_attn_combine takes."""
+    per = recv.view(world, -1)
+    rows = B * nq * H
+    out = per[:, :rows * D].reshape(world, B, nq, H, D)
+    lse = per[:, rows * D:].reshape(world, B, nq, H).transpose(2, 3)
+    return out, lse
+
+
+def exchange(send, group=None):
+    """One all-gather of every rank's packed partial into (world * len) floats (world = 1: send)."""
+    world = _world(group)
+    if world == 1:
+        return send
+    recv = send.new_empty(world * send.numel())
+    dist.all_gather_into_tensor(recv, send, group=group)
+    return recv
+
+
 def decode_kv_split(q, k_cache_local, v_cache_local, block_table_local, local_lengths, softmax_scale=None,
-                    group=None, num_splits=0):
+                    group=None, num_splits=0, phase_events=None):
     """Decode against a context split across ranks (no rotary / alibi / window: those depend on
     the global query position and are served by the single-GPU flash_attn_with_kvcache).
     Each rank passes its local paged cache and local lengths; every rank returns the full
-    output (B, nq, H, D) in q's dtype.  The rank's partial stays fp32 until the LSE merge (its
-    16-bit rounding would otherwise add to the final one)."""
+    output (B, nq, H, D) in q's dtype.
+      1. the decode kernels write this rank's partial output (fp32: its 16-bit rounding would add
+         to the final one) and LSE straight into one packed send buffer;
+      2. one all-gather (NCCL over NVLink) of the packed buffers;
+      3. the merge kernel reads the gathered buffer in place (no unpacking copies).
+    phase_events: optional list of 4 CUDA events recorded at the phase boundaries (timing)."""
     from . import _C
-    from .flash_attn_interface import flash_attn_combine
     scale = softmax_scale if softmax_scale is not None else q.shape[-1] ** -0.5
+    B, nq, H, D = q.shape
     lens = local_lengths.to(device=q.device, dtype=torch.int32).contiguous()
-    out_r, lse_r = _C.dec(q.contiguous(), k_cache_local, v_cache_local, block_table_local.to(torch.int32).contiguous(),
-                          lens, None, None, None, None, False, float(scale), -1, int(num_splits), None, True,
-                          out_fp32=True)
-    out_all, lse_all = gather_partials(out_r, lse_r.transpose(1, 2).contiguous(), group)
-    return flash_attn_combine(out_all, lse_all, out_dtype=q.dtype)
+    send = torch.empty(B * nq * H * (D + 1), device=q.device, dtype=torch.float32)
+    out_v, lse_v = packed_partial_views(send, B, nq, H, D)
+    ev = phase_events or [None] * 4
+    if ev[0] is not None:
+        ev[0].record()
+    _C.dec(q.contiguous(), k_cache_local, v_cache_local, block_table_local.to(torch.int32).contiguous(), lens, None,
+           None, None, None, False, float(scale), -1, int(num_splits), None, True, out_fp32=True, out=out_v,
+           lse_out=lse_v)
+    if ev[1] is not None:
+        ev[1].record()
+    recv = exchange(send, group)
+    if ev[2] is not None:
+        ev[2].record()
+    out = _C.combine_packed(recv, recv.numel() // send.numel(), B, nq, H, D, q.dtype)
+    if ev[3] is not None:
+        ev[3].record()
+    return out

@@ -298,6 +298,12 @@ typedef struct FaCombineParams {
   void* out; int out_dtype;
   float* lse_out;
   int nsplit, B, S, H, D;
+  /* Packed partials, e.g. the buffer one all-gather of every rank's (out, lse) produces (0 = the
+   * contiguous layouts above): out_split_stride = elements from one split's partial output to the
+   * next, lse_split_stride = floats from one split's LSE to the next, lse_bsh = 1 when each split's
+   * LSE rows are ordered (b, s, h) like the output rows instead of (b, h, s). */
+  long long out_split_stride, lse_split_stride;
+  int lse_bsh;
 } FaCombineParams;
 
 FA_API int fa_combine_launch(const FaCombineParams* p, void* stream);

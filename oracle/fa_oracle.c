@@ -55,6 +55,18 @@ void fa_oracle_dropout_mask(uint64_t seed, int h, int SQ, int SK, float p, uint8
     }
 }
 
+/* keep bits for the block rows [q0,q1) x keys [k0,k1) of query head h (problem SQ x SK):
+ * out[(q-q0)*(k1-k0) + (k-k0)] = 1 kept / 0 dropped */
+void fa_oracle_dropout_block(uint64_t seed, int h, int SQ, int SK, float p, int q0, int q1, int k0, int k1,
+                             uint8_t* out) {
+  const int w = k1 - k0;
+  for (int q = q0; q < q1; ++q)
+    for (int k = k0; k < k1; ++k) {
+      const uint64_t idx = ((uint64_t)h * SQ + q) * SK + k;
+      out[(size_t)(q - q0) * w + (k - k0)] = fa_oracle_dropout_mul(seed, idx, p) != 0.0f;
+    }
+}
+
 static int visible(int q, int k, int SQ, int SK, int causal, int wl, int wr, int chunk) {
   const int diag = q + SK - SQ;
   if (k < 0 || k >= SK) return 0;

@@ -51,6 +51,7 @@ def lib():
                                        C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, f32p, f32p] + [
             C.c_int] * 8 + [C.c_double, C.c_double]
         L.fa_oracle_combine.argtypes = [f32p, f32p, f32p, f32p] + [C.c_int] * 5
+        L.fa_oracle_dropout_block.argtypes = [C.c_uint64, C.c_int, C.c_int, C.c_int, C.c_float] + [C.c_int] * 4 + [u8p]
         _LIB = L
     return _LIB
 
@@ -73,6 +74,14 @@ def ref_lib():
 
 
 # ------------------------------------------------------------------ numpy-level helpers
+def dropout_block(seed, h, SQ, SK, p, q0, q1, k0, k1):
+    """Keep bits (1 kept) of rows [q0,q1) x keys [k0,k1) of query head h, as uint8 (q1-q0, k1-k0)."""
+    out = np.empty((max(q1 - q0, 0), max(k1 - k0, 0)), dtype=np.uint8)
+    if out.size:
+        lib().fa_oracle_dropout_block(seed, h, SQ, SK, p, q0, q1, k0, k1, out)
+    return out
+
+
 def philox_r0(seed, idx):
     return int(lib().fa_oracle_philox_r0(seed, idx))
 
@@ -148,6 +157,100 @@ def combine(out_partial, lse_partial):
     lo = np.zeros((B, H, S), dtype=np.float32)
     lib().fa_oracle_combine(op, lp, out, lo, ns, B, S, H, D)
     return out, lo
+
+
+def _key_bounds(rows, SQ, SK, causal, wl, wr, chunk):
+    """Visible key range [lo, hi] of each query row (bottom-right aligned masks), int64 arrays."""
+    diag = rows + (SK - SQ)
+    lo = np.zeros_like(rows)
+    hi = np.full_like(rows, SK - 1)
+    if causal:
+        hi = np.minimum(hi, diag)
+    if wl >= 0:
+        lo = np.maximum(lo, diag - wl)
+    if wr >= 0:
+        hi = np.minimum(hi, diag + wr)
+    if chunk > 0:
+        cs = (np.maximum(diag, 0) // chunk) * chunk
+        lo = np.maximum(lo, cs)
+        hi = np.minimum(hi, cs + chunk - 1)
+    return lo, hi
+
+
+def attention_head(q, k, v, scale, causal=False, wl=-1, wr=-1, softcap=0.0, slope=None, chunk=0, dropout_p=0.0,
+                   seed=0, h=0, do=None, rows=None, block=512):
+    """One (sequence, query head) in float64, vectorised over row blocks: the arithmetic of
+    fa_oracle.c (fwd_row / fa_oracle_backward, i.e. kernels/fa_common.hpp:102-134 and
+    kernels/backward.hip:570-597) for problems too large for the scalar loops.
+      q (SQ, D), k / v (SK, D) float32 holding the tested dtype's values; h = the global query
+      head (the Philox counter is (h*SQ + q)*SK + key); slope = alibi slope of h or None.
+    Returns dict(O (SQ, D), LSE (SQ,)) and, with do (SQ, D), dQ / dK / dV (dK / dV of this query
+    head only: sum them over the heads of a kv group).  rows=(r0, r1) restricts the forward to a
+    row range (no backward then).  Only keys a row block can see are touched, so banded masks
+    (sliding windows) cost O(rows x window)."""
+    q = np.asarray(q, np.float64)
+    k = np.asarray(k, np.float64)
+    v = np.asarray(v, np.float64)
+    SQ, D = q.shape
+    SK = k.shape[0]
+    r_begin, r_end = rows if rows is not None else (0, SQ)
+    if do is not None and rows is not None:
+        raise ValueError("attention_head: the backward needs every row")
+    O = np.zeros((SQ, D))
+    LSE = np.full(SQ, -np.inf)
+    res = {"O": O, "LSE": LSE}
+    if do is not None:
+        do = np.asarray(do, np.float64)
+        dQ, dK, dV = np.zeros((SQ, D)), np.zeros((SK, D)), np.zeros((SK, D))
+        res.update(dQ=dQ, dK=dK, dV=dV)
+    for r0 in range(r_begin, r_end, block):
+        r1 = min(r0 + block, r_end)
+        rr = np.arange(r0, r1, dtype=np.int64)
+        lo, hi = _key_bounds(rr, SQ, SK, causal, wl, wr, chunk)
+        lo, hi = np.maximum(lo, 0), np.minimum(hi, SK - 1)
+        if not (lo <= hi).any():
+            continue
+        k0 = int(lo[lo <= hi].min())
+        k1 = int(hi[lo <= hi].max()) + 1
+        kk = np.arange(k0, k1, dtype=np.int64)
+        vis = (kk[None, :] >= lo[:, None]) & (kk[None, :] <= hi[:, None])
+        g0 = scale * (q[r0:r1] @ k[k0:k1].T)
+        if softcap > 0:
+            t = np.tanh(g0 / softcap)
+            logit, deriv = softcap * t, 1.0 - t * t
+        else:
+            logit, deriv = g0, None
+        if slope is not None:
+            logit = logit + float(slope) * (kk[None, :] - rr[:, None]).astype(np.float64)
+        logit = np.where(vis, logit, -np.inf)
+        mx = logit.max(axis=1, keepdims=True)
+        live = np.isfinite(mx[:, 0])
+        e = np.where(vis, np.exp(logit - np.where(live[:, None], mx, 0.0)), 0.0)
+        ssum = e.sum(axis=1)
+        lse = np.where(live, mx[:, 0] + np.log(np.where(live, ssum, 1.0)), -np.inf)
+        LSE[r0:r1] = lse
+        p = np.where(live[:, None], e / np.where(live, ssum, 1.0)[:, None], 0.0)
+        if dropout_p > 0:
+            z = dropout_block(seed, h, SQ, SK, dropout_p, r0, r1, k0, k1).astype(np.float64)
+            z *= np.float64(np.float32(1.0) / (np.float32(1.0) - np.float32(dropout_p)))
+        else:
+            z = None
+        pz = p * z if z is not None else p
+        O[r0:r1] = pz @ v[k0:k1]
+        if do is None:
+            continue
+        dob = do[r0:r1]
+        Di = (O[r0:r1] * dob).sum(axis=1, keepdims=True)
+        dp = dob @ v[k0:k1].T
+        zdp = dp * z if z is not None else dp
+        ds = p * (zdp - Di)
+        if deriv is not None:
+            ds = ds * deriv
+        ds = np.where(vis, ds, 0.0)
+        dV[k0:k1] += pz.T @ dob
+        dK[k0:k1] += scale * (ds.T @ q[r0:r1])
+        dQ[r0:r1] = scale * (ds @ k[k0:k1])
+    return res
 
 
 def ref_forward(q, k, v, scale, causal=False, wl=-1, wr=-1, softcap=0.0, alibi=None, chunk=0):

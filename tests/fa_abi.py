@@ -58,7 +58,8 @@ class FaDecParams(C.Structure):
 class FaCombineParams(C.Structure):
     _fields_ = [("struct_size", C.c_uint), ("out_partial", C.c_void_p), ("in_dtype", C.c_int),
                 ("lse_partial", C.c_void_p), ("out", C.c_void_p), ("out_dtype", C.c_int), ("lse_out", C.c_void_p),
-                ("nsplit", C.c_int), ("B", C.c_int), ("S", C.c_int), ("H", C.c_int), ("D", C.c_int)]
+                ("nsplit", C.c_int), ("B", C.c_int), ("S", C.c_int), ("H", C.c_int), ("D", C.c_int),
+                ("out_split_stride", C.c_longlong), ("lse_split_stride", C.c_longlong), ("lse_bsh", C.c_int)]
 
 
 _LIB = None

@@ -76,3 +76,71 @@ def test_decode_kv_split_nccl_two_gpus():
         p.join(180)
         assert p.exitcode == 0
     assert len(ret) == 2 and max(ret.values()) < 2.5e-3
+
+
+def _chunked_case(dev, world):
+    """A paged cache and, per emulated rank, its contiguous chunk of every sequence copied into its
+    own pages (what each rank of decode_kv_split holds)."""
+    from fable_attn import multigpu as M
+    B, H, Hk, D, page = 4, 16, 4, 128, 64
+    rng = np.random.default_rng(1)
+    lens = np.array([3000, 640, 1999, 129])
+    nper = int((lens.max() + page - 1) // page)
+    kc = torch.from_numpy(rng.standard_normal((B * nper, page, Hk, D)).astype(np.float32)).to(dev, torch.bfloat16)
+    vc = torch.from_numpy(rng.standard_normal((B * nper, page, Hk, D)).astype(np.float32)).to(dev, torch.bfloat16)
+    bt = torch.from_numpy(rng.permutation(B * nper).astype(np.int32).reshape(B, nper)).to(dev)
+    q = torch.from_numpy(rng.standard_normal((B, 1, H, D)).astype(np.float32)).to(dev, torch.bfloat16)
+    starts, ends = M.plan_kv_split(torch.from_numpy(lens), world)
+    chunks = []
+    for r in range(world):
+        s, e = starts[r], ends[r]
+        loc = (e - s).to(torch.int32)
+        lp = max(int((int(loc.max()) + page - 1) // page), 1)
+        kl = torch.zeros(B * lp, page, Hk, D, device=dev, dtype=torch.bfloat16)
+        vl = torch.zeros_like(kl)
+        for b in range(B):
+            kl.view(B, lp * page, Hk, D)[b, :int(e[b] - s[b])] = kc[bt[b].long()].reshape(-1, Hk, D)[int(s[b]):int(e[b])]
+            vl.view(B, lp * page, Hk, D)[b, :int(e[b] - s[b])] = vc[bt[b].long()].reshape(-1, Hk, D)[int(s[b]):int(e[b])]
+        chunks.append((kl, vl, torch.arange(B * lp, device=dev, dtype=torch.int32).view(B, lp), loc.to(dev)))
+    return q, kc, vc, bt, lens, chunks
+
+
+def test_decode_kv_split_one_process_equals_decode():
+    """The N=1 form of decode_kv_split (no process group: the exchange is the local buffer)."""
+    import fable_attn as fa
+    from fable_attn import multigpu as M
+    dev = torch.device("cuda", 0)
+    q, kc, vc, bt, lens, chunks = _chunked_case(dev, 1)
+    ref = fa.flash_attn_with_kvcache(q, kc, vc, cache_seqlens=torch.from_numpy(lens.astype(np.int32)).to(dev),
+                                     block_table=bt)
+    out = M.decode_kv_split(q, *chunks[0])
+    assert (out.float() - ref.float()).norm() / ref.float().norm() < 2.5e-3
+
+
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_packed_partials_merge_in_place(world):
+    """What every rank of decode_kv_split computes after its all-gather, with the ranks emulated as
+    context chunks on one GPU: each chunk's decode writes its packed (out, lse) buffer, the buffers
+    are concatenated in rank order (the all-gather's layout) and merged in place."""
+    import fable_attn as fa
+    from fable_attn import _C
+    from fable_attn import multigpu as M
+    dev = torch.device("cuda", 0)
+    q, kc, vc, bt, lens, chunks = _chunked_case(dev, world)
+    ref = fa.flash_attn_with_kvcache(q, kc, vc, cache_seqlens=torch.from_numpy(lens.astype(np.int32)).to(dev),
+                                     block_table=bt)
+    B, nq, H, D = q.shape
+    sends = []
+    for kl, vl, btl, loc in chunks:
+        send = torch.empty(B * nq * H * (D + 1), device=dev, dtype=torch.float32)
+        o_v, l_v = M.packed_partial_views(send, B, nq, H, D)
+        _C.dec(q, kl, vl, btl, loc, None, None, None, None, False, D ** -0.5, -1, 0, None, True, out_fp32=True,
+               out=o_v, lse_out=l_v)
+        sends.append(send)
+    recv = torch.cat(sends)
+    out = _C.combine_packed(recv, world, B, nq, H, D, q.dtype)
+    assert (out.float() - ref.float()).norm() / ref.float().norm() < 2.5e-3
+    # the same merge through flash_attn_combine on the unpacked layout agrees bitwise
+    o_all, l_all = M.unpack_partials(recv, world, B, nq, H, D)
+    out2 = fa.flash_attn_combine(o_all.contiguous(), l_all.contiguous(), out_dtype=q.dtype)
+    assert torch.equal(out, out2)

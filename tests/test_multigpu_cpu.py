@@ -48,8 +48,15 @@ def _worker(rank, world, port, ret):
             kl[b, : e[b] - s[b]] = full_k[s[b]:e[b]]
             vl[b, : e[b] - s[b]] = full_v[s[b]:e[b]]
         o_r, l_r = O.decode(q, kl, vl, np.arange(B, dtype=np.int32)[:, None], (e - s).astype(np.int32))
-        out_all, lse_all = M.gather_partials(torch.from_numpy(o_r), torch.from_numpy(l_r).transpose(1, 2).contiguous())
+        # the exchange decode_kv_split makes: one packed (out rows, LSE) buffer per rank, one all-gather
+        send = M.pack_partials(torch.from_numpy(o_r), torch.from_numpy(l_r))
+        views = M.packed_partial_views(send, B, 1, H, D)
+        assert np.array_equal(views[0].numpy(), o_r) and np.array_equal(views[1].numpy(), l_r)
+        out_all, lse_all = M.unpack_partials(M.exchange(send), world, B, 1, H, D)
         merged, _ = O.combine(out_all.numpy(), lse_all.numpy())
+        # and the two-collective form agrees with it
+        out2, lse2 = M.gather_partials(torch.from_numpy(o_r), torch.from_numpy(l_r).transpose(1, 2).contiguous())
+        assert torch.equal(out2, out_all) and torch.equal(lse2, lse_all)
         ref, _ = O.decode(q, kc, vc, bt, lens)
         ret[rank] = float(np.abs(merged - ref).max())
     finally:
