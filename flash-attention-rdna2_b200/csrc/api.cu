@@ -45,6 +45,14 @@ int num_sms() {
   return cached[d];
 }
 
+// FABLE_ATTN_REQUIRE_TC=1: fp16/bf16 forward / backward requests that the tensor-core kernels do
+// not take fail with FA_ERR_UNSUPPORTED instead of running on the CUDA-core kernels (lets a caller,
+// or a test, be sure which kernels ran)
+bool require_tc() {
+  const char* v = getenv("FABLE_ATTN_REQUIRE_TC");
+  return v && v[0] && v[0] != '0';
+}
+
 int ensure_smem(const void* func, int bytes, unsigned long long* done_mask) {
   const int d = current_device();
   const unsigned long long bit = 1ull << (d & 63);
@@ -116,10 +124,15 @@ extern "C" int fa_forward_launch(const FaFwdParams* pp, int dtype, void* stream)
   if (dtype != FA_DTYPE_F32) {
     const int rc = fa::fwd_sm100(p, dtype, st, &taken);
     if (taken || rc) return rc;
+    if (fa::require_tc()) {
+      set_error("forward: FABLE_ATTN_REQUIRE_TC is set and the tensor-core kernels do not take this request "
+                "(head_dim=%d, alignment or strides)", p.HD);
+      return FA_ERR_UNSUPPORTED;
+    }
   }
   if (p.rot_cos) {
-    set_error("forward: in-kernel rotary needs the tensor-core path (fp16/bf16, head_dim 64 or 128, 16-byte "
-              "aligned rows); rotate q with fa_rotary_launch instead");
+    set_error("forward: in-kernel rotary needs the tensor-core path (fp16/bf16, head_dim a multiple of 16 up to "
+              "256, 16-byte aligned rows); rotate q with fa_rotary_launch instead");
     return FA_ERR_UNSUPPORTED;
   }
   return fa::fwd_simt(p, dtype, st);
@@ -147,6 +160,11 @@ extern "C" int fable_attn_backward_launch(const FaBwdParams* pp, int dtype, void
   bool taken = false;
   const int rc = fa::bwd_sm100(p, dtype, (cudaStream_t)stream, &taken);
   if (taken || rc) return rc;
+  if (dtype != FA_DTYPE_F32 && fa::require_tc()) {
+    set_error("backward: FABLE_ATTN_REQUIRE_TC is set and the tensor-core kernels do not take this request "
+              "(head_dim=%d, alignment or strides)", p.D);
+    return FA_ERR_UNSUPPORTED;
+  }
   return fa::bwd_simt(p, dtype, (cudaStream_t)stream);
 }
 

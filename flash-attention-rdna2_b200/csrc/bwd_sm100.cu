@@ -88,6 +88,41 @@ __device__ __forceinline__ void split2p(float2 d, uint32_t& hi, uint32_t& lo) {
   lo = pack2<BF16>(r.x, r.y);
 }
 
+// Per-sequence geometry: dense uses the batch index z; varlen reads the token offsets and lengths
+// of sequence z from cu_seqlens (clipped by seqused) and addresses the packed (total, H, D) rows.
+struct BwdGeom {
+  int SQ, SK;        // this sequence's lengths
+  int qtok0, ktok0;  // first token of the sequence in the packed q / k (varlen), else 0
+  int bcoord;        // batch coordinate of the 4-D TMA maps (0 for varlen)
+};
+__device__ __forceinline__ BwdGeom bwd_geom(const FaBwdParams& p, int z) {
+  BwdGeom g{p.SQ, p.SK, 0, 0, z};
+  if (p.cu_q) {
+    g.qtok0 = p.cu_q[z];
+    g.ktok0 = p.cu_k[z];
+    g.SQ = p.cu_q[z + 1] - g.qtok0;
+    g.SK = p.cu_k[z + 1] - g.ktok0;
+    if (p.seqused_q && p.seqused_q[z] < g.SQ) g.SQ = p.seqused_q[z];
+    if (p.seqused_k && p.seqused_k[z] < g.SK) g.SK = p.seqused_k[z];
+    g.SQ = max(g.SQ, 0);
+    g.SK = max(g.SK, 0);
+    g.bcoord = 0;
+  }
+  return g;
+}
+
+// Varlen tiles can hold rows of the next sequence (or unused rows past seqused): the warp zeroes
+// tile rows [r0, rows) of a [rows][D] tile (D/64 chunks of rows x 128 B) so that a probability or
+// dS of 0 never meets a non-finite value in an MMA.  Generic-proxy stores, then the fence that
+// makes them visible to the tensor core.
+template <int D>
+__device__ __forceinline__ void zero_tile_rows(uint8_t* tile, int rows, int r0, int lane) {
+  constexpr int NCH = D / 64;
+  for (int c = 0; c < NCH; ++c)   // rows [r0, rows) of every 64-column chunk, 16 bytes per lane
+    for (int e = r0 * 8 + lane; e < rows * 8; e += 32)
+      *reinterpret_cast<uint4*>(tile + c * rows * 128 + (e / 8) * 128 + (e % 8) * 16) = make_uint4(0, 0, 0, 0);
+}
+
 // K-major / MN-major descriptors of a [rows][D] tile stored as D/64 chunks of rows x 128 B
 // (TMA SWIZZLE_128B boxes).  kstep = 16-element step along the contracted dimension.
 __device__ __forceinline__ uint64_t desc_kmajor(uint32_t tile, int rows, int kstep) {
@@ -134,7 +169,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int z = blockIdx.z, h = blockIdx.y, kvh = h / p.gqa;
-  const int SQ = p.SQ, SK = p.SK;
+  const bool varlen = p.cu_q != nullptr;
+  const BwdGeom g = bwd_geom(p, z);
+  const int SQ = g.SQ, SK = g.SK;
   const int qb = (gridDim.x - 1 - blockIdx.x) * BM;
   if (qb >= SQ) return;
 
@@ -176,19 +213,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (lane == 0 && ntiles > 0) {
       mbar_expect_tx(bar + Bz::Q_FULL, 2 * C::Q_BYTES);
       for (int c = 0; c < C::NCH; ++c) {
-        tma_load_4d(sQ + c * BM * 128, &tmQ, c * 64, qb, h, z, bar + Bz::Q_FULL);
-        tma_load_4d(sDO + c * BM * 128, &tmDO, c * 64, qb, h, z, bar + Bz::Q_FULL);
+        tma_load_4d(sQ + c * BM * 128, &tmQ, c * 64, g.qtok0 + qb, h, g.bcoord, bar + Bz::Q_FULL);
+        tma_load_4d(sDO + c * BM * 128, &tmDO, c * 64, g.qtok0 + qb, h, g.bcoord, bar + Bz::Q_FULL);
       }
       for (int j = 0; j < ntiles; ++j) {
-        const int s = j % C::NS, krow = (t0 + j) * BN;
+        const int s = j % C::NS, krow = g.ktok0 + (t0 + j) * BN;
         if (j >= C::NS && !mbar_wait(bar + Bz::K_EMPTY + 8 * s, ((j / C::NS) - 1) & 1)) { record_error(1); break; }
         mbar_expect_tx(bar + Bz::K_FULL + 8 * s, C::KV_BYTES);
         for (int c = 0; c < C::NCH; ++c)
-          tma_load_4d(sK + s * C::KV_BYTES + c * BN * 128, &tmK, c * 64, krow, kvh, z, bar + Bz::K_FULL + 8 * s);
+          tma_load_4d(sK + s * C::KV_BYTES + c * BN * 128, &tmK, c * 64, krow, kvh, g.bcoord, bar + Bz::K_FULL + 8 * s);
         if (j >= C::NS && !mbar_wait(bar + Bz::V_EMPTY + 8 * s, ((j / C::NS) - 1) & 1)) { record_error(1); break; }
         mbar_expect_tx(bar + Bz::V_FULL + 8 * s, C::KV_BYTES);
         for (int c = 0; c < C::NCH; ++c)
-          tma_load_4d(sV + s * C::KV_BYTES + c * BN * 128, &tmV, c * 64, krow, kvh, z, bar + Bz::V_FULL + 8 * s);
+          tma_load_4d(sV + s * C::KV_BYTES + c * BN * 128, &tmV, c * 64, krow, kvh, g.bcoord, bar + Bz::V_FULL + 8 * s);
       }
       for (int j = max(0, ntiles - C::NS); j < ntiles; ++j) {
         mbar_wait(bar + Bz::K_FULL + 8 * (j % C::NS), (j / C::NS) & 1);
@@ -224,6 +261,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const int s = j % C::NS;
       if (!mbar_wait_warp(bar + Bz::K_FULL + 8 * s, (j / C::NS) & 1) ||
           !mbar_wait_warp(bar + Bz::V_FULL + 8 * s, (j / C::NS) & 1)) { ok = false; break; }
+      const int kb = (t0 + j) * BN;
+      if (varlen && kb + BN > SK) {   // key rows past the sequence: zero (dQ += dS K reads K)
+        zero_tile_rows<D>(sgen + C::OFF_K + s * C::KV_BYTES, BN, max(SK - kb, 0), lane);
+        zero_tile_rows<D>(sgen + C::OFF_V + s * C::KV_BYTES, BN, max(SK - kb, 0), lane);
+        fence_proxy_async_smem();
+        __syncwarp();
+      }
       tc_fence_after();
       if (lane == 0) {
         const uint32_t kt = sK + s * C::KV_BYTES, vt = sV + s * C::KV_BYTES;
@@ -253,7 +297,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     fa_key_range(q, SQ, SK, p.causal, p.win_left, p.win_right, 0, rlo, rhi);
     float lse2 = 0.f, dsum = 0.f;
     if (q < SQ) {
-      const long long li = fa_lse_index(false, z, h, p.Hq, SQ, 0, 0, q);
+      const long long li = fa_lse_index(varlen, z, h, p.Hq, p.SQ, g.qtok0, p.lse_total_q, q);
       lse2 = p.lse[li] * FA_LOG2E;
       dsum = p.dsum[li];
       if (!(lse2 > -INFINITY)) { rlo = 1; rhi = 0; }   // row saw no key in the forward
@@ -385,7 +429,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (have && !mbar_wait_warp(bar + Bz::DQ_DONE, 0)) record_error(16);
     tc_fence_after();
     using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-    T* qrow = (T*)p.dQ + (long long)z * p.dqs.b + (long long)h * p.dqs.h + (long long)q * p.dqs.s + hf * (D / 2);
+    T* qrow = (T*)p.dQ + (varlen ? (long long)g.qtok0 * p.dqs.s : (long long)z * p.dqs.b) + (long long)h * p.dqs.h +
+              (long long)q * p.dqs.s + hf * (D / 2);
 #pragma unroll
     for (int c = 0; c < D / 2; c += 32) {
       float o[32];
@@ -401,8 +446,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
         for (int i = 0; i < 16; ++i) w[i] = pack2<BF16>(o[2 * i] * p.scale, o[2 * i + 1] * p.scale);
         uint4* dst = reinterpret_cast<uint4*>(qrow + c);
+        // 8-column units; columns at or past the real head_dim are padding (never stored)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+        for (int i = 0; i < 4; ++i)
+          if (hf * (D / 2) + c + 8 * i < p.D) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
       }
     }
   }
@@ -451,7 +498,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int z = blockIdx.z, kvh = blockIdx.y;
-  const int SQ = p.SQ, SK = p.SK;
+  const bool varlen = p.cu_q != nullptr;
+  const BwdGeom g = bwd_geom(p, z);
+  const int SQ = g.SQ, SK = g.SK;
   const int kb = blockIdx.x * BK;
   if (kb >= SK) return;
 
@@ -492,16 +541,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (lane == 0 && niter > 0) {
       mbar_expect_tx(bar + Bz::KV_FULL, 2 * C::KV_BYTES);
       for (int c = 0; c < C::NCH; ++c) {
-        tma_load_4d(sK + c * BK * 128, &tmK, c * 64, kb, kvh, z, bar + Bz::KV_FULL);
-        tma_load_4d(sV + c * BK * 128, &tmV, c * 64, kb, kvh, z, bar + Bz::KV_FULL);
+        tma_load_4d(sK + c * BK * 128, &tmK, c * 64, g.ktok0 + kb, kvh, g.bcoord, bar + Bz::KV_FULL);
+        tma_load_4d(sV + c * BK * 128, &tmV, c * 64, g.ktok0 + kb, kvh, g.bcoord, bar + Bz::KV_FULL);
       }
       for (int i = 0; i < niter; ++i) {
-        const int s = i % C::NS, h = kvh * p.gqa + i / nqt, qrow = (qt0 + i % nqt) * BQ;
+        const int s = i % C::NS, h = kvh * p.gqa + i / nqt, qrow = g.qtok0 + (qt0 + i % nqt) * BQ;
         if (i >= C::NS && !mbar_wait(bar + Bz::Q_EMPTY + 8 * s, ((i / C::NS) - 1) & 1)) { record_error(1); break; }
         mbar_expect_tx(bar + Bz::Q_FULL + 8 * s, 2 * C::QT_BYTES);
         for (int c = 0; c < C::NCH; ++c) {
-          tma_load_4d(sQ + s * C::QT_BYTES + c * BQ * 128, &tmQ, c * 64, qrow, h, z, bar + Bz::Q_FULL + 8 * s);
-          tma_load_4d(sDO + s * C::QT_BYTES + c * BQ * 128, &tmDO, c * 64, qrow, h, z, bar + Bz::Q_FULL + 8 * s);
+          tma_load_4d(sQ + s * C::QT_BYTES + c * BQ * 128, &tmQ, c * 64, qrow, h, g.bcoord, bar + Bz::Q_FULL + 8 * s);
+          tma_load_4d(sDO + s * C::QT_BYTES + c * BQ * 128, &tmDO, c * 64, qrow, h, g.bcoord, bar + Bz::Q_FULL + 8 * s);
         }
       }
       for (int i = max(0, niter - C::NS); i < niter; ++i) mbar_wait(bar + Bz::Q_FULL + 8 * (i % C::NS), (i / C::NS) & 1);
@@ -534,6 +583,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     for (int i = 0; ok && i < niter; ++i) {
       const int s = i % C::NS;
       if (!mbar_wait_warp(bar + Bz::Q_FULL + 8 * s, (i / C::NS) & 1)) { ok = false; break; }
+      const int qbase = (qt0 + i % nqt) * BQ;
+      if (varlen && qbase + BQ > SQ) {   // query rows past the sequence: zero (dV, dK sum over rows)
+        zero_tile_rows<D>(sgen + C::OFF_Q + s * C::QT_BYTES, BQ, max(SQ - qbase, 0), lane);
+        zero_tile_rows<D>(sgen + C::OFF_DO + s * C::QT_BYTES, BQ, max(SQ - qbase, 0), lane);
+        fence_proxy_async_smem();
+        __syncwarp();
+      }
       tc_fence_after();
       if (lane == 0) {
         const uint32_t qt = sQ + s * C::QT_BYTES, dot = sDO + s * C::QT_BYTES;
@@ -605,7 +661,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const int qi = tid & 63, q = qbase + qi;
         float v = 0.f;
         if (q < SQ) {
-          const long long li = fa_lse_index(false, z, h, p.Hq, SQ, 0, 0, q);
+          const long long li = fa_lse_index(varlen, z, h, p.Hq, p.SQ, g.qtok0, p.lse_total_q, q);
           if (tid < 64) {
             const float l = p.lse[li];
             v = (l > -INFINITY) ? -l * FA_LOG2E : -INFINITY;
@@ -663,8 +719,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 logit = s[cc] * p.scale;
               }
               const float pr = vis ? ex2(fmaf(logit, FA_LOG2E, nl2)) : 0.f;
-              const float zm = drop ? (((cw[h32 / 32] >> (c + u)) & 1u) ? p.keep_scale : 0.f) : 1.f;
-              pv[u] = zm * pr;
+              const bool kept = !drop || ((cw[h32 / 32] >> (c + u)) & 1u);
+              const float zm = drop ? (kept ? p.keep_scale : 0.f) : 1.f;
+              pv[u] = kept ? pr : 0.f;   // Z P unscaled: dV gets 1/(1-p) in fp32 (epilogue)
               dsv[u] = pr * (zm * dp[cc] + stb[64 + 32 * hf + cc]) * deriv;
             }
             pk[c / 2] = pack2<BF16>(pv[0], pv[1]);
@@ -691,17 +748,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             b = (qh + c + 1 >= qlo && qh + c + 1 <= qhi) ? b : 0.f;
           }
           const float2 pr = make_float2(a, b), dp2 = make_float2(dp[c], dp[c + 1]);
-          float2 pv = pr, dsv;
-          if constexpr (kDrop) {   // P~ = Z P by a sign-extended keep bit; dS = P~ dP - P D
+          float2 pm = pr, dsv;
+          if constexpr (kDrop) {   // Z P by a sign-extended keep bit; dS = (Z P / (1-p)) dP - P D
             const uint32_t m0 = (uint32_t)((int32_t)(cw[0] << (31 - c)) >> 31);
             const uint32_t m1 = (uint32_t)((int32_t)(cw[0] << (30 - c)) >> 31);
-            pv = __fmul2_rn(make_float2(__uint_as_float(__float_as_uint(a) & m0), __uint_as_float(__float_as_uint(b) & m1)),
-                            make_float2(p.keep_scale, p.keep_scale));
-            dsv = __ffma2_rn(pr, nds, __fmul2_rn(pv, dp2));
+            pm = make_float2(__uint_as_float(__float_as_uint(a) & m0), __uint_as_float(__float_as_uint(b) & m1));
+            dsv = __ffma2_rn(pr, nds, __fmul2_rn(__fmul2_rn(pm, make_float2(p.keep_scale, p.keep_scale)), dp2));
           } else {
             dsv = __fmul2_rn(pr, __fadd2_rn(dp2, nds));
           }
-          pk[c / 2] = pack2<BF16>(pv.x, pv.y);
+          pk[c / 2] = pack2<BF16>(pm.x, pm.y);   // Z P unscaled: dV gets 1/(1-p) in fp32 (epilogue)
           split2p<BF16>(dsv, hi[c / 2], lo[c / 2]);
         }
         tmem_st16(la + C::S_COL + (i & 1) * 64 + 32 * hf, pk);
@@ -730,12 +786,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (have && !mbar_wait_warp(bar + Bz::DONE, 0)) record_error(256);
     tc_fence_after();
     using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-    T* vrow = (T*)p.dV + (long long)z * p.dvs.b + (long long)kvh * p.dvs.h + (long long)key * p.dvs.s + hf * (D / 2);
-    T* krow = (T*)p.dK + (long long)z * p.dks.b + (long long)kvh * p.dks.h + (long long)key * p.dks.s + hf * (D / 2);
+    T* vrow = (T*)p.dV + (varlen ? (long long)g.ktok0 * p.dvs.s : (long long)z * p.dvs.b) + (long long)kvh * p.dvs.h +
+              (long long)key * p.dvs.s + hf * (D / 2);
+    T* krow = (T*)p.dK + (varlen ? (long long)g.ktok0 * p.dks.s : (long long)z * p.dks.b) + (long long)kvh * p.dks.h +
+              (long long)key * p.dks.s + hf * (D / 2);
 #pragma unroll
     for (int part = 0; part < 2; ++part) {
       const uint32_t col = (part == 0 ? C::DV_COL : C::DK_COL) + hf * (D / 2);
-      const float mul = part == 0 ? 1.f : p.scale;
+      const float mul = part == 0 ? (drop ? p.keep_scale : 1.f) : p.scale;
       T* row = part == 0 ? vrow : krow;
 #pragma unroll
       for (int c = 0; c < D / 2; c += 32) {
@@ -752,8 +810,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
           for (int i = 0; i < 16; ++i) w[i] = pack2<BF16>(o[2 * i] * mul, o[2 * i + 1] * mul);
           uint4* dst = reinterpret_cast<uint4*>(row + c);
+          // 8-column units; columns at or past the real head_dim are padding (never stored)
 #pragma unroll
-          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+          for (int i = 0; i < 4; ++i)
+            if (hf * (D / 2) + c + 8 * i < p.D) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
         }
       }
     }
@@ -799,56 +859,68 @@ bool out_ok(const void* ptr, const FaStrides& s, int B) {
   return ((uintptr_t)ptr) % 16 == 0 && s.s % 8 == 0 && s.h % 8 == 0 && (B <= 1 || s.b % 8 == 0);
 }
 
-template <bool BF16, bool FEAT>
+template <int D, bool BF16, bool FEAT>
 int launch_all(const FaBwdParams& p, cudaStream_t st, const CUtensorMap* maps) {
   const CUtensorMap &mq128 = maps[0], &mdo128 = maps[1], &mk64 = maps[2], &mv64 = maps[3];
   const CUtensorMap &mq64 = maps[4], &mdo64 = maps[5], &mk128 = maps[6], &mv128 = maps[7];
-  using Cq = DqCfg<128>;
-  using Ck = DkvCfg<128>;
+  using Cq = DqCfg<D>;
+  using Ck = DkvCfg<D>;
   static unsigned long long done_q = 0, done_k = 0;
-  if (int rc = fa::ensure_smem((const void*)bwd_dq_tc_kernel<128, BF16, FEAT>, Cq::SMEM, &done_q)) return rc;
-  if (int rc = fa::ensure_smem((const void*)bwd_dkdv_tc_kernel<128, BF16, FEAT>, Ck::SMEM, &done_k)) return rc;
-  bwd_dkdv_tc_kernel<128, BF16, FEAT><<<dim3((p.SK + Ck::BK - 1) / Ck::BK, p.Hk, p.B), NTHREADS, Ck::SMEM, st>>>(
+  if (int rc = fa::ensure_smem((const void*)bwd_dq_tc_kernel<D, BF16, FEAT>, Cq::SMEM, &done_q)) return rc;
+  if (int rc = fa::ensure_smem((const void*)bwd_dkdv_tc_kernel<D, BF16, FEAT>, Ck::SMEM, &done_k)) return rc;
+  bwd_dkdv_tc_kernel<D, BF16, FEAT><<<dim3((p.SK + Ck::BK - 1) / Ck::BK, p.Hk, p.B), NTHREADS, Ck::SMEM, st>>>(
       mq64, mdo64, mk128, mv128, p);
-  bwd_dq_tc_kernel<128, BF16, FEAT><<<dim3((p.SQ + Cq::BM - 1) / Cq::BM, p.Hq, p.B), NTHREADS, Cq::SMEM, st>>>(
+  bwd_dq_tc_kernel<D, BF16, FEAT><<<dim3((p.SQ + Cq::BM - 1) / Cq::BM, p.Hq, p.B), NTHREADS, Cq::SMEM, st>>>(
       mq128, mdo128, mk64, mv64, p);
   fa::count_launch(2);
   return fa::cuda_status(cudaGetLastError(), "bwd_sm100 launch");
+}
+
+template <bool BF16, bool FEAT>
+int launch_d(const FaBwdParams& p, cudaStream_t st, const CUtensorMap* maps) {
+  return p.D <= 64 ? launch_all<64, BF16, FEAT>(p, st, maps) : launch_all<128, BF16, FEAT>(p, st, maps);
 }
 
 }  // namespace
 
 namespace fa {
 
-// fp16/bf16, dense (no varlen), head_dim 128, 16-byte aligned rows: dsum on the CUDA cores, then
-// the dK/dV and dQ tensor-core kernels.  Anything else: *taken = false.
+// fp16/bf16, dense or varlen, head_dim a multiple of 16 up to 128 (tiles of 64 or 128 columns,
+// the columns past head_dim zero-filled by the TMA), 16-byte aligned rows: dsum on the CUDA
+// cores, then the dK/dV and dQ tensor-core kernels.  Anything else: *taken = false.
 int bwd_sm100(const FaBwdParams& p, int dtype, cudaStream_t st, bool* taken) {
   *taken = false;
-  if (p.D != 128 || p.cu_q != nullptr || dtype == FA_DTYPE_F32) return FA_OK;
+  if (p.D % 16 != 0 || p.D < 16 || p.D > 128 || dtype == FA_DTYPE_F32) return FA_OK;
   if (getenv("FABLE_ATTN_DISABLE_TC")) return FA_OK;
   int dev = current_device(), major = 0, minor = 0;
   cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
   cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
   if (major != 10 || minor != 0) return FA_OK;
   const bool bf16 = dtype == FA_DTYPE_BF16;
+  const bool varlen = p.cu_q != nullptr;
+  // varlen tensors are (total, H, D): 4-D maps with one batch entry whose rows are the packed
+  // tokens, bounded by the true row counts (rows past the last token read as zeros)
+  if (varlen && (p.lse_total_q <= 0 || p.total_k <= 0)) return FA_OK;
+  const long long rq = varlen ? p.lse_total_q : p.SQ, rk = varlen ? p.total_k : p.SK;
+  const int nb = varlen ? 1 : p.B;
   CUtensorMap maps[8];
-  if (!map4(&maps[0], p.Q, bf16, p.D, p.SQ, p.Hq, p.B, p.qs, 128) ||
-      !map4(&maps[1], p.dO, bf16, p.D, p.SQ, p.Hq, p.B, p.dos, 128) ||
-      !map4(&maps[2], p.K, bf16, p.D, p.SK, p.Hk, p.B, p.ks, 64) ||
-      !map4(&maps[3], p.V, bf16, p.D, p.SK, p.Hk, p.B, p.vs, 64) ||
-      !map4(&maps[4], p.Q, bf16, p.D, p.SQ, p.Hq, p.B, p.qs, 64) ||
-      !map4(&maps[5], p.dO, bf16, p.D, p.SQ, p.Hq, p.B, p.dos, 64) ||
-      !map4(&maps[6], p.K, bf16, p.D, p.SK, p.Hk, p.B, p.ks, 128) ||
-      !map4(&maps[7], p.V, bf16, p.D, p.SK, p.Hk, p.B, p.vs, 128))
+  if (!map4(&maps[0], p.Q, bf16, p.D, rq, p.Hq, nb, p.qs, 128) ||
+      !map4(&maps[1], p.dO, bf16, p.D, rq, p.Hq, nb, p.dos, 128) ||
+      !map4(&maps[2], p.K, bf16, p.D, rk, p.Hk, nb, p.ks, 64) ||
+      !map4(&maps[3], p.V, bf16, p.D, rk, p.Hk, nb, p.vs, 64) ||
+      !map4(&maps[4], p.Q, bf16, p.D, rq, p.Hq, nb, p.qs, 64) ||
+      !map4(&maps[5], p.dO, bf16, p.D, rq, p.Hq, nb, p.dos, 64) ||
+      !map4(&maps[6], p.K, bf16, p.D, rk, p.Hk, nb, p.ks, 128) ||
+      !map4(&maps[7], p.V, bf16, p.D, rk, p.Hk, nb, p.vs, 128))
     return FA_OK;
-  if (!out_ok(p.dQ, p.dqs, p.B) || !out_ok(p.dK, p.dks, p.B) || !out_ok(p.dV, p.dvs, p.B)) return FA_OK;
+  if (!out_ok(p.dQ, p.dqs, nb) || !out_ok(p.dK, p.dks, nb) || !out_ok(p.dV, p.dvs, nb)) return FA_OK;
   *taken = true;
   if (int rc = bwd_dsum(p, dtype, st)) return rc;
   if (p.dropout && p.dropout_bits && p.dropout_bits_t)
     if (int rc = dropout_mask_transpose(p.dropout_bits, p.dropout_bits_t, p.Hq, p.SQ, p.SK, st)) return rc;
   const bool feat = p.softcap > 0.f || p.alibi != nullptr || p.dropout;
-  if (bf16) return feat ? launch_all<true, true>(p, st, maps) : launch_all<true, false>(p, st, maps);
-  return feat ? launch_all<false, true>(p, st, maps) : launch_all<false, false>(p, st, maps);
+  if (bf16) return feat ? launch_d<true, true>(p, st, maps) : launch_d<true, false>(p, st, maps);
+  return feat ? launch_d<false, true>(p, st, maps) : launch_d<false, false>(p, st, maps);
 }
 
 int bwd_device_error(int clear) {

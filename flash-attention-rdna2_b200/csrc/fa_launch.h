@@ -22,6 +22,7 @@ int dec_tc_device_error(int clear);
 int rot_device_error(int clear);
 int fwd_simt_device_error(int clear);   // bit 0: an invalid block-table entry (paged forward)   // bit 0: a rotary position outside the cos/sin table
 int num_sms();
+bool require_tc();   // FABLE_ATTN_REQUIRE_TC set: no CUDA-core fallback for fp16/bf16 fwd / bwd
 
 int current_device();
 // Raise the dynamic shared-memory limit of `func` to `bytes` once per device.

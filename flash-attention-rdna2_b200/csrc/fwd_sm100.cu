@@ -1,7 +1,8 @@
 // fwd_sm100.cu — exact attention forward on the Blackwell tensor cores (tcgen05 + TMEM + TMA).
 //
 // Two kernels.  fwd_tc_kernel (below) takes one 128-row query tile per CTA and every feature
-// (softcap, alibi, dropout, varlen, paged K/V, in-kernel rotary of Q, head_dim 64 or 128);
+// (softcap, alibi, dropout, varlen, paged K/V, in-kernel rotary of Q, every head_dim: tiles of 64,
+// 128 or 256 columns with the columns past head_dim zero-filled by the TMA);
 // fwd_pp_kernel (further down) takes two query tiles per CTA for dense head_dim-128 requests
 // without softcap / alibi (dropout from a precomputed mask), and is chosen when its half-as-many
 // CTAs do not cost whole waves (launch_d).
@@ -58,10 +59,13 @@ __device__ __forceinline__ void bar_sync_pair(uint32_t id) { asm volatile("bar.s
 
 __device__ int g_fwd_error = 0;       // non-zero after a pipeline wait timed out
 
+// D is the tile width (64, 128 or 256); the request's head_dim p.HD may be smaller (a multiple of
+// 16): the TMA maps span only p.HD columns, so the columns past it land as zeros (adding nothing
+// to Q.K^T and giving zero O columns), and the epilogue stores only the real columns.
 template <int D>
 struct Cfg {
-  static constexpr int NSK = (D <= 64) ? 4 : 2;                // K ring depth (freed after S)
-  static constexpr int NSV = (D <= 64) ? 4 : 3;                // V ring depth (freed after PV)
+  static constexpr int NSK = (D <= 64) ? 4 : (D <= 128 ? 2 : 1);   // K ring depth (freed after S)
+  static constexpr int NSV = (D <= 64) ? 4 : (D <= 128 ? 3 : 1);   // V ring depth (freed after PV)
   static constexpr int NCH = D / 64;                           // 64-column (128-byte) chunks per row
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int KV_BYTES = BN * D * 2;                  // one K (or V) tile
@@ -74,6 +78,8 @@ struct Cfg {
   static constexpr int SMEM = OFF_X + 6 * BM * 4 + 1024;       // + alignment slack
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t O_COL = 256;
+  static_assert(SMEM <= 232448, "shared memory per CTA");
+  static_assert(O_COL + D <= TMEM_COLS, "S double buffer and O must fit in TMEM");
 };
 
 struct Bars {   // mbarrier offsets inside the barrier block (8 bytes each; rings of up to 4)
@@ -234,13 +240,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // rows past the sequence end belong to other sequences (or are unused): zero them so
         // that P = 0 never meets a non-finite value
         const int r0 = max(SK - kb, 0);
-        for (int e = r0 * 8 * C::NCH + lane; e < BN * 8 * C::NCH; e += 32) {
-          const int c = e / (BN * 8), rem = e % (BN * 8);
-          const int r = rem / 8, w16 = rem % 8;
-          if (r >= r0)
-            *reinterpret_cast<uint4*>(sgen + C::OFF_V + s * C::KV_BYTES + c * C::CH_BYTES + r * 128 + w16 * 16) =
-                make_uint4(0, 0, 0, 0);
-        }
+        for (int c = 0; c < C::NCH; ++c)   // rows [r0, BN) of every 64-column chunk, 16 bytes per lane
+          for (int e = r0 * 8 + lane; e < BN * 8; e += 32)
+            *reinterpret_cast<uint4*>(sgen + C::OFF_V + s * C::KV_BYTES + c * C::CH_BYTES + (e / 8) * 128 +
+                                      (e % 8) * 16) = make_uint4(0, 0, 0, 0);
         fence_proxy_async_smem();
         __syncwarp();
       }
@@ -499,15 +502,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                                          make_float2(-muse, -muse));
             float a = ex2(x2.x), b = ex2(x2.y);
             lsum2 = __fadd2_rn(lsum2, make_float2(a, b));
-            if constexpr (kDrop) {   // keys kh + c0 + 2i, +1: bits 2i, 2i + 1 of word c0/32, sign-extended
+            if constexpr (kDrop) {   // keys kh + c0 + 2i, +1: bits 2i, 2i + 1 of word c0/32, sign-extended;
+              // dropped scores become 0; 1/(1-p) is applied to O in fp32 (epilogue), so a kept
+              // probability reaches the 16-bit P operand unscaled (1.0 stays exact)
               const uint32_t w = dw[c0 / 32];
               const uint32_t m0 = (uint32_t)((int32_t)(w << (31 - 2 * i)) >> 31);
               const uint32_t m1 = (uint32_t)((int32_t)(w << (30 - 2 * i)) >> 31);
-              const float2 z = __fmul2_rn(make_float2(__uint_as_float(__float_as_uint(a) & m0),
-                                                      __uint_as_float(__float_as_uint(b) & m1)),
-                                          make_float2(inv_keep, inv_keep));
-              a = z.x;
-              b = z.y;
+              a = __uint_as_float(__float_as_uint(a) & m0);
+              b = __uint_as_float(__float_as_uint(b) & m1);
             }
             if constexpr (BF16) {
               const __nv_bfloat162 t2 = __floats2bfloat162_rn(a, b);
@@ -559,7 +561,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     xl[hf * BM + r] = l;
     bar_sync_pair(pair_bar);
     l += xl[(1 - hf) * BM + r];
-    const float inv = l > 0.f ? 1.f / l : 0.f;
+    const float inv = l > 0.f ? inv_keep / l : 0.f;   // 1/(1-p) of the kept probabilities (1 without dropout)
     using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
     T* orow = (T*)p.O + (varlen ? (long long)qtok0 * p.sO.s : (long long)z * p.sO.b) + (long long)h * p.sO.h +
               (long long)q * p.sO.s + hf * HD2;
@@ -586,8 +588,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           }
         }
         uint4* dst = reinterpret_cast<uint4*>(orow + c);
+        // 8-column units; columns at or past the real head_dim are padding (never stored)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+        for (int i = 0; i < 4; ++i)
+          if (hf * HD2 + c + 8 * i < p.HD) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
       }
     }
     if (hf == 0 && q < SQ && p.LSE) {
@@ -893,15 +897,13 @@ __global__ void __launch_bounds__(PP_THREADS, 1)
                                        make_float2(-muse, -muse));
           float a = ex2(x2.x), b = ex2(x2.y);
           lsum2 = __fadd2_rn(lsum2, make_float2(a, b));   // the row sum is taken before dropout
-          if constexpr (DROP) {   // keys kb + c0 + 2i, +1: bits 2i, 2i + 1 of word c0 / 32, sign-extended
+          if constexpr (DROP) {   // keys kb + c0 + 2i, +1: bits 2i, 2i + 1 of word c0 / 32, sign-extended;
+            // 1/(1-p) is applied to O in fp32 (epilogue), not to the 16-bit P operand
             const uint32_t w = dw[c0 / 32];
             const uint32_t m0 = (uint32_t)((int32_t)(w << (31 - 2 * i)) >> 31);
             const uint32_t m1 = (uint32_t)((int32_t)(w << (30 - 2 * i)) >> 31);
-            const float2 z = __fmul2_rn(make_float2(__uint_as_float(__float_as_uint(a) & m0),
-                                                    __uint_as_float(__float_as_uint(b) & m1)),
-                                        make_float2(inv_keep, inv_keep));
-            a = z.x;
-            b = z.y;
+            a = __uint_as_float(__float_as_uint(a) & m0);
+            b = __uint_as_float(__float_as_uint(b) & m1);
           }
           if constexpr (BF16) {
             const __nv_bfloat162 t2 = __floats2bfloat162_rn(a, b);
@@ -941,7 +943,7 @@ __global__ void __launch_bounds__(PP_THREADS, 1)
     const bool have_o = ok && ntiles > 0;
     if (have_o && !mbar_wait_warp(bar + Bz::O_DONE + 8 * tt, (ntiles - 1) & 1)) record_error(16);
     tc_fence_after();
-    const float inv = l > 0.f ? 1.f / l : 0.f;
+    const float inv = l > 0.f ? inv_keep / l : 0.f;   // 1/(1-p) of the kept probabilities (1 without dropout)
     using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
     T* orow = (T*)p.O + (long long)z * p.sO.b + (long long)h * p.sO.h + (long long)q * p.sO.s;
 #pragma unroll
@@ -1088,19 +1090,21 @@ int launch_d(const FaFwdParams& p, cudaStream_t st, const CUtensorMap& mq, const
     const int rc = drop ? launch_pp<BF16, true>(p, st, mq, mk, mv) : launch_pp<BF16, false>(p, st, mq, mk, mv);
     if (rc >= 0) return rc;
   }
-  if (p.HD == 64) return launch<64, BF16, FEAT>(p, st, mq, mk, mv);
-  return launch<128, BF16, FEAT>(p, st, mq, mk, mv);
+  if (p.HD <= 64) return launch<64, BF16, FEAT>(p, st, mq, mk, mv);
+  if (p.HD <= 128) return launch<128, BF16, FEAT>(p, st, mq, mk, mv);
+  return launch<256, BF16, FEAT>(p, st, mq, mk, mv);
 }
 
 }  // namespace
 
 namespace fa {
 
-// Takes fp16/bf16 requests with head_dim 64 or 128, 16-byte aligned rows and strides;
-// everything else is left to the CUDA-core kernel (*taken = false).
+// Takes fp16/bf16 requests with any head_dim that is a multiple of 16 up to 256 (tiles of 64, 128
+// or 256 columns, zero-padded by the TMA), 16-byte aligned rows and strides; everything else is
+// left to the CUDA-core kernel (*taken = false).
 int fwd_sm100(const FaFwdParams& p, int dtype, cudaStream_t st, bool* taken) {
   *taken = false;
-  if (p.HD != 64 && p.HD != 128) return FA_OK;
+  if (p.HD % 16 != 0 || p.HD < 16 || p.HD > 256) return FA_OK;
   if (getenv("FABLE_ATTN_DISABLE_TC")) return FA_OK;
   int dev = current_device(), major = 0, minor = 0;
   cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);

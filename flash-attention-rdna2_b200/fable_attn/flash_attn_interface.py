@@ -120,8 +120,8 @@ def _rotary_plan(q, k, v, rotary_cos, rotary_sin, rotary_interleaved, return_att
                  paged=False):
     """Rotary embedding of q and k requested with the attention call (keyword-only extension;
     equivalent to layers.rotary.apply_rotary_emb on q and k first, positions restarting per
-    sequence).  Inference calls on fp16/bf16 with head_dim 64 or 128 rotate q inside the forward
-    kernel and k in one pass (returns the cos/sin/interleaved triple to hand to _C); anything else
+    sequence).  Inference calls on fp16/bf16 with an instantiated head_dim rotate q inside the
+    forward kernel and k in one pass (returns the cos/sin/interleaved triple to hand to _C); anything else
     rotates both here, differentiably, and returns (q, k, None)."""
     if rotary_cos is None and rotary_sin is None:
         return q, k, None
@@ -137,7 +137,7 @@ def _rotary_plan(q, k, v, rotary_cos, rotary_sin, rotary_interleaved, return_att
                          f"rotary_dim / 2) with seqlen_ro >= the longest sequence ({longest})")
     grad = torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad)
     if (not grad and not return_attn_probs and qv is None and not paged and q.is_cuda
-            and q.dtype in (torch.float16, torch.bfloat16) and q.shape[-1] in (64, 128)):
+            and q.dtype in (torch.float16, torch.bfloat16) and q.shape[-1] in _VALID_D):
         return q, k, (rotary_cos, rotary_sin, bool(rotary_interleaved))
     from .layers.rotary import apply_rotary_emb
     q = apply_rotary_emb(q, rotary_cos, rotary_sin, rotary_interleaved, cu_seqlens=cu_q)

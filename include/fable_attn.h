@@ -107,7 +107,7 @@ typedef struct FaFwdParams {
    * arithmetic, layers/rotary.py:20-68); position = the row's index in its sequence, rot_cos /
    * rot_sin fp32 [rot_seqlen_ro, rot_dim / 2], NeoX pairs (j, j + rot_dim/2) or interleaved
    * (2j, 2j + 1).  K is not rotated here: rotate it once beforehand (fa_rotary_launch); it is read
-   * by many CTAs.  fp16/bf16 with head_dim 64 or 128 only (FA_ERR_UNSUPPORTED otherwise).  A
+   * by many CTAs.  fp16/bf16 only (FA_ERR_UNSUPPORTED otherwise).  A
    * position past the table leaves its row unrotated and raises fa_device_error bit 4096. */
   const float* rot_cos;
   const float* rot_sin;

@@ -118,7 +118,7 @@ def test_config3_causal_fwd_bwd_fp16_dropout():
             vis = np.arange(S) <= r
             got = (words[h, np.arange(S) // 32, r] >> (np.arange(S) % 32).astype(np.uint32)) & 1
             assert np.array_equal(got[vis], ref[vis]), f"keep bits of head {h} row {r} differ"
-    on, ln = to_np(out), lse.cpu().numpy()
+    on, ln = to_np(out.detach()), lse.cpu().numpy()
     gq, gk, gv = to_np(q.grad), to_np(k.grad), to_np(v.grad)
     for b, h in ((0, 5), (1, 30)):
         r = O.attention_head(qn[b, :, h], kn[b, :, h], vn[b, :, h], D ** -0.5, causal=True, dropout_p=p, seed=seed,
