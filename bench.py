@@ -835,6 +835,17 @@ def profile_case(which, dev):
         bench_fwd_bwd_causal(dev, steps=1, warmup=0)
     elif which == "bwd_plain":   # config 3 shapes without dropout (the plain tensor-core kernels)
         bench_fwd_bwd_causal(dev, steps=1, warmup=0, dropout_p=0.0)
+    elif which == "varlen":   # config 5 in full (1.2 GB of q/k/v): three launches of the forward kernel
+        rng = np.random.default_rng(5)
+        lens = rng.integers(256, 8193, size=16)
+        cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32, device=dev)
+        tot, mx = int(lens.sum()), int(lens.max())
+        g = torch.Generator(device=dev).manual_seed(5)
+        q = torch.randn(tot, 64, 128, device=dev, dtype=torch.bfloat16, generator=g)
+        k = torch.randn(tot, 8, 128, device=dev, dtype=torch.bfloat16, generator=g)
+        v = torch.randn(tot, 8, 128, device=dev, dtype=torch.bfloat16, generator=g)
+        for _ in range(3):
+            _C.fwd_varlen(q, k, v, cu, cu, mx, mx, 128 ** -0.5, True, 512, 0, 30.0, None, 0.0, 0)
     torch.cuda.synchronize()
     print(json.dumps({"profile": which, "ok": True}))
 
@@ -847,7 +858,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-extra", action="store_true", help="skip the config 3/4 figures")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
-    ap.add_argument("--profile", choices=["fwd", "decode", "bwd", "bwd_plain"],
+    ap.add_argument("--profile", choices=["fwd", "decode", "bwd", "bwd_plain", "varlen"],
                     help="run one reduced case for ncu and exit")
     args = ap.parse_args()
     if args.profile:
