@@ -54,12 +54,24 @@ const int* opt_i32(const c10::optional<torch::Tensor>& t) {
 }
 
 // ------------------------------------------------------------------ dropout keep mask
-constexpr long long kMaxMaskBytes = 1ll << 30;   // above this the kernels evaluate Philox themselves
+// The keep mask (one bit per score, O(H*SQ*SK/8) bytes) saves the backward from evaluating Philox
+// again, but autograd keeps it alive until the backward: above this many bytes per call it is not
+// built and every kernel evaluates Philox itself (the reference's O(S) memory).  Default 256 MiB
+// (config 3's mask is 64 MiB), FABLE_ATTN_DROPOUT_MASK_MAX_MB overrides it (0 = never build one).
+long long max_mask_bytes() {
+  const char* v = getenv("FABLE_ATTN_DROPOUT_MASK_MAX_MB");
+  if (v && *v) {
+    char* end = nullptr;
+    const long long mb = strtoll(v, &end, 10);
+    if (end != v && mb >= 0) return mb << 20;
+  }
+  return 256ll << 20;
+}
 
 c10::optional<torch::Tensor> make_mask(const torch::Tensor& like, int64_t seed, double dropout_p, int NH, int SQ,
                                        int SK, bool causal, int64_t wl, int64_t wr) {
   const long long words = fa_dropout_mask_words(NH, SQ, SK);
-  if (!(dropout_p > 0) || words * 4 > kMaxMaskBytes || words == 0) return c10::nullopt;
+  if (!(dropout_p > 0) || words * 4 > max_mask_bytes() || words == 0) return c10::nullopt;
   auto bits = torch::empty({words}, like.options().dtype(torch::kInt32));
   check(fa_dropout_mask_launch((unsigned long long)seed, (float)dropout_p, NH, SQ, SK, causal ? 1 : 0, (int)wl,
                                (int)wr, (unsigned int*)bits.data_ptr<int>(), cur_stream(like)),

@@ -336,19 +336,26 @@ def _check_paged(k, v, block_table, cu_seqlens_k):
     return bt
 
 
-def _unpage(k, v, block_table, cu_seqlens_k, seqused_k):
-    """Paged (num_blocks, page, nheads_k, d) K/V + block_table -> packed varlen K/V (the autograd
-    path: the backward reads packed K/V)."""
+def _unpage(k, v, block_table, cu_seqlens_k, seqused_k, max_seqlen_k):
+    """Paged (num_blocks, page, nheads_k, d) K/V + block_table -> a padded varlen K/V, gathered on
+    the device with no host synchronisation: sequence b's positions 0 .. max_seqlen_k-1 occupy rows
+    b*max_seqlen_k + p (row of page block_table[b, p // page], slot p % page), its length is given
+    as seqused_k, and cu_seqlens_k becomes b*max_seqlen_k.  The gather is differentiable (the
+    gradient of each cache row is the sum of its gathered rows' gradients), so autograd carries
+    dK / dV back into the caches.  Used where the kernels cannot read the pages in place
+    (gradients, return_attn_probs, qv, padded head dims)."""
     bt = _check_paged(k, v, block_table, cu_seqlens_k)
-    page = k.shape[1]
-    lens = (seqused_k if seqused_k is not None else cu_seqlens_k[1:] - cu_seqlens_k[:-1]).tolist()
-    ks, vs = [], []
-    for i, L in enumerate(int(x) for x in lens):
-        idx = bt[i, :(L + page - 1) // page].long()
-        ks.append(k[idx].reshape(-1, k.shape[2], k.shape[3])[:L])
-        vs.append(v[idx].reshape(-1, v.shape[2], v.shape[3])[:L])
-    cu = torch.tensor([0] + list(itertools.accumulate(int(x) for x in lens)), device=k.device, dtype=torch.int32)
-    return torch.cat(ks, 0), torch.cat(vs, 0), cu
+    nb, page = k.shape[0], k.shape[1]
+    B, mx = bt.shape[0], int(max_seqlen_k)
+    dev = k.device
+    pos = torch.arange(mx, device=dev)
+    blk = bt[:, (pos // page).clamp_max(bt.shape[1] - 1)].long().clamp(0, nb - 1)   # positions past a table row or
+    rows = (blk * page + (pos % page)).reshape(-1)                                    # invalid entries: masked below
+    kd = k.reshape(-1, k.shape[2], k.shape[3])[rows]
+    vd = v.reshape(-1, v.shape[2], v.shape[3])[rows]
+    cu = torch.arange(B + 1, device=dev, dtype=torch.int32) * mx
+    lens = (seqused_k if seqused_k is not None else cu_seqlens_k[1:] - cu_seqlens_k[:-1]).to(dev, torch.int32)
+    return kd, vd, cu, lens.clamp(0, mx).contiguous()
 
 
 def flash_attn_varlen_func(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k, dropout_p=0.0,
@@ -373,8 +380,7 @@ def flash_attn_varlen_func(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, ma
         grad = torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad)
         if (grad or return_attn_probs or qv is not None or _pad_dim(q.shape[-1]) != q.shape[-1]
                 or not k.is_cuda or not k.is_contiguous() or not v.is_contiguous()):
-            k, v, cu_seqlens_k = _unpage(k, v, block_table, cu_seqlens_k, seqused_k)
-            seqused_k = None
+            k, v, cu_seqlens_k, seqused_k = _unpage(k, v, block_table, cu_seqlens_k, seqused_k, max_seqlen_k)
         else:   # the forward kernel reads the pages in place (no gather, no host sync)
             paged_bt = _check_paged(k, v, block_table, cu_seqlens_k).contiguous()
     keep_cols = None
@@ -485,8 +491,6 @@ def flash_attn_with_kvcache(q, k_cache, v_cache, k=None, v=None, qv=None, rotary
     (out, softmax_lse (batch, nheads, seqlen_q)) with return_softmax_lse."""
     _reject_fp8(q_descale, k_descale, v_descale)
     _accept_hints(num_splits, pack_gqa, sm_margin)
-    if q.dim() != 4:
-        raise ValueError(f"fable_attn: decode expects q as (batch, seqlen_q, nheads, headdim), got {tuple(q.shape)}")
     if softmax_scale is None:
         softmax_scale = (q.shape[-1] + (qv.shape[-1] if qv is not None else 0)) ** -0.5
     del scheduler_metadata  # precomputed FA-3 schedules are not needed: the launcher plans per call
@@ -495,7 +499,42 @@ def flash_attn_with_kvcache(q, k_cache, v_cache, k=None, v=None, qv=None, rotary
                                   "same number of tokens to every sequence")
     if not q.is_cuda:
         raise ValueError("fable_attn: tensors must be on a CUDA device (q.is_cuda is False)")
+    if cu_seqlens_q is not None and k is None and v is None and qv is None:
+        # Varlen queries (q (total_q, nheads, d), sequence i = tokens cu[i] .. cu[i+1]-1 attending to
+        # cache row i) as ONE decode launch, with no host synchronisation: the tokens are scattered on
+        # the device into a (batch, max_seqlen_q) query block, decoded as multi-token decode (token t
+        # of sequence i sits at position cache_seqlens[i] + t), and gathered back.  Rows past a
+        # sequence's length are computed on zeros and dropped.  max_seqlen_q bounds the block (when it
+        # is not given it is read from cu_seqlens_q, the one synchronising step).
+        q3 = q if q.dim() == 3 else q.reshape(-1, q.shape[-2], q.shape[-1])
+        cu = cu_seqlens_q.to(device=q.device, dtype=torch.long)
+        B = cu.numel() - 1
+        mq = int(max_seqlen_q) if max_seqlen_q is not None else int((cu[1:] - cu[:-1]).max())
+        tok = torch.arange(q3.shape[0], device=q.device)
+        seq = torch.searchsorted(cu[1:], tok, right=True).clamp_max(max(B - 1, 0))
+        slot = (seq * mq + (tok - cu[seq])).clamp(0, max(B * mq - 1, 0))
+        qpad = q3.new_zeros((B * mq,) + tuple(q3.shape[1:])).index_copy_(0, slot, q3).view(B, mq, *q3.shape[1:])
+        r = flash_attn_with_kvcache(qpad, k_cache, v_cache, rotary_cos=rotary_cos, rotary_sin=rotary_sin,
+                                    cache_seqlens=cache_seqlens, cache_batch_idx=cache_batch_idx,
+                                    cache_leftpad=cache_leftpad, block_table=block_table,
+                                    softmax_scale=softmax_scale, causal=causal, window_size=window_size,
+                                    softcap=softcap, rotary_interleaved=rotary_interleaved, alibi_slopes=alibi_slopes,
+                                    num_splits=num_splits, return_softmax_lse=return_softmax_lse,
+                                    page_table=page_table, attention_chunk=attention_chunk, pack_gqa=pack_gqa,
+                                    sm_margin=sm_margin, rotary_seqlens=rotary_seqlens)
+        o = r[0] if return_softmax_lse else r
+        out = o.reshape(B * mq, *o.shape[2:]).index_select(0, slot)
+        if q.dim() == 4:
+            out = out.unsqueeze(0)
+        if not return_softmax_lse:
+            return out
+        lse = r[1].transpose(0, 1).reshape(r[1].shape[1], B * mq).index_select(1, slot)   # (nheads, total_q)
+        return out, lse
+    if q.dim() != 4:
+        raise ValueError(f"fable_attn: decode expects q as (batch, seqlen_q, nheads, headdim), got {tuple(q.shape)}")
     if cu_seqlens_q is not None:
+        # with new k / v appended, each sequence's call gets the whole k / v (the reference's
+        # per-sequence form, package/fable_attn/flash_attn_interface.py:636-658)
         cu = cu_seqlens_q.to(torch.int32).cpu()
         outs, lses = [], []
         for i in range(cu.numel() - 1):

@@ -2,6 +2,7 @@
 lab/parity_new_api.py and package/tests/test_fable_attn.py, against an exact torch fp32
 reference of the same op (ref_attn below restates lab/parity_new_api.py:36-75)."""
 import math
+import random
 
 import pytest
 import torch
@@ -350,3 +351,33 @@ def test_vram_no_s_by_s():
     peak = torch.cuda.max_memory_allocated() - base
     del o
     assert peak < 2 * 4096 * 16 * 128 * 2 * 2   # out + LSE, far below the 4 GiB of an SxS fp32 matrix
+
+
+@pytest.mark.parametrize("cap_mb", ["0", "4"])
+def test_vram_no_s_by_s_with_dropout(monkeypatch, cap_mb):
+    """Training with dropout keeps O(S) memory once the per-call keep-mask cap is exceeded (here
+    16 heads x 4096^2 causal bits = 32 MiB > the cap): nothing S x S lives from the forward to the
+    backward, and the gradients equal those computed with the mask (bitwise)."""
+    torch.manual_seed(14)
+    q, k, v, do = (rnd(2, 4096, 16, 128) for _ in range(4))
+    # the same forward kernel in both runs (the keep bits come from the mask or from Philox in the
+    # kernel: the same decisions, so the same bits everywhere)
+    monkeypatch.setenv("FABLE_ATTN_FWD_TILES", "1")
+    grads = {}
+    for mode in ("mask", "philox"):
+        if mode == "philox":
+            monkeypatch.setenv("FABLE_ATTN_DROPOUT_MASK_MAX_MB", cap_mb)
+        qa, ka, va = (t.clone().requires_grad_() for t in (q, k, v))
+        torch.cuda.synchronize()
+        torch.cuda.reset_peak_memory_stats()
+        base = torch.cuda.memory_allocated()
+        random.seed(5)
+        o = fa.flash_attn_func(qa, ka, va, dropout_p=0.1, causal=True)
+        torch.cuda.synchronize()
+        held = torch.cuda.memory_allocated() - base        # what autograd keeps until the backward
+        o.backward(do)
+        grads[mode] = (o.detach(), qa.grad, ka.grad, va.grad)
+        if mode == "philox":
+            assert held < 2 * (2 * 4096 * 16 * 128 * 2) + 2 * 16 * 4096 * 4 * 2, held   # out + LSE (+ slack)
+    for a, b in zip(grads["mask"], grads["philox"]):
+        assert torch.equal(a, b)

@@ -229,3 +229,49 @@ def test_decode_tensor_core_split_invariance(nsplit):
     s = _setup(case, "bf16", nsplit=nsplit, page=tc[1], ctxs=tc[2])
     _launch(s, "bf16")
     assert O.rel_rms(to_np(s["o"]), s["ref"][0]) < TOL["bf16"]
+
+
+@pytest.mark.parametrize("paged", [True, False])
+@pytest.mark.parametrize("rotary", [False, True])
+def test_kvcache_varlen_queries_one_launch_no_host_sync(paged, rotary):
+    """flash_attn_with_kvcache(q (total_q, H, D), cu_seqlens_q=, max_seqlen_q=): sequence i's tokens
+    attend to cache row i at positions cache_seqlens[i] + t, computed in one decode launch with no
+    host synchronisation (torch's sync debug mode raises on one) and equal to per-sequence calls."""
+    import fable_attn as fa
+    g = torch.Generator(device="cuda").manual_seed(4)
+    B, H, Hk, D, page = 3, 8, 2, 128, 64
+    nq = [3, 1, 5]
+    ctx = torch.tensor([500, 64, 1000], dtype=torch.int32, device="cuda")
+    nper = 20
+    if paged:
+        kc = torch.randn(B * nper, page, Hk, D, device="cuda", dtype=torch.bfloat16, generator=g)
+        vc = torch.randn_like(kc)
+        bt = torch.randperm(B * nper, generator=torch.Generator().manual_seed(1)).view(B, nper).int().cuda()
+    else:
+        kc = torch.randn(B, 1024 + 64, Hk, D, device="cuda", dtype=torch.bfloat16, generator=g)
+        vc = torch.randn_like(kc)
+        bt = None
+    q = torch.randn(sum(nq), H, D, device="cuda", dtype=torch.bfloat16, generator=g)
+    cu = torch.tensor([0, 3, 4, 9], dtype=torch.int32, device="cuda")
+    kw = {}
+    if rotary:
+        ang = torch.arange(2048, device="cuda", dtype=torch.float32)[:, None] * 0.01 * torch.arange(
+            1, 33, device="cuda", dtype=torch.float32)[None]
+        kw = dict(rotary_cos=ang.cos(), rotary_sin=ang.sin(), rotary_interleaved=False)
+    if not paged:   # a dense cache must be a power-of-two long per row
+        kc, vc = kc[:, :1024].contiguous(), vc[:, :1024].contiguous()
+    torch.cuda.synchronize()
+    torch.cuda.set_sync_debug_mode("error")
+    try:
+        out, lse = fa.flash_attn_with_kvcache(q, kc, vc, cache_seqlens=ctx, block_table=bt, cu_seqlens_q=cu,
+                                              max_seqlen_q=5, return_softmax_lse=True, **kw)
+    finally:
+        torch.cuda.set_sync_debug_mode(0)
+    assert out.shape == q.shape and lse.shape == (H, sum(nq))
+    for i in range(B):
+        a, b = int(cu[i]), int(cu[i + 1])
+        ref, rl = fa.flash_attn_with_kvcache(q[a:b][None], kc if paged else kc[i:i + 1], vc if paged else vc[i:i + 1],
+                                             cache_seqlens=ctx[i:i + 1], block_table=bt[i:i + 1] if paged else None,
+                                             return_softmax_lse=True, **kw)
+        assert (out[a:b].float() - ref[0].float()).norm() <= 2e-3 * ref.float().norm()
+        assert torch.allclose(lse[:, a:b], rl[0], rtol=1e-4, atol=1e-4)

@@ -65,3 +65,44 @@ def test_paged_prefill_seqused_and_autograd_path():
     out = fa.flash_attn_varlen_func(qg, kc, vc, cq, ck, mq, mk, causal=True, block_table=bt)
     out.float().sum().backward()
     assert qg.grad is not None and bool(torch.isfinite(qg.grad).all())
+
+
+@pytest.mark.parametrize("seqused", [False, True])
+def test_paged_prefill_gradients_reach_the_cache_without_host_sync(seqused):
+    """Autograd through a paged cache: dQ and the gradients of k_cache / v_cache (page rows the
+    block table does not name get 0) equal those of the same attention on packed K/V, and neither
+    the forward nor the backward synchronises with the host (torch's sync debug mode raises)."""
+    q, kc, vc, bt, cq, ck, kp, vp, mq, mk = _case(torch.bfloat16, 128, 64, seed=5)
+    page = kc.shape[1]
+    used = torch.tensor([650, 17, 100, 299], dtype=torch.int32, device="cuda") if seqused else None
+    g = torch.Generator(device="cuda").manual_seed(9)
+    dout = torch.randn(q.shape, device="cuda", dtype=q.dtype, generator=g)
+    qa, kca, vca = (t.clone().requires_grad_() for t in (q, kc, vc))
+    torch.cuda.synchronize()
+    torch.cuda.set_sync_debug_mode("error")
+    try:
+        out = fa.flash_attn_varlen_func(qa, kca, vca, cq, ck, mq, mk, causal=True, block_table=bt, seqused_k=used)
+        out.backward(dout)
+    finally:
+        torch.cuda.set_sync_debug_mode(0)
+    # reference: the same keys packed by hand, gradients scattered back to the pages
+    lk = (ck[1:] - ck[:-1]).tolist()
+    lu = used.tolist() if seqused else lk
+    qb, kb, vb = q.clone().requires_grad_(), kp.clone().requires_grad_(), vp.clone().requires_grad_()
+    ks = [kb[int(ck[i]):int(ck[i]) + lu[i]] for i in range(len(lk))]
+    vs = [vb[int(ck[i]):int(ck[i]) + lu[i]] for i in range(len(lk))]
+    cu = torch.tensor([0] + list(torch.tensor(lu).cumsum(0)), dtype=torch.int32, device="cuda")
+    ref = fa.flash_attn_varlen_func(qb, torch.cat(ks), torch.cat(vs), cq, cu, mq, max(lu), causal=True)
+    ref.backward(dout)
+    assert torch.equal(out, ref)
+    assert (qa.grad.float() - qb.grad.float()).norm() <= 1e-6 * qb.grad.float().norm() + 1e-6
+    dkc, dvc = torch.zeros_like(kc, dtype=torch.float32), torch.zeros_like(vc, dtype=torch.float32)
+    for i, L in enumerate(lk):
+        for p in range((L + page - 1) // page):
+            n = min(page, L - p * page)
+            dkc[int(bt[i, p]), :n] += kb.grad[int(ck[i]) + p * page:int(ck[i]) + p * page + n].float()
+            dvc[int(bt[i, p]), :n] += vb.grad[int(ck[i]) + p * page:int(ck[i]) + p * page + n].float()
+    for nm, got, want in (("dk_cache", kca.grad, dkc), ("dv_cache", vca.grad, dvc)):
+        # each cache row receives its one gathered row's gradient (plus exact zeros): same values
+        e = (got.float() - want).norm() / want.norm()
+        assert e < 1e-6, f"{nm} differs: rel {e:.3e}"
