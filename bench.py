@@ -410,17 +410,26 @@ def bench_decode_split(dev, ws, rank, steps=20, warmup=5):
     def call(e=None):
         return M.decode_kv_split(q, kc, vc, bt, lc, softmax_scale=D ** -0.5, phase_events=e)
 
-    for _ in range(warmup):
-        call()
-    torch.cuda.synchronize()
-    _barrier(ws)
-    a, b = _events()
-    a.record()
-    for i in range(steps):
-        call()
-    b.record()
-    torch.cuda.synchronize()
-    ms = _max_over_ranks(a.elapsed_time(b) / steps, ws, dev)
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        _barrier(ws)
+        a, b = _events()
+        a.record()
+        for i in range(steps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return _max_over_ranks(a.elapsed_time(b) / steps, ws, dev)
+
+    # one decode step = one replay of the captured step (the decode partial, the all-gather and the
+    # merge as graph nodes); the same step launched op by op from Python is reported beside it
+    graph = M.DecodeKVSplitGraph(q, kc, vc, bt, lc, softmax_scale=D ** -0.5)
+    ms = timed(graph.replay)
+    ms_eager = timed(call)
+    graph.close()
+    del graph
     # per-phase times (a separate pass: the events between the phases would otherwise be in the
     # timed region): partial decode / all-gather / merge, mean over steps, max over ranks
     for i in range(steps):
@@ -432,6 +441,8 @@ def bench_decode_split(dev, ws, rank, steps=20, warmup=5):
     return {"config": f"paged decode B16 Hq32 Hk8 D128 bf16 page256 L~U[16K,32K] (same lengths as decode_paged), "
                       f"KV range split over {ws} GPU(s) + one NCCL all-gather of packed fp32 partials + LSE merge",
             "ms": round(ms, 4), "GBps": round(nbytes / ms / 1e6, 1), "bytes": nbytes,
+            "step": "one CUDA-graph replay per step (decode partial + NCCL all-gather + merge captured once)",
+            "ms_eager": round(ms_eager, 4),
             "phase_ms": {"partial": round(ph[0], 4), "all_gather": round(ph[1], 4), "merge": round(ph[2], 4)}}
 
 

@@ -130,3 +130,38 @@ def decode_kv_split(q, k_cache_local, v_cache_local, block_table_local, local_le
     if ev[3] is not None:
         ev[3].record()
     return out
+
+
+class DecodeKVSplitGraph:
+    """decode_kv_split captured once in a CUDA graph and replayed per decode step.
+
+    A split decode step is three short launches (the decode partial, the all-gather, the merge);
+    at 1/8 of a context each takes tens of microseconds, so launching them from Python every step
+    costs as much as running them.  The graph is captured for fixed input tensors (q, the local
+    cache, block table and lengths are read in place, so a caller updates them between steps) and
+    one replay runs the whole step; `out` is the graph's output tensor.  NCCL collectives are
+    captured as graph nodes; every rank must capture and replay in the same order.  Call close()
+    (or drop the object) before destroying the process group."""
+
+    def __init__(self, q, k_cache_local, v_cache_local, block_table_local, local_lengths, softmax_scale=None,
+                 group=None, num_splits=0, warmup=3):
+        args = (q, k_cache_local, v_cache_local, block_table_local, local_lengths)
+        self._args, self._kw = args, dict(softmax_scale=softmax_scale, group=group, num_splits=num_splits)
+        side = torch.cuda.Stream(device=q.device)
+        side.wait_stream(torch.cuda.current_stream(q.device))
+        with torch.cuda.stream(side):   # warm-up off the capture (allocator pools, NCCL communicator)
+            for _ in range(warmup):
+                decode_kv_split(*args, **self._kw)
+        torch.cuda.current_stream(q.device).wait_stream(side)
+        torch.cuda.synchronize(q.device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.out = decode_kv_split(*args, **self._kw)
+
+    def replay(self):
+        self.graph.replay()
+        return self.out
+
+    def close(self):
+        self.graph = None
+        self.out = None

@@ -58,6 +58,16 @@ def _worker(rank, world, port, ret):
         btl = torch.arange(B * lp, device=dev, dtype=torch.int32).view(B, lp)
         out = M.decode_kv_split(q, kl, vl, btl, loc.to(dev))
         err = ((out.float() - ref.float()).norm() / ref.float().norm()).item()
+        # the same step captured in a CUDA graph (all-gather as a graph node) replays bitwise
+        graph = M.DecodeKVSplitGraph(q, kl, vl, btl, loc.to(dev))
+        try:
+            for _ in range(2):
+                if not torch.equal(graph.replay(), out):
+                    err = float("inf")
+            torch.cuda.synchronize()
+        finally:
+            graph.close()
+            del graph
         ret[rank] = err
     finally:
         dist.destroy_process_group()
@@ -144,3 +154,22 @@ def test_packed_partials_merge_in_place(world):
     o_all, l_all = M.unpack_partials(recv, world, B, nq, H, D)
     out2 = fa.flash_attn_combine(o_all.contiguous(), l_all.contiguous(), out_dtype=q.dtype)
     assert torch.equal(out, out2)
+
+
+def test_decode_kv_split_graph_replays_the_step():
+    """The captured decode step (N=1 form) equals the op-by-op step, replay after replay, and picks
+    up new query values written into the captured q in place."""
+    from fable_attn import multigpu as M
+    dev = torch.device("cuda", 0)
+    q, kc, vc, bt, lens, chunks = _chunked_case(dev, 1)
+    g = M.DecodeKVSplitGraph(q, *chunks[0])
+    try:
+        for it in range(3):
+            if it == 2:
+                q.copy_(torch.randn_like(q))
+            want = M.decode_kv_split(q, *chunks[0])
+            got = g.replay().clone()
+            torch.cuda.synchronize()
+            assert torch.equal(got, want)
+    finally:
+        g.close()
