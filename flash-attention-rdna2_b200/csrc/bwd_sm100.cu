@@ -359,7 +359,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               const int cc = h32 + c + u, key = kb + cc;
               float logit, deriv = 1.f;
               if constexpr (kCap) {
-                const float tn = fa_tanh(s[cc] * cap_in);
+                const float tn = fa_tanh_tc<BF16>(s[cc] * cap_in);
                 logit = fmaf(p.softcap, tn, slope * (d0 + (float)cc));
                 deriv = 1.f - tn * tn;
               } else if constexpr (FEAT) {
@@ -710,7 +710,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               const bool vis = q >= qlo && q <= qhi && nl2 > -INFINITY;
               float logit, deriv = 1.f;
               if constexpr (kCap) {
-                const float tn = fa_tanh(s[cc] * cap_in);
+                const float tn = fa_tanh_tc<BF16>(s[cc] * cap_in);
                 logit = fmaf(p.softcap, tn, slope * (d0 - (float)cc));
                 deriv = 1.f - tn * tn;
               } else if constexpr (FEAT) {

@@ -195,6 +195,23 @@ __device__ __forceinline__ float fa_tanh(float x) {
   return 1.f - __fdividef(2.f, e + 1.f);
 }
 
+// Softcap tanh of the tensor-core kernels: bf16 requests use the SFU's tanh (tanh.approx.f32, one
+// SFU operation, relative error below 2^-10.9): with the logit capped at c the error is at most
+// c * |tanh| * 2^-10.9, a few 1e-4 of a probability, inside bf16's 2.5e-3 rel_rms budget and
+// half the SFU work of fa_tanh (exponential + reciprocal).  fp16 requests (a 3e-4 budget) keep
+// fa_tanh.  Forward and backward use the same one, so the backward's recomputed probabilities
+// match the forward's LSE.
+template <bool BF16>
+__device__ __forceinline__ float fa_tanh_tc(float x) {
+  if constexpr (BF16) {
+    float y;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+  } else {
+    return fa_tanh(x);
+  }
+}
+
 // ---------------------------------------------------------------- host bookkeeping
 namespace fa {
 void set_error(const char* fmt, ...);

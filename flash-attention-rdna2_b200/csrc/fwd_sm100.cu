@@ -1,14 +1,16 @@
 // fwd_sm100.cu — exact attention forward on the Blackwell tensor cores (tcgen05 + TMEM + TMA).
 //
-// Two kernels.  fwd_tc_kernel (below) takes one 128-row query tile per CTA and every feature
-// (softcap, alibi, dropout, varlen, paged K/V, in-kernel rotary of Q, every head_dim: tiles of 64,
-// 128 or 256 columns with the columns past head_dim zero-filled by the TMA);
+// Two kernels.  fwd_tc_kernel (below) works on one 128-row query tile at a time and takes every
+// feature (softcap, alibi, dropout, varlen, paged K/V, in-kernel rotary of Q, every head_dim: tiles
+// of 64, 128 or 256 columns with the columns past head_dim zero-filled by the TMA);
 // fwd_pp_kernel (further down) takes two query tiles per CTA for dense head_dim-128 requests
 // without softcap / alibi (dropout from a precomputed mask), and is chosen when its half-as-many
 // CTAs do not cost whole waves (launch_d).
 //
-// fwd_tc_kernel: one CTA = one 128-row query tile of one head of one sequence.  With rotary,
-// the softmax warps first rotate the Q tile in shared memory.  Warp roles (320 threads):
+// fwd_tc_kernel: persistent, one CTA per SM walking the work items (a 128-row query tile of one
+// head of one sequence) heavy first; the pipelines run on across items (short items, as under a
+// sliding window, would otherwise pay their prologue and pipeline fill each time).  With rotary,
+// the softmax warps first rotate each Q tile in shared memory.  Warp roles (320 threads):
 //   warps 0-7  softmax: warps w and w+4 share query rows 32 (w%4) .. +31 (their TMEM lane
 //              quadrant); w / 4 picks the half of each S row (64 keys) and of each O row (D/2
 //              columns) the thread owns.  Each thread reads its half row of S from TMEM, applies
@@ -19,7 +21,8 @@
 //              normalises its half of O and writes O and LSE.  Two softmax warps per scheduler
 //              keep the exponentials of two half rows in flight; the scale / subtract and the
 //              row sums run as packed fp32x2 operations.
-//   warp 8     TMA producer: Q once, then K and V tiles (128 keys x D) into separate rings.
+//   warp 8     TMA producer: per item its Q tile (double-buffered), then its K and V tiles
+//              (128 keys x D) into separate rings.
 //   warp 9     MMA issuer: owns the TMEM allocation; S_j = Q K_j^T into one of two S buffers
 //              (SS form), then O += P_j V_j with P read from TMEM (TS form).
 // TMEM columns: S0 [0,128), S1 [128,256), O [256, 256+D).  K/V tiles are 128-byte swizzled
@@ -62,16 +65,20 @@ __device__ int g_fwd_error = 0;       // non-zero after a pipeline wait timed ou
 // D is the tile width (64, 128 or 256); the request's head_dim p.HD may be smaller (a multiple of
 // 16): the TMA maps span only p.HD columns, so the columns past it land as zeros (adding nothing
 // to Q.K^T and giving zero O columns), and the epilogue stores only the real columns.
+// D is the tile width (64, 128 or 256); the request's head_dim p.HD may be smaller (a multiple of
+// 16): the TMA maps span only p.HD columns, so the columns past it land as zeros (adding nothing
+// to Q.K^T and giving zero O columns), and the epilogue stores only the real columns.
 template <int D>
 struct Cfg {
+  static constexpr int NQB = (D <= 128) ? 2 : 1;                   // Q buffers (next item's Q prefetched)
   static constexpr int NSK = (D <= 64) ? 4 : (D <= 128 ? 2 : 1);   // K ring depth (freed after S)
-  static constexpr int NSV = (D <= 64) ? 4 : (D <= 128 ? 3 : 1);   // V ring depth (freed after PV)
+  static constexpr int NSV = (D <= 64) ? 4 : (D <= 128 ? 2 : 1);   // V ring depth (freed after PV)
   static constexpr int NCH = D / 64;                           // 64-column (128-byte) chunks per row
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int KV_BYTES = BN * D * 2;                  // one K (or V) tile
   static constexpr int CH_BYTES = BN * 128;                    // one 64-column chunk of a tile
   static constexpr int OFF_Q = 0;
-  static constexpr int OFF_K = Q_BYTES;
+  static constexpr int OFF_K = NQB * Q_BYTES;
   static constexpr int OFF_V = OFF_K + NSK * KV_BYTES;
   static constexpr int OFF_BAR = OFF_V + NSV * KV_BYTES;
   static constexpr int OFF_X = OFF_BAR + 256;                  // row-max / row-sum exchange
@@ -83,60 +90,123 @@ struct Cfg {
 };
 
 struct Bars {   // mbarrier offsets inside the barrier block (8 bytes each; rings of up to 4)
-  static constexpr int Q_FULL = 0, K_FULL = 8, K_EMPTY = 40, V_FULL = 72, V_EMPTY = 104, S_FULL = 136,
-                       P_FULL = 152, O_DONE = 168, MMA_DRAIN = 176, TMEM_ADDR = 184,
-                       Q_ROT = 192;   // Q rotated in shared memory (rotary requests only)
+  static constexpr int Q_FULL = 0, Q_EMPTY = 16, Q_ROT = 32,   // [Q buffer]; Q_ROT: rotated (rotary only)
+                       K_FULL = 48, K_EMPTY = 80, V_FULL = 112, V_EMPTY = 144, S_FULL = 176, P_FULL = 192,
+                       O_DONE = 208, MMA_DRAIN = 216, TMEM_ADDR = 224;
 };
 
 __device__ __forceinline__ void record_error(int code) { atomicOr(&g_fwd_error, code); }
 
+// One work item of the persistent forward: a 128-row query tile of one head of one sequence.
+struct FwdItem {
+  int z, h, SQ, SK, qtok0, ktok0, qb;   // sequence, head, lengths, token offsets, first row
+  int t0, ntiles;                       // visible key tiles [t0, t0 + ntiles)
+  bool live;                            // the tile holds rows of its sequence
+};
+
+// Geometry of item `idx` (warp-collective: every lane of the calling warp takes part).  Items are
+// numbered heavy first: dense requests run every (head, batch) of the last query tile, then of
+// the one before, ...; varlen requests enumerate the query tiles of all sequences back to back
+// (sequence z owns ceil(SQ_z / BM) consecutive tile indices, its last tile first), each for
+// every head, and a prefix sum over cu_seqlens finds the sequence of a tile index.
+__device__ __forceinline__ FwdItem fwd_item(const FaFwdParams& p, int idx, int lane) {
+  FwdItem it;
+  it.live = false;
+  it.ntiles = 0;
+  it.t0 = 0;
+  if (p.cu_q == nullptr) {
+    const int nb = p.NH * p.batch, ntq = (p.SQ + BM - 1) / BM;
+    const int trev = idx / nb, rest = idx % nb;
+    it.h = rest % p.NH;
+    it.z = rest / p.NH;
+    it.SQ = p.SQ;
+    it.SK = p.SK;
+    it.qtok0 = it.ktok0 = 0;
+    it.qb = (ntq - 1 - trev) * BM;
+  } else {
+    const int ft = idx / p.NH;
+    it.h = idx % p.NH;
+    int base = 0, zz = -1, loc = 0;
+    for (int s0 = 0; s0 < p.batch; s0 += 32) {
+      const int si = s0 + lane;
+      int n = 0;
+      if (si < p.batch) {
+        int len = p.cu_q[si + 1] - p.cu_q[si];
+        if (p.seqused_q && p.seqused_q[si] < len) len = p.seqused_q[si];
+        n = (max(len, 0) + BM - 1) / BM;
+      }
+      int inc = n;   // inclusive warp scan of the tile counts
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += t;
+      }
+      const int first = base + inc - n;
+      const unsigned hit = __ballot_sync(0xffffffffu, n > 0 && ft >= first && ft < first + n);
+      if (hit) {
+        const int src = __ffs(hit) - 1;
+        zz = s0 + src;
+        loc = ft - __shfl_sync(0xffffffffu, first, src);
+        break;
+      }
+      base += __shfl_sync(0xffffffffu, inc, 31);
+    }
+    if (zz < 0) return it;   // past the last tile of the last sequence
+    it.z = zz;
+    it.qtok0 = p.cu_q[zz];
+    it.ktok0 = p.cu_k[zz];
+    it.SQ = p.cu_q[zz + 1] - it.qtok0;
+    it.SK = p.cu_k[zz + 1] - it.ktok0;
+    if (p.seqused_q && p.seqused_q[zz] < it.SQ) it.SQ = p.seqused_q[zz];
+    if (p.seqused_k && p.seqused_k[zz] < it.SK) it.SK = p.seqused_k[zz];
+    it.SQ = max(it.SQ, 0);
+    it.SK = max(it.SK, 0);
+    it.qb = ((it.SQ + BM - 1) / BM - 1 - loc) * BM;
+  }
+  if (it.qb < 0 || it.qb >= it.SQ) return it;
+  it.live = true;
+  int klo, khi, dmy;
+  fa_key_range(it.qb, it.SQ, it.SK, p.causal, p.win_left, p.win_right, p.attn_chunk, klo, dmy);
+  fa_key_range(min(it.qb + BM, it.SQ) - 1, it.SQ, it.SK, p.causal, p.win_left, p.win_right, p.attn_chunk, dmy, khi);
+  klo = max(klo, 0);
+  khi = min(khi, it.SK - 1);
+  it.t0 = klo / BN;
+  it.ntiles = (khi >= klo) ? (khi / BN - it.t0 + 1) : 0;
+  return it;
+}
+
+// Persistent one-tile forward: each CTA (one per SM) walks the items blockIdx.x,
+// blockIdx.x + gridDim.x, ...  The pipelines never drain between items: K/V ring slots, S
+// buffers and their barrier phases follow a key-tile counter g that runs across the CTA's items,
+// Q is double-buffered (the next item's tile is loaded while the current one computes; one buffer
+// at D = 256), and the first P.V of an item overwrites O (which the softmax warps have read out
+// before they release that item's first P).
 template <int D, bool BF16, bool FEAT>
 __global__ void __launch_bounds__(NTHREADS, 1)
     fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                  const __grid_constant__ CUtensorMap tmV, const FaFwdParams p) {
+                  const __grid_constant__ CUtensorMap tmV, const FaFwdParams p, int n_items) {
   using C = Cfg<D>;
   constexpr int HB = BN / 2;            // S columns (keys) per softmax thread
   constexpr int HD2 = D / 2;            // O columns per softmax thread
   extern __shared__ uint8_t smem_raw[];
   const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
   uint8_t* sgen = smem_raw + (sbase - smem_u32(smem_raw));
-  const uint32_t sQ = sbase + C::OFF_Q, sK = sbase + C::OFF_K, sV = sbase + C::OFF_V;
+  const uint32_t sK = sbase + C::OFF_K, sV = sbase + C::OFF_V;
   const uint32_t bar = sbase + C::OFF_BAR;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sgen + C::OFF_BAR + Bars::TMEM_ADDR);
   float* xch = reinterpret_cast<float*>(sgen + C::OFF_X);   // [2 parity][2 halves][BM] row maxima, then l
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int z = blockIdx.z, h = blockIdx.y, kvh = h / p.gqa;
   const bool varlen = p.cu_q != nullptr;
-
-  // ---- sequence geometry (uniform over the CTA; exits before any barrier or TMEM work)
-  int SQ = p.SQ, SK = p.SK, qtok0 = 0, ktok0 = 0;
-  if (varlen) {
-    qtok0 = p.cu_q[z];
-    ktok0 = p.cu_k[z];
-    SQ = p.cu_q[z + 1] - qtok0;
-    SK = p.cu_k[z + 1] - ktok0;
-    if (p.seqused_q && p.seqused_q[z] < SQ) SQ = p.seqused_q[z];
-    if (p.seqused_k && p.seqused_k[z] < SK) SK = p.seqused_k[z];
-    SQ = max(SQ, 0);
-    SK = max(SK, 0);
-  }
-  const int qb = (gridDim.x - 1 - blockIdx.x) * BM;   // heavy (late, causal) tiles first
-  if (qb >= SQ) return;
-  const int bcoord = varlen ? 0 : z;
-
-  int klo, khi, dmy;
-  fa_key_range(qb, SQ, SK, p.causal, p.win_left, p.win_right, p.attn_chunk, klo, dmy);
-  fa_key_range(min(qb + BM, SQ) - 1, SQ, SK, p.causal, p.win_left, p.win_right, p.attn_chunk, dmy, khi);
-  klo = max(klo, 0);
-  khi = min(khi, SK - 1);
-  const int t0 = klo / BN;
-  const int ntiles = (khi >= klo) ? (khi / BN - t0 + 1) : 0;
+  const bool rot = p.rot_cos != nullptr;   // the softmax warps rotate each Q tile before its first MMA
 
   // ---- set-up: barriers (thread 0), TMEM (MMA warp)
   if (tid == 0) {
-    mbar_init(bar + Bars::Q_FULL, 1);
-    mbar_init(bar + Bars::Q_ROT, NSOFT);
+    for (int s = 0; s < C::NQB; ++s) {
+      mbar_init(bar + Bars::Q_FULL + 8 * s, 1);
+      mbar_init(bar + Bars::Q_EMPTY + 8 * s, 1);
+      mbar_init(bar + Bars::Q_ROT + 8 * s, NSOFT);
+    }
     for (int s = 0; s < C::NSK; ++s) {
       mbar_init(bar + Bars::K_FULL + 8 * s, 1);
       mbar_init(bar + Bars::K_EMPTY + 8 * s, 1);
@@ -168,74 +238,97 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == WARP_TMA) {
-    // ======================= TMA producer
-    if (lane == 0 && ntiles > 0) {
-      mbar_expect_tx(bar + Bars::Q_FULL, C::Q_BYTES);
-      for (int c = 0; c < C::NCH; ++c)
-        tma_load_4d(sQ + c * (BM * 128), &tmQ, c * 64, qtok0 + qb, h, bcoord, bar + Bars::Q_FULL);
-      // paged K/V: a tile is loaded as page slices of R rows (3-D maps over the cache rows);
-      // positions past the block table's row, and invalid entries, read page 0 (an invalid entry
-      // for a real key also raises the error flag), so every slice lands and expect_tx is fixed
-      const bool paged = p.block_table != nullptr;
-      const int R = paged ? min(p.page, BN) : BN;
-      auto page_row = [&](int pos) -> int {
-        const int pi = pos / p.page;
-        long long blk = 0;
-        if (pi < p.max_blocks) {
-          blk = p.block_table[(long long)z * p.max_blocks + pi];
-          if (blk < 0 || blk >= p.num_blocks) {
-            if (pos < SK) record_error(1024);
-            blk = 0;
-          }
+    // ======================= TMA producer: per item its Q tile, then its K and V tiles
+    const bool paged = p.block_table != nullptr;
+    const int R = paged ? min(p.page, BN) : BN;
+    bool ok = true;
+    int g = 0, w = 0;   // key tiles and items (with keys) issued so far
+    for (int idx = blockIdx.x; ok && idx < n_items; idx += gridDim.x) {
+      const FwdItem it = fwd_item(p, idx, lane);
+      if (!it.live || it.ntiles == 0) continue;
+      if (lane == 0) {
+        const int kvh = it.h / p.gqa, bcoord = varlen ? 0 : it.z;
+        const int qs = w % C::NQB;
+        if (w >= C::NQB && !mbar_wait(bar + Bars::Q_EMPTY + 8 * qs, ((w / C::NQB) - 1) & 1)) {
+          record_error(1);
+          ok = false;
         }
-        return (int)(blk * p.page + pos % p.page);
-      };
-      auto load_tile = [&](uint32_t dst, const CUtensorMap* map, int kpos, uint32_t fb) {
-        if (!paged) {
+        if (ok) {
+          mbar_expect_tx(bar + Bars::Q_FULL + 8 * qs, C::Q_BYTES);
           for (int c = 0; c < C::NCH; ++c)
-            tma_load_4d(dst + c * C::CH_BYTES, map, c * 64, ktok0 + kpos, kvh, bcoord, fb);
-          return;
+            tma_load_4d(sbase + C::OFF_Q + qs * C::Q_BYTES + c * (BM * 128), &tmQ, c * 64, it.qtok0 + it.qb, it.h,
+                        bcoord, bar + Bars::Q_FULL + 8 * qs);
         }
-        for (int sl = 0; sl < BN / R; ++sl) {
-          const int row = page_row(kpos + sl * R);
-          for (int c = 0; c < C::NCH; ++c) tma_load_3d(dst + c * C::CH_BYTES + sl * R * 128, map, c * 64, kvh, row, fb);
+        // paged K/V: a tile is loaded as page slices of R rows (3-D maps over the cache rows);
+        // positions past the block table's row, and invalid entries, read page 0 (an invalid entry
+        // for a real key also raises the error flag), so every slice lands and expect_tx is fixed
+        auto page_row = [&](int pos) -> int {
+          const int pi = pos / p.page;
+          long long blk = 0;
+          if (pi < p.max_blocks) {
+            blk = p.block_table[(long long)it.z * p.max_blocks + pi];
+            if (blk < 0 || blk >= p.num_blocks) {
+              if (pos < it.SK) record_error(1024);
+              blk = 0;
+            }
+          }
+          return (int)(blk * p.page + pos % p.page);
+        };
+        auto load_tile = [&](uint32_t dst, const CUtensorMap* map, int kpos, uint32_t fb) {
+          if (!paged) {
+            for (int c = 0; c < C::NCH; ++c)
+              tma_load_4d(dst + c * C::CH_BYTES, map, c * 64, it.ktok0 + kpos, kvh, bcoord, fb);
+            return;
+          }
+          for (int sl = 0; sl < BN / R; ++sl) {
+            const int row = page_row(kpos + sl * R);
+            for (int c = 0; c < C::NCH; ++c) tma_load_3d(dst + c * C::CH_BYTES + sl * R * 128, map, c * 64, kvh, row, fb);
+          }
+        };
+        for (int j = 0; ok && j < it.ntiles; ++j) {
+          const int gg = g + j, kpos = (it.t0 + j) * BN;
+          const int sk = gg % C::NSK, sv = gg % C::NSV;
+          if (gg >= C::NSK && !mbar_wait(bar + Bars::K_EMPTY + 8 * sk, ((gg / C::NSK) - 1) & 1)) {
+            record_error(1);
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(bar + Bars::K_FULL + 8 * sk, C::KV_BYTES);
+          load_tile(sK + sk * C::KV_BYTES, &tmK, kpos, bar + Bars::K_FULL + 8 * sk);
+          if (gg >= C::NSV && !mbar_wait(bar + Bars::V_EMPTY + 8 * sv, ((gg / C::NSV) - 1) & 1)) {
+            record_error(1);
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(bar + Bars::V_FULL + 8 * sv, C::KV_BYTES);
+          load_tile(sV + sv * C::KV_BYTES, &tmV, kpos, bar + Bars::V_FULL + 8 * sv);
         }
-      };
-      for (int j = 0; j < ntiles; ++j) {
-        const int kpos = (t0 + j) * BN;
-        const int sk = j % C::NSK, sv = j % C::NSV;
-        if (j >= C::NSK && !mbar_wait(bar + Bars::K_EMPTY + 8 * sk, ((j / C::NSK) - 1) & 1)) {
-          record_error(1);
-          break;
-        }
-        mbar_expect_tx(bar + Bars::K_FULL + 8 * sk, C::KV_BYTES);
-        load_tile(sK + sk * C::KV_BYTES, &tmK, kpos, bar + Bars::K_FULL + 8 * sk);
-        if (j >= C::NSV && !mbar_wait(bar + Bars::V_EMPTY + 8 * sv, ((j / C::NSV) - 1) & 1)) {
-          record_error(1);
-          break;
-        }
-        mbar_expect_tx(bar + Bars::V_FULL + 8 * sv, C::KV_BYTES);
-        load_tile(sV + sv * C::KV_BYTES, &tmV, kpos, bar + Bars::V_FULL + 8 * sv);
       }
-      // do not leave while copies of this CTA are still landing in shared memory
-      for (int j = max(0, ntiles - C::NSK); j < ntiles; ++j)
-        mbar_wait(bar + Bars::K_FULL + 8 * (j % C::NSK), (j / C::NSK) & 1);
-      for (int j = max(0, ntiles - C::NSV); j < ntiles; ++j)
-        mbar_wait(bar + Bars::V_FULL + 8 * (j % C::NSV), (j / C::NSV) & 1);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      g += it.ntiles;
+      ++w;
+    }
+    // do not leave while copies of this CTA are still landing in shared memory (a Q tile is only
+    // ever in flight while the K/V loads behind it are)
+    if (lane == 0) {
+      for (int j = max(0, g - C::NSK); j < g; ++j) mbar_wait(bar + Bars::K_FULL + 8 * (j % C::NSK), (j / C::NSK) & 1);
+      for (int j = max(0, g - C::NSV); j < g; ++j) mbar_wait(bar + Bars::V_FULL + 8 * (j % C::NSV), (j / C::NSV) & 1);
+      for (int j = max(0, w - C::NQB); j < w; ++j) mbar_wait(bar + Bars::Q_FULL + 8 * (j % C::NQB), (j / C::NQB) & 1);
     }
     __syncwarp();
   } else if (warp == WARP_MMA) {
     // ======================= MMA issuer (whole warp follows; lane 0 issues)
     constexpr uint32_t IDESC_S = idesc_f16(BF16 ? 1 : 0, BM, BN, 0, 0);
     constexpr uint32_t IDESC_O = idesc_f16(BF16 ? 1 : 0, BM, D, 0, 1);
-    const bool rot = p.rot_cos != nullptr;   // then the softmax warps rotate Q before the first MMA
-    bool ok = ntiles == 0 || mbar_wait_warp(bar + (rot ? Bars::Q_ROT : Bars::Q_FULL), 0);
-    if (!ok) record_error(2);
-    auto issue_pv = [&](int i) -> bool {
-      const int s = i % C::NSV;
-      if (!mbar_wait_warp(bar + Bars::P_FULL + 8 * (i & 1), (i >> 1) & 1)) return false;
-      if (!mbar_wait_warp(bar + Bars::V_FULL + 8 * s, (i / C::NSV) & 1)) return false;
-      const int kb = (t0 + i) * BN;
+    bool ok = true;
+    int g = 0, w = 0;
+    // P.V of key tile gg (item tile t0 + jj of an item with SK keys): O (+)= P V, zero-initialised by
+    // the item's first one
+    auto issue_pv = [&](int gg, int jj, int t0, int SK) -> bool {
+      const int s = gg % C::NSV;
+      if (!mbar_wait_warp(bar + Bars::P_FULL + 8 * (gg & 1), (gg >> 1) & 1)) return false;
+      if (!mbar_wait_warp(bar + Bars::V_FULL + 8 * s, (gg / C::NSV) & 1)) return false;
+      const int kb = (t0 + jj) * BN;
       if (varlen && kb + BN > SK) {
         // rows past the sequence end belong to other sequences (or are unused): zero them so
         // that P = 0 never meets a non-finite value
@@ -249,14 +342,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
       tc_fence_after();
       if (lane == 0) {
-        const uint32_t pt = tmem + (uint32_t)(i & 1) * 128u;
+        const uint32_t pt = tmem + (uint32_t)(gg & 1) * 128u;
         const uint32_t vbase = sV + s * C::KV_BYTES;
         for (int kk = 0; kk < BN / 16; ++kk) {
           // A = P from TMEM: keys [64 hf, 64 hf + 64) sit packed in columns [64 hf, 64 hf + 32)
           // B = V tile, MN-major: 16 keys = 16 rows of 128 B; D spans NCH swizzle atoms (LBO apart)
           const uint32_t pa = pt + (uint32_t)((kk * 16) / HB) * 64u + (uint32_t)(((kk * 16) % HB) / 2);
           const uint64_t bd = sdesc_sw128(vbase + kk * 16 * 128, C::CH_BYTES, 1024);
-          mma_ts(tmem + C::O_COL, pa, bd, IDESC_O, (i > 0 || kk > 0) ? 1u : 0u);
+          mma_ts(tmem + C::O_COL, pa, bd, IDESC_O, (jj > 0 || kk > 0) ? 1u : 0u);
         }
         mma_commit(bar + Bars::V_EMPTY + 8 * s);
         mma_commit(bar + Bars::O_DONE);
@@ -264,26 +357,39 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       __syncwarp();
       return true;
     };
-    for (int j = 0; ok && j < ntiles; ++j) {
-      const int s = j % C::NSK;
-      if (!mbar_wait_warp(bar + Bars::K_FULL + 8 * s, (j / C::NSK) & 1)) { ok = false; break; }
-      tc_fence_after();
-      if (lane == 0) {
-        const uint32_t st = tmem + (uint32_t)(j & 1) * 128u;
-        const uint32_t kbase = sK + s * C::KV_BYTES;
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const int c = kk / 4, off = (kk % 4) * 32;   // 16 columns = 32 bytes inside a 128-byte chunk
-          const uint64_t ad = sdesc_sw128(sQ + c * (BM * 128) + off, 16, 1024);
-          const uint64_t bd = sdesc_sw128(kbase + c * C::CH_BYTES + off, 16, 1024);
-          mma_ss(st, ad, bd, IDESC_S, kk > 0 ? 1u : 0u);
-        }
-        mma_commit(bar + Bars::S_FULL + 8 * (j & 1));
-        mma_commit(bar + Bars::K_EMPTY + 8 * s);
+    for (int idx = blockIdx.x; ok && idx < n_items; idx += gridDim.x) {
+      const FwdItem it = fwd_item(p, idx, lane);
+      if (!it.live || it.ntiles == 0) continue;
+      const int qs = w % C::NQB;
+      if (!mbar_wait_warp(bar + (rot ? Bars::Q_ROT : Bars::Q_FULL) + 8 * qs, (w / C::NQB) & 1)) {
+        ok = false;
+        break;
       }
-      __syncwarp();
-      if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+      const uint32_t sQ = sbase + C::OFF_Q + qs * C::Q_BYTES;
+      for (int j = 0; ok && j < it.ntiles; ++j) {
+        const int gg = g + j, s = gg % C::NSK;
+        if (!mbar_wait_warp(bar + Bars::K_FULL + 8 * s, (gg / C::NSK) & 1)) { ok = false; break; }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t st = tmem + (uint32_t)(gg & 1) * 128u;
+          const uint32_t kbase = sK + s * C::KV_BYTES;
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const int c = kk / 4, off = (kk % 4) * 32;   // 16 columns = 32 bytes inside a 128-byte chunk
+            const uint64_t ad = sdesc_sw128(sQ + c * (BM * 128) + off, 16, 1024);
+            const uint64_t bd = sdesc_sw128(kbase + c * C::CH_BYTES + off, 16, 1024);
+            mma_ss(st, ad, bd, IDESC_S, kk > 0 ? 1u : 0u);
+          }
+          mma_commit(bar + Bars::S_FULL + 8 * (gg & 1));
+          mma_commit(bar + Bars::K_EMPTY + 8 * s);
+          if (j == it.ntiles - 1) mma_commit(bar + Bars::Q_EMPTY + 8 * qs);   // the item's last read of Q
+        }
+        __syncwarp();
+        if (j >= 1 && !issue_pv(gg - 1, j - 1, it.t0, it.SK)) { ok = false; break; }
+      }
+      if (ok && !issue_pv(g + it.ntiles - 1, it.ntiles - 1, it.t0, it.SK)) ok = false;
+      g += it.ntiles;
+      ++w;
     }
-    if (ok && ntiles > 0 && !issue_pv(ntiles - 1)) ok = false;
     if (!ok) record_error(4);
     // every MMA this warp issued has completed before TMEM can be released (also on error paths)
     if (lane == 0) mma_commit(bar + Bars::MMA_DRAIN);
@@ -295,309 +401,335 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     // [64 hf, 64 hf + 64) and O columns [D/2 hf, D/2 hf + D/2).  The two halves of a row agree on
     // the row max through shared memory and a 64-thread named barrier per quadrant.
     const int qd = warp & 3, hf = warp >> 2;
-    const int r = qd * 32 + lane, q = qb + r;
+    const int r = qd * 32 + lane;
     const uint32_t pair_bar = 1 + qd;
-    if (p.rot_cos != nullptr && ntiles > 0) {
-      // rotary embedding of the Q tile in shared memory (before any MMA reads it): thread pair
-      // (2 rr, 2 rr + 1) takes row rr, alternate rotary pairs; the roundings are the reference's
-      // (cos / sin cast to the dtype, each product and the sum rounded, no fused multiply-add).
-      // Element d of row rr sits in 64-column chunk d / 64 at 16-byte unit (d % 64) / 8 XOR rr % 8
-      // (the TMA 128-byte swizzle).
-      using RT = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-      auto rnd = [](float x) { return Elem<RT>::to_f(Elem<RT>::from_f(x)); };
-      auto qel = [&](int rr, int d) -> RT* {
-        const int e = d & 63;
-        return reinterpret_cast<RT*>(sgen + C::OFF_Q + (d >> 6) * (BM * 128) + rr * 128 + (((e >> 3) ^ (rr & 7)) << 4) +
-                                     ((e & 7) << 1));
-      };
-      // 16-byte unit of row rr holding elements d .. d + 7 (d a multiple of 8)
-      auto qunit = [&](int rr, int d) -> uint4* {
-        const int e = d & 63;
-        return reinterpret_cast<uint4*>(sgen + C::OFF_Q + (d >> 6) * (BM * 128) + rr * 128 + (((e >> 3) ^ (rr & 7)) << 4));
-      };
-      auto rot1 = [&](float a, float b, float c, float sn, float& o1, float& o2) {
-        c = rnd(c);
-        sn = rnd(sn);
-        o1 = Elem<RT>::to_f(Elem<RT>::from_f(__fsub_rn(rnd(__fmul_rn(a, c)), rnd(__fmul_rn(b, sn)))));
-        o2 = Elem<RT>::to_f(Elem<RT>::from_f(__fadd_rn(rnd(__fmul_rn(b, c)), rnd(__fmul_rn(a, sn)))));
-      };
-      const int rr = tid >> 1, pos = qb + rr, half = p.rot_dim / 2;
-      // cos / sin of this thread's pairs are loaded before the wait for Q: thread (2 rr + t) owns the
-      // contiguous pairs [t * half/2, (t + 1) * half/2) of row rr, whole 16-byte units when
-      // half/2 is a multiple of 8 (rot_dim 32, 64, 96, 128)
-      const int per = half / 2, j0 = (tid & 1) * per;
-      const bool vec = per % 8 == 0 && per <= 32 && ((uintptr_t)p.rot_cos | (uintptr_t)p.rot_sin) % 16 == 0;
-      const bool row_ok = pos < SQ && pos < p.rot_seqlen_ro;
-      float4 c4[8], s4[8];
-#pragma unroll
-      for (int g = 0; g < 8; ++g) {
-        c4[g] = s4[g] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (vec && row_ok && 4 * g < per) {
-          c4[g] = __ldg(reinterpret_cast<const float4*>(p.rot_cos + (long long)pos * half + j0) + g);
-          s4[g] = __ldg(reinterpret_cast<const float4*>(p.rot_sin + (long long)pos * half + j0) + g);
+    const uint32_t lane_addr = tmem + ((uint32_t)(qd * 32) << 16);
+    const float scale2 = p.scale * FA_LOG2E;
+    const bool drop = FEAT && p.dropout_p > 0.f;
+    const float inv_keep = drop ? 1.0f / (1.0f - p.dropout_p) : 1.f;
+    const bool use_bits = drop && p.dropout_bits != nullptr;
+    const uint32_t thresh = fa_drop_thresh(p.dropout_p);
+    const bool cap_on = FEAT && p.softcap > 0.f;
+    const float cap_in = cap_on ? p.scale / p.softcap : 0.f, cap2 = p.softcap * FA_LOG2E;
+    using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+    bool ok = true;
+    int g = 0, w = 0;
+    for (int idx = blockIdx.x; ok && idx < n_items; idx += gridDim.x) {
+      const FwdItem it = fwd_item(p, idx, lane);
+      if (!it.live) continue;
+      const int z = it.z, h = it.h, SQ = it.SQ, SK = it.SK, qb = it.qb, q = qb + r, ntiles = it.ntiles;
+      T* orow = (T*)p.O + (varlen ? (long long)it.qtok0 * p.sO.s : (long long)z * p.sO.b) + (long long)h * p.sO.h +
+                (long long)q * p.sO.s + hf * HD2;
+      if (ntiles == 0) {   // rows that see no key: O = 0, LSE = -inf (no pipeline work)
+        if (q < SQ) {
+          uint4* dst = reinterpret_cast<uint4*>(orow);
+          for (int i = 0; i < HD2 / 8; ++i)
+            if (hf * HD2 + 8 * i < p.HD) dst[i] = make_uint4(0, 0, 0, 0);
+          if (hf == 0 && p.LSE) p.LSE[fa_lse_index(varlen, z, h, p.NH, p.SQ, it.qtok0, p.lse_total_q, q)] = -INFINITY;
         }
+        continue;
       }
-      const bool got = mbar_wait(bar + Bars::Q_FULL, 0);
-      if (got && pos < SQ && pos >= p.rot_seqlen_ro) record_error(4096);
-      if (got && row_ok && vec) {
-        const float* cf = reinterpret_cast<const float*>(c4);
-        const float* sf = reinterpret_cast<const float*>(s4);
+      const int qs = w % C::NQB;
+      if (rot) {
+        // rotary embedding of the Q tile in shared memory (before any MMA reads it): thread pair
+        // (2 rr, 2 rr + 1) takes row rr, alternate rotary pairs; the roundings are the reference's
+        // (cos / sin cast to the dtype, each product and the sum rounded, no fused multiply-add).
+        // Element d of row rr sits in 64-column chunk d / 64 at 16-byte unit (d % 64) / 8 XOR rr % 8
+        // (the TMA 128-byte swizzle).
+        using RT = T;
+        uint8_t* qbuf = sgen + C::OFF_Q + qs * C::Q_BYTES;
+        auto rnd = [](float x) { return Elem<RT>::to_f(Elem<RT>::from_f(x)); };
+        auto qel = [&](int rr, int d) -> RT* {
+          const int e = d & 63;
+          return reinterpret_cast<RT*>(qbuf + (d >> 6) * (BM * 128) + rr * 128 + (((e >> 3) ^ (rr & 7)) << 4) +
+                                       ((e & 7) << 1));
+        };
+        // 16-byte unit of row rr holding elements d .. d + 7 (d a multiple of 8)
+        auto qunit = [&](int rr, int d) -> uint4* {
+          const int e = d & 63;
+          return reinterpret_cast<uint4*>(qbuf + (d >> 6) * (BM * 128) + rr * 128 + (((e >> 3) ^ (rr & 7)) << 4));
+        };
+        auto rot1 = [&](float a, float b, float c, float sn, float& o1, float& o2) {
+          c = rnd(c);
+          sn = rnd(sn);
+          o1 = Elem<RT>::to_f(Elem<RT>::from_f(__fsub_rn(rnd(__fmul_rn(a, c)), rnd(__fmul_rn(b, sn)))));
+          o2 = Elem<RT>::to_f(Elem<RT>::from_f(__fadd_rn(rnd(__fmul_rn(b, c)), rnd(__fmul_rn(a, sn)))));
+        };
+        const int rr = tid >> 1, pos = qb + rr, half = p.rot_dim / 2;
+        // cos / sin of this thread's pairs are loaded before the wait for Q: thread (2 rr + t) owns the
+        // contiguous pairs [t * half/2, (t + 1) * half/2) of row rr, whole 16-byte units when
+        // half/2 is a multiple of 8 (rot_dim 32, 64, 96, 128)
+        const int per = half / 2, j0 = (tid & 1) * per;
+        const bool vec = per % 8 == 0 && per <= 32 && ((uintptr_t)p.rot_cos | (uintptr_t)p.rot_sin) % 16 == 0;
+        const bool row_ok = pos < SQ && pos < p.rot_seqlen_ro;
+        float4 c4[8], s4[8];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          if (8 * u >= per) break;
-          if (!p.rot_interleaved) {   // pairs (j, j + half): one unit of each side
-            uint4* pa = qunit(rr, j0 + 8 * u);
-            uint4* pb = qunit(rr, j0 + half + 8 * u);
-            uint4 ua = *pa, ub = *pb;
-            RT* xa = reinterpret_cast<RT*>(&ua);
-            RT* xb = reinterpret_cast<RT*>(&ub);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              float o1, o2;
-              rot1(Elem<RT>::to_f(xa[e]), Elem<RT>::to_f(xb[e]), cf[8 * u + e], sf[8 * u + e], o1, o2);
-              xa[e] = Elem<RT>::from_f(o1);
-              xb[e] = Elem<RT>::from_f(o2);
-            }
-            *pa = ua;
-            *pb = ub;
-          } else {   // pairs (2j, 2j + 1): 8 pairs = two units
-            uint4* pa = qunit(rr, 2 * (j0 + 8 * u));
-            uint4* pb = qunit(rr, 2 * (j0 + 8 * u) + 8);
-            uint4 ua = *pa, ub = *pb;
-            RT* x = reinterpret_cast<RT*>(&ua);
-            RT* y = reinterpret_cast<RT*>(&ub);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              RT* w = e < 4 ? x : y;
-              const int o = 2 * (e & 3);
-              float o1, o2;
-              rot1(Elem<RT>::to_f(w[o]), Elem<RT>::to_f(w[o + 1]), cf[8 * u + e], sf[8 * u + e], o1, o2);
-              w[o] = Elem<RT>::from_f(o1);
-              w[o + 1] = Elem<RT>::from_f(o2);
-            }
-            *pa = ua;
-            *pb = ub;
+        for (int gi = 0; gi < 8; ++gi) {
+          c4[gi] = s4[gi] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (vec && row_ok && 4 * gi < per) {
+            c4[gi] = __ldg(reinterpret_cast<const float4*>(p.rot_cos + (long long)pos * half + j0) + gi);
+            s4[gi] = __ldg(reinterpret_cast<const float4*>(p.rot_sin + (long long)pos * half + j0) + gi);
           }
         }
-      } else if (got && row_ok) {
-        {
-          for (int j = tid & 1; j < half; j += 2) {
-            const int d1 = p.rot_interleaved ? 2 * j : j, d2 = p.rot_interleaved ? 2 * j + 1 : j + half;
+        const bool got = mbar_wait(bar + Bars::Q_FULL + 8 * qs, (w / C::NQB) & 1);
+        if (got && pos < SQ && pos >= p.rot_seqlen_ro) record_error(4096);
+        if (got && row_ok && vec) {
+          const float* cf = reinterpret_cast<const float*>(c4);
+          const float* sf = reinterpret_cast<const float*>(s4);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            if (8 * u >= per) break;
+            if (!p.rot_interleaved) {   // pairs (j, j + half): one unit of each side
+              uint4* pa = qunit(rr, j0 + 8 * u);
+              uint4* pb = qunit(rr, j0 + half + 8 * u);
+              uint4 ua = *pa, ub = *pb;
+              RT* xa = reinterpret_cast<RT*>(&ua);
+              RT* xb = reinterpret_cast<RT*>(&ub);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                float o1, o2;
+                rot1(Elem<RT>::to_f(xa[e]), Elem<RT>::to_f(xb[e]), cf[8 * u + e], sf[8 * u + e], o1, o2);
+                xa[e] = Elem<RT>::from_f(o1);
+                xb[e] = Elem<RT>::from_f(o2);
+              }
+              *pa = ua;
+              *pb = ub;
+            } else {   // pairs (2j, 2j + 1): 8 pairs = two units
+              uint4* pa = qunit(rr, 2 * (j0 + 8 * u));
+              uint4* pb = qunit(rr, 2 * (j0 + 8 * u) + 8);
+              uint4 ua = *pa, ub = *pb;
+              RT* x = reinterpret_cast<RT*>(&ua);
+              RT* y = reinterpret_cast<RT*>(&ub);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                RT* wv = e < 4 ? x : y;
+                const int o = 2 * (e & 3);
+                float o1, o2;
+                rot1(Elem<RT>::to_f(wv[o]), Elem<RT>::to_f(wv[o + 1]), cf[8 * u + e], sf[8 * u + e], o1, o2);
+                wv[o] = Elem<RT>::from_f(o1);
+                wv[o + 1] = Elem<RT>::from_f(o2);
+              }
+              *pa = ua;
+              *pb = ub;
+            }
+          }
+        } else if (got && row_ok) {
+          for (int jr = tid & 1; jr < half; jr += 2) {
+            const int d1 = p.rot_interleaved ? 2 * jr : jr, d2 = p.rot_interleaved ? 2 * jr + 1 : jr + half;
             RT* x1 = qel(rr, d1);
             RT* x2 = qel(rr, d2);
             const float a = Elem<RT>::to_f(*x1), b = Elem<RT>::to_f(*x2);
-            const float c = rnd(p.rot_cos[(long long)pos * half + j]), sn = rnd(p.rot_sin[(long long)pos * half + j]);
+            const float c = rnd(p.rot_cos[(long long)pos * half + jr]), sn = rnd(p.rot_sin[(long long)pos * half + jr]);
             *x1 = Elem<RT>::from_f(__fsub_rn(rnd(__fmul_rn(a, c)), rnd(__fmul_rn(b, sn))));
             *x2 = Elem<RT>::from_f(__fadd_rn(rnd(__fmul_rn(b, c)), rnd(__fmul_rn(a, sn))));
           }
         }
+        if (!got) record_error(8);
+        fence_proxy_async_smem();   // generic-proxy stores, read next by the tensor core
+        mbar_arrive(bar + Bars::Q_ROT + 8 * qs);
       }
-      if (!got) record_error(8);
-      fence_proxy_async_smem();   // generic-proxy stores, read next by the tensor core
-      mbar_arrive(bar + Bars::Q_ROT);
-    }
-    const uint32_t lane_addr = tmem + ((uint32_t)(qd * 32) << 16);
-    int rlo, rhi;
-    fa_key_range(q, SQ, SK, p.causal, p.win_left, p.win_right, p.attn_chunk, rlo, rhi);
-    if (q >= SQ) { rlo = 1; rhi = 0; }
-    // CTA-uniform bounds used to classify tiles as fully visible
-    int lo_last, hi_first;
-    {
-      int a, b;
-      fa_key_range(min(qb + BM, SQ) - 1, SQ, SK, p.causal, p.win_left, p.win_right, p.attn_chunk, lo_last, a);
-      fa_key_range(qb, SQ, SK, p.causal, p.win_left, p.win_right, p.attn_chunk, b, hi_first);
-    }
-    const bool full_rows = qb + BM <= SQ;
-    const float scale2 = p.scale * FA_LOG2E;
-    const float slope2 = (FEAT && p.alibi_slopes) ? p.alibi_slopes[h] * FA_LOG2E : 0.f;
-    const bool drop = FEAT && p.dropout_p > 0.f;
-    const float inv_keep = drop ? 1.0f / (1.0f - p.dropout_p) : 1.f;
-    float m_ref = -INFINITY, l = 0.f;
-    bool ok = true;
-    float s[HB];
-    const bool use_bits = drop && p.dropout_bits != nullptr;
-    const int mask_w = (SK + 31) / 32;
-    const uint32_t thresh = fa_drop_thresh(p.dropout_p);
-    const bool cap_on = FEAT && p.softcap > 0.f;
-    const float cap_in = cap_on ? p.scale / p.softcap : 0.f, cap2 = p.softcap * FA_LOG2E;
-    for (int j = 0; j < ntiles; ++j) {
-      const int kb = (t0 + j) * BN, kh = kb + hf * HB;   // first key of this thread's half
-      // this half's keep bits, one word per 32 keys (bit b <-> key kh + 32i + b), prepared before
-      // the wait so that they overlap it: loaded from the mask (its layout puts the warp's 32 rows
-      // on one line) or evaluated with Philox.  Mask words past the row's visible keys may be
-      // unwritten: they only multiply probabilities that are already 0.
-      uint32_t dw[HB / 32];
+      int rlo, rhi;
+      fa_key_range(q, SQ, SK, p.causal, p.win_left, p.win_right, p.attn_chunk, rlo, rhi);
+      if (q >= SQ) { rlo = 1; rhi = 0; }
+      // tile-uniform bounds used to classify key tiles as fully visible
+      int lo_last, hi_first;
+      {
+        int a, b;
+        fa_key_range(min(qb + BM, SQ) - 1, SQ, SK, p.causal, p.win_left, p.win_right, p.attn_chunk, lo_last, a);
+        fa_key_range(qb, SQ, SK, p.causal, p.win_left, p.win_right, p.attn_chunk, b, hi_first);
+      }
+      const bool full_rows = qb + BM <= SQ;
+      const float slope2 = (FEAT && p.alibi_slopes) ? p.alibi_slopes[h] * FA_LOG2E : 0.f;
+      const int mask_w = (SK + 31) / 32;
+      float m_ref = -INFINITY, l = 0.f;
+      float s[HB];
+      for (int j = 0; j < ntiles; ++j) {
+        const int gg = g + j;
+        const int kb = (it.t0 + j) * BN, kh = kb + hf * HB;   // first key of this thread's half
+        // this half's keep bits, one word per 32 keys (bit b <-> key kh + 32i + b), prepared before
+        // the wait so that they overlap it: loaded from the mask (its layout puts the warp's 32 rows
+        // on one line) or evaluated with Philox.  Mask words past the row's visible keys may be
+        // unwritten: they only multiply probabilities that are already 0.
+        uint32_t dw[HB / 32];
 #pragma unroll
-      for (int i = 0; i < HB / 32; ++i) {
-        const int kw = kh / 32 + i;
-        dw[i] = 0u;
-        if (drop && q < SQ && kw < mask_w)
-          dw[i] = use_bits ? __ldg(p.dropout_bits + fa_mask_word(h, SQ, SK, q, kw))
-                           : fa_keep_word(p.philox_seed, ((uint64_t)h * SQ + q) * SK + 32 * kw, 1, thresh,
-                                          SK - 32 * kw);
+        for (int i = 0; i < HB / 32; ++i) {
+          const int kw = kh / 32 + i;
+          dw[i] = 0u;
+          if (drop && q < SQ && kw < mask_w)
+            dw[i] = use_bits ? __ldg(p.dropout_bits + fa_mask_word(h, SQ, SK, q, kw))
+                             : fa_keep_word(p.philox_seed, ((uint64_t)h * SQ + q) * SK + 32 * kw, 1, thresh,
+                                            SK - 32 * kw);
+        }
+        // both warps of the pair leave together (the exchange below is a barrier without timeout)
+        const bool got = mbar_wait_warp(bar + Bars::S_FULL + 8 * (gg & 1), (gg >> 1) & 1);
+        if (!bar_and_pair(pair_bar, got && ok)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sa = lane_addr + (uint32_t)(gg & 1) * 128u + (uint32_t)(hf * HB);
+#pragma unroll
+        for (int c = 0; c < HB; c += 32) tmem_ld32(sa + c, s + c);
+        tc_wait_ld();
+        // ---- scores (log2 domain) and masks
+        float tmax = -INFINITY;
+        if constexpr (FEAT) {
+          // logits in log2 units; alibi adds slope2 * (key - q), and key - q = d0 + c exactly in
+          // fp32.  Two tight loops (softcap or not) keep the unrolled code small.
+          const float d0 = (float)(kh - q);
+          if (cap_on) {
+#pragma unroll
+            for (int c = 0; c < HB; ++c) s[c] = fmaf(cap2, fa_tanh_tc<BF16>(s[c] * cap_in), slope2 * (d0 + (float)c));
+          } else {
+#pragma unroll
+            for (int c = 0; c < HB; ++c) s[c] = fmaf(s[c], scale2, slope2 * (d0 + (float)c));
+          }
+        }
+        const bool interior = full_rows && kb >= lo_last && kb + BN - 1 <= hi_first && kb + BN <= SK;
+        if (!interior) {
+#pragma unroll
+          for (int c = 0; c < HB; ++c) {
+            const int key = kh + c;
+            if (key < rlo || key > rhi) s[c] = -INFINITY;
+          }
+        }
+#pragma unroll
+        for (int c = 0; c < HB; ++c) tmax = fmaxf(tmax, s[c]);
+        if constexpr (!FEAT) tmax = (tmax == -INFINITY) ? -INFINITY : tmax * scale2;
+        // ---- row max over both halves (slots alternate by key-tile parity, so a slot is rewritten
+        //      only after the partner has passed the next exchange)
+        float* xs = xch + (gg & 1) * (2 * BM);
+        xs[hf * BM + r] = tmax;
+        bar_sync_pair(pair_bar);
+        tmax = fmaxf(tmax, xs[(1 - hf) * BM + r]);
+        // ---- lazy online-softmax update: the reference max moves only when it grows by > 2^8
+        const bool move = tmax > m_ref + LAZY_THRESH || (m_ref == -INFINITY && tmax != -INFINITY);
+        float corr = 1.f;
+        if (move) {
+          corr = ex2(m_ref - tmax);   // 0 when the row had no visible key yet (its O row is 0)
+          l *= corr;
+          m_ref = tmax;
+        }
+        const float muse = (m_ref == -INFINITY) ? 0.f : m_ref;
+        const float sc = FEAT ? 1.f : scale2;
+        // ---- P = 2^(s - m): row sum (before dropout), dropout, 16-bit pairs into the first HB/2
+        //      columns of this half's S range (already read into registers).
+        // one straight-line instantiation per dropout setting (a runtime test inside the unrolled
+        // pair loop would be compiled as predicated code that runs both sides)
+        auto p_pass = [&](auto drop_tag) -> float2 {
+          constexpr bool kDrop = decltype(drop_tag)::value;
+          float2 lsum2 = make_float2(0.f, 0.f);
+#pragma unroll
+          for (int c0 = 0; c0 < HB; c0 += 32) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              // packed fp32x2 arithmetic (one FFMA2 / FADD2 per pair) around the two SFU exponentials
+              const float2 x2 = __ffma2_rn(make_float2(s[c0 + 2 * i], s[c0 + 2 * i + 1]), make_float2(sc, sc),
+                                           make_float2(-muse, -muse));
+              float a = ex2(x2.x), b = ex2(x2.y);
+              lsum2 = __fadd2_rn(lsum2, make_float2(a, b));
+              if constexpr (kDrop) {   // keys kh + c0 + 2i, +1: bits 2i, 2i + 1 of word c0/32, sign-extended;
+                // dropped scores become 0; 1/(1-p) is applied to O in fp32 (epilogue), so a kept
+                // probability reaches the 16-bit P operand unscaled (1.0 stays exact)
+                const uint32_t wd = dw[c0 / 32];
+                const uint32_t m0 = (uint32_t)((int32_t)(wd << (31 - 2 * i)) >> 31);
+                const uint32_t m1 = (uint32_t)((int32_t)(wd << (30 - 2 * i)) >> 31);
+                a = __uint_as_float(__float_as_uint(a) & m0);
+                b = __uint_as_float(__float_as_uint(b) & m1);
+              }
+              if constexpr (BF16) {
+                const __nv_bfloat162 t2 = __floats2bfloat162_rn(a, b);
+                pk[i] = *reinterpret_cast<const uint32_t*>(&t2);
+              } else {
+                const __half2 t2 = __floats2half2_rn(a, b);
+                pk[i] = *reinterpret_cast<const uint32_t*>(&t2);
+              }
+            }
+            tmem_st16(sa + c0 / 2, pk);
+          }
+          return lsum2;
+        };
+        float2 lsum2;
+        if constexpr (FEAT) {
+          lsum2 = drop ? p_pass(std::true_type{}) : p_pass(std::false_type{});
+        } else {
+          lsum2 = p_pass(std::false_type{});
+        }
+        // ---- O rescale of this half's columns.  Every key tile j >= 1 of an item waits exactly once
+        //      for the P.V of the tile before (so the parity wait can never alias an older phase);
+        //      that P.V normally finished while P_j was computed.  tcgen05.ld/st are warp-collective:
+        //      rows that did not move scale by 1.
+        if (j > 0) {
+          if (!mbar_wait_warp(bar + Bars::O_DONE, (gg - 1) & 1)) ok = false;   // leaves at the next exchange
+          if (ok && __any_sync(0xffffffffu, corr != 1.f)) {
+            tc_fence_after();
+#pragma unroll
+            for (int c = 0; c < HD2; c += 32) {
+              float o[32];
+              tmem_ld32(lane_addr + C::O_COL + hf * HD2 + c, o);
+              tc_wait_ld();
+#pragma unroll
+              for (int i = 0; i < 32; ++i) o[i] *= corr;
+              tmem_st32(lane_addr + C::O_COL + hf * HD2 + c, reinterpret_cast<const uint32_t*>(o));
+            }
+          }
+        }
+        l += lsum2.x + lsum2.y;
+        tc_wait_st();
+        tc_fence_before();
+        mbar_arrive(bar + Bars::P_FULL + 8 * (gg & 1));
       }
-      // both warps of the pair leave together (the exchange below is a barrier without timeout)
-      const bool got = mbar_wait_warp(bar + Bars::S_FULL + 8 * (j & 1), (j >> 1) & 1);
-      if (!bar_and_pair(pair_bar, got && ok)) { ok = false; break; }
+      // ---- epilogue: row sum over both halves, this half's O columns / l, LSE (first half).  The
+      //      TMEM reads complete before this warp releases the next item's first P, which is when
+      //      the next item's first P.V may overwrite O.
+      if (ok && !mbar_wait_warp(bar + Bars::O_DONE, (g + ntiles - 1) & 1)) {
+        record_error(16);
+        ok = false;
+      }
       tc_fence_after();
-      const uint32_t sa = lane_addr + (uint32_t)(j & 1) * 128u + (uint32_t)(hf * HB);
+      // the pair's exchanges AND-reduce `ok`: both warps of a quadrant go on to the next item or
+      // both stop (their named barrier has no timeout, so they must never part ways)
+      float* xl = xch + 4 * BM;
+      xl[hf * BM + r] = l;
+      ok = bar_and_pair(pair_bar, ok);
+      l += xl[(1 - hf) * BM + r];
+      ok = bar_and_pair(pair_bar, ok);   // both halves have read xl before either writes the next item's
+      const float inv = l > 0.f ? inv_keep / l : 0.f;   // 1/(1-p) of the kept probabilities (1 without dropout)
 #pragma unroll
-      for (int c = 0; c < HB; c += 32) tmem_ld32(sa + c, s + c);
-      tc_wait_ld();
-      // ---- scores (log2 domain) and masks
-      float tmax = -INFINITY;
-      if constexpr (FEAT) {
-        // logits in log2 units; alibi adds slope2 * (key - q), and key - q = d0 + c exactly in
-        // fp32.  Two tight loops (softcap or not) keep the unrolled code small.
-        const float d0 = (float)(kh - q);
-        if (cap_on) {
-#pragma unroll
-          for (int c = 0; c < HB; ++c) s[c] = fmaf(cap2, fa_tanh(s[c] * cap_in), slope2 * (d0 + (float)c));
+      for (int c = 0; c < HD2; c += 32) {
+        float o[32];
+        if (ok) {
+          tmem_ld32(lane_addr + C::O_COL + hf * HD2 + c, o);
+          tc_wait_ld();
         } else {
 #pragma unroll
-          for (int c = 0; c < HB; ++c) s[c] = fmaf(s[c], scale2, slope2 * (d0 + (float)c));
+          for (int i = 0; i < 32; ++i) o[i] = 0.f;
         }
-      }
-      const bool interior = full_rows && kb >= lo_last && kb + BN - 1 <= hi_first && kb + BN <= SK;
-      if (!interior) {
-#pragma unroll
-        for (int c = 0; c < HB; ++c) {
-          const int key = kh + c;
-          if (key < rlo || key > rhi) s[c] = -INFINITY;
-        }
-      }
-#pragma unroll
-      for (int c = 0; c < HB; ++c) tmax = fmaxf(tmax, s[c]);
-      if constexpr (!FEAT) tmax = (tmax == -INFINITY) ? -INFINITY : tmax * scale2;
-      // ---- row max over both halves (slots alternate by tile parity, so a slot is rewritten only
-      //      after the partner has passed the next exchange)
-      float* xs = xch + (j & 1) * (2 * BM);
-      xs[hf * BM + r] = tmax;
-      bar_sync_pair(pair_bar);
-      tmax = fmaxf(tmax, xs[(1 - hf) * BM + r]);
-      // ---- lazy online-softmax update: the reference max moves only when it grows by > 2^8
-      const bool move = tmax > m_ref + LAZY_THRESH || (m_ref == -INFINITY && tmax != -INFINITY);
-      float corr = 1.f;
-      if (move) {
-        corr = ex2(m_ref - tmax);   // 0 when the row had no visible key yet (its O row is 0)
-        l *= corr;
-        m_ref = tmax;
-      }
-      const float muse = (m_ref == -INFINITY) ? 0.f : m_ref;
-      const float sc = FEAT ? 1.f : scale2;
-      // ---- P = 2^(s - m): row sum (before dropout), dropout, 16-bit pairs into the first HB/2
-      //      columns of this half's S range (already read into registers).
-      // one straight-line instantiation per dropout setting (a runtime test inside the unrolled
-      // pair loop would be compiled as predicated code that runs both sides)
-      auto p_pass = [&](auto drop_tag) -> float2 {
-        constexpr bool kDrop = decltype(drop_tag)::value;
-        float2 lsum2 = make_float2(0.f, 0.f);
-#pragma unroll
-        for (int c0 = 0; c0 < HB; c0 += 32) {
-          uint32_t pk[16];
+        if (q < SQ) {
+          uint32_t wv[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            // packed fp32x2 arithmetic (one FFMA2 / FADD2 per pair) around the two SFU exponentials
-            const float2 x2 = __ffma2_rn(make_float2(s[c0 + 2 * i], s[c0 + 2 * i + 1]), make_float2(sc, sc),
-                                         make_float2(-muse, -muse));
-            float a = ex2(x2.x), b = ex2(x2.y);
-            lsum2 = __fadd2_rn(lsum2, make_float2(a, b));
-            if constexpr (kDrop) {   // keys kh + c0 + 2i, +1: bits 2i, 2i + 1 of word c0/32, sign-extended;
-              // dropped scores become 0; 1/(1-p) is applied to O in fp32 (epilogue), so a kept
-              // probability reaches the 16-bit P operand unscaled (1.0 stays exact)
-              const uint32_t w = dw[c0 / 32];
-              const uint32_t m0 = (uint32_t)((int32_t)(w << (31 - 2 * i)) >> 31);
-              const uint32_t m1 = (uint32_t)((int32_t)(w << (30 - 2 * i)) >> 31);
-              a = __uint_as_float(__float_as_uint(a) & m0);
-              b = __uint_as_float(__float_as_uint(b) & m1);
-            }
             if constexpr (BF16) {
-              const __nv_bfloat162 t2 = __floats2bfloat162_rn(a, b);
-              pk[i] = *reinterpret_cast<const uint32_t*>(&t2);
+              const __nv_bfloat162 t2 = __floats2bfloat162_rn(o[2 * i] * inv, o[2 * i + 1] * inv);
+              wv[i] = *reinterpret_cast<const uint32_t*>(&t2);
             } else {
-              const __half2 t2 = __floats2half2_rn(a, b);
-              pk[i] = *reinterpret_cast<const uint32_t*>(&t2);
+              const __half2 t2 = __floats2half2_rn(o[2 * i] * inv, o[2 * i + 1] * inv);
+              wv[i] = *reinterpret_cast<const uint32_t*>(&t2);
             }
           }
-          tmem_st16(sa + c0 / 2, pk);
-        }
-        return lsum2;
-      };
-      float2 lsum2;
-      if constexpr (FEAT) {
-        lsum2 = drop ? p_pass(std::true_type{}) : p_pass(std::false_type{});
-      } else {
-        lsum2 = p_pass(std::false_type{});
-      }
-      // ---- O rescale of this half's columns.  Every tile j >= 1 waits exactly once for PV_{j-1}
-      //      (so the parity wait can never alias an older phase); PV_{j-1} normally finished while
-      //      P_j was computed.  tcgen05.ld/st are warp-collective: rows that did not move scale by 1.
-      if (j > 0) {
-        if (!mbar_wait_warp(bar + Bars::O_DONE, (j - 1) & 1)) ok = false;   // leaves at the next exchange
-        if (ok && __any_sync(0xffffffffu, corr != 1.f)) {
-          tc_fence_after();
+          uint4* dst = reinterpret_cast<uint4*>(orow + c);
+          // 8-column units; columns at or past the real head_dim are padding (never stored)
 #pragma unroll
-          for (int c = 0; c < HD2; c += 32) {
-            float o[32];
-            tmem_ld32(lane_addr + C::O_COL + hf * HD2 + c, o);
-            tc_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] *= corr;
-            tmem_st32(lane_addr + C::O_COL + hf * HD2 + c, reinterpret_cast<const uint32_t*>(o));
-          }
+          for (int i = 0; i < 4; ++i)
+            if (hf * HD2 + c + 8 * i < p.HD) dst[i] = make_uint4(wv[4 * i], wv[4 * i + 1], wv[4 * i + 2], wv[4 * i + 3]);
         }
       }
-      l += lsum2.x + lsum2.y;
-      tc_wait_st();
-      tc_fence_before();
-      mbar_arrive(bar + Bars::P_FULL + 8 * (j & 1));
+      if (hf == 0 && q < SQ && p.LSE) {
+        const long long li = fa_lse_index(varlen, z, h, p.NH, p.SQ, it.qtok0, p.lse_total_q, q);
+        p.LSE[li] = l > 0.f ? m_ref * FA_LN2 + logf(l) : -INFINITY;
+      }
+      g += ntiles;
+      ++w;
     }
     if (!ok) record_error(8);
-    // ---- epilogue: row sum over both halves, this half's O columns / l, LSE (first half)
-    const bool have_o = ok && ntiles > 0;
-    if (have_o && !mbar_wait_warp(bar + Bars::O_DONE, (ntiles - 1) & 1)) record_error(16);
-    tc_fence_after();
-    float* xl = xch + 4 * BM;
-    xl[hf * BM + r] = l;
-    bar_sync_pair(pair_bar);
-    l += xl[(1 - hf) * BM + r];
-    const float inv = l > 0.f ? inv_keep / l : 0.f;   // 1/(1-p) of the kept probabilities (1 without dropout)
-    using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-    T* orow = (T*)p.O + (varlen ? (long long)qtok0 * p.sO.s : (long long)z * p.sO.b) + (long long)h * p.sO.h +
-              (long long)q * p.sO.s + hf * HD2;
-#pragma unroll
-    for (int c = 0; c < HD2; c += 32) {
-      float o[32];
-      if (have_o) {
-        tmem_ld32(lane_addr + C::O_COL + hf * HD2 + c, o);
-        tc_wait_ld();
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o[i] = 0.f;
-      }
-      if (q < SQ) {
-        uint32_t w[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          if constexpr (BF16) {
-            const __nv_bfloat162 t2 = __floats2bfloat162_rn(o[2 * i] * inv, o[2 * i + 1] * inv);
-            w[i] = *reinterpret_cast<const uint32_t*>(&t2);
-          } else {
-            const __half2 t2 = __floats2half2_rn(o[2 * i] * inv, o[2 * i + 1] * inv);
-            w[i] = *reinterpret_cast<const uint32_t*>(&t2);
-          }
-        }
-        uint4* dst = reinterpret_cast<uint4*>(orow + c);
-        // 8-column units; columns at or past the real head_dim are padding (never stored)
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          if (hf * HD2 + c + 8 * i < p.HD) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
-      }
-    }
-    if (hf == 0 && q < SQ && p.LSE) {
-      const long long li = fa_lse_index(varlen, z, h, p.NH, p.SQ, qtok0, p.lse_total_q, q);
-      p.LSE[li] = l > 0.f ? m_ref * FA_LN2 + logf(l) : -INFINITY;
-    }
   }
   tc_fence_before();
   __syncthreads();
@@ -1039,8 +1171,17 @@ int launch(const FaFwdParams& p, cudaStream_t st, const CUtensorMap& mq, const C
   using C = Cfg<D>;
   static unsigned long long done = 0;
   if (int rc = fa::ensure_smem((const void*)fwd_tc_kernel<D, BF16, FEAT>, C::SMEM, &done)) return rc;
-  dim3 grid((p.SQ + BM - 1) / BM, p.NH, p.batch);
-  fwd_tc_kernel<D, BF16, FEAT><<<grid, NTHREADS, C::SMEM, st>>>(mq, mk, mv, p);
+  // work items: (query tile, head, batch) for dense requests; varlen requests enumerate every
+  // sequence's query tiles back to back (at most ceil(total_q / BM) + batch of them, each for every
+  // head).  One persistent CTA per SM walks them.
+  const long long tiles = p.cu_q ? (p.lse_total_q + BM - 1) / BM + p.batch : (long long)((p.SQ + BM - 1) / BM) * p.batch;
+  const long long n_items = tiles * p.NH;
+  if (n_items > 0x7fffffffLL) {
+    fa::set_error("forward: %lld query tiles exceed the work-item range", n_items);
+    return FA_ERR_SIZE;
+  }
+  const int grid = (int)std::min<long long>(n_items, fa::num_sms());
+  fwd_tc_kernel<D, BF16, FEAT><<<grid, NTHREADS, C::SMEM, st>>>(mq, mk, mv, p, (int)n_items);
   fa::count_launch();
   return fa::cuda_status(cudaGetLastError(), "fwd_sm100 launch");
 }
