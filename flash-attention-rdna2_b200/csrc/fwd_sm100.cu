@@ -1246,6 +1246,9 @@ namespace fa {
 int fwd_sm100(const FaFwdParams& p, int dtype, cudaStream_t st, bool* taken) {
   *taken = false;
   if (p.HD % 16 != 0 || p.HD < 16 || p.HD > 256) return FA_OK;
+  // the kernels scale the row max of the raw scores (the max commutes with a positive factor); a
+  // zero or negative softmax scale runs on the CUDA-core kernel
+  if (!(p.scale > 0.f)) return FA_OK;
   if (getenv("FABLE_ATTN_DISABLE_TC")) return FA_OK;
   int dev = current_device(), major = 0, minor = 0;
   cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
