@@ -389,8 +389,9 @@ def bench_decode(dev, steps=20, warmup=5):
 def bench_decode_split(dev, ws, rank, steps=20, warmup=5):
     """Config 4 across ranks: each sequence's context (lengths ~ U[16K, 32K], seeded) is cut into
     ws contiguous chunks; rank r holds the pages of its chunks (bf16, page 256, permuted block
-    table) and decodes against them, then one NCCL all-gather of the (out, lse) partials and the
-    LSE merge (fable_attn.multigpu.decode_kv_split).  Every rank runs this (collectives); the
+    table) and decodes against them, then the partials are merged by one kernel reading every
+    rank's buffer over NVLink (fable_attn.multigpu.PeerDecodeExchange); the NCCL all-gather path
+    (decode_kv_split) is timed beside it.  Every rank runs this (same steps on every rank); the
     time is the max over ranks, GB/s counts the K/V bytes of the whole job."""
     from fable_attn import multigpu as M
     B, Hq, Hk, D, page = 16, 32, 8, 128, 256
@@ -405,11 +406,6 @@ def bench_decode_split(dev, ws, rank, steps=20, warmup=5):
     q = torch.randn(B, 1, Hq, D, device=dev, dtype=torch.bfloat16, generator=torch.Generator(device=dev).manual_seed(7))
     lc = local.to(dev)
 
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
-
-    def call(e=None):
-        return M.decode_kv_split(q, kc, vc, bt, lc, softmax_scale=D ** -0.5, phase_events=e)
-
     def timed(fn):
         for _ in range(warmup):
             fn()
@@ -423,27 +419,56 @@ def bench_decode_split(dev, ws, rank, steps=20, warmup=5):
         torch.cuda.synchronize()
         return _max_over_ranks(a.elapsed_time(b) / steps, ws, dev)
 
-    # one decode step = one replay of the captured step (the decode partial, the all-gather and the
-    # merge as graph nodes); the same step launched op by op from Python is reported beside it
-    graph = M.DecodeKVSplitGraph(q, kc, vc, bt, lc, softmax_scale=D ** -0.5)
-    ms = timed(graph.replay)
-    ms_eager = timed(call)
-    graph.close()
-    del graph
-    # per-phase times (a separate pass: the events between the phases would otherwise be in the
-    # timed region): partial decode / all-gather / merge, mean over steps, max over ranks
-    for i in range(steps):
-        call(ev[i])
-    torch.cuda.synchronize()
-    ph = [statistics.mean(e[j].elapsed_time(e[j + 1]) for e in ev) for j in range(3)]
-    ph = [_max_over_ranks(x, ws, dev) for x in ph]
+    def phases(fn):
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
+        for i in range(steps):
+            fn(ev[i])
+        torch.cuda.synchronize()
+        ph = [statistics.mean(e[j].elapsed_time(e[j + 1]) for e in ev) for j in range(3)]
+        return [_max_over_ranks(x, ws, dev) for x in ph]
+
+    def graphed(fn):
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                fn()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        return g
+
+    # the product path: this rank's decode into its buffer of a symmetric allocation, then one
+    # kernel that merges straight from every rank's buffer over NVLink (and a step-end handshake);
+    # one decode step = one replay of the captured step
+    ex = M.PeerDecodeExchange(B, 1, Hq, D, dev)
+    peer = lambda e=None: ex.step(q, kc, vc, bt, lc, softmax_scale=D ** -0.5, phase_events=e)   # noqa: E731
+    g = graphed(peer)
+    ms = timed(g.replay)
+    ms_eager = timed(peer)
+    ph = phases(peer)
+    peer_err = int(ex.err.item())
+    del g
+    # beside it: the same step with an NCCL all-gather of the packed partials and the merge kernel
+    nccl = lambda e=None: M.decode_kv_split(q, kc, vc, bt, lc, softmax_scale=D ** -0.5, phase_events=e)  # noqa: E731
+    g2 = graphed(nccl)
+    ms_nccl = timed(g2.replay)
+    ph2 = phases(nccl)
+    del g2
+    ex.close()
     nbytes = float(lens.sum()) * Hk * D * 2 * 2
     return {"config": f"paged decode B16 Hq32 Hk8 D128 bf16 page256 L~U[16K,32K] (same lengths as decode_paged), "
-                      f"KV range split over {ws} GPU(s) + one NCCL all-gather of packed fp32 partials + LSE merge",
+                      f"KV range split over {ws} GPU(s); partials merged by one kernel over peer memory (NVLink)",
             "ms": round(ms, 4), "GBps": round(nbytes / ms / 1e6, 1), "bytes": nbytes,
-            "step": "one CUDA-graph replay per step (decode partial + NCCL all-gather + merge captured once)",
-            "ms_eager": round(ms_eager, 4),
-            "phase_ms": {"partial": round(ph[0], 4), "all_gather": round(ph[1], 4), "merge": round(ph[2], 4)}}
+            "step": "one CUDA-graph replay per step (decode partial + peer merge + step-end handshake)",
+            "ms_eager": round(ms_eager, 4), "wait_errors": peer_err,
+            "phase_ms": {"partial": round(ph[0], 4), "peer_merge": round(ph[1], 4), "step_end": round(ph[2], 4)},
+            "nccl_path": {"ms": round(ms_nccl, 4), "GBps": round(nbytes / ms_nccl / 1e6, 1),
+                          "step": "graph replay: decode partial + NCCL all-gather of packed partials + merge",
+                          "phase_ms": {"partial": round(ph2[0], 4), "all_gather": round(ph2[1], 4),
+                                       "merge": round(ph2[2], 4)}}}
 
 
 def bench_varlen_swa(dev, steps=10, warmup=3, kv_groups=8):

@@ -25,7 +25,8 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVFLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
            "--expt-relaxed-constexpr", "-I", INC, "-I", CSRC]
 
-KERNEL_SOURCES = ["api.cu", "fwd_simt.cu", "fwd_sm100.cu", "bwd_simt.cu", "bwd_sm100.cu", "decode.cu", "decode_sm100.cu", "dropout.cu", "rotary.cu"]
+KERNEL_SOURCES = ["api.cu", "fwd_simt.cu", "fwd_sm100.cu", "bwd_simt.cu", "bwd_sm100.cu", "decode.cu", "decode_sm100.cu", "dropout.cu", "rotary.cu",
+                  "decode_peer.cu"]
 LIB = os.path.join(PKG, "libfable_attn.so")
 
 

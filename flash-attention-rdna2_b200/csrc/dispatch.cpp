@@ -428,6 +428,47 @@ torch::Tensor combine_packed(torch::Tensor buf, int64_t nsplit, int64_t B, int64
   return out;
 }
 
+// Multi-GPU decode exchange over peer memory (fa_peer_merge_launch / fa_peer_step_end_launch):
+// peer_bufs / peer_signals are int64 CUDA tensors [world] holding the ranks' device addresses of
+// their packed partials and signal words; step / err are int32 CUDA tensors [1] of this rank.
+FaPeerMergeParams peer_params(torch::Tensor peer_bufs, torch::Tensor peer_signals, int64_t rank, int64_t world,
+                              int64_t B, int64_t S, int64_t H, int64_t D, torch::Tensor step, torch::Tensor err) {
+  TORCH_CHECK_VALUE(peer_bufs.is_cuda() && peer_signals.is_cuda() && peer_bufs.scalar_type() == torch::kInt64 &&
+                        peer_signals.scalar_type() == torch::kInt64 && peer_bufs.numel() == world &&
+                        peer_signals.numel() == world,
+                    "fable_attn: peer_bufs / peer_signals must be int64 CUDA tensors of `world` addresses");
+  TORCH_CHECK_VALUE(step.is_cuda() && step.scalar_type() == torch::kInt32 && err.is_cuda() &&
+                        err.scalar_type() == torch::kInt32,
+                    "fable_attn: step and err must be int32 CUDA tensors");
+  FaPeerMergeParams p{};
+  p.struct_size = sizeof(FaPeerMergeParams);
+  p.peer_bufs = reinterpret_cast<const float* const*>(peer_bufs.data_ptr<int64_t>());
+  p.peer_signals = reinterpret_cast<unsigned int* const*>(peer_signals.data_ptr<int64_t>());
+  p.rank = (int)rank; p.world = (int)world;
+  p.B = (int)B; p.S = (int)S; p.H = (int)H; p.D = (int)D;
+  p.step = step.data_ptr<int>(); p.err_flag = err.data_ptr<int>();
+  return p;
+}
+
+torch::Tensor peer_merge(torch::Tensor peer_bufs, torch::Tensor peer_signals, int64_t rank, int64_t world, int64_t B,
+                         int64_t S, int64_t H, int64_t D, torch::Tensor step, torch::Tensor err,
+                         c10::ScalarType out_dtype, c10::optional<torch::Tensor> lse_out) {
+  const c10::cuda::CUDAGuard guard(step.device());
+  FaPeerMergeParams p = peer_params(peer_bufs, peer_signals, rank, world, B, S, H, D, step, err);
+  auto out = torch::empty({B, S, H, D}, step.options().dtype(out_dtype));
+  p.out = out.data_ptr(); p.out_dtype = dt_of(out);
+  p.lse_out = const_cast<float*>(opt_f32(lse_out));
+  check(fa_peer_merge_launch(&p, cur_stream(step)), "peer merge");
+  return out;
+}
+
+void peer_step_end(torch::Tensor peer_bufs, torch::Tensor peer_signals, int64_t rank, int64_t world, int64_t B,
+                   int64_t S, int64_t H, int64_t D, torch::Tensor step, torch::Tensor err) {
+  const c10::cuda::CUDAGuard guard(step.device());
+  FaPeerMergeParams p = peer_params(peer_bufs, peer_signals, rank, world, B, S, H, D, step, err);
+  check(fa_peer_step_end_launch(&p, cur_stream(step)), "peer step end");
+}
+
 }  // namespace
 
 // ------------------------------------------------------------------ rotary (q / k, one pass)
@@ -518,6 +559,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("return_lse") = false);
   m.def("combine_packed", &combine_packed, py::arg("buf"), py::arg("nsplit"), py::arg("B"), py::arg("S"),
         py::arg("H"), py::arg("D"), py::arg("out_dtype"));
+  m.def("peer_merge", &peer_merge, py::arg("peer_bufs"), py::arg("peer_signals"), py::arg("rank"), py::arg("world"),
+        py::arg("B"), py::arg("S"), py::arg("H"), py::arg("D"), py::arg("step"), py::arg("err"),
+        py::arg("out_dtype"), py::arg("lse_out") = c10::optional<torch::Tensor>());
+  m.def("peer_step_end", &peer_step_end, py::arg("peer_bufs"), py::arg("peer_signals"), py::arg("rank"),
+        py::arg("world"), py::arg("B"), py::arg("S"), py::arg("H"), py::arg("D"), py::arg("step"), py::arg("err"));
   m.def("kernel_launch_count", []() { return fa_kernel_launch_count(); });
   m.def("device_error", [](bool clear) { return fa_device_error(clear ? 1 : 0); }, py::arg("clear") = false);
   m.def("wait_selftest", [](int64_t limit_ns) {

@@ -165,3 +165,89 @@ class DecodeKVSplitGraph:
     def close(self):
         self.graph = None
         self.out = None
+
+
+class PeerDecodeExchange:
+    """decode_kv_split with the all-gather and the merge replaced by one kernel over peer memory.
+
+    Every rank's packed partial lives in one symmetric allocation (torch's symmetric memory: each
+    rank can load every other rank's buffer through NVLink).  A step is: this rank's decode writes
+    its partial into its own buffer; the merge kernel tells every peer this rank is ready, waits
+    until every peer is, and merges each row straight from all ranks' buffers (P2P loads, no
+    copy); the step-end kernel tells every peer this rank is done reading and waits for every
+    peer's done, so the next step may overwrite the buffers.  The step number is a device counter,
+    so `step()` can be captured in a CUDA graph.  Waits are bounded: a peer that does not arrive
+    sets `err` (read it with int(err)) instead of hanging the GPU.  Every rank of `group` must
+    construct the exchange and run the same steps; drop it before destroying the process group."""
+
+    SIGNAL_WORDS_OFFSET = 256   # our words start past the part of the signal pad torch may use itself
+
+    def __init__(self, B, nq, H, D, device, group=None):
+        import os
+        # plain peer loads only: no NVLink multicast object is created for the buffers
+        os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
+        import torch.distributed._symmetric_memory as symm_mem
+        self.world = _world(group)
+        self.B, self.nq, self.H, self.D = B, nq, H, D
+        if self.world > 8:
+            raise ValueError("PeerDecodeExchange: at most 8 ranks")
+        per = B * nq * H * (D + 1)
+        dev = torch.device(device)
+        if self.world > 1:
+            self.buf = symm_mem.empty(per, dtype=torch.float32, device=dev)
+            g = group if group is not None else dist.group.WORLD
+            self.hdl = symm_mem.rendezvous(self.buf, g)
+            self.rank = self.hdl.rank
+            pad_words = self.hdl.signal_pad_size // 4
+            if pad_words < self.SIGNAL_WORDS_OFFSET + 2 * self.world:
+                raise RuntimeError("PeerDecodeExchange: signal pad too small")
+            own = self.hdl.get_signal_pad(self.rank, (pad_words,), dtype=torch.int32)
+            own.zero_()
+            torch.cuda.synchronize(dev)
+            dist.barrier(group=group)
+            # the buffer sits at the same offset in every rank's block of the symmetric allocation
+            off = self.buf.data_ptr() - self.hdl.buffer_ptrs[self.rank]
+            if not 0 <= off <= self.hdl.buffer_size - 4 * per:
+                raise RuntimeError("PeerDecodeExchange: buffer outside its symmetric block")
+            bufs = [a + off for a in self.hdl.buffer_ptrs]
+            sigs = [a + 4 * self.SIGNAL_WORDS_OFFSET for a in self.hdl.signal_pad_ptrs]
+        else:
+            self.buf = torch.empty(per, dtype=torch.float32, device=dev)
+            self.hdl, self.rank = None, 0
+            self._own_signal = torch.zeros(2, dtype=torch.int32, device=dev)
+            bufs, sigs = [self.buf.data_ptr()], [self._own_signal.data_ptr()]
+        self.peer_bufs = torch.tensor(bufs, dtype=torch.int64, device=dev)
+        self.peer_signals = torch.tensor(sigs, dtype=torch.int64, device=dev)
+        self.step_count = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.out_view, self.lse_view = packed_partial_views(self.buf, B, nq, H, D)
+
+    def step(self, q, k_cache_local, v_cache_local, block_table_local, local_lengths, softmax_scale=None,
+             num_splits=0, phase_events=None):
+        """One decode step over this rank's chunk of the context; returns the merged output
+        (B, nq, H, D) in q's dtype.  phase_events: optional 4 CUDA events around the partial, the
+        peer merge and the step end."""
+        from . import _C
+        scale = softmax_scale if softmax_scale is not None else q.shape[-1] ** -0.5
+        ev = phase_events or [None] * 4
+        lens = local_lengths.to(device=q.device, dtype=torch.int32)
+        args = (self.peer_bufs, self.peer_signals, self.rank, self.world, self.B, self.nq, self.H, self.D,
+                self.step_count, self.err)
+        if ev[0] is not None:
+            ev[0].record()
+        _C.dec(q.contiguous(), k_cache_local, v_cache_local, block_table_local.to(torch.int32).contiguous(),
+               lens.contiguous(), None, None, None, None, False, float(scale), -1, int(num_splits), None, True,
+               out_fp32=True, out=self.out_view, lse_out=self.lse_view)
+        if ev[1] is not None:
+            ev[1].record()
+        out = _C.peer_merge(*args, q.dtype)
+        if ev[2] is not None:
+            ev[2].record()
+        _C.peer_step_end(*args)
+        if ev[3] is not None:
+            ev[3].record()
+        return out
+
+    def close(self):
+        self.hdl = None
+        self.buf = None

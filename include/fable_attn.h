@@ -308,6 +308,45 @@ typedef struct FaCombineParams {
 
 FA_API int fa_combine_launch(const FaCombineParams* p, void* stream);
 
+/* ------------------------------------------------------------------------------------------
+ * Multi-GPU decode exchange over peer memory (no counterpart in the reference, which has no
+ * multi-GPU layer; its merge rule is flash_attn_combine, package/fable_attn/flash_attn_interface.py
+ * :567-580).  A decode whose KV range is split across `world` GPUs leaves on every rank a packed
+ * partial: rows = B*S*H output rows of D fp32 values, then the rows' fp32 LSE, rows in (b, s, h)
+ * order (fa_decode_launch with o_f32 and lse_out pointing into the buffer).  All ranks' buffers
+ * live in one symmetric allocation, so every rank reaches every other rank's through a peer
+ * pointer (NVLink P2P loads; no multicast, no library kernel on peer memory).
+ *   fa_peer_merge_launch    : publishes "ready" for the current step to every peer, waits (bounded)
+ *                             until every peer is ready, then merges each row from all ranks'
+ *                             buffers into out [B, S, H, D] (out_dtype) and optionally lse_out
+ *                             [B, H, S].
+ *   fa_peer_step_end_launch : publishes "done", waits (bounded) until every peer is done (the
+ *                             buffers may then be overwritten by the next step), advances *step.
+ * Enqueue per decode step, in this order on one stream: the decode into the own buffer, the merge,
+ * the step end; every rank runs the same steps.  The step number lives on the device (*step, start
+ * at 0), so a captured CUDA graph replays correctly.  peer_signals[r] points at rank r's signal
+ * words (at least 2 * world uint32, zero before the first step): word r' of rank r holds rank r''s
+ * ready step, word world + r' its done step.  A wait that exceeds wait_ns (0 = 2 s) sets
+ * FA_PEER_ERR_WAIT in *err_flag (when given) and the kernel carries on without hanging.
+ * -------------------------------------------------------------------------------------------*/
+#define FA_PEER_MAX_WORLD 8
+#define FA_PEER_ERR_WAIT 1
+typedef struct FaPeerMergeParams {
+  unsigned int struct_size;
+  const float* const* peer_bufs;       /* device array [world]: each rank's packed partial */
+  unsigned int* const* peer_signals;   /* device array [world]: each rank's signal words */
+  int rank, world;
+  int B, S, H, D;                      /* D a multiple of 4 */
+  void* out; int out_dtype;
+  float* lse_out;                      /* optional [B, H, S] */
+  int* step;                           /* this rank's device step counter */
+  int* err_flag;                       /* optional device int */
+  unsigned long long wait_ns;          /* bound of each wait; 0 = 2 s */
+} FaPeerMergeParams;
+
+FA_API int fa_peer_merge_launch(const FaPeerMergeParams* p, void* stream);
+FA_API int fa_peer_step_end_launch(const FaPeerMergeParams* p, void* stream);
+
 /* ---- introspection ---- */
 FA_API int fa_abi_version(void);
 FA_API const char* fa_last_error(void);       /* message of the last failing call on this thread */

@@ -68,6 +68,30 @@ def _worker(rank, world, port, ret):
         finally:
             graph.close()
             del graph
+        # the exchange over peer memory (one merge kernel reading every rank's buffer over NVLink),
+        # eager and graph-replayed, gives the NCCL path's result
+        ex = M.PeerDecodeExchange(B, 1, H, D, dev)
+        try:
+            for _ in range(2):
+                got = ex.step(q, kl, vl, btl, loc.to(dev))
+                err = max(err, ((got.float() - ref.float()).norm() / ref.float().norm()).item())
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                ex.step(q, kl, vl, btl, loc.to(dev))
+            torch.cuda.current_stream().wait_stream(side)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                gout = ex.step(q, kl, vl, btl, loc.to(dev))
+            for _ in range(3):
+                g.replay()
+                torch.cuda.synchronize()
+                err = max(err, ((gout.float() - ref.float()).norm() / ref.float().norm()).item())
+            if int(ex.err.item()) != 0:
+                err = float("inf")
+            del g
+        finally:
+            ex.close()
         ret[rank] = err
     finally:
         dist.destroy_process_group()
@@ -173,3 +197,32 @@ def test_decode_kv_split_graph_replays_the_step():
             assert torch.equal(got, want)
     finally:
         g.close()
+
+
+def test_peer_exchange_one_process():
+    """PeerDecodeExchange with one rank (no process group): the merge kernel reads only its own
+    buffer; eager and graph-replayed steps equal the decode, and the device step counter advances."""
+    from fable_attn import multigpu as M
+    dev = torch.device("cuda", 0)
+    q, kc, vc, bt, lens, chunks = _chunked_case(dev, 1)
+    import fable_attn as fa
+    ref = fa.flash_attn_with_kvcache(q, kc, vc, cache_seqlens=torch.from_numpy(lens.astype(np.int32)).to(dev),
+                                     block_table=bt)
+    ex = M.PeerDecodeExchange(q.shape[0], 1, q.shape[2], q.shape[3], dev)
+    out = ex.step(q, *chunks[0])
+    assert (out.float() - ref.float()).norm() / ref.float().norm() < 2.5e-3
+    g = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        ex.step(q, *chunks[0])
+    torch.cuda.current_stream().wait_stream(side)
+    with torch.cuda.graph(g):
+        gout = ex.step(q, *chunks[0])
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(gout, out)
+    assert int(ex.step_count.item()) == 5 and int(ex.err.item()) == 0
+    del g
+    ex.close()
