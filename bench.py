@@ -419,56 +419,79 @@ def bench_decode_split(dev, ws, rank, steps=20, warmup=5):
         torch.cuda.synchronize()
         return _max_over_ranks(a.elapsed_time(b) / steps, ws, dev)
 
-    def phases(fn):
-        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
+    def phases(fn, n):
+        # n phases: n + 1 events per step
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(n + 1)] for _ in range(steps)]
         for i in range(steps):
             fn(ev[i])
         torch.cuda.synchronize()
-        ph = [statistics.mean(e[j].elapsed_time(e[j + 1]) for e in ev) for j in range(3)]
+        ph = [statistics.mean(e[j].elapsed_time(e[j + 1]) for e in ev) for j in range(n)]
         return [_max_over_ranks(x, ws, dev) for x in ph]
 
-    def graphed(fn):
+    def graphed(fn, per):
+        # per steps in one graph (the peer exchange alternates between two buffer slots)
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(side):
-            for _ in range(3):
+            for _ in range(4):
                 fn()
         torch.cuda.current_stream().wait_stream(side)
         torch.cuda.synchronize()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
-            fn()
+            for _ in range(per):
+                fn()
         return g
 
-    # the product path: this rank's decode into its buffer of a symmetric allocation, then one
-    # kernel that merges straight from every rank's buffer over NVLink (and a step-end handshake);
-    # one decode step = one replay of the captured step
-    ex = M.PeerDecodeExchange(B, 1, Hq, D, dev)
-    peer = lambda e=None: ex.step(q, kc, vc, bt, lc, softmax_scale=D ** -0.5, phase_events=e)   # noqa: E731
-    g = graphed(peer)
-    ms = timed(g.replay)
-    ms_eager = timed(peer)
-    ph = phases(peer)
-    peer_err = int(ex.err.item())
-    del g
+    # the product path: this rank's decode into its slot of a symmetric allocation (two slots,
+    # alternating), then one kernel that merges straight from every rank's slot over NVLink; the
+    # graph holds two steps (one per slot), so one decode step = half a replay
+    try:
+        ex = M.PeerDecodeExchange(B, 1, Hq, D, dev)
+        made = 1
+    except Exception as e:   # every rank learns whether every rank has the exchange before using it
+        ex, made, why = None, 0, f"{type(e).__name__}: {e}"[:200]
+    if ws > 1:
+        t = torch.tensor([made], device=dev, dtype=torch.int32)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MIN)
+        made = int(t.item())
+    peer_res = None
+    if made:
+        peer = lambda e=None: ex.step(q, kc, vc, bt, lc, softmax_scale=D ** -0.5, phase_events=e)   # noqa: E731
+        g = graphed(peer, 2)
+        ms_p = timed(g.replay) / 2
+        ms_eager = timed(peer)
+        ph = phases(peer, 2)
+        peer_err = int(ex.err.item())
+        del g
+        peer_res = {"ms": round(ms_p, 4), "ms_eager": round(ms_eager, 4), "wait_errors": peer_err,
+                    "step": "graph replay (two steps per replay): decode partial into this step's slot + one merge "
+                            "kernel reading every rank's slot over NVLink",
+                    "phase_ms": {"partial": round(ph[0], 4), "peer_merge": round(ph[1], 4)}}
+    if ex is not None:
+        ex.close()
     # beside it: the same step with an NCCL all-gather of the packed partials and the merge kernel
     nccl = lambda e=None: M.decode_kv_split(q, kc, vc, bt, lc, softmax_scale=D ** -0.5, phase_events=e)  # noqa: E731
-    g2 = graphed(nccl)
+    g2 = graphed(nccl, 1)
     ms_nccl = timed(g2.replay)
-    ph2 = phases(nccl)
+    ph2 = phases(nccl, 3)
     del g2
-    ex.close()
     nbytes = float(lens.sum()) * Hk * D * 2 * 2
-    return {"config": f"paged decode B16 Hq32 Hk8 D128 bf16 page256 L~U[16K,32K] (same lengths as decode_paged), "
-                      f"KV range split over {ws} GPU(s); partials merged by one kernel over peer memory (NVLink)",
-            "ms": round(ms, 4), "GBps": round(nbytes / ms / 1e6, 1), "bytes": nbytes,
-            "step": "one CUDA-graph replay per step (decode partial + peer merge + step-end handshake)",
-            "ms_eager": round(ms_eager, 4), "wait_errors": peer_err,
-            "phase_ms": {"partial": round(ph[0], 4), "peer_merge": round(ph[1], 4), "step_end": round(ph[2], 4)},
-            "nccl_path": {"ms": round(ms_nccl, 4), "GBps": round(nbytes / ms_nccl / 1e6, 1),
-                          "step": "graph replay: decode partial + NCCL all-gather of packed partials + merge",
-                          "phase_ms": {"partial": round(ph2[0], 4), "all_gather": round(ph2[1], 4),
-                                       "merge": round(ph2[2], 4)}}}
+    nccl_res = {"ms": round(ms_nccl, 4), "step": "graph replay: decode partial + NCCL all-gather of packed partials "
+                "+ merge kernel", "phase_ms": {"partial": round(ph2[0], 4), "all_gather": round(ph2[1], 4),
+                                               "merge": round(ph2[2], 4)}}
+    # both exchanges are product paths (multigpu.PeerDecodeExchange, multigpu.decode_kv_split): the
+    # line reports the faster one as `ms` and both in full
+    best = "peer_memory" if peer_res and peer_res["ms"] <= ms_nccl else "nccl_all_gather"
+    ms = peer_res["ms"] if best == "peer_memory" else ms_nccl
+    out = {"config": f"paged decode B16 Hq32 Hk8 D128 bf16 page256 L~U[16K,32K] (same lengths as decode_paged), "
+                     f"KV range split over {ws} GPU(s), partials merged across ranks", "ms": round(ms, 4),
+           "GBps": round(nbytes / ms / 1e6, 1), "bytes": nbytes, "path": best, "nccl_all_gather": nccl_res}
+    if peer_res:
+        out["peer_memory"] = peer_res
+    else:
+        out["peer_memory"] = {"unavailable": why if not made and ex is None else "not every rank could set it up"}
+    return out
 
 
 def bench_varlen_swa(dev, steps=10, warmup=3, kv_groups=8):

@@ -54,6 +54,7 @@ template <typename TO>
 __global__ void peer_merge_kernel(const FaPeerMergeParams p) {
   const unsigned int step = (unsigned int)(*p.step) + 1u;
   const uint64_t limit = p.wait_ns ? p.wait_ns : 2000000000ull;
+  const long long slot = p.slot_floats ? (long long)((step - 1u) & 1u) * p.slot_floats : 0;
   // publish: every CTA's threads 0 .. world-1 store this rank's ready word into each peer (same
   // value, so the redundancy is harmless, and no CTA depends on another being resident)
   if (threadIdx.x < (unsigned)p.world && (int)threadIdx.x != p.rank) {
@@ -76,7 +77,7 @@ __global__ void peer_merge_kernel(const FaPeerMergeParams p) {
     float lse[FA_PEER_MAX_WORLD];
 #pragma unroll
     for (int r = 0; r < FA_PEER_MAX_WORLD; ++r) {
-      lse[r] = (ok && r < p.world) ? __ldcg(p.peer_bufs[r] + rows * p.D + row) : -INFINITY;
+      lse[r] = (ok && r < p.world) ? __ldcg(p.peer_bufs[r] + slot + rows * p.D + row) : -INFINITY;
       M = fmaxf(M, lse[r]);
     }
     float W = 0.f;
@@ -91,7 +92,7 @@ __global__ void peer_merge_kernel(const FaPeerMergeParams p) {
 #pragma unroll
       for (int r = 0; r < FA_PEER_MAX_WORLD; ++r) {
         if (r < p.world && lse[r] > 0.f) {
-          const float4 v = __ldcg(reinterpret_cast<const float4*>(p.peer_bufs[r] + row * p.D + d));
+          const float4 v = __ldcg(reinterpret_cast<const float4*>(p.peer_bufs[r] + slot + row * p.D + d));
           a.x = fmaf(lse[r], v.x, a.x);
           a.y = fmaf(lse[r], v.y, a.y);
           a.z = fmaf(lse[r], v.z, a.z);
@@ -107,6 +108,18 @@ __global__ void peer_merge_kernel(const FaPeerMergeParams p) {
     if (p.lse_out && lane == 0) {
       const long long h = row % p.H, bs = row / p.H, s = bs % p.S, b = bs / p.S;
       p.lse_out[(b * p.H + h) * p.S + s] = W > 0.f ? M + logf(W) : -INFINITY;
+    }
+  }
+  if (p.slot_floats) {
+    // two-slot mode: the last CTA to finish advances the step (every CTA read it when it started)
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      if (atomicAdd(p.done_ctas, 1) == (int)gridDim.x - 1) {
+        *p.done_ctas = 0;
+        *p.step = (int)step;
+        __threadfence();
+      }
     }
   }
 }
@@ -145,6 +158,10 @@ extern "C" FA_API int fa_peer_merge_launch(const FaPeerMergeParams* pp, void* st
   FA_CHECK_ARG(p.B >= 0 && p.S >= 0 && p.H >= 0 && p.D > 0 && p.D % 4 == 0, "peer merge: bad sizes (D a multiple of 4)");
   FA_CHECK_ARG(p.out_dtype == FA_DTYPE_F16 || p.out_dtype == FA_DTYPE_BF16 || p.out_dtype == FA_DTYPE_F32,
                "peer merge: out_dtype %d", p.out_dtype);
+  FA_CHECK_ARG(p.slot_floats >= 0 && (p.slot_floats == 0 || p.done_ctas),
+               "peer merge: two-slot mode needs done_ctas");
+  FA_CHECK_ARG(p.slot_floats == 0 || p.slot_floats >= (long long)p.B * p.S * p.H * (p.D + 1),
+               "peer merge: slot_floats %lld below one packed partial", p.slot_floats);
   const long long rows = (long long)p.B * p.S * p.H;
   cudaStream_t st = (cudaStream_t)stream;
   // one warp per row, 8 warps per CTA, at most two CTAs per SM's worth

@@ -432,7 +432,8 @@ torch::Tensor combine_packed(torch::Tensor buf, int64_t nsplit, int64_t B, int64
 // peer_bufs / peer_signals are int64 CUDA tensors [world] holding the ranks' device addresses of
 // their packed partials and signal words; step / err are int32 CUDA tensors [1] of this rank.
 FaPeerMergeParams peer_params(torch::Tensor peer_bufs, torch::Tensor peer_signals, int64_t rank, int64_t world,
-                              int64_t B, int64_t S, int64_t H, int64_t D, torch::Tensor step, torch::Tensor err) {
+                              int64_t B, int64_t S, int64_t H, int64_t D, torch::Tensor step, torch::Tensor err,
+                              int64_t slot_floats = 0, c10::optional<torch::Tensor> done_ctas = c10::nullopt) {
   TORCH_CHECK_VALUE(peer_bufs.is_cuda() && peer_signals.is_cuda() && peer_bufs.scalar_type() == torch::kInt64 &&
                         peer_signals.scalar_type() == torch::kInt64 && peer_bufs.numel() == world &&
                         peer_signals.numel() == world,
@@ -447,14 +448,22 @@ FaPeerMergeParams peer_params(torch::Tensor peer_bufs, torch::Tensor peer_signal
   p.rank = (int)rank; p.world = (int)world;
   p.B = (int)B; p.S = (int)S; p.H = (int)H; p.D = (int)D;
   p.step = step.data_ptr<int>(); p.err_flag = err.data_ptr<int>();
+  p.slot_floats = slot_floats;
+  if (done_ctas.has_value() && done_ctas->defined()) {
+    TORCH_CHECK_VALUE(done_ctas->is_cuda() && done_ctas->scalar_type() == torch::kInt32,
+                      "fable_attn: done_ctas must be an int32 CUDA tensor");
+    p.done_ctas = done_ctas->data_ptr<int>();
+  }
   return p;
 }
 
 torch::Tensor peer_merge(torch::Tensor peer_bufs, torch::Tensor peer_signals, int64_t rank, int64_t world, int64_t B,
                          int64_t S, int64_t H, int64_t D, torch::Tensor step, torch::Tensor err,
-                         c10::ScalarType out_dtype, c10::optional<torch::Tensor> lse_out) {
+                         c10::ScalarType out_dtype, c10::optional<torch::Tensor> lse_out, int64_t slot_floats,
+                         c10::optional<torch::Tensor> done_ctas) {
   const c10::cuda::CUDAGuard guard(step.device());
-  FaPeerMergeParams p = peer_params(peer_bufs, peer_signals, rank, world, B, S, H, D, step, err);
+  FaPeerMergeParams p = peer_params(peer_bufs, peer_signals, rank, world, B, S, H, D, step, err, slot_floats,
+                                    done_ctas);
   auto out = torch::empty({B, S, H, D}, step.options().dtype(out_dtype));
   p.out = out.data_ptr(); p.out_dtype = dt_of(out);
   p.lse_out = const_cast<float*>(opt_f32(lse_out));
@@ -561,7 +570,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("H"), py::arg("D"), py::arg("out_dtype"));
   m.def("peer_merge", &peer_merge, py::arg("peer_bufs"), py::arg("peer_signals"), py::arg("rank"), py::arg("world"),
         py::arg("B"), py::arg("S"), py::arg("H"), py::arg("D"), py::arg("step"), py::arg("err"),
-        py::arg("out_dtype"), py::arg("lse_out") = c10::optional<torch::Tensor>());
+        py::arg("out_dtype"), py::arg("lse_out") = c10::optional<torch::Tensor>(), py::arg("slot_floats") = 0,
+        py::arg("done_ctas") = c10::optional<torch::Tensor>());
   m.def("peer_step_end", &peer_step_end, py::arg("peer_bufs"), py::arg("peer_signals"), py::arg("rank"),
         py::arg("world"), py::arg("B"), py::arg("S"), py::arg("H"), py::arg("D"), py::arg("step"), py::arg("err"));
   m.def("kernel_launch_count", []() { return fa_kernel_launch_count(); });

@@ -10,9 +10,11 @@ Only two kinds of work are split, and only one of them communicates:
   NVLink) brings every rank's packed buffer to every rank, and the merge kernel applies the LSE
   rule out = sum_r exp(lse_r - M) out_r / sum_r exp(lse_r - M), M = max_r lse_r, reading the
   gathered buffer in place.
+  PeerDecodeExchange replaces the all-gather and the merge with one kernel that loads every
+  rank's packed partial over NVLink (peer pointers of a symmetric allocation, plain loads, no
+  multicast) after a bounded ready handshake.
   The reference has no multi-GPU layer; the merge rule is its flash_attn_combine
   (package/fable_attn/flash_attn_interface.py:567-580).
-Remote partials always arrive through NCCL into local buffers: no kernel reads peer memory.
 """
 import torch
 import torch.distributed as dist
@@ -173,28 +175,39 @@ class PeerDecodeExchange:
     Every rank's packed partial lives in one symmetric allocation (torch's symmetric memory: each
     rank can load every other rank's buffer through NVLink).  A step is: this rank's decode writes
     its partial into its own buffer; the merge kernel tells every peer this rank is ready, waits
-    until every peer is, and merges each row straight from all ranks' buffers (P2P loads, no
-    copy); the step-end kernel tells every peer this rank is done reading and waits for every
-    peer's done, so the next step may overwrite the buffers.  The step number is a device counter,
-    so `step()` can be captured in a CUDA graph.  Waits are bounded: a peer that does not arrive
-    sets `err` (read it with int(err)) instead of hanging the GPU.  Every rank of `group` must
-    construct the exchange and run the same steps; drop it before destroying the process group."""
+    until every peer is, and merges each row straight from all ranks' buffers (P2P loads, no copy).
+
+    slots=2 (default): the buffer holds two partials and steps alternate between them.  A slot is
+    rewritten two steps later, and by then every peer has said "ready" for the step in between,
+    which it only does after its previous merge finished reading, so a step is two launches (the
+    decode and the merge, which also advances the device step counter).  slots=1: one partial and a
+    third launch per step, the step end, which tells every peer this rank is done reading and waits
+    for every peer's done before the buffer may be overwritten.
+
+    The step number is a device counter, so steps can be captured in a CUDA graph; with slots=2 a
+    captured graph must hold an even number of steps (the host picks the slot of each step).  Waits
+    are bounded: a peer that does not arrive sets `err` (read it with int(err)) instead of hanging
+    the GPU.  Every rank of `group` must construct the exchange and run the same steps; drop it
+    before destroying the process group."""
 
     SIGNAL_WORDS_OFFSET = 256   # our words start past the part of the signal pad torch may use itself
 
-    def __init__(self, B, nq, H, D, device, group=None):
+    def __init__(self, B, nq, H, D, device, group=None, slots=2):
         import os
         # plain peer loads only: no NVLink multicast object is created for the buffers
         os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
         import torch.distributed._symmetric_memory as symm_mem
+        if slots not in (1, 2):
+            raise ValueError("PeerDecodeExchange: slots must be 1 or 2")
         self.world = _world(group)
-        self.B, self.nq, self.H, self.D = B, nq, H, D
+        self.B, self.nq, self.H, self.D, self.slots = B, nq, H, D, slots
         if self.world > 8:
             raise ValueError("PeerDecodeExchange: at most 8 ranks")
         per = B * nq * H * (D + 1)
+        self.per = per
         dev = torch.device(device)
         if self.world > 1:
-            self.buf = symm_mem.empty(per, dtype=torch.float32, device=dev)
+            self.buf = symm_mem.empty(slots * per, dtype=torch.float32, device=dev)
             g = group if group is not None else dist.group.WORLD
             self.hdl = symm_mem.rendezvous(self.buf, g)
             self.rank = self.hdl.rank
@@ -207,39 +220,49 @@ class PeerDecodeExchange:
             dist.barrier(group=group)
             # the buffer sits at the same offset in every rank's block of the symmetric allocation
             off = self.buf.data_ptr() - self.hdl.buffer_ptrs[self.rank]
-            if not 0 <= off <= self.hdl.buffer_size - 4 * per:
+            if not 0 <= off <= self.hdl.buffer_size - 4 * slots * per:
                 raise RuntimeError("PeerDecodeExchange: buffer outside its symmetric block")
             bufs = [a + off for a in self.hdl.buffer_ptrs]
             sigs = [a + 4 * self.SIGNAL_WORDS_OFFSET for a in self.hdl.signal_pad_ptrs]
         else:
-            self.buf = torch.empty(per, dtype=torch.float32, device=dev)
+            self.buf = torch.empty(slots * per, dtype=torch.float32, device=dev)
             self.hdl, self.rank = None, 0
             self._own_signal = torch.zeros(2, dtype=torch.int32, device=dev)
             bufs, sigs = [self.buf.data_ptr()], [self._own_signal.data_ptr()]
         self.peer_bufs = torch.tensor(bufs, dtype=torch.int64, device=dev)
         self.peer_signals = torch.tensor(sigs, dtype=torch.int64, device=dev)
         self.step_count = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.done_ctas = torch.zeros(1, dtype=torch.int32, device=dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
-        self.out_view, self.lse_view = packed_partial_views(self.buf, B, nq, H, D)
+        self.views = [packed_partial_views(self.buf[i * per:(i + 1) * per], B, nq, H, D) for i in range(slots)]
+        self.out_view, self.lse_view = self.views[0]
+        self._issued = 0   # steps enqueued by this host (the slot of the next one is _issued % slots)
 
     def step(self, q, k_cache_local, v_cache_local, block_table_local, local_lengths, softmax_scale=None,
              num_splits=0, phase_events=None):
         """One decode step over this rank's chunk of the context; returns the merged output
-        (B, nq, H, D) in q's dtype.  phase_events: optional 4 CUDA events around the partial, the
-        peer merge and the step end."""
+        (B, nq, H, D) in q's dtype.  phase_events: optional CUDA events (3, or 4 with slots=1)
+        recorded around the partial, the peer merge and the step end."""
         from . import _C
         scale = softmax_scale if softmax_scale is not None else q.shape[-1] ** -0.5
-        ev = phase_events or [None] * 4
+        ev = list(phase_events or []) + [None] * 4
         lens = local_lengths.to(device=q.device, dtype=torch.int32)
         args = (self.peer_bufs, self.peer_signals, self.rank, self.world, self.B, self.nq, self.H, self.D,
                 self.step_count, self.err)
+        out_v, lse_v = self.views[self._issued % self.slots]
+        self._issued += 1
         if ev[0] is not None:
             ev[0].record()
         _C.dec(q.contiguous(), k_cache_local, v_cache_local, block_table_local.to(torch.int32).contiguous(),
                lens.contiguous(), None, None, None, None, False, float(scale), -1, int(num_splits), None, True,
-               out_fp32=True, out=self.out_view, lse_out=self.lse_view)
+               out_fp32=True, out=out_v, lse_out=lse_v)
         if ev[1] is not None:
             ev[1].record()
+        if self.slots == 2:
+            out = _C.peer_merge(*args, q.dtype, slot_floats=self.per, done_ctas=self.done_ctas)
+            if ev[2] is not None:
+                ev[2].record()
+            return out
         out = _C.peer_merge(*args, q.dtype)
         if ev[2] is not None:
             ev[2].record()

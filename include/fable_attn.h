@@ -322,12 +322,20 @@ FA_API int fa_combine_launch(const FaCombineParams* p, void* stream);
  *                             [B, H, S].
  *   fa_peer_step_end_launch : publishes "done", waits (bounded) until every peer is done (the
  *                             buffers may then be overwritten by the next step), advances *step.
- * Enqueue per decode step, in this order on one stream: the decode into the own buffer, the merge,
- * the step end; every rank runs the same steps.  The step number lives on the device (*step, start
- * at 0), so a captured CUDA graph replays correctly.  peer_signals[r] points at rank r's signal
- * words (at least 2 * world uint32, zero before the first step): word r' of rank r holds rank r''s
- * ready step, word world + r' its done step.  A wait that exceeds wait_ns (0 = 2 s) sets
- * FA_PEER_ERR_WAIT in *err_flag (when given) and the kernel carries on without hanging.
+ * Two ways to run it, every rank running the same steps on one stream:
+ *   one slot  (slot_floats = 0): per step the decode into the own buffer, the merge, the step end;
+ *   two slots (slot_floats = the floats of one packed partial, each buffer holding two): step s
+ *             (counted from 1) uses slot (s - 1) % 2; per step the decode into that slot and the
+ *             merge, which then also advances *step (its last CTA).  A slot is rewritten two steps
+ *             later, after every peer has published "ready" for the step in between (which it does
+ *             only once its previous merge has finished reading), so no step end is needed.
+ * The step number lives on the device (*step, start at 0; done_ctas, a device int starting at 0,
+ * counts the merge's finished CTAs in two-slot mode), so captured CUDA graphs replay correctly
+ * (in two-slot mode a graph holds an even number of steps, the host picking the slot).
+ * peer_signals[r] points at rank r's signal words (at least 2 * world uint32, zero before the first
+ * step): word r' of rank r holds rank r''s ready step, word world + r' its done step.  A wait that
+ * exceeds wait_ns (0 = 2 s) sets FA_PEER_ERR_WAIT in *err_flag (when given) and the kernel carries
+ * on without hanging.
  * -------------------------------------------------------------------------------------------*/
 #define FA_PEER_MAX_WORLD 8
 #define FA_PEER_ERR_WAIT 1
@@ -342,6 +350,8 @@ typedef struct FaPeerMergeParams {
   int* step;                           /* this rank's device step counter */
   int* err_flag;                       /* optional device int */
   unsigned long long wait_ns;          /* bound of each wait; 0 = 2 s */
+  long long slot_floats;               /* two-slot mode: floats per slot; 0 = one slot */
+  int* done_ctas;                      /* two-slot mode: device int, 0 before the first step */
 } FaPeerMergeParams;
 
 FA_API int fa_peer_merge_launch(const FaPeerMergeParams* p, void* stream);

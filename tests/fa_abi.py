@@ -62,6 +62,14 @@ class FaCombineParams(C.Structure):
                 ("out_split_stride", C.c_longlong), ("lse_split_stride", C.c_longlong), ("lse_bsh", C.c_int)]
 
 
+class FaPeerMergeParams(C.Structure):
+    _fields_ = [("struct_size", C.c_uint), ("peer_bufs", C.c_void_p), ("peer_signals", C.c_void_p),
+                ("rank", C.c_int), ("world", C.c_int), ("B", C.c_int), ("S", C.c_int), ("H", C.c_int),
+                ("D", C.c_int), ("out", C.c_void_p), ("out_dtype", C.c_int), ("lse_out", C.c_void_p),
+                ("step", C.c_void_p), ("err_flag", C.c_void_p), ("wait_ns", C.c_ulonglong),
+                ("slot_floats", C.c_longlong), ("done_ctas", C.c_void_p)]
+
+
 _LIB = None
 
 
@@ -76,6 +84,8 @@ def lib():
         L.fa_decode_scratch_floats.restype = C.c_longlong
         L.fa_decode_scratch_floats.argtypes = [C.c_int] * 5
         L.fa_combine_launch.argtypes = [C.POINTER(FaCombineParams), C.c_void_p]
+        L.fa_peer_merge_launch.argtypes = [C.POINTER(FaPeerMergeParams), C.c_void_p]
+        L.fa_peer_step_end_launch.argtypes = [C.POINTER(FaPeerMergeParams), C.c_void_p]
         L.fa_dropout_mask_words.restype = C.c_longlong
         L.fa_dropout_mask_words.argtypes = [C.c_int] * 3
         L.fa_dropout_mask_launch.argtypes = [C.c_ulonglong, C.c_float] + [C.c_int] * 6 + [C.c_void_p, C.c_void_p]

@@ -13,6 +13,7 @@ import fa_abi as A
 STRUCTS = {
     "FaStrides": A.FaStrides, "FaFwdParams": A.FaFwdParams, "FaBwdParams": A.FaBwdParams,
     "FaDecParams": A.FaDecParams, "FaCombineParams": A.FaCombineParams,
+    "FaPeerMergeParams": A.FaPeerMergeParams,
 }
 
 
@@ -94,6 +95,28 @@ def test_decode_rejects_bad_requests():
     assert L.fa_decode_launch(C.byref(p), 1, None, None, None) == A.FA_ERR_INVALID
     p.nsplit = 1
     assert L.fa_decode_launch(C.byref(p), 1, None, C.c_void_p(16), None) == A.FA_ERR_INVALID  # new_k without new_v
+
+
+def test_peer_merge_rejects_bad_requests():
+    """Argument checks of the peer-memory merge run before any launch (no GPU needed)."""
+    L = A.lib()
+    p = A.FaPeerMergeParams()
+    p.struct_size = C.sizeof(A.FaPeerMergeParams) - 8
+    assert L.fa_peer_merge_launch(C.byref(p), None) == A.FA_ERR_ABI
+    p.struct_size = C.sizeof(A.FaPeerMergeParams)
+    p.peer_bufs = p.peer_signals = p.out = p.step = 16
+    p.rank, p.world, p.B, p.S, p.H, p.D, p.out_dtype = 0, 9, 1, 1, 8, 128, 1
+    assert L.fa_peer_merge_launch(C.byref(p), None) == A.FA_ERR_INVALID     # more than 8 ranks
+    p.world, p.rank = 2, 2
+    assert L.fa_peer_merge_launch(C.byref(p), None) == A.FA_ERR_INVALID     # rank outside the world
+    p.rank, p.D = 1, 126
+    assert L.fa_peer_merge_launch(C.byref(p), None) == A.FA_ERR_INVALID     # D not a multiple of 4
+    p.D, p.slot_floats = 128, 8 * 129
+    assert L.fa_peer_merge_launch(C.byref(p), None) == A.FA_ERR_INVALID     # two slots without done_ctas
+    p.done_ctas, p.slot_floats = 16, 8 * 128
+    assert L.fa_peer_merge_launch(C.byref(p), None) == A.FA_ERR_INVALID     # slot smaller than a partial
+    p.world = 0
+    assert L.fa_peer_step_end_launch(C.byref(p), None) == A.FA_ERR_INVALID
 
 
 def test_split_heuristic_bounds():

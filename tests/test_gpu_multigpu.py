@@ -71,23 +71,25 @@ def _worker(rank, world, port, ret):
         # the exchange over peer memory (one merge kernel reading every rank's buffer over NVLink),
         # eager and graph-replayed, gives the NCCL path's result
         ex = M.PeerDecodeExchange(B, 1, H, D, dev)
+        loc = loc.to(dev)   # device tensors only: the step is captured below
         try:
             for _ in range(2):
-                got = ex.step(q, kl, vl, btl, loc.to(dev))
+                got = ex.step(q, kl, vl, btl, loc)
                 err = max(err, ((got.float() - ref.float()).norm() / ref.float().norm()).item())
             side = torch.cuda.Stream()
             side.wait_stream(torch.cuda.current_stream())
             with torch.cuda.stream(side):
-                ex.step(q, kl, vl, btl, loc.to(dev))
+                ex.step(q, kl, vl, btl, loc)
             torch.cuda.current_stream().wait_stream(side)
             g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
-                gout = ex.step(q, kl, vl, btl, loc.to(dev))
+            with torch.cuda.graph(g):   # two steps: one per slot of the double buffer
+                gouts = [ex.step(q, kl, vl, btl, loc) for _ in range(2)]
             for _ in range(3):
                 g.replay()
                 torch.cuda.synchronize()
-                err = max(err, ((gout.float() - ref.float()).norm() / ref.float().norm()).item())
-            if int(ex.err.item()) != 0:
+                for gout in gouts:
+                    err = max(err, ((gout.float() - ref.float()).norm() / ref.float().norm()).item())
+            if int(ex.err.item()) != 0 or int(ex.step_count.item()) != 3 + 6:
                 err = float("inf")
             del g
         finally:
@@ -199,16 +201,18 @@ def test_decode_kv_split_graph_replays_the_step():
         g.close()
 
 
-def test_peer_exchange_one_process():
+@pytest.mark.parametrize("slots", [1, 2])
+def test_peer_exchange_one_process(slots):
     """PeerDecodeExchange with one rank (no process group): the merge kernel reads only its own
-    buffer; eager and graph-replayed steps equal the decode, and the device step counter advances."""
+    buffer; eager and graph-replayed steps equal the decode, and the device step counter advances
+    (a two-slot graph holds two steps)."""
     from fable_attn import multigpu as M
     dev = torch.device("cuda", 0)
     q, kc, vc, bt, lens, chunks = _chunked_case(dev, 1)
     import fable_attn as fa
     ref = fa.flash_attn_with_kvcache(q, kc, vc, cache_seqlens=torch.from_numpy(lens.astype(np.int32)).to(dev),
                                      block_table=bt)
-    ex = M.PeerDecodeExchange(q.shape[0], 1, q.shape[2], q.shape[3], dev)
+    ex = M.PeerDecodeExchange(q.shape[0], 1, q.shape[2], q.shape[3], dev, slots=slots)
     out = ex.step(q, *chunks[0])
     assert (out.float() - ref.float()).norm() / ref.float().norm() < 2.5e-3
     g = torch.cuda.CUDAGraph()
@@ -217,12 +221,14 @@ def test_peer_exchange_one_process():
     with torch.cuda.stream(side):
         ex.step(q, *chunks[0])
     torch.cuda.current_stream().wait_stream(side)
+    per_graph = 2 if slots == 2 else 1
     with torch.cuda.graph(g):
-        gout = ex.step(q, *chunks[0])
+        gouts = [ex.step(q, *chunks[0]) for _ in range(per_graph)]
     for _ in range(3):
         g.replay()
     torch.cuda.synchronize()
-    assert torch.equal(gout, out)
-    assert int(ex.step_count.item()) == 5 and int(ex.err.item()) == 0
+    for gout in gouts:
+        assert torch.equal(gout, out)
+    assert int(ex.step_count.item()) == 2 + 3 * per_graph and int(ex.err.item()) == 0
     del g
     ex.close()
