@@ -124,7 +124,10 @@ __device__ __forceinline__ void zero_tile_rows(uint8_t* tile, int rows, int r0, 
 }
 
 // K-major / MN-major descriptors of a [rows][D] tile stored as D/64 chunks of rows x 128 B
-// (TMA SWIZZLE_128B boxes).  kstep = 16-element step along the contracted dimension.
+// (TMA SWIZZLE_128B boxes).  kstep = 16-element step along the contracted dimension.  The MMA
+// issuers build the step-0 descriptor once and add each step's byte offset / 16 to it (the start
+// address field holds address / 16 in 14 bits, and every shared-memory address stays below 2^18):
+// the single issuing thread spends fewer instructions per MMA, which the short N = 64 MMAs need.
 __device__ __forceinline__ uint64_t desc_kmajor(uint32_t tile, int rows, int kstep) {
   const int c = kstep / 4, off = (kstep % 4) * 32;
   return sdesc_sw128(tile + c * rows * 128 + off, 16, 1024);
@@ -246,8 +249,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // dS of keys [32 hf, 32 hf + 32) sits packed in the first 16 columns of half hf's own
         // S (hi) and dP (lo) columns
         const uint32_t hi = tmem + C::S_COL + (i & 1) * 64, lo = tmem + C::DP_COL + (i & 1) * 64;
+        const uint64_t bd0 = desc_mnmajor(kt, BN, 0);
+#pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t bd = desc_mnmajor(kt, BN, kk);
+          const uint64_t bd = bd0 + (uint64_t)(kk * 128);
           const uint32_t off = (uint32_t)(32 * (kk / 2) + 8 * (kk % 2));
           mma_ts(tmem + C::DQ_COL, hi + off, bd, ID_Q, (i > 0 || kk > 0) ? 1u : 0u);
           mma_ts(tmem + C::DQ_COL, lo + off, bd, ID_Q, 1u);
@@ -271,9 +276,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       tc_fence_after();
       if (lane == 0) {
         const uint32_t kt = sK + s * C::KV_BYTES, vt = sV + s * C::KV_BYTES;
+        const uint64_t aq = desc_kmajor(sQ, BM, 0), ado = desc_kmajor(sDO, BM, 0), bk = desc_kmajor(kt, BN, 0),
+                       bv = desc_kmajor(vt, BN, 0);
+#pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          mma_ss(tmem + C::S_COL + (j & 1) * 64, desc_kmajor(sQ, BM, kk), desc_kmajor(kt, BN, kk), ID_S, kk > 0);
-          mma_ss(tmem + C::DP_COL + (j & 1) * 64, desc_kmajor(sDO, BM, kk), desc_kmajor(vt, BN, kk), ID_S, kk > 0);
+          const uint64_t oa = (uint64_t)(((kk / 4) * BM * 128 + (kk % 4) * 32) >> 4);
+          const uint64_t ob = (uint64_t)(((kk / 4) * BN * 128 + (kk % 4) * 32) >> 4);
+          mma_ss(tmem + C::S_COL + (j & 1) * 64, aq + oa, bk + ob, ID_S, kk > 0);
+          mma_ss(tmem + C::DP_COL + (j & 1) * 64, ado + oa, bv + ob, ID_S, kk > 0);
         }
         mma_commit(bar + Bz::SP_FULL + 8 * (j & 1));
         mma_commit(bar + Bz::V_EMPTY + 8 * s);
@@ -569,11 +579,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // half hf (query rows [32 hf, 32 hf + 32)) keeps, in its own 32 S^T columns, P~^T packed at
         // [0,16) and dS^T hi at [16,32), and dS^T lo in the first 16 of its dP^T columns
         const uint32_t pb = tmem + C::S_COL + (i & 1) * 64, lo = tmem + C::DP_COL + (i & 1) * 64;
+        const uint64_t mdo = desc_mnmajor(dot, BQ, 0), mq = desc_mnmajor(qt, BQ, 0);
+#pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk) {
           const uint32_t off = (uint32_t)(32 * (kk / 2) + 8 * (kk % 2));
-          mma_ts(tmem + C::DV_COL, pb + off, desc_mnmajor(dot, BQ, kk), ID_O, (i > 0 || kk > 0) ? 1u : 0u);
-          mma_ts(tmem + C::DK_COL, pb + 16 + off, desc_mnmajor(qt, BQ, kk), ID_O, (i > 0 || kk > 0) ? 1u : 0u);
-          mma_ts(tmem + C::DK_COL, lo + off, desc_mnmajor(qt, BQ, kk), ID_O, 1u);
+          const uint64_t step = (uint64_t)(kk * 128);
+          mma_ts(tmem + C::DV_COL, pb + off, mdo + step, ID_O, (i > 0 || kk > 0) ? 1u : 0u);
+          mma_ts(tmem + C::DK_COL, pb + 16 + off, mq + step, ID_O, (i > 0 || kk > 0) ? 1u : 0u);
+          mma_ts(tmem + C::DK_COL, lo + off, mq + step, ID_O, 1u);
         }
         mma_commit(bar + Bz::Q_EMPTY + 8 * s);
       }
@@ -593,9 +606,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       tc_fence_after();
       if (lane == 0) {
         const uint32_t qt = sQ + s * C::QT_BYTES, dot = sDO + s * C::QT_BYTES;
+        const uint64_t ak = desc_kmajor(sK, BK, 0), av = desc_kmajor(sV, BK, 0), bq = desc_kmajor(qt, BQ, 0),
+                       bdo = desc_kmajor(dot, BQ, 0);
+#pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          mma_ss(tmem + C::S_COL + (i & 1) * 64, desc_kmajor(sK, BK, kk), desc_kmajor(qt, BQ, kk), ID_S, kk > 0);
-          mma_ss(tmem + C::DP_COL + (i & 1) * 64, desc_kmajor(sV, BK, kk), desc_kmajor(dot, BQ, kk), ID_S, kk > 0);
+          const uint64_t oa = (uint64_t)(((kk / 4) * BK * 128 + (kk % 4) * 32) >> 4);
+          const uint64_t ob = (uint64_t)(((kk / 4) * BQ * 128 + (kk % 4) * 32) >> 4);
+          mma_ss(tmem + C::S_COL + (i & 1) * 64, ak + oa, bq + ob, ID_S, kk > 0);
+          mma_ss(tmem + C::DP_COL + (i & 1) * 64, av + oa, bdo + ob, ID_S, kk > 0);
         }
         mma_commit(bar + Bz::SP_FULL + 8 * (i & 1));
       }
