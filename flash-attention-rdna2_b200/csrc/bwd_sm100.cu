@@ -252,7 +252,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const uint64_t bd0 = desc_mnmajor(kt, BN, 0);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t bd = bd0 + (uint64_t)(kk * 128);
+          const uint64_t bd = desc_add(bd0, kk * 128);
           const uint32_t off = (uint32_t)(32 * (kk / 2) + 8 * (kk % 2));
           mma_ts(tmem + C::DQ_COL, hi + off, bd, ID_Q, (i > 0 || kk > 0) ? 1u : 0u);
           mma_ts(tmem + C::DQ_COL, lo + off, bd, ID_Q, 1u);
@@ -280,10 +280,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                        bv = desc_kmajor(vt, BN, 0);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint64_t oa = (uint64_t)(((kk / 4) * BM * 128 + (kk % 4) * 32) >> 4);
-          const uint64_t ob = (uint64_t)(((kk / 4) * BN * 128 + (kk % 4) * 32) >> 4);
-          mma_ss(tmem + C::S_COL + (j & 1) * 64, aq + oa, bk + ob, ID_S, kk > 0);
-          mma_ss(tmem + C::DP_COL + (j & 1) * 64, ado + oa, bv + ob, ID_S, kk > 0);
+          const uint32_t oa = (uint32_t)(((kk / 4) * BM * 128 + (kk % 4) * 32) >> 4);
+          const uint32_t ob = (uint32_t)(((kk / 4) * BN * 128 + (kk % 4) * 32) >> 4);
+          mma_ss(tmem + C::S_COL + (j & 1) * 64, desc_add(aq, oa), desc_add(bk, ob), ID_S, kk > 0);
+          mma_ss(tmem + C::DP_COL + (j & 1) * 64, desc_add(ado, oa), desc_add(bv, ob), ID_S, kk > 0);
         }
         mma_commit(bar + Bz::SP_FULL + 8 * (j & 1));
         mma_commit(bar + Bz::V_EMPTY + 8 * s);
@@ -583,10 +583,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk) {
           const uint32_t off = (uint32_t)(32 * (kk / 2) + 8 * (kk % 2));
-          const uint64_t step = (uint64_t)(kk * 128);
-          mma_ts(tmem + C::DV_COL, pb + off, mdo + step, ID_O, (i > 0 || kk > 0) ? 1u : 0u);
-          mma_ts(tmem + C::DK_COL, pb + 16 + off, mq + step, ID_O, (i > 0 || kk > 0) ? 1u : 0u);
-          mma_ts(tmem + C::DK_COL, lo + off, mq + step, ID_O, 1u);
+          const uint32_t step = (uint32_t)(kk * 128);
+          mma_ts(tmem + C::DV_COL, pb + off, desc_add(mdo, step), ID_O, (i > 0 || kk > 0) ? 1u : 0u);
+          mma_ts(tmem + C::DK_COL, pb + 16 + off, desc_add(mq, step), ID_O, (i > 0 || kk > 0) ? 1u : 0u);
+          mma_ts(tmem + C::DK_COL, lo + off, desc_add(mq, step), ID_O, 1u);
         }
         mma_commit(bar + Bz::Q_EMPTY + 8 * s);
       }
@@ -610,10 +610,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                        bdo = desc_kmajor(dot, BQ, 0);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint64_t oa = (uint64_t)(((kk / 4) * BK * 128 + (kk % 4) * 32) >> 4);
-          const uint64_t ob = (uint64_t)(((kk / 4) * BQ * 128 + (kk % 4) * 32) >> 4);
-          mma_ss(tmem + C::S_COL + (i & 1) * 64, ak + oa, bq + ob, ID_S, kk > 0);
-          mma_ss(tmem + C::DP_COL + (i & 1) * 64, av + oa, bdo + ob, ID_S, kk > 0);
+          const uint32_t oa = (uint32_t)(((kk / 4) * BK * 128 + (kk % 4) * 32) >> 4);
+          const uint32_t ob = (uint32_t)(((kk / 4) * BQ * 128 + (kk % 4) * 32) >> 4);
+          mma_ss(tmem + C::S_COL + (i & 1) * 64, desc_add(ak, oa), desc_add(bq, ob), ID_S, kk > 0);
+          mma_ss(tmem + C::DP_COL + (i & 1) * 64, desc_add(av, oa), desc_add(bdo, ob), ID_S, kk > 0);
         }
         mma_commit(bar + Bz::SP_FULL + 8 * (i & 1));
       }

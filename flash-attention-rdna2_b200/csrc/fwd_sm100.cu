@@ -343,12 +343,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       tc_fence_after();
       if (lane == 0) {
         const uint32_t pt = tmem + (uint32_t)(gg & 1) * 128u;
-        const uint32_t vbase = sV + s * C::KV_BYTES;
+        const uint64_t vd0 = sdesc_sw128(sV + s * C::KV_BYTES, C::CH_BYTES, 1024);
+#pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
           // A = P from TMEM: keys [64 hf, 64 hf + 64) sit packed in columns [64 hf, 64 hf + 32)
           // B = V tile, MN-major: 16 keys = 16 rows of 128 B; D spans NCH swizzle atoms (LBO apart)
           const uint32_t pa = pt + (uint32_t)((kk * 16) / HB) * 64u + (uint32_t)(((kk * 16) % HB) / 2);
-          const uint64_t bd = sdesc_sw128(vbase + kk * 16 * 128, C::CH_BYTES, 1024);
+          const uint64_t bd = desc_add(vd0, (uint32_t)(kk * 128));
           mma_ts(tmem + C::O_COL, pa, bd, IDESC_O, (jj > 0 || kk > 0) ? 1u : 0u);
         }
         mma_commit(bar + Bars::V_EMPTY + 8 * s);
@@ -372,12 +373,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         tc_fence_after();
         if (lane == 0) {
           const uint32_t st = tmem + (uint32_t)(gg & 1) * 128u;
-          const uint32_t kbase = sK + s * C::KV_BYTES;
+          const uint64_t ad0 = sdesc_sw128(sQ, 16, 1024), bd0 = sdesc_sw128(sK + s * C::KV_BYTES, 16, 1024);
+#pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const int c = kk / 4, off = (kk % 4) * 32;   // 16 columns = 32 bytes inside a 128-byte chunk
-            const uint64_t ad = sdesc_sw128(sQ + c * (BM * 128) + off, 16, 1024);
-            const uint64_t bd = sdesc_sw128(kbase + c * C::CH_BYTES + off, 16, 1024);
-            mma_ss(st, ad, bd, IDESC_S, kk > 0 ? 1u : 0u);
+            mma_ss(st, desc_add(ad0, (uint32_t)((c * (BM * 128) + off) >> 4)),
+                   desc_add(bd0, (uint32_t)((c * C::CH_BYTES + off) >> 4)), IDESC_S, kk > 0 ? 1u : 0u);
           }
           mma_commit(bar + Bars::S_FULL + 8 * (gg & 1));
           mma_commit(bar + Bars::K_EMPTY + 8 * s);
@@ -888,11 +889,12 @@ __global__ void __launch_bounds__(PP_THREADS, 1)
       if (!ok) record_error(2);
       auto issue_s = [&](int j, int t) {   // lane 0; K tile j has landed
         const uint32_t kbase = sK + (j % C::NSK) * C::KV_BYTES, qbase = sQ + t * C::Q_BYTES;
+        const uint64_t ad0 = sdesc_sw128(qbase, 16, 1024), bd0 = sdesc_sw128(kbase, 16, 1024);
+#pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const int c = kk / 4, off = (kk % 4) * 32;   // 16 columns = 32 bytes inside a 128-byte chunk
-          const uint64_t ad = sdesc_sw128(qbase + c * (BM * 128) + off, 16, 1024);
-          const uint64_t bd = sdesc_sw128(kbase + c * C::CH_BYTES + off, 16, 1024);
-          mma_ss(tmem + (uint32_t)(t * BN), ad, bd, IDESC_S, kk > 0 ? 1u : 0u);
+          mma_ss(tmem + (uint32_t)(t * BN), desc_add(ad0, (uint32_t)((c * (BM * 128) + off) >> 4)),
+                 desc_add(bd0, (uint32_t)((c * C::CH_BYTES + off) >> 4)), IDESC_S, kk > 0 ? 1u : 0u);
         }
         mma_commit(bar + Bz::S_FULL + 8 * t);
       };
@@ -908,10 +910,11 @@ __global__ void __launch_bounds__(PP_THREADS, 1)
         tc_fence_after();
         if (lane == 0) {
           const uint32_t pt = tmem + (uint32_t)(t * BN);
-          const uint32_t vbase = sV + s * C::KV_BYTES;
+          const uint64_t vd0 = sdesc_sw128(sV + s * C::KV_BYTES, C::CH_BYTES, 1024);
+#pragma unroll
           for (int kk = 0; kk < BN / 16; ++kk) {
             // A = P from TMEM (keys packed two per column); B = V tile, MN-major
-            const uint64_t bd = sdesc_sw128(vbase + kk * 16 * 128, C::CH_BYTES, 1024);
+            const uint64_t bd = desc_add(vd0, (uint32_t)(kk * 128));
             mma_ts(tmem + C::O_COL + (uint32_t)(t * D), pt + kk * 8, bd, IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
           }
           mma_commit(bar + Bz::O_DONE + 8 * t);

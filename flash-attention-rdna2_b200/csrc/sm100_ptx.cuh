@@ -167,6 +167,12 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo_byt
   return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16) |
          ((uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
 }
+// descriptor d advanced by `units` 16-byte units: only the low word's start-address field changes
+__device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t units) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"((uint32_t)d + units), "r"((uint32_t)(d >> 32)));
+  return r;
+}
 // Instruction descriptor of tcgen05.mma kind::f16 with fp32 accumulation.
 //   ab_fmt: 0 = f16, 1 = bf16 (A and B always the same type); a_mn / b_mn: operand is MN-major
 __host__ __device__ constexpr uint32_t idesc_f16(int ab_fmt, int M, int N, int a_mn, int b_mn) {
