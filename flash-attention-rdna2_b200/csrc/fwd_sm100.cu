@@ -773,41 +773,6 @@ struct PpCfg {   // D = 128
   static constexpr uint32_t O_COL = 256;
   static_assert(SMEM <= 232448, "shared memory per CTA");
 };
-// Wave-tail split of the two-tile kernel (dense inputs whose every row sees every key).  With U
-// work units (256 query rows of one head) on P SMs, the last U % P units would run as a partly
-// empty wave; instead each of them is cut into `nsplit` key ranges run by separate CTAs.  A 1-D
-// grid: CTAs [0, n_full) take units [0, n_full) whole, CTA n_full + t takes key range t % nsplit
-// of unit n_full + t / nsplit and writes its rows' O / l (fp32) and LSE to ws; the merge kernel
-// combines the key ranges (flash_attn_combine's rule) into O and LSE.  nsplit = 0: the plain
-// (q tiles, heads, batch) grid.
-struct PpSplit {
-  int nsplit, n_full, nqb2;   // key ranges per tail unit, whole units, 256-row tiles per head
-  float* ws;                  // [tail unit][range][256 rows][D] then [tail unit][range][256 rows] LSE
-  long long ws_lse;           // float offset of the LSE block
-};
-
-// unit of the CTA: (batch z, head h, first row qb) and, for a tail CTA, (tail unit, key range)
-__device__ __forceinline__ void pp_unit(const PpSplit& sp, int NH, int& z, int& h, int& qb, int& tail, int& part) {
-  tail = -1;
-  part = 0;
-  if (sp.nsplit == 0) {
-    z = blockIdx.z;
-    h = blockIdx.y;
-    qb = (gridDim.x - 1 - blockIdx.x) * (2 * BM);   // heavy (late, causal) tiles first
-    return;
-  }
-  long long u = blockIdx.x;
-  if (u >= sp.n_full) {
-    const long long t = u - sp.n_full;
-    tail = (int)(t / sp.nsplit);
-    part = (int)(t % sp.nsplit);
-    u = sp.n_full + tail;
-  }
-  qb = (int)(u % sp.nqb2) * (2 * BM);
-  h = (int)((u / sp.nqb2) % NH);
-  z = (int)(u / ((long long)sp.nqb2 * NH));
-}
-
 struct PpBars {   // S_FULL / P_FULL / O_DONE: [tile A, tile B]
   static constexpr int Q_FULL = 0, K_FULL = 8, K_EMPTY = 24, V_FULL = 40, V_EMPTY = 64, S_FULL = 88,
                        P_FULL = 104, O_DONE = 120, MMA_DRAIN = 136, TMEM_ADDR = 144;
@@ -822,7 +787,7 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 template <bool BF16, bool DROP>
 __global__ void __launch_bounds__(PP_THREADS, 1)
     fwd_pp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                  const __grid_constant__ CUtensorMap tmV, const FaFwdParams p, const PpSplit sp) {
+                  const __grid_constant__ CUtensorMap tmV, const FaFwdParams p) {
   using C = PpCfg;
   using Bz = PpBars;
   constexpr int D = C::D;
@@ -834,25 +799,19 @@ __global__ void __launch_bounds__(PP_THREADS, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sgen + C::OFF_BAR + Bz::TMEM_ADDR);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  int z, h, qb, tail, part;   // tail >= 0: this CTA computes key range `part` of tail unit `tail`
-  pp_unit(sp, p.NH, z, h, qb, tail, part);
-  const int kvh = h / p.gqa;
+  const int z = blockIdx.z, h = blockIdx.y, kvh = h / p.gqa;
   const int SQ = p.SQ, SK = p.SK;
+  const int qb = (gridDim.x - 1 - blockIdx.x) * (2 * BM);   // heavy (late, causal) tiles first
   if (qb >= SQ) return;
 
-  // key tiles: the union of what the CTA's 256 rows can see (a tail CTA: its share of them)
+  // key tiles: the union of what the CTA's 256 rows can see
   int klo, khi, dmy;
   fa_key_range(qb, SQ, SK, p.causal, p.win_left, p.win_right, p.attn_chunk, klo, dmy);
   fa_key_range(min(qb + 2 * BM, SQ) - 1, SQ, SK, p.causal, p.win_left, p.win_right, p.attn_chunk, dmy, khi);
   klo = max(klo, 0);
   khi = min(khi, SK - 1);
-  int t0 = klo / BN;
-  int ntiles = (khi >= klo) ? (khi / BN - t0 + 1) : 0;
-  if (tail >= 0) {
-    const int a = part * ntiles / sp.nsplit, b = (part + 1) * ntiles / sp.nsplit;
-    t0 += a;
-    ntiles = b - a;
-  }
+  const int t0 = klo / BN;
+  const int ntiles = (khi >= klo) ? (khi / BN - t0 + 1) : 0;
 
   if (tid == 0) {
     mbar_init(bar + Bz::Q_FULL, 1);
@@ -1122,14 +1081,6 @@ __global__ void __launch_bounds__(PP_THREADS, 1)
     const float inv = l > 0.f ? inv_keep / l : 0.f;   // 1/(1-p) of the kept probabilities (1 without dropout)
     using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
     T* orow = (T*)p.O + (long long)z * p.sO.b + (long long)h * p.sO.h + (long long)q * p.sO.s;
-    // a tail CTA's rows go to the workspace: O / l in fp32 and the range's LSE (the unit is
-    // decoded again here rather than kept live through the key loop)
-    int tail_e, part_e;
-    {
-      int z2, h2, qb2;
-      pp_unit(sp, p.NH, z2, h2, qb2, tail_e, part_e);
-    }
-    const long long wrow = tail_e >= 0 ? ((long long)(tail_e * sp.nsplit + part_e) * (2 * BM) + tt * BM + r) : 0;
 #pragma unroll
     for (int c = 0; c < D; c += 32) {
       float o[32];
@@ -1140,12 +1091,7 @@ __global__ void __launch_bounds__(PP_THREADS, 1)
 #pragma unroll
         for (int i = 0; i < 32; ++i) o[i] = 0.f;
       }
-      if (q < SQ && tail_e >= 0) {
-        float4* dst = reinterpret_cast<float4*>(sp.ws + wrow * D + c);
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          dst[i] = make_float4(o[4 * i] * inv, o[4 * i + 1] * inv, o[4 * i + 2] * inv, o[4 * i + 3] * inv);
-      } else if (q < SQ) {
+      if (q < SQ) {
         uint32_t w[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
@@ -1162,9 +1108,7 @@ __global__ void __launch_bounds__(PP_THREADS, 1)
         for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
       }
     }
-    if (q < SQ && tail_e >= 0) {
-      sp.ws[sp.ws_lse + wrow] = l > 0.f ? m_ref * FA_LN2 + logf(l) : -INFINITY;
-    } else if (q < SQ && p.LSE) {
+    if (q < SQ && p.LSE) {
       const long long li = fa_lse_index(false, z, h, p.NH, p.SQ, 0, p.lse_total_q, q);
       p.LSE[li] = l > 0.f ? m_ref * FA_LN2 + logf(l) : -INFINITY;
     }
@@ -1174,50 +1118,6 @@ __global__ void __launch_bounds__(PP_THREADS, 1)
   if (warp == WARP_MMA) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
-  }
-}
-
-// Merge of the wave-tail split: one warp per (tail unit, row) combines the unit's nsplit key
-// ranges, out = sum_r w_r O_r / sum_r w_r l_r-normalised, w_r = exp(lse_r - max lse) (the rule of
-// flash_attn_combine, package/fable_attn/flash_attn_interface.py:567-580), and writes O and LSE.
-template <bool BF16>
-__global__ void __launch_bounds__(256) fwd_pp_merge_kernel(const FaFwdParams p, const PpSplit sp, int n_tail) {
-  using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-  constexpr int D = PpCfg::D, R = 2 * BM;
-  const int lane = threadIdx.x & 31;
-  const long long rows = (long long)n_tail * R;
-  for (long long wr = (long long)blockIdx.x * 8 + threadIdx.x / 32; wr < rows; wr += (long long)gridDim.x * 8) {
-    const int tail = (int)(wr / R), rr = (int)(wr % R);
-    const long long u = sp.n_full + tail;
-    const int qb = (int)(u % sp.nqb2) * R, h = (int)((u / sp.nqb2) % p.NH);
-    const int z = (int)(u / ((long long)sp.nqb2 * p.NH)), q = qb + rr;
-    if (q >= p.SQ) continue;
-    float m = -INFINITY;
-    for (int r = 0; r < sp.nsplit; ++r)
-      m = fmaxf(m, sp.ws[sp.ws_lse + (long long)(tail * sp.nsplit + r) * R + rr]);
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    float wsum = 0.f;
-    for (int r = 0; r < sp.nsplit; ++r) {
-      const long long row = (long long)(tail * sp.nsplit + r) * R + rr;
-      const float lse = sp.ws[sp.ws_lse + row];
-      const float w = (m == -INFINITY) ? 0.f : __expf(lse - m);
-      wsum += w;
-      if (w > 0.f) {
-        const float4 v = reinterpret_cast<const float4*>(sp.ws + row * D)[lane];
-        acc.x = fmaf(w, v.x, acc.x);
-        acc.y = fmaf(w, v.y, acc.y);
-        acc.z = fmaf(w, v.z, acc.z);
-        acc.w = fmaf(w, v.w, acc.w);
-      }
-    }
-    const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
-    T* o = (T*)p.O + (long long)z * p.sO.b + (long long)h * p.sO.h + (long long)q * p.sO.s + 4 * lane;
-    o[0] = Elem<T>::from_f(acc.x * inv);
-    o[1] = Elem<T>::from_f(acc.y * inv);
-    o[2] = Elem<T>::from_f(acc.z * inv);
-    o[3] = Elem<T>::from_f(acc.w * inv);
-    if (lane == 0 && p.LSE)
-      p.LSE[fa_lse_index(false, z, h, p.NH, p.SQ, 0, p.lse_total_q, q)] = wsum > 0.f ? m + logf(wsum) : -INFINITY;
   }
 }
 
@@ -1308,55 +1208,8 @@ int launch_pp(const FaFwdParams& p, cudaStream_t st, const CUtensorMap& mq, cons
   if (!pp_ready<BF16, DROP>()) return -1;
   static unsigned long long done = 0;
   if (int rc = fa::ensure_smem((const void*)fwd_pp_kernel<BF16, DROP>, PpCfg::SMEM, &done)) return rc;
-  const int nqb2 = (p.SQ + 2 * BM - 1) / (2 * BM);
-  PpSplit sp{0, 0, nqb2, nullptr, 0};
-  // Wave-tail split (dense rows that all see every key, no dropout): the key ranges per tail unit
-  // that minimise the whole-wave count, F + ceil(R s / P) / s for F full waves and R tail units,
-  // taken when it saves at least 5 % (the merge and the partials' traffic cost ~2-4 %).
-  // FABLE_ATTN_FWD_SPLIT=s forces s key ranges per tail unit wherever the split applies.
-  const long long U = (long long)nqb2 * p.NH * p.batch, P = fa::num_sms();
-  const bool all_keys = !p.causal && p.win_left < 0 && p.win_right < 0 && p.attn_chunk <= 0 && !DROP;
-  const int key_tiles = (p.SK + BN - 1) / BN;
-  int nsplit = 0;
-  if (all_keys && U > 0 && U % P != 0 && U <= 0x7fffffffLL / 8) {
-    const long long F = U / P, R = U % P;
-    double best = (double)(F + 1);
-    for (int s = 2; s <= 8; s *= 2) {
-      if (key_tiles < 2 * s) break;
-      const double t = (double)F + (double)((R * s + P - 1) / P) / s;
-      if (t < best * 0.95) { best = t; nsplit = s; }
-    }
-    if (const char* force = getenv("FABLE_ATTN_FWD_SPLIT")) {
-      const int s = atoi(force);
-      nsplit = (s >= 2 && s <= 8 && key_tiles >= s) ? s : 0;
-    }
-  }
-  if (nsplit) {
-    sp.nsplit = nsplit;
-    sp.n_full = (int)((U / P) * P);
-    const long long n_tail = U - sp.n_full, parts = n_tail * nsplit;
-    sp.ws_lse = parts * (2 * BM) * PpCfg::D;
-    // stream-ordered workspace (capturable in a CUDA graph); without it the plain grid runs
-    if (cudaMallocAsync((void**)&sp.ws, (size_t)(sp.ws_lse + parts * (2 * BM)) * sizeof(float), st) != cudaSuccess) {
-      (void)cudaGetLastError();
-      sp = PpSplit{0, 0, nqb2, nullptr, 0};
-    } else {
-      fwd_pp_kernel<BF16, DROP><<<(unsigned)(sp.n_full + parts), PP_THREADS, PpCfg::SMEM, st>>>(mq, mk, mv, p, sp);
-      fa::count_launch();
-      if (int rc = fa::cuda_status(cudaGetLastError(), "fwd_sm100 launch")) {
-        cudaFreeAsync(sp.ws, st);
-        return rc;
-      }
-      const int mctas = (int)std::min<long long>((n_tail * 2 * BM + 7) / 8, 4 * P);
-      fwd_pp_merge_kernel<BF16><<<mctas, 256, 0, st>>>(p, sp, (int)n_tail);
-      fa::count_launch();
-      const int rc = fa::cuda_status(cudaGetLastError(), "fwd_sm100 merge launch");
-      cudaFreeAsync(sp.ws, st);
-      return rc;
-    }
-  }
-  dim3 grid(nqb2, p.NH, p.batch);
-  fwd_pp_kernel<BF16, DROP><<<grid, PP_THREADS, PpCfg::SMEM, st>>>(mq, mk, mv, p, sp);
+  dim3 grid((p.SQ + 2 * BM - 1) / (2 * BM), p.NH, p.batch);
+  fwd_pp_kernel<BF16, DROP><<<grid, PP_THREADS, PpCfg::SMEM, st>>>(mq, mk, mv, p);
   fa::count_launch();
   return fa::cuda_status(cudaGetLastError(), "fwd_sm100 launch");
 }
