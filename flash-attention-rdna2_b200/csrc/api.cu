@@ -53,6 +53,11 @@ bool require_tc() {
   return v && v[0] && v[0] != '0';
 }
 
+bool pdl_enabled() {
+  const char* v = getenv("FABLE_ATTN_NO_PDL");
+  return !(v && v[0] && v[0] != '0');
+}
+
 int ensure_smem(const void* func, int bytes, unsigned long long* done_mask) {
   const int d = current_device();
   const unsigned long long bit = 1ull << (d & 63);

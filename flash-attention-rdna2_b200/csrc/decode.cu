@@ -242,8 +242,11 @@ __global__ void __launch_bounds__(DEC_THREADS) dec_partial_kernel(const FaDecPar
 }
 
 // ---------------------------------------------------------------- split merge -> O, LSE
+constexpr int FA_DEC_MAX_SPLITS = 512;   // fa_decode_launch refuses nsplit above it
 template <typename T>
 __global__ void dec_merge_kernel(const FaDecParams p) {
+  pdl_wait();      // the partials of the kernel before (a programmatic launch starts early)
+  pdl_trigger();   // and the kernel after may start its own prologue
   const int row = blockIdx.x, h = blockIdx.y, HD = p.HD;
   {   // an empty context has no partials to read: O = 0, LSE = -inf
     const int b = row / p.nq, tk = row % p.nq, ctx0 = p.ctx_len[b];
@@ -259,24 +262,41 @@ __global__ void dec_merge_kernel(const FaDecParams p) {
       return;
     }
   }
+  // split weights: the first warp loads every split's (m, l) at once (lane s, s + 32, ...), reduces
+  // the max and the weighted sum by shuffles, and leaves w_s = 2^(m_s - M) in shared memory
+  __shared__ float wsh[FA_DEC_MAX_SPLITS];
+  __shared__ float lsh[2];
   const float* base = p.scratch + ((long long)row * p.NH + h) * (long long)p.nsplit * (HD + 2);
-  float M = -INFINITY;
-  for (int s = 0; s < p.nsplit; ++s) M = fmaxf(M, base[(long long)s * (HD + 2)]);
-  float L = 0.f;
-  if (M != -INFINITY)
-    for (int s = 0; s < p.nsplit; ++s) {
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    float M = -INFINITY;
+    for (int s = lane; s < p.nsplit; s += 32) M = fmaxf(M, base[(long long)s * (HD + 2)]);
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    float L = 0.f;
+    for (int s = lane; s < p.nsplit; s += 32) {
       const float ms = base[(long long)s * (HD + 2)];
-      if (ms != -INFINITY) L += base[(long long)s * (HD + 2) + 1] * exp2f(ms - M);
+      const float w = (M != -INFINITY && ms != -INFINITY) ? exp2f(ms - M) : 0.f;
+      wsh[s] = w;
+      if (w > 0.f) L += base[(long long)s * (HD + 2) + 1] * w;
     }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+    if (lane == 0) {
+      lsh[0] = M;
+      lsh[1] = L;
+    }
+  }
+  __syncthreads();
+  const float M = lsh[0], L = lsh[1];
   const float invL = L > 0.f ? 1.f / L : 0.f;
   const long long obase = ((long long)row * p.NH + h) * HD;
   for (int d = threadIdx.x; d < HD; d += blockDim.x) {
     float a = 0.f;
-    if (M != -INFINITY)
-      for (int s = 0; s < p.nsplit; ++s) {
-        const float ms = base[(long long)s * (HD + 2)];
-        if (ms != -INFINITY) a += base[(long long)s * (HD + 2) + 2 + d] * exp2f(ms - M);
-      }
+    for (int s = 0; s < p.nsplit; ++s) {
+      const float w = wsh[s];
+      if (w > 0.f) a = fmaf(base[(long long)s * (HD + 2) + 2 + d], w, a);
+    }
     if (p.o_f32) ((float*)p.o)[obase + d] = a * invL;
     else ((T*)p.o)[obase + d] = Elem<T>::from_f(a * invL);
   }
@@ -649,9 +669,11 @@ int launch_t(const FaDecParams& p, cudaStream_t st, const void* nk, const void* 
   }
   if (rc) return rc;
   const int thr = p.HD < 32 ? 32 : p.HD;
-  dec_merge_kernel<T><<<dim3(p.batch * p.nq, p.NH), thr, 0, st>>>(p);
+  // programmatic launch: the merge's CTAs start while the partial kernel drains (they wait in
+  // pdl_wait for its results)
+  const cudaError_t le = fa::launch_pdl(dec_merge_kernel<T>, dim3(p.batch * p.nq, p.NH), dim3(thr), 0, st, p);
   fa::count_launch();
-  return fa::cuda_status(cudaGetLastError(), "decode merge launch");
+  return fa::cuda_status(le != cudaSuccess ? le : cudaGetLastError(), "decode merge launch");
 }
 
 // ---------------------------------------------------------------- flash_attn_combine

@@ -52,6 +52,7 @@ __device__ __forceinline__ bool wait_words(const unsigned int* base, int rank, i
 
 template <typename TO>
 __global__ void peer_merge_kernel(const FaPeerMergeParams p) {
+  pdl_wait();   // this rank's partial (written by the kernels before) is complete and visible
   const unsigned int step = (unsigned int)(*p.step) + 1u;
   const uint64_t limit = p.wait_ns ? p.wait_ns : 2000000000ull;
   const long long slot = p.slot_floats ? (long long)((step - 1u) & 1u) * p.slot_floats : 0;
@@ -166,11 +167,13 @@ extern "C" FA_API int fa_peer_merge_launch(const FaPeerMergeParams* pp, void* st
   cudaStream_t st = (cudaStream_t)stream;
   // one warp per row, 8 warps per CTA, at most two CTAs per SM's worth
   const long long ctas = std::min<long long>(std::max<long long>((rows + 7) / 8, 1), 2LL * fa::num_sms());
-  if (p.out_dtype == FA_DTYPE_F16) peer_merge_kernel<__half><<<(unsigned)ctas, 256, 0, st>>>(p);
-  else if (p.out_dtype == FA_DTYPE_BF16) peer_merge_kernel<__nv_bfloat16><<<(unsigned)ctas, 256, 0, st>>>(p);
-  else peer_merge_kernel<float><<<(unsigned)ctas, 256, 0, st>>>(p);
+  cudaError_t le;
+  if (p.out_dtype == FA_DTYPE_F16) le = fa::launch_pdl(peer_merge_kernel<__half>, dim3((unsigned)ctas), dim3(256), 0, st, p);
+  else if (p.out_dtype == FA_DTYPE_BF16)
+    le = fa::launch_pdl(peer_merge_kernel<__nv_bfloat16>, dim3((unsigned)ctas), dim3(256), 0, st, p);
+  else le = fa::launch_pdl(peer_merge_kernel<float>, dim3((unsigned)ctas), dim3(256), 0, st, p);
   fa::count_launch();
-  return fa::cuda_status(cudaGetLastError(), "peer merge launch");
+  return fa::cuda_status(le != cudaSuccess ? le : cudaGetLastError(), "peer merge launch");
 }
 
 extern "C" FA_API int fa_peer_step_end_launch(const FaPeerMergeParams* pp, void* stream) {

@@ -565,6 +565,7 @@ __global__ void __launch_bounds__(NTH, 1)
     }
     if (!ok) record_error(16);
   }
+  pdl_trigger();   // the merge kernel may start (it waits for this grid's completion before reading)
   tc_fence_before();
   __syncthreads();
   if (warp == 5) {

@@ -9,6 +9,16 @@
 #include <math.h>
 #include "fable_attn.h"
 
+#include <utility>
+
+// ---------------------------------------------------------------- programmatic dependent launch
+// A kernel launched with fa::launch_pdl may start while the kernel before it on the stream is
+// still finishing: pdl_wait() returns once that kernel has completed and its writes are visible
+// (a no-op after a plain launch), and pdl_trigger() lets the next kernel start early (it still
+// waits in its own pdl_wait() before reading anything this kernel writes).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 #define FA_LOG2E 1.4426950408889634f
 #define FA_LN2 0.6931471805599453f
 
@@ -227,3 +237,23 @@ int num_sms();
       return FA_ERR_INVALID;                \
     }                                       \
   } while (0)
+
+namespace fa {
+bool pdl_enabled();
+// cudaLaunchKernelEx with programmatic stream serialization (a plain launch when disabled)
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+}  // namespace fa

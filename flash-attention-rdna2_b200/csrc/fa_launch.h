@@ -19,8 +19,10 @@ int dec_device_error(int clear);   // bit 0: a decode pipeline wait timed out
 // tensor-core split-K decode partials; *taken = false when the call is outside its envelope
 int dec_tc_partial(const FaDecParams& p, int dtype, cudaStream_t st, bool* taken);
 int dec_tc_device_error(int clear);
-int rot_device_error(int clear);
-int fwd_simt_device_error(int clear);   // bit 0: an invalid block-table entry (paged forward)   // bit 0: a rotary position outside the cos/sin table
+int rot_device_error(int clear);        // bit 0: a rotary position outside the cos/sin table
+int fwd_simt_device_error(int clear);   // bit 0: an invalid block-table entry (paged forward)
+// FABLE_ATTN_NO_PDL set: launch every kernel plainly (no programmatic dependent launch)
+bool pdl_enabled();
 int num_sms();
 bool require_tc();   // FABLE_ATTN_REQUIRE_TC set: no CUDA-core fallback for fp16/bf16 fwd / bwd
 
