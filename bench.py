@@ -890,6 +890,23 @@ def profile_case(which, dev):
     elif which == "decode":
         for _ in range(1):
             bench_decode(dev, steps=3, warmup=0)
+    elif which == "decode_share8":   # one rank's 1/8 share of config 4's contexts: the decode alone
+        from fable_attn import multigpu as M
+        B, Hq, Hk, D, page = 16, 32, 8, 128, 256
+        lens = decode_lengths(B).astype(np.int64)
+        starts, ends = M.plan_kv_split(torch.from_numpy(lens), 8)
+        local = (ends[0] - starts[0]).to(torch.int32)
+        nper = int((int(local.max()) + page - 1) // page)
+        g = torch.Generator(device=dev).manual_seed(100)
+        kc = torch.randn(B * nper, page, Hk, D, device=dev, dtype=torch.bfloat16, generator=g)
+        vc = torch.randn(B * nper, page, Hk, D, device=dev, dtype=torch.bfloat16, generator=g)
+        bt = torch.from_numpy(np.random.default_rng(200).permutation(B * nper).astype(np.int32).reshape(B, nper)).to(dev)
+        q = torch.randn(B, 1, Hq, D, device=dev, dtype=torch.bfloat16, generator=g)
+        buf = torch.empty(B * Hq * (D + 1), device=dev, dtype=torch.float32)
+        ov, lv = M.packed_partial_views(buf, B, 1, Hq, D)
+        for _ in range(3):
+            _C.dec(q, kc, vc, bt, local.to(dev), None, None, None, None, False, D ** -0.5, -1, 0, None, True,
+                   out_fp32=True, out=ov, lse_out=lv)
     elif which == "bwd":
         bench_fwd_bwd_causal(dev, steps=1, warmup=0)
     elif which == "bwd_plain":   # config 3 shapes without dropout (the plain tensor-core kernels)
@@ -917,7 +934,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-extra", action="store_true", help="skip the config 3/4 figures")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
-    ap.add_argument("--profile", choices=["fwd", "decode", "bwd", "bwd_plain", "varlen"],
+    ap.add_argument("--profile", choices=["fwd", "decode", "decode_share8", "bwd", "bwd_plain", "varlen"],
                     help="run one reduced case for ncu and exit")
     args = ap.parse_args()
     if args.profile:
