@@ -119,11 +119,13 @@ __device__ __forceinline__ unsigned short bits16(float a) {
   else return __half_as_ushort(__float2half_rn(a));
 }
 
-// context of sequence b for its single new token: keys [lo, ctx); returns its tile count
-// (tiles lo/TT .. (ctx-1)/TT)
+// keys of sequence b's new tokens: the union [lo, ctx) of every token's range (token tk at
+// position ctx0 + tk sees [max(leftpad, ctx0 + tk - window + 1), ctx0 + tk + 1) with append,
+// [.., ctx0) without, so the union runs from the first token's start to the last token's end);
+// returns its tile count (tiles lo/TT .. (ctx-1)/TT)
 __device__ __forceinline__ int seq_tiles(const FaDecParams& p, int b, int& lo, int& ctx) {
   const int ctx0 = p.ctx_len[b];
-  ctx = ctx0 + (p.append ? 1 : 0);
+  ctx = ctx0 + (p.append ? p.nq : 0);
   int l = p.leftpad ? p.leftpad[b] : 0;
   if (p.window >= 0 && ctx0 - p.window + 1 > l) l = ctx0 - p.window + 1;
   lo = l > 0 ? l : 0;
@@ -174,13 +176,15 @@ __global__ void __launch_bounds__(NTH, 1)
   __shared__ uint32_t s_tmem;
   __shared__ long long s_part[NTH];   // per-thread tile sums, then their exclusive prefix
   __shared__ int s_maxn, s_b0;
+  __shared__ int s_rlo[16], s_rhi[16];   // several new tokens: each query row's keys [rlo, rhi)
+  __shared__ float s_rtk[16];            // and its token index
   __shared__ long long s_total, s_off0;
   const uint32_t sb = (smem_u32(smraw) + 1023u) & ~1023u;
   uint8_t* sg = smraw + (sb - smem_u32(smraw));
   auto bar = [&](int i) { return sb + (uint32_t)L::BAR + 8u * (uint32_t)i; };
 
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-  const int NKV = p.NH / p.gqa, nh = p.gqa;
+  const int NKV = p.NH / p.gqa, nh = p.nq * p.gqa;   // live query rows: (new token, head) pairs
   const int shift = __ffs(p.page) - 1, pmask = p.page - 1;
   const int R = p.page < TT ? p.page : TT;   // rows of one page-slice box
   const int c = blockIdx.x;
@@ -383,9 +387,8 @@ __global__ void __launch_bounds__(NTH, 1)
     // (one job = one pair of dims that rotate together)
     auto write_q = [&](const Seg& sq, int buf) {
       const int hb = sq.kvh * p.gqa;
-      const T* qg = (const T*)p.q + ((long long)sq.b * p.NH + hb) * HD;
       const int mode = p.rotary, rdim = p.rotary_dim > 0 ? p.rotary_dim : HD, half = rdim / 2;
-      const int rp = p.rotary_pos ? p.rotary_pos[sq.b] : p.ctx_len[sq.b];
+      const int rp0 = p.rotary_pos ? p.rotary_pos[sq.b] : p.ctx_len[sq.b];
       uint8_t* qs = sg + L::Q + buf * L::QB;
       for (int j = t; j < NRV * (HD / 2); j += 128) {
         const int r = j / (HD / 2), jj = j % (HD / 2);
@@ -399,9 +402,11 @@ __global__ void __launch_bounds__(NTH, 1)
           rot = mode == 2 && jj < half;
         }
         float x1 = 0.f, x2 = 0.f;
-        if (r < nh) {
-          x1 = Elem<T>::to_f(qg[r * HD + d1]);
-          x2 = Elem<T>::to_f(qg[r * HD + d2]);
+        if (r < nh) {   // row r = (new token r / gqa, head r % gqa of the group)
+          const int tk = r / p.gqa, rp = rp0 + tk;
+          const T* qg = (const T*)p.q + (((long long)sq.b * p.nq + tk) * p.NH + hb + r % p.gqa) * HD;
+          x1 = Elem<T>::to_f(qg[d1]);
+          x2 = Elem<T>::to_f(qg[d2]);
           if (rot) {
             const float cs = p.cos[(long long)rp * half + jj], sn = p.sin[(long long)rp * half + jj];
             const float y1 = x1 * cs - x2 * sn, y2 = x2 * cs + x1 * sn;
@@ -434,9 +439,22 @@ __global__ void __launch_bounds__(NTH, 1)
 #pragma unroll
       for (int r = 0; r < NRV; ++r) {
         acc[r] = 0.f; mref[r] = -INFINITY; lt[r] = 0.f; cprev[r] = 1.f;
-        slope2[r] = (p.alibi && r < nh) ? p.alibi[hbase + r] * FA_LOG2E : 0.f;
+        slope2[r] = (p.alibi && r < nh) ? p.alibi[hbase + r % p.gqa] * FA_LOG2E : 0.f;
       }
       const int qpos = p.ctx_len[cur.b];
+      // several new tokens: each row's own keys [rlo, rhi) and its offset from the first token
+      const bool multi = p.nq > 1;
+      if (multi) {
+        if (t < NRV) {
+          const int tk = t / p.gqa, ctx0 = qpos;
+          int l = p.leftpad ? p.leftpad[cur.b] : 0;
+          if (p.window >= 0 && ctx0 + tk - p.window + 1 > l) l = ctx0 + tk - p.window + 1;
+          s_rlo[t] = t < nh ? max(l, 0) : 0;
+          s_rhi[t] = t < nh ? ctx0 + (p.append ? tk + 1 : 0) : 0;
+          s_rtk[t] = (float)tk;
+        }
+        bar_sync_128();
+      }
       // O^T of tile gg into the accumulators (thread = head dim), scaled by that tile's change
       auto consume = [&](int gg) -> bool {
         const bool got = mbar_wait_warp(bar(L::OF + (gg & 1)), (gg >> 1) & 1);
@@ -468,13 +486,24 @@ __global__ void __launch_bounds__(NTH, 1)
         float v[NRV];
         bool need = false;
         const float dpos = (float)(pos - qpos);
+        if (!multi) {
 #pragma unroll
-        for (int r = 0; r < NRV; ++r) {
-          const float sr = s[r] + s[NRV + r];   // q_hi . k + q_lo . k
-          float x = cap_on ? cap2 * fa_tanh(sr * cap_in) : sr * scale2;
-          x = fmaf(slope2[r], dpos, x);
-          v[r] = (valid && r < nh) ? x : -INFINITY;
-          need |= v[r] > mref[r] + LAZY;
+          for (int r = 0; r < NRV; ++r) {
+            const float sr = s[r] + s[NRV + r];   // q_hi . k + q_lo . k
+            float x = cap_on ? cap2 * fa_tanh(sr * cap_in) : sr * scale2;
+            x = fmaf(slope2[r], dpos, x);
+            v[r] = (valid && r < nh) ? x : -INFINITY;
+            need |= v[r] > mref[r] + LAZY;
+          }
+        } else {
+#pragma unroll
+          for (int r = 0; r < NRV; ++r) {
+            const float sr = s[r] + s[NRV + r];
+            float x = cap_on ? cap2 * fa_tanh(sr * cap_in) : sr * scale2;
+            x = fmaf(slope2[r], dpos - s_rtk[r], x);   // key - this row's position
+            v[r] = (valid && r < nh && pos >= s_rlo[r] && pos < s_rhi[r]) ? x : -INFINITY;
+            need |= v[r] > mref[r] + LAZY;
+          }
         }
         float corr[NRV];
         if (bar_or_128(need)) {   // exact tile max per row, new reference
@@ -542,11 +571,14 @@ __global__ void __launch_bounds__(NTH, 1)
       bar_sync_128();
 #pragma unroll
       for (int r = 0; r < NRV; ++r) lsum[r] = (red[r] + red[NRV + r]) + (red[2 * NRV + r] + red[3 * NRV + r]);
-      const long long row0 = ((long long)cur.b * p.NH + hbase) * p.nsplit;
+      // split slots of row r = (token tk, head g): scratch row ((b * nq + tk) * NH + hbase + g)
+      auto slot_row = [&](int r) -> long long {
+        return (((long long)cur.b * p.nq + r / p.gqa) * p.NH + hbase + r % p.gqa) * p.nsplit;
+      };
 #pragma unroll
       for (int r = 0; r < NRV; ++r) {
         if (r < nh) {
-          float* o = p.scratch + (row0 + (long long)r * p.nsplit + cur.slot) * (HD + 2);
+          float* o = p.scratch + (slot_row(r) + cur.slot) * (HD + 2);
           o[2 + t] = acc[r];
           if (t == 0) { o[0] = mref[r]; o[1] = lsum[r]; }
         }
@@ -554,7 +586,7 @@ __global__ void __launch_bounds__(NTH, 1)
       if (cur.last) {
         const int rest = p.nsplit - 1 - cur.slot;
         for (int e = t; e < nh * rest; e += 128) {
-          float* o = p.scratch + (row0 + (long long)(e / rest) * p.nsplit + cur.slot + 1 + e % rest) * (HD + 2);
+          float* o = p.scratch + (slot_row(e / rest) + cur.slot + 1 + e % rest) * (HD + 2);
           o[0] = -INFINITY;
           o[1] = 0.f;
         }
@@ -617,7 +649,8 @@ namespace fa {
 int dec_tc_partial(const FaDecParams& p, int dtype, cudaStream_t st, bool* taken) {
   *taken = false;
   if (dtype != FA_DTYPE_F16 && dtype != FA_DTYPE_BF16) return FA_OK;
-  if (p.HD != HD || p.nq != 1 || p.gqa > 16 || p.page < 8 || p.num_blocks <= 0 || p.nsplit < 2) return FA_OK;
+  // query rows = new tokens x heads of a kv group, at most 16 (more run on the CUDA-core kernel)
+  if (p.HD != HD || p.nq < 1 || p.nq * p.gqa > 16 || p.page < 8 || p.num_blocks <= 0 || p.nsplit < 2) return FA_OK;
   if (getenv("FABLE_ATTN_DECODE_NO_TC")) return FA_OK;
   const long long rows = p.num_blocks * (long long)p.page;
   if (rows >= (1ll << 31)) return FA_OK;
@@ -628,13 +661,14 @@ int dec_tc_partial(const FaDecParams& p, int dtype, cudaStream_t st, bool* taken
   if (!tc_map(&mk, p.Kc, bf16, NKV, rows, R) || !tc_map(&mv, p.Vc, bf16, NKV, rows, R)) return FA_OK;
   *taken = true;
 #define FA_DEC_TC(TT_, N_) return launch<TT_, N_>(p, mk, mv, st);
+  const int qrows = p.nq * p.gqa;
   if (bf16) {
-    if (p.gqa <= 4) FA_DEC_TC(__nv_bfloat16, 4)
-    if (p.gqa <= 8) FA_DEC_TC(__nv_bfloat16, 8)
+    if (qrows <= 4) FA_DEC_TC(__nv_bfloat16, 4)
+    if (qrows <= 8) FA_DEC_TC(__nv_bfloat16, 8)
     FA_DEC_TC(__nv_bfloat16, 16)
   } else {
-    if (p.gqa <= 4) FA_DEC_TC(__half, 4)
-    if (p.gqa <= 8) FA_DEC_TC(__half, 8)
+    if (qrows <= 4) FA_DEC_TC(__half, 4)
+    if (qrows <= 8) FA_DEC_TC(__half, 8)
     FA_DEC_TC(__half, 16)
   }
 #undef FA_DEC_TC
