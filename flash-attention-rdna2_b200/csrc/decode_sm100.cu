@@ -1,5 +1,8 @@
-// decode_sm100.cu — paged-KV decode on the 5th-generation tensor cores (sm_100a): one new token
-// per sequence, fp16/bf16 cache, head_dim 128, up to 16 query heads per kv head.
+// decode_sm100.cu — paged-KV decode on the 5th-generation tensor cores (sm_100a): fp16/bf16 cache,
+// head_dim 128, up to 16 query rows per kv head, a query row being one (new token, query head)
+// pair of the kv head's group (one token with gqa <= 16, or several tokens of a speculative /
+// multi-token step, each row with its own key range: causal among appended tokens, its own window
+// start, alibi offset and rotary position).
 //
 // Decode streams every K/V byte of a sequence's context once per kv head; with GQA 4 that is
 // two multiply-adds per streamed byte, more than the CUDA cores sustain next to HBM3e.  Both
