@@ -126,11 +126,13 @@ __device__ __forceinline__ unsigned short bits16(float a) {
 // position ctx0 + tk sees [max(leftpad, ctx0 + tk - window + 1), ctx0 + tk + 1) with append,
 // [.., ctx0) without, so the union runs from the first token's start to the last token's end);
 // returns its tile count (tiles lo/TT .. (ctx-1)/TT)
-__device__ __forceinline__ int seq_tiles(const FaDecParams& p, int b, int& lo, int& ctx) {
+// A launch covers new tokens [tk0, tk0 + nqc) (groups of more than 16 query rows run in token
+// chunks, one launch each); the range is that of its tokens.
+__device__ __forceinline__ int seq_tiles(const FaDecParams& p, int b, int& lo, int& ctx, int tk0, int nqc) {
   const int ctx0 = p.ctx_len[b];
-  ctx = ctx0 + (p.append ? p.nq : 0);
+  ctx = ctx0 + (p.append ? tk0 + nqc : 0);
   int l = p.leftpad ? p.leftpad[b] : 0;
-  if (p.window >= 0 && ctx0 - p.window + 1 > l) l = ctx0 - p.window + 1;
+  if (p.window >= 0 && ctx0 + tk0 - p.window + 1 > l) l = ctx0 + tk0 - p.window + 1;
   lo = l > 0 ? l : 0;
   return ctx > lo ? (ctx - 1) / TT + 1 - lo / TT : 0;
 }
@@ -143,11 +145,11 @@ struct Seg {
 };
 struct Walk {
   long long start, end, Q, off;   // off: global tile offset of group (b, kvh)
-  int b, kvh, c;
+  int b, kvh, c, tk0, nqc;
   __device__ bool next(const FaDecParams& p, int NKV, Seg& s) {
     while (b < p.batch) {
       int lo, ctx;
-      const int n = seq_tiles(p, b, lo, ctx);
+      const int n = seq_tiles(p, b, lo, ctx, tk0, nqc);
       if (n == 0) {   // empty context: no tiles, the merge handles it
         ++b;
         kvh = 0;
@@ -171,7 +173,8 @@ struct Walk {
 // NRV: query rows handled (a power of two >= gqa, <= 16)
 template <typename T, int NRV>
 __global__ void __launch_bounds__(NTH, 1)
-    dec_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, const FaDecParams p) {
+    dec_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, const FaDecParams p,
+                  const int tk0, const int nqc) {
   using L = Lay<NRV>;
   constexpr int NQ = L::NQ;
   constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
@@ -187,7 +190,7 @@ __global__ void __launch_bounds__(NTH, 1)
   auto bar = [&](int i) { return sb + (uint32_t)L::BAR + 8u * (uint32_t)i; };
 
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-  const int NKV = p.NH / p.gqa, nh = p.nq * p.gqa;   // live query rows: (new token, head) pairs
+  const int NKV = p.NH / p.gqa, nh = nqc * p.gqa;   // live query rows: (new token, head) pairs
   const int shift = __ffs(p.page) - 1, pmask = p.page - 1;
   const int R = p.page < TT ? p.page : TT;   // rows of one page-slice box
   const int c = blockIdx.x;
@@ -199,7 +202,7 @@ __global__ void __launch_bounds__(NTH, 1)
     int mx = 0;
     for (int b = t * CB; b < min(p.batch, (t + 1) * CB); ++b) {
       int lo, ctx;
-      const int n = seq_tiles(p, b, lo, ctx);
+      const int n = seq_tiles(p, b, lo, ctx, tk0, nqc);
       sum += n;
       mx = max(mx, n);
     }
@@ -248,7 +251,7 @@ __global__ void __launch_bounds__(NTH, 1)
       long long off = lo_t;
       for (int b = t * CB; b < min(p.batch, (t + 1) * CB); ++b) {
         int lo, ctx;
-        const int n = seq_tiles(p, b, lo, ctx);
+        const int n = seq_tiles(p, b, lo, ctx, tk0, nqc);
         if (start < off + (long long)n * NKV) {
           s_b0 = b;
           s_off0 = off;
@@ -265,10 +268,10 @@ __global__ void __launch_bounds__(NTH, 1)
   auto walk0 = [&]() {
     Walk w;
     w.start = start; w.end = end; w.Q = Qt; w.c = c;
-    w.b = s_b0; w.kvh = 0; w.off = s_off0;
+    w.b = s_b0; w.kvh = 0; w.off = s_off0; w.tk0 = tk0; w.nqc = nqc;
     if (w.b < p.batch) {   // the group of sequence b0 that holds tile `start`
       int lo, ctx;
-      const int n = seq_tiles(p, w.b, lo, ctx);
+      const int n = seq_tiles(p, w.b, lo, ctx, tk0, nqc);
       w.kvh = (int)((start - w.off) / n);
       w.off += (long long)w.kvh * n;
     }
@@ -406,7 +409,7 @@ __global__ void __launch_bounds__(NTH, 1)
         }
         float x1 = 0.f, x2 = 0.f;
         if (r < nh) {   // row r = (new token r / gqa, head r % gqa of the group)
-          const int tk = r / p.gqa, rp = rp0 + tk;
+          const int tk = tk0 + r / p.gqa, rp = rp0 + tk;
           const T* qg = (const T*)p.q + (((long long)sq.b * p.nq + tk) * p.NH + hb + r % p.gqa) * HD;
           x1 = Elem<T>::to_f(qg[d1]);
           x2 = Elem<T>::to_f(qg[d2]);
@@ -449,7 +452,7 @@ __global__ void __launch_bounds__(NTH, 1)
       const bool multi = p.nq > 1;
       if (multi) {
         if (t < NRV) {
-          const int tk = t / p.gqa, ctx0 = qpos;
+          const int tk = tk0 + t / p.gqa, ctx0 = qpos;
           int l = p.leftpad ? p.leftpad[cur.b] : 0;
           if (p.window >= 0 && ctx0 + tk - p.window + 1 > l) l = ctx0 + tk - p.window + 1;
           s_rlo[t] = t < nh ? max(l, 0) : 0;
@@ -576,7 +579,7 @@ __global__ void __launch_bounds__(NTH, 1)
       for (int r = 0; r < NRV; ++r) lsum[r] = (red[r] + red[NRV + r]) + (red[2 * NRV + r] + red[3 * NRV + r]);
       // split slots of row r = (token tk, head g): scratch row ((b * nq + tk) * NH + hbase + g)
       auto slot_row = [&](int r) -> long long {
-        return (((long long)cur.b * p.nq + r / p.gqa) * p.NH + hbase + r % p.gqa) * p.nsplit;
+        return (((long long)cur.b * p.nq + tk0 + r / p.gqa) * p.NH + hbase + r % p.gqa) * p.nsplit;
       };
 #pragma unroll
       for (int r = 0; r < NRV; ++r) {
@@ -636,10 +639,10 @@ bool tc_map(CUtensorMap* m, const void* base, bool bf16, int NKV, long long rows
 }
 
 template <typename T, int NRV>
-int launch(const FaDecParams& p, const CUtensorMap& mk, const CUtensorMap& mv, cudaStream_t st) {
+int launch(const FaDecParams& p, const CUtensorMap& mk, const CUtensorMap& mv, cudaStream_t st, int tk0, int nqc) {
   static unsigned long long done = 0;
   if (int rc = fa::ensure_smem((const void*)dec_tc_kernel<T, NRV>, Lay<NRV>::SMEM, &done)) return rc;
-  dec_tc_kernel<T, NRV><<<fa::num_sms(), NTH, Lay<NRV>::SMEM, st>>>(mk, mv, p);
+  dec_tc_kernel<T, NRV><<<fa::num_sms(), NTH, Lay<NRV>::SMEM, st>>>(mk, mv, p, tk0, nqc);
   fa::count_launch();
   return fa::cuda_status(cudaGetLastError(), "decode partial (tcgen05) launch");
 }
@@ -652,8 +655,11 @@ namespace fa {
 int dec_tc_partial(const FaDecParams& p, int dtype, cudaStream_t st, bool* taken) {
   *taken = false;
   if (dtype != FA_DTYPE_F16 && dtype != FA_DTYPE_BF16) return FA_OK;
-  // query rows = new tokens x heads of a kv group, at most 16 (more run on the CUDA-core kernel)
-  if (p.HD != HD || p.nq < 1 || p.nq * p.gqa > 16 || p.page < 8 || p.num_blocks <= 0 || p.nsplit < 2) return FA_OK;
+  // query rows = new tokens x heads of a kv group, at most 16 per launch: larger groups run their
+  // tokens in chunks of 16 / gqa, one launch (one pass over the cache) each, up to 8 launches
+  if (p.HD != HD || p.nq < 1 || p.gqa > 16 || p.page < 8 || p.num_blocks <= 0 || p.nsplit < 2) return FA_OK;
+  const int per = 16 / p.gqa;
+  if ((p.nq + per - 1) / per > 8) return FA_OK;
   if (getenv("FABLE_ATTN_DECODE_NO_TC")) return FA_OK;
   const long long rows = p.num_blocks * (long long)p.page;
   if (rows >= (1ll << 31)) return FA_OK;
@@ -663,18 +669,21 @@ int dec_tc_partial(const FaDecParams& p, int dtype, cudaStream_t st, bool* taken
   CUtensorMap mk, mv;
   if (!tc_map(&mk, p.Kc, bf16, NKV, rows, R) || !tc_map(&mv, p.Vc, bf16, NKV, rows, R)) return FA_OK;
   *taken = true;
-#define FA_DEC_TC(TT_, N_) return launch<TT_, N_>(p, mk, mv, st);
-  const int qrows = p.nq * p.gqa;
-  if (bf16) {
-    if (qrows <= 4) FA_DEC_TC(__nv_bfloat16, 4)
-    if (qrows <= 8) FA_DEC_TC(__nv_bfloat16, 8)
-    FA_DEC_TC(__nv_bfloat16, 16)
-  } else {
-    if (qrows <= 4) FA_DEC_TC(__half, 4)
-    if (qrows <= 8) FA_DEC_TC(__half, 8)
-    FA_DEC_TC(__half, 16)
+  for (int tk0 = 0; tk0 < p.nq; tk0 += per) {
+    const int nqc = std::min(per, p.nq - tk0), qrows = nqc * p.gqa;
+    int rc;
+    if (bf16) {
+      rc = qrows <= 4 ? launch<__nv_bfloat16, 4>(p, mk, mv, st, tk0, nqc)
+         : qrows <= 8 ? launch<__nv_bfloat16, 8>(p, mk, mv, st, tk0, nqc)
+                      : launch<__nv_bfloat16, 16>(p, mk, mv, st, tk0, nqc);
+    } else {
+      rc = qrows <= 4 ? launch<__half, 4>(p, mk, mv, st, tk0, nqc)
+         : qrows <= 8 ? launch<__half, 8>(p, mk, mv, st, tk0, nqc)
+                      : launch<__half, 16>(p, mk, mv, st, tk0, nqc);
+    }
+    if (rc) return rc;
   }
-#undef FA_DEC_TC
+  return FA_OK;
 }
 
 int dec_tc_device_error(int clear) {

@@ -223,7 +223,7 @@ def test_decode_tensor_core_envelope(tc, dt):
 
 
 # Several new tokens per sequence on the tensor-core decode (query rows = tokens x heads of a kv
-# group, up to 16): token tk sits at position ctx + tk and, with append, sees the cache and new
+# group, up to 16 per launch, larger groups in token chunks): token tk sits at position ctx + tk and, with append, sees the cache and new
 # tokens 0..tk (the reference's multi-token decode, kernels/fa_decode.hip:57-252, nq <= 8).
 TC_MULTI = [
     # (name, page, ctxs, NH, gqa, nq, window, leftpad, append, rotary, softcap, alibi)
@@ -232,6 +232,10 @@ TC_MULTI = [
     ("p128_gqa2_nq8_window", 128, [4000, 260], 16, 2, 8, 700, 0, True, 0, 0.0, False),
     ("p32_gqa3_nq5_leftpad_cap_alibi", 32, [3000, 900], 12, 3, 5, -1, 130, True, 0, 30.0, True),
     ("p256_gqa1_nq7_empty_seq", 256, [2000, 0, 777], 8, 1, 7, 64, 0, False, 2, 0.0, False),
+    # more than 16 query rows: tokens in chunks of 16 / gqa, one launch each
+    ("p64_gqa4_nq8_append_rot", 64, [2300, 1100], 32, 4, 8, -1, 0, True, 1, 0.0, False),
+    ("p16_gqa16_nq3", 16, [900, 1300], 32, 16, 3, -1, 0, True, 0, 0.0, False),
+    ("p128_gqa3_nq7_window_alibi", 128, [3000, 500], 12, 3, 7, 300, 0, True, 0, 0.0, True),
 ]
 
 
