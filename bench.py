@@ -386,6 +386,33 @@ def bench_decode(dev, steps=20, warmup=5):
             "GBps": round(nbytes / ms / 1e6, 1), "bytes": nbytes, "_setup": c}
 
 
+def bench_decode_multi_token(dev, c, nqs=(2, 4, 8), steps=20, warmup=5):
+    """Config 4's caches with several new tokens per sequence (speculative / multi-token decode, the
+    reference's nq <= 8): the tensor-core decode over the same K/V; GB/s counts the K/V bytes once."""
+    from fable_attn import _C
+    kc, vc, bt, cs, D, lens, Hk = c["kc"], c["vc"], c["bt"], c["cs"], c["D"], c["lens"], c["Hk"]
+    g = torch.Generator(device=dev).manual_seed(13)
+    out = {"config": "config 4 caches (B16 Hq32 Hk8 D128 bf16 page256 L~U[16K,32K]), nq new tokens per sequence"}
+    for nq in nqs:
+        q = torch.randn(c["B"], nq, c["Hq"], D, device=dev, dtype=torch.bfloat16, generator=g)
+
+        def call():
+            return _C.dec(q, kc, vc, bt, cs, None, None, None, None, False, D ** -0.5, -1, 0, None, False, 0.0, None, 0,
+                          None)
+        for _ in range(warmup):
+            call()
+        torch.cuda.synchronize()
+        a, b = _events()
+        a.record()
+        for _ in range(steps):
+            call()
+        b.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / steps
+        out[f"nq{nq}"] = {"ms": round(ms, 4), "GBps": round(float(lens.sum()) * Hk * D * 4 / ms / 1e6, 1)}
+    return out
+
+
 def bench_decode_split(dev, ws, rank, steps=20, warmup=5):
     """Config 4 across ranks: each sequence's context (lengths ~ U[16K, 32K], seeded) is cut into
     ws contiguous chunks; rank r holds the pages of its chunks (bf16, page 256, permuted block
@@ -1034,6 +1061,7 @@ def main():
             r4 = bench_decode(dev)
             extra["decode_paged"] = r4
             r4.update(measure_config4(dev, peaks, r4))
+            extra["decode_paged_multi_token"] = bench_decode_multi_token(dev, r4["_setup"])
         except Exception as e:
             extra.setdefault("decode_paged", {}).update(err(e))
         finally:
