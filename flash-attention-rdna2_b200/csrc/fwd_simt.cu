@@ -2,15 +2,16 @@
 //
 // Serves the fp32 dtype (the reference's fp32 path, kernels/fa_forward.hip:317-400) and every
 // fp16/bf16 configuration the tensor-core kernel (fwd_sm100.cu) does not take.  One CTA owns
-// a 32-row query tile of one head of one sequence and streams 32-key tiles of K/V through
-// shared memory with an online softmax (log2 domain).  Every mask, softcap, alibi, Philox
+// a 32-row query tile of one head of one sequence and streams 64-key tiles of K/V through
+// shared memory with an online softmax (log2 domain); for head dims up to 64 the next tile's K/V
+// are loaded into registers while the current one computes.  Every mask, softcap, alibi, Philox
 // dropout, varlen/seqused and LSE output follows the FaFwdParams contract in fable_attn.h.
 #include "fa_common.cuh"
 #include "fa_launch.h"
 
 namespace {
 
-constexpr int BR = 32, BC = 32;
+constexpr int BR = 32, BC = 64;
 __device__ int g_simt_error = 0;   // bit 0: an invalid block-table entry of a real key
 
 template <typename T, int HD>
@@ -66,44 +67,80 @@ __global__ void __launch_bounds__(256) fwd_simt_kernel(const FaFwdParams p) {
     for (int e = 0; e < DPT; ++e) acc[i][e] = 0.f;
   }
 
-  for (int kb = (klo / BC) * BC; kb <= khi; kb += BC) {
+  // element e of a K/V tile (thread t takes e = t, t + 256, ...): K and V of key kb + e / HD, dim
+  // e % HD, as fp32 (0 past SK)
+  auto fetch = [&](int kb, int e, float& kx, float& vx) {
+    const int r = e / HD, d = e % HD, k = kb + r;
+    const bool ok = k < SK;
+    if (p.block_table) {   // paged cache [num_blocks * page rows][NKV][HD]
+      bool bad = false;
+      const long long row = ok ? fa_paged_row(p, z, k, SK, bad) : 0;
+      if (bad && d == 0) atomicOr(&g_simt_error, 1);
+      const long long off = (row * (p.NH / p.gqa) + kvh) * HD + d;
+      kx = ok ? Elem<T>::to_f(((const T*)p.K)[off]) : 0.f;
+      vx = ok ? Elem<T>::to_f(((const T*)p.V)[off]) : 0.f;
+    } else {
+      kx = ok ? Elem<T>::to_f(Kg[(long long)k * p.sK.s + d]) : 0.f;
+      vx = ok ? Elem<T>::to_f(Vg[(long long)k * p.sV.s + d]) : 0.f;
+    }
+  };
+  // head dims up to 64: the next tile's K/V are loaded into registers while this tile computes
+  constexpr int NE = BC * HD / 256;
+  constexpr bool PF = NE <= 16;
+  float kpf[PF ? NE : 1], vpf[PF ? NE : 1];
+  const int kb0 = (klo / BC) * BC;
+  if constexpr (PF) {
+    if (kb0 <= khi) {
+#pragma unroll
+      for (int i = 0; i < NE; ++i) fetch(kb0, t + 256 * i, kpf[i], vpf[i]);
+    }
+  }
+  for (int kb = kb0; kb <= khi; kb += BC) {
     __syncthreads();
-    for (int e = t; e < BC * HD; e += 256) {
-      const int r = e / HD, d = e % HD, k = kb + r;
-      const bool ok = k < SK;
-      if (p.block_table) {   // paged cache [num_blocks * page rows][NKV][HD]
-        bool bad = false;
-        const long long row = ok ? fa_paged_row(p, z, k, SK, bad) : 0;
-        if (bad && d == 0) atomicOr(&g_simt_error, 1);
-        const long long off = (row * (p.NH / p.gqa) + kvh) * HD + d;
-        Ks[r * LDQ + d] = ok ? Elem<T>::to_f(((const T*)p.K)[off]) : 0.f;
-        Vs[r * HD + d] = ok ? Elem<T>::to_f(((const T*)p.V)[off]) : 0.f;
-      } else {
-        Ks[r * LDQ + d] = ok ? Elem<T>::to_f(Kg[(long long)k * p.sK.s + d]) : 0.f;
-        Vs[r * HD + d] = ok ? Elem<T>::to_f(Vg[(long long)k * p.sV.s + d]) : 0.f;
+    if constexpr (PF) {
+#pragma unroll
+      for (int i = 0; i < NE; ++i) {
+        const int e = t + 256 * i, r = e / HD, d = e % HD;
+        Ks[r * LDQ + d] = kpf[i];
+        Vs[r * HD + d] = vpf[i];
+      }
+      if (kb + BC <= khi) {
+#pragma unroll
+        for (int i = 0; i < NE; ++i) fetch(kb + BC, t + 256 * i, kpf[i], vpf[i]);
+      }
+    } else {
+      for (int e = t; e < BC * HD; e += 256) {
+        float kx, vx;
+        fetch(kb, e, kx, vx);
+        Ks[(e / HD) * LDQ + e % HD] = kx;
+        Vs[(e / HD) * HD + e % HD] = vx;
       }
     }
     __syncthreads();
 
-    float s[2][2];
+    constexpr int KJ = BC / 16;   // keys per thread: tx, tx + 16, ...
+    float s[2][KJ];
 #pragma unroll
     for (int i = 0; i < 2; ++i)
 #pragma unroll
-      for (int j = 0; j < 2; ++j) s[i][j] = 0.f;
+      for (int j = 0; j < KJ; ++j) s[i][j] = 0.f;
 #pragma unroll 4
     for (int d = 0; d < HD; ++d) {
       const float q0 = Qs[(ty * 2) * LDQ + d], q1 = Qs[(ty * 2 + 1) * LDQ + d];
-      const float k0 = Ks[tx * LDQ + d], k1 = Ks[(tx + 16) * LDQ + d];
-      s[0][0] = fmaf(q0, k0, s[0][0]); s[0][1] = fmaf(q0, k1, s[0][1]);
-      s[1][0] = fmaf(q1, k0, s[1][0]); s[1][1] = fmaf(q1, k1, s[1][1]);
+#pragma unroll
+      for (int j = 0; j < KJ; ++j) {
+        const float kv = Ks[(tx + 16 * j) * LDQ + d];
+        s[0][j] = fmaf(q0, kv, s[0][j]);
+        s[1][j] = fmaf(q1, kv, s[1][j]);
+      }
     }
 
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
       const int q = qb + ty * 2 + i;
-      float sv[2], tmax = -INFINITY;
+      float sv[KJ], tmax = -INFINITY;
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
+      for (int j = 0; j < KJ; ++j) {
         const int key = kb + tx + 16 * j;
         float v;
         if (p.softcap > 0.f) v = p.softcap * tanhf(s[i][j] * p.scale / p.softcap) * FA_LOG2E;
@@ -118,9 +155,9 @@ __global__ void __launch_bounds__(256) fwd_simt_kernel(const FaFwdParams p) {
       const float mnew = fmaxf(m[i], tmax);
       // a row that has seen no visible key yet keeps m = -inf and contributes nothing
       const float muse = (mnew == -INFINITY) ? 0.f : mnew;
-      float pj[2], ls = 0.f;
+      float pj[KJ], ls = 0.f;
 #pragma unroll
-      for (int j = 0; j < 2; ++j) { pj[j] = exp2f(sv[j] - muse); ls += pj[j]; }
+      for (int j = 0; j < KJ; ++j) { pj[j] = exp2f(sv[j] - muse); ls += pj[j]; }
 #pragma unroll
       for (int o = 8; o >= 1; o >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
       if (mnew != -INFINITY) {
@@ -131,15 +168,15 @@ __global__ void __launch_bounds__(256) fwd_simt_kernel(const FaFwdParams p) {
         m[i] = mnew;
         if (drop) {
 #pragma unroll
-          for (int j = 0; j < 2; ++j) {
+          for (int j = 0; j < KJ; ++j) {
             const int key = kb + tx + 16 * j;
             if (q < SQ && key < SK)
               pj[j] *= fa_keep_mul(p.dropout_bits, p.philox_seed, h, SQ, SK, q, key, p.dropout_p, inv_keep);
           }
         }
       }
-      Ps[(ty * 2 + i) * (BC + 1) + tx] = pj[0];
-      Ps[(ty * 2 + i) * (BC + 1) + tx + 16] = pj[1];
+#pragma unroll
+      for (int j = 0; j < KJ; ++j) Ps[(ty * 2 + i) * (BC + 1) + tx + 16 * j] = pj[j];
     }
     __syncthreads();
 #pragma unroll 4
