@@ -15,13 +15,19 @@ constexpr int BR = 32, BC = 64;
 __device__ int g_simt_error = 0;   // bit 0: an invalid block-table entry of a real key
 
 template <typename T, int HD>
-__global__ void __launch_bounds__(256) fwd_simt_kernel(const FaFwdParams p) {
-  constexpr int DPT = HD / 16, LDQ = HD + 1;
+__global__ void __launch_bounds__(256, 2) fwd_simt_kernel(const FaFwdParams p) {
+  // rows of Q and K padded to HD + 4 floats (16-byte aligned float4 reads along the head dim);
+  // P rows to BC + 4.  With DPT a multiple of 4 a thread owns the 4-dim groups 64 g + 4 tx .. + 3
+  // (float4 reads of V and P; the 16 threads of a row read consecutive 16-byte units), else the
+  // dims tx, tx + 16, ...
+  constexpr int DPT = HD / 16, LDQ = HD + 4, LDP = BC + 4;
+  constexpr bool VEC = DPT % 4 == 0;
   extern __shared__ float smem[];
-  float* Qs = smem;                 // [BR][HD+1]
-  float* Ks = Qs + BR * LDQ;        // [BC][HD+1]
+  float* Qs = smem;                 // [BR][HD+4]
+  float* Ks = Qs + BR * LDQ;        // [BC][HD+4]
   float* Vs = Ks + BC * LDQ;        // [BC][HD]
-  float* Ps = Vs + BC * HD;         // [BR][BC+1]
+  float* Ps = Vs + BC * HD;         // [BR][BC+4]
+  auto dim = [&](int e) { return VEC ? 64 * (e / 4) + 4 * (threadIdx.x & 15) + e % 4 : (threadIdx.x & 15) + 16 * e; };
 
   const int t = threadIdx.x, tx = t & 15, ty = t >> 4;
   const int z = blockIdx.z, h = blockIdx.y, kvh = h / p.gqa;
@@ -124,14 +130,15 @@ __global__ void __launch_bounds__(256) fwd_simt_kernel(const FaFwdParams p) {
     for (int i = 0; i < 2; ++i)
 #pragma unroll
       for (int j = 0; j < KJ; ++j) s[i][j] = 0.f;
-#pragma unroll 4
-    for (int d = 0; d < HD; ++d) {
-      const float q0 = Qs[(ty * 2) * LDQ + d], q1 = Qs[(ty * 2 + 1) * LDQ + d];
+#pragma unroll 2
+    for (int d = 0; d < HD; d += 4) {
+      const float4 q0 = *reinterpret_cast<const float4*>(Qs + (ty * 2) * LDQ + d);
+      const float4 q1 = *reinterpret_cast<const float4*>(Qs + (ty * 2 + 1) * LDQ + d);
 #pragma unroll
       for (int j = 0; j < KJ; ++j) {
-        const float kv = Ks[(tx + 16 * j) * LDQ + d];
-        s[0][j] = fmaf(q0, kv, s[0][j]);
-        s[1][j] = fmaf(q1, kv, s[1][j]);
+        const float4 kv = *reinterpret_cast<const float4*>(Ks + (tx + 16 * j) * LDQ + d);
+        s[0][j] = fmaf(q0.x, kv.x, fmaf(q0.y, kv.y, fmaf(q0.z, kv.z, fmaf(q0.w, kv.w, s[0][j]))));
+        s[1][j] = fmaf(q1.x, kv.x, fmaf(q1.y, kv.y, fmaf(q1.z, kv.z, fmaf(q1.w, kv.w, s[1][j]))));
       }
     }
 
@@ -176,17 +183,41 @@ __global__ void __launch_bounds__(256) fwd_simt_kernel(const FaFwdParams p) {
         }
       }
 #pragma unroll
-      for (int j = 0; j < KJ; ++j) Ps[(ty * 2 + i) * (BC + 1) + tx + 16 * j] = pj[j];
+      for (int j = 0; j < KJ; ++j) Ps[(ty * 2 + i) * LDP + tx + 16 * j] = pj[j];
     }
     __syncthreads();
-#pragma unroll 4
-    for (int c = 0; c < BC; ++c) {
-      const float p0 = Ps[(ty * 2) * (BC + 1) + c], p1 = Ps[(ty * 2 + 1) * (BC + 1) + c];
+    if constexpr (VEC) {
+#pragma unroll 2
+      for (int c = 0; c < BC; c += 4) {
+        const float4 p0 = *reinterpret_cast<const float4*>(Ps + (ty * 2) * LDP + c);
+        const float4 p1 = *reinterpret_cast<const float4*>(Ps + (ty * 2 + 1) * LDP + c);
+        const float pa[4] = {p0.x, p0.y, p0.z, p0.w}, pb[4] = {p1.x, p1.y, p1.z, p1.w};
 #pragma unroll
-      for (int e = 0; e < DPT; ++e) {
-        const float v = Vs[c * HD + tx + 16 * e];
-        acc[0][e] = fmaf(p0, v, acc[0][e]);
-        acc[1][e] = fmaf(p1, v, acc[1][e]);
+        for (int u = 0; u < 4; ++u) {
+#pragma unroll
+          for (int e = 0; e < DPT; e += 4) {
+            const float4 v = *reinterpret_cast<const float4*>(Vs + (c + u) * HD + 16 * e + 4 * tx);
+            acc[0][e] = fmaf(pa[u], v.x, acc[0][e]);
+            acc[0][e + 1] = fmaf(pa[u], v.y, acc[0][e + 1]);
+            acc[0][e + 2] = fmaf(pa[u], v.z, acc[0][e + 2]);
+            acc[0][e + 3] = fmaf(pa[u], v.w, acc[0][e + 3]);
+            acc[1][e] = fmaf(pb[u], v.x, acc[1][e]);
+            acc[1][e + 1] = fmaf(pb[u], v.y, acc[1][e + 1]);
+            acc[1][e + 2] = fmaf(pb[u], v.z, acc[1][e + 2]);
+            acc[1][e + 3] = fmaf(pb[u], v.w, acc[1][e + 3]);
+          }
+        }
+      }
+    } else {
+#pragma unroll 4
+      for (int c = 0; c < BC; ++c) {
+        const float p0 = Ps[(ty * 2) * LDP + c], p1 = Ps[(ty * 2 + 1) * LDP + c];
+#pragma unroll
+        for (int e = 0; e < DPT; ++e) {
+          const float v = Vs[c * HD + tx + 16 * e];
+          acc[0][e] = fmaf(p0, v, acc[0][e]);
+          acc[1][e] = fmaf(p1, v, acc[1][e]);
+        }
       }
     }
   }
@@ -198,7 +229,7 @@ __global__ void __launch_bounds__(256) fwd_simt_kernel(const FaFwdParams p) {
     if (q >= SQ) continue;
     const float inv = l[i] > 0.f ? 1.f / l[i] : 0.f;
 #pragma unroll
-    for (int e = 0; e < DPT; ++e) Og[(long long)q * p.sO.s + tx + 16 * e] = Elem<T>::from_f(acc[i][e] * inv);
+    for (int e = 0; e < DPT; ++e) Og[(long long)q * p.sO.s + dim(e)] = Elem<T>::from_f(acc[i][e] * inv);
     if (p.LSE && tx == 0) {
       const long long li = fa_lse_index(varlen, z, h, p.NH, p.SQ, g.tok_q, p.lse_total_q, q);
       p.LSE[li] = l[i] > 0.f ? m[i] * FA_LN2 + logf(l[i]) : -INFINITY;
@@ -208,7 +239,7 @@ __global__ void __launch_bounds__(256) fwd_simt_kernel(const FaFwdParams p) {
 
 template <typename T, int HD>
 int launch_hd(const FaFwdParams& p, cudaStream_t st) {
-  const size_t smem = sizeof(float) * (size_t)(BR * (HD + 1) + BC * (HD + 1) + BC * HD + BR * (BC + 1));
+  const size_t smem = sizeof(float) * (size_t)(BR * (HD + 4) + BC * (HD + 4) + BC * HD + BR * (BC + 4));
   static unsigned long long done = 0;
   if (int rc = fa::ensure_smem((const void*)fwd_simt_kernel<T, HD>, (int)smem, &done)) return rc;
   dim3 grid((p.SQ + BR - 1) / BR, p.NH, p.batch);
