@@ -30,26 +30,35 @@ __global__ void __launch_bounds__(256) dropout_mask_kernel(unsigned long long se
 }
 
 // One warp per 32 x 32 block (32 query rows x 32 keys): lane l reads the row-major word of row
-// 32 qw + l, 32 ballots turn rows-of-keys into keys-of-rows, lane b writes the word of key 32 kw + b.
+// 32 qw + l, a 32 x 32 bit transpose across the warp turns rows-of-keys into keys-of-rows, lane b
+// writes the word of key 32 kw + b.  The transpose swaps, for each bit j of the index (16, 8, 4, 2,
+// 1), the off-diagonal j x j sub-blocks between lanes l and l ^ j: the lane without bit j keeps its
+// bits whose index lacks bit j and takes its partner's such bits shifted up by j; the lane with bit
+// j keeps its bits whose index has bit j and takes its partner's shifted down by j (five shuffles
+// instead of 32 ballots).
 // Warps run query blocks fastest, so reads and writes are 128-byte lines.  Words the mask kernel
 // skipped (no row can see their keys) transpose to words of the same unseen (row, key) pairs.
+// IDX: the integer type of the block index (32-bit whenever the block count fits, so that the
+// per-warp index split is not a 64-bit division)
+template <typename IDX>
 __global__ void __launch_bounds__(256) dropout_mask_t_kernel(const unsigned int* __restrict__ bits,
                                                              unsigned int* __restrict__ bits_t, int NH, int SQ,
                                                              int SK) {
-  const int W = (SK + 31) / 32, QW = (SQ + 31) / 32;
-  const long long wid = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const IDX W = (SK + 31) / 32, QW = (SQ + 31) / 32;
+  const IDX wid = ((IDX)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (wid >= (long long)NH * W * QW) return;   // whole warps
+  if (wid >= (IDX)NH * W * QW) return;   // whole warps
   const int qw = (int)(wid % QW);
-  const long long hk = wid / QW;
+  const IDX hk = wid / QW;
   const int kw = (int)(hk % W), h = (int)(hk / W);
   const int q = qw * 32 + lane;
-  const unsigned int w = q < SQ ? bits[((long long)h * W + kw) * SQ + q] : 0u;
-  unsigned int t = 0u;
+  unsigned int t = q < SQ ? bits[((long long)h * W + kw) * SQ + q] : 0u;
+  // bits whose index lacks bit j: 0x0000FFFF, 0x00FF00FF, 0x0F0F0F0F, 0x33333333, 0x55555555
+  const unsigned int lo_mask[5] = {0x0000FFFFu, 0x00FF00FFu, 0x0F0F0F0Fu, 0x33333333u, 0x55555555u};
 #pragma unroll
-  for (int b = 0; b < 32; ++b) {
-    const unsigned int m = __ballot_sync(0xffffffffu, (w >> b) & 1u);
-    t = (lane == b) ? m : t;
+  for (int i = 0, j = 16; i < 5; ++i, j >>= 1) {
+    const unsigned int m = lo_mask[i], o = __shfl_xor_sync(0xffffffffu, t, j);
+    t = (lane & j) ? ((t & ~m) | ((o & ~m) >> j)) : ((t & m) | ((o & m) << j));
   }
   const int k = kw * 32 + lane;
   if (k < SK) bits_t[((long long)h * QW + qw) * SK + k] = t;
@@ -67,7 +76,10 @@ int dropout_mask_transpose(const unsigned int* bits, unsigned int* bits_t, int N
     set_error("dropout mask transpose: %lld blocks is too large", blocks);
     return FA_ERR_SIZE;
   }
-  dropout_mask_t_kernel<<<(unsigned)blocks, 256, 0, st>>>(bits, bits_t, NH, SQ, SK);
+  if (blocks * 256 < (1ll << 32))
+    dropout_mask_t_kernel<unsigned int><<<(unsigned)blocks, 256, 0, st>>>(bits, bits_t, NH, SQ, SK);
+  else
+    dropout_mask_t_kernel<unsigned long long><<<(unsigned)blocks, 256, 0, st>>>(bits, bits_t, NH, SQ, SK);
   count_launch();
   return cuda_status(cudaGetLastError(), "dropout mask transpose launch");
 }
