@@ -2,7 +2,7 @@
 //
 // Same decomposition as the reference (kernels/backward.hip:86-387), so the result is
 // bit-reproducible run to run:
-//   1. preprocess: dsum[row] = sum_d O*dO                       (one warp per row)
+//   1. preprocess: dsum[row] = sum_d O*dO                       (one warp per 4 rows)
 //   2. dK/dV     : one CTA per 32-key tile; loops over every query head of the kv group and
 //                  every 32-row query tile that can see the keys; dK, dV live in registers
 //   3. dQ        : one CTA per 32-row query tile; loops over the visible key tiles
@@ -12,6 +12,8 @@
 // reference's fwd_ok, kernels/backward.hip:76-83).  Varlen via cu_seqlens like the forward.
 #include "fa_common.cuh"
 #include "fa_launch.h"
+
+#include <type_traits>
 
 namespace {
 
@@ -27,20 +29,58 @@ __device__ __forceinline__ long long row0(const FaBwdParams& p, int z, const FaS
   return (long long)z * s.b;
 }
 
+// dsum rows per warp: their loads are all issued before the first multiply, so each lane has
+// 2 * DSUM_ROWS loads in flight (a lone 128-dim row per warp left HBM at 40 % of its bandwidth)
+constexpr int DSUM_ROWS = 4;
+
 template <typename T>
 __global__ void __launch_bounds__(256) bwd_pre_kernel(const FaBwdParams p) {
   const int z = blockIdx.z, h = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int q = blockIdx.x * 8 + warp;
+  const int q0 = (blockIdx.x * 8 + warp) * DSUM_ROWS;
   const SeqGeom g = bwd_geom(p, z);
-  if (q >= g.SQ) return;
-  const T* O = (const T*)p.O + g.o0 + (long long)h * p.os.h + (long long)q * p.os.s;
-  const T* dO = (const T*)p.dO + row0(p, z, p.dos, true) + (long long)h * p.dos.h + (long long)q * p.dos.s;
-  float acc = 0.f;
-  for (int d = lane; d < p.D; d += 32) acc += Elem<T>::to_f(O[d]) * Elem<T>::to_f(dO[d]);
+  if (q0 >= g.SQ) return;
+  const T* O = (const T*)p.O + g.o0 + (long long)h * p.os.h + (long long)q0 * p.os.s;
+  const T* dO = (const T*)p.dO + row0(p, z, p.dos, true) + (long long)h * p.dos.h + (long long)q0 * p.dos.s;
+  const int nr = min(DSUM_ROWS, g.SQ - q0);
+  float acc[DSUM_ROWS];
 #pragma unroll
-  for (int o = 16; o >= 1; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-  if (lane == 0)
-    p.dsum[fa_lse_index(p.cu_q != nullptr, z, h, p.Hq, p.SQ, g.tok_q, p.lse_total_q, q)] = acc;
+  for (int r = 0; r < DSUM_ROWS; ++r) acc[r] = 0.f;
+  // 4 elements per lane in one vector load (8 bytes of a 16-bit type, 16 of fp32) when every row
+  // start allows it, so a row of up to 128 dims is one load per tensor and lane
+  constexpr int VB = 4 * (int)sizeof(T);
+  if ((p.D & 3) == 0 && ((uintptr_t)O % VB) == 0 && ((uintptr_t)dO % VB) == 0 && (p.os.s & 3) == 0 &&
+      (p.dos.s & 3) == 0) {
+    using V = typename std::conditional<sizeof(T) == 2, uint2, float4>::type;
+    for (int d = 4 * lane; d < p.D; d += 128) {
+      V va[DSUM_ROWS], vb[DSUM_ROWS];
+#pragma unroll
+      for (int r = 0; r < DSUM_ROWS; ++r)
+        if (r < nr) {
+          va[r] = *reinterpret_cast<const V*>(O + (long long)r * p.os.s + d);
+          vb[r] = *reinterpret_cast<const V*>(dO + (long long)r * p.dos.s + d);
+        }
+#pragma unroll
+      for (int r = 0; r < DSUM_ROWS; ++r) {
+        if (r >= nr) continue;
+        const T* ea = reinterpret_cast<const T*>(&va[r]);
+        const T* eb = reinterpret_cast<const T*>(&vb[r]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[r] += Elem<T>::to_f(ea[i]) * Elem<T>::to_f(eb[i]);
+      }
+    }
+  } else {
+    for (int r = 0; r < nr; ++r)
+#pragma unroll 4
+      for (int d = lane; d < p.D; d += 32)
+        acc[r] += Elem<T>::to_f(O[(long long)r * p.os.s + d]) * Elem<T>::to_f(dO[(long long)r * p.dos.s + d]);
+  }
+#pragma unroll
+  for (int r = 0; r < DSUM_ROWS; ++r) {
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+    if (lane == 0 && r < nr)
+      p.dsum[fa_lse_index(p.cu_q != nullptr, z, h, p.Hq, p.SQ, g.tok_q, p.lse_total_q, q0 + r)] = acc[r];
+  }
 }
 
 // Shared tile computation: given Q/dO rows [BQ] and K/V rows [BK] in smem, write
@@ -286,7 +326,7 @@ int launch_hd(const FaBwdParams& p, cudaStream_t st) {
   static unsigned long long done_kv = 0, done_q = 0;
   if (int rc = fa::ensure_smem((const void*)bwd_dkdv_kernel<T, HD>, (int)smem, &done_kv)) return rc;
   if (int rc = fa::ensure_smem((const void*)bwd_dq_kernel<T, HD>, (int)smem, &done_q)) return rc;
-  bwd_pre_kernel<T><<<dim3((p.SQ + 7) / 8, p.Hq, p.B), 256, 0, st>>>(p);
+  bwd_pre_kernel<T><<<dim3((p.SQ + 8 * DSUM_ROWS - 1) / (8 * DSUM_ROWS), p.Hq, p.B), 256, 0, st>>>(p);
   bwd_dkdv_kernel<T, HD><<<dim3((p.SK + BK - 1) / BK, p.Hk, p.B), 256, smem, st>>>(p);
   bwd_dq_kernel<T, HD><<<dim3((p.SQ + BQ - 1) / BQ, p.Hq, p.B), 256, smem, st>>>(p);
   fa::count_launch(3);
@@ -317,7 +357,7 @@ int launch_t(const FaBwdParams& p, cudaStream_t st) {
 
 namespace fa {
 int bwd_dsum(const FaBwdParams& p, int dtype, cudaStream_t st) {
-  const dim3 grid((p.SQ + 7) / 8, p.Hq, p.B);
+  const dim3 grid((p.SQ + 8 * DSUM_ROWS - 1) / (8 * DSUM_ROWS), p.Hq, p.B);
   if (dtype == FA_DTYPE_F16) bwd_pre_kernel<__half><<<grid, 256, 0, st>>>(p);
   else if (dtype == FA_DTYPE_BF16) bwd_pre_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(p);
   else bwd_pre_kernel<float><<<grid, 256, 0, st>>>(p);
