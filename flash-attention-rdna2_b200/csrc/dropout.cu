@@ -2,17 +2,76 @@
 //
 // One thread per 32-bit word = 32 consecutive keys of one (head, query row); consecutive threads
 // take consecutive query rows, so stores are coalesced in the [NH][ceil(SK/32)][SQ] layout.  The
-// 32 Philox evaluations of a word are independent and are issued 8 at a time to keep the integer
-// pipes busy (fa_keep_word).  The keep decision is the reference's (kernels/fa_common.hpp:71-88),
-// u = (r0 >> 8) / 2^24, keep iff u >= p, evaluated as the equivalent integer test of
-// fa_drop_thresh.  Words that hold no key the row can see (causal / window) are skipped: no
-// consumer reads them.
+// 32 Philox evaluations of a word are independent and are issued 8 at a time.  The keep decision
+// is the reference's (kernels/fa_common.hpp:71-88), u = (r0 >> 8) / 2^24, keep iff u >= p,
+// evaluated as the equivalent integer test r0 >= fa_drop_thresh(p) * 2^8.  Words that hold no key
+// the row can see (causal / window) are skipped: no consumer reads them.
+//
+// The kernel is bound by the integer multiply pipe: a Philox4x32-10 draw is ~17 32 x 32 -> 64-bit
+// products and ~17 three-input XORs, and with every product on the integer multiplier that pipe
+// ran 91 % busy while issue ran at 64 %.  So the high halves of the M0 products of rounds 1-9 come
+// from the otherwise idle fp64 pipe instead (philox_r0_split); the draw is the same function, bit
+// for bit, as fa_philox_r0.
 #include "fa_common.cuh"
 #include "fa_launch.h"
 
+#include <cstdlib>
+
 namespace {
 
-__global__ void __launch_bounds__(256) dropout_mask_kernel(unsigned long long seed, unsigned int thresh, int NH,
+constexpr uint32_t kPhiloxM0 = 0xD2511F53u, kPhiloxM1 = 0xCD9E8D57u;
+
+// High 32 bits of M * x for the 32-bit x: with the double 2^52 + x (its bit pattern is x below the
+// exponent of 2^52), fma_rd(M * 2^-32, 2^52 + x, 2^52 - M * 2^20) = 2^52 + M * x / 2^32 rounded
+// down.  The fused product and sum are exact, and the exact result lies in [2^52, 2^53), where
+// doubles are the integers, so rounding down gives 2^52 + floor(M * x / 2^32) exactly; its low
+// 32 bits are the high half of the product.
+__device__ __forceinline__ uint32_t mulhi_fp64(double m_scaled, double bias, uint32_t x) {
+  return (uint32_t)__double2loint(__fma_rd(m_scaled, __hiloint2double(0x43300000, (int)x), bias));
+}
+
+// fa_philox_r0(seed, (c1 << 32) | c0): Philox4x32-10, first output word, with the M0 products'
+// high halves of rounds 1-9 by mulhi_fp64 and their low halves by a 32-bit multiply (the M1
+// products stay 64-bit integer products).  Moving more products measured slower: the kernel
+// becomes issue bound.
+__device__ __forceinline__ uint32_t philox_r0_split(uint64_t seed, uint32_t c0, uint32_t c1) {
+  const double m0s = (double)kPhiloxM0 * 0x1p-32, bias0 = 0x1p52 - (double)kPhiloxM0 * 0x1p20;
+  uint32_t k0 = (uint32_t)seed, k1 = (uint32_t)(seed >> 32), c2 = 0u, c3 = 0u;
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    const uint32_t hi0 = mulhi_fp64(m0s, bias0, c0), lo0 = c0 * kPhiloxM0;
+    const uint64_t p1 = (uint64_t)kPhiloxM1 * c2;
+    const uint32_t n0 = (uint32_t)(p1 >> 32) ^ c1 ^ k0, n2 = hi0 ^ c3 ^ k1;
+    c0 = n0; c1 = (uint32_t)p1; c2 = n2; c3 = lo0;
+    k0 += 0x9E3779B9u; k1 += 0xBB67AE85u;
+  }
+  return c0;
+}
+
+// Keep bits of counters base .. base + 31 (bit b set iff draw base + b is kept), bits b >= nvalid
+// cleared.  WIDE: counters may exceed 2^32 (64-bit counter per draw); otherwise the high counter
+// word is 0 for every draw of the launch.
+template <bool WIDE>
+__device__ __forceinline__ uint32_t keep_word_split(uint64_t seed, uint64_t base, uint32_t thr8, int nvalid) {
+  uint32_t word = 0;
+#pragma unroll 1
+  for (int b0 = 0; b0 < 32; b0 += 8) {
+    uint32_t r[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const uint64_t idx = base + (uint64_t)(b0 + u);
+      r[u] = philox_r0_split(seed, (uint32_t)idx, WIDE ? (uint32_t)(idx >> 32) : 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (r[u] >= thr8) word |= 1u << (b0 + u);
+  }
+  return nvalid >= 32 ? word : word & ((1u << nvalid) - 1u);
+}
+
+// thr8 = fa_drop_thresh(p) << 8 (fits: p < 1 gives a threshold below 2^24)
+template <bool WIDE>
+__global__ void __launch_bounds__(256) dropout_mask_kernel(unsigned long long seed, unsigned int thr8, int NH,
                                                            int SQ, int SK, int causal, int wl, int wr,
                                                            unsigned int* bits) {
   const int W = (SK + 31) / 32;
@@ -26,7 +85,7 @@ __global__ void __launch_bounds__(256) dropout_mask_kernel(unsigned long long se
   fa_key_range(q, SQ, SK, causal, wl, wr, 0, lo, hi);
   const int k0 = kw * 32;
   if (hi < k0 || lo > k0 + 31 || lo > hi) return;
-  bits[gid] = fa_keep_word(seed, ((uint64_t)h * SQ + q) * SK + k0, 1, thresh, SK - k0);
+  bits[gid] = keep_word_split<WIDE>(seed, ((uint64_t)h * SQ + q) * SK + k0, thr8, SK - k0);
 }
 
 // One warp per 32 x 32 block (32 query rows x 32 keys): lane l reads the row-major word of row
@@ -108,9 +167,17 @@ extern "C" FA_API int fa_dropout_mask_launch(unsigned long long seed, float p, i
     fa::set_error("dropout mask: %lld words is too large", total);
     return FA_ERR_SIZE;
   }
-  const unsigned int thresh = fa_drop_thresh(p);
-  dropout_mask_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(seed, thresh, NH, SQ, SK, causal,
-                                                                         win_left, win_right, bits);
+  const unsigned int thr8 = fa_drop_thresh(p) << 8;
+  // 32-bit counters when every counter drawn, at most (NH*SQ - 1)*SK + ceil(SK/32)*32 - 1, is
+  // below 2^32; FABLE_ATTN_MASK_WIDE forces the 64-bit form (a test hook: both give the same bits)
+  const bool wide = (unsigned long long)NH * SQ * ((SK + 31) / 32 * 32) > (1ull << 32) ||
+                    getenv("FABLE_ATTN_MASK_WIDE") != nullptr;
+  if (wide)
+    dropout_mask_kernel<true><<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(seed, thr8, NH, SQ, SK, causal,
+                                                                               win_left, win_right, bits);
+  else
+    dropout_mask_kernel<false><<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(seed, thr8, NH, SQ, SK, causal,
+                                                                                win_left, win_right, bits);
   fa::count_launch();
   return fa::cuda_status(cudaGetLastError(), "dropout mask launch");
 }

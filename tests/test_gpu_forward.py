@@ -211,10 +211,14 @@ def test_forward_deterministic(dt):
     assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
 
 
+@pytest.mark.parametrize("wide", [False, True])
 @pytest.mark.parametrize("causal,wl,wr", [(False, -1, -1), (True, -1, -1), (False, 40, 8)])
-def test_dropout_bitmask_matches_oracle(causal, wl, wr):
-    """fa_dropout_mask_launch writes exactly the oracle's keep bits for every word a row can see."""
+def test_dropout_bitmask_matches_oracle(causal, wl, wr, wide, monkeypatch):
+    """fa_dropout_mask_launch writes exactly the oracle's keep bits for every word a row can see,
+    with 32-bit counters and with the 64-bit counter form that masks past 2^32 draws use."""
     import ctypes as C
+    if wide:
+        monkeypatch.setenv("FABLE_ATTN_MASK_WIDE", "1")
     NH, SQ, SK, p_drop, seed = 3, 77, 150, 0.3, 0xABCDEF0123
     W = (SK + 31) // 32
     words = A.lib().fa_dropout_mask_words(NH, SQ, SK)
