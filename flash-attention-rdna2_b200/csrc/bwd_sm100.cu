@@ -935,7 +935,8 @@ int bwd_sm100(const FaBwdParams& p, int dtype, cudaStream_t st, bool* taken) {
   *taken = true;
   if (int rc = bwd_dsum(p, dtype, st)) return rc;
   if (p.dropout && p.dropout_bits && p.dropout_bits_t)
-    if (int rc = dropout_mask_transpose(p.dropout_bits, p.dropout_bits_t, p.Hq, p.SQ, p.SK, st)) return rc;
+    if (int rc = dropout_mask_transpose(p.dropout_bits, p.dropout_bits_t, p.Hq, p.SQ, p.SK, p.causal,
+                                          p.win_left, p.win_right, st)) return rc;
   const bool feat = p.softcap > 0.f || p.alibi != nullptr || p.dropout;
   if (bf16) return feat ? launch_d<true, true>(p, st, maps) : launch_d<true, false>(p, st, maps);
   return feat ? launch_d<false, true>(p, st, maps) : launch_d<false, false>(p, st, maps);

@@ -95,40 +95,64 @@ __global__ void __launch_bounds__(256) dropout_mask_kernel(unsigned long long se
 // bits whose index lacks bit j and takes its partner's such bits shifted up by j; the lane with bit
 // j keeps its bits whose index has bit j and takes its partner's shifted down by j (five shuffles
 // instead of 32 ballots).
-// Warps run query blocks fastest, so reads and writes are 128-byte lines.  Words the mask kernel
-// skipped (no row can see their keys) transpose to words of the same unseen (row, key) pairs.
-// IDX: the integer type of the block index (32-bit whenever the block count fits, so that the
-// per-warp index split is not a 64-bit division)
+// Each warp takes T_BLOCKS consecutive query blocks of one key word and issues their loads before
+// the first shuffle (one 128-byte line per lane and block in flight left HBM at 1.6 TB/s).  Warps
+// run query blocks fastest, so reads and writes are 128-byte lines.  Blocks whose 32 rows see
+// none of the word's keys (causal / window) are neither read nor written: the mask kernel did not
+// write them and the dK/dV kernel masks those scores to zero probability whatever their bits.
+// IDX: the integer type of the warp index (32-bit whenever the count fits, so that the per-warp
+// index split is not a 64-bit division)
+constexpr int T_BLOCKS = 4;
+
 template <typename IDX>
 __global__ void __launch_bounds__(256) dropout_mask_t_kernel(const unsigned int* __restrict__ bits,
                                                              unsigned int* __restrict__ bits_t, int NH, int SQ,
-                                                             int SK) {
-  const IDX W = (SK + 31) / 32, QW = (SQ + 31) / 32;
+                                                             int SK, int causal, int wl, int wr) {
+  const IDX W = (SK + 31) / 32, QW = (SQ + 31) / 32, QG = (QW + T_BLOCKS - 1) / T_BLOCKS;
   const IDX wid = ((IDX)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (wid >= (IDX)NH * W * QW) return;   // whole warps
-  const int qw = (int)(wid % QW);
-  const IDX hk = wid / QW;
+  if (wid >= (IDX)NH * W * QG) return;   // whole warps
+  const int qg = (int)(wid % QG);
+  const IDX hk = wid / QG;
   const int kw = (int)(hk % W), h = (int)(hk / W);
-  const int q = qw * 32 + lane;
-  unsigned int t = q < SQ ? bits[((long long)h * W + kw) * SQ + q] : 0u;
+  const int k0 = kw * 32;
+  unsigned int t[T_BLOCKS], live = 0;
+#pragma unroll
+  for (int i = 0; i < T_BLOCKS; ++i) {
+    const int q = (qg * T_BLOCKS + i) * 32 + lane;
+    bool sees = false;
+    if (q < SQ) {
+      int lo, hi;
+      fa_key_range(q, SQ, SK, causal, wl, wr, 0, lo, hi);
+      sees = !(hi < k0 || lo > k0 + 31 || lo > hi);
+    }
+    if (__ballot_sync(0xffffffffu, sees)) live |= 1u << i;
+    t[i] = (q < SQ && ((live >> i) & 1u)) ? bits[((long long)h * W + kw) * SQ + q] : 0u;
+  }
   // bits whose index lacks bit j: 0x0000FFFF, 0x00FF00FF, 0x0F0F0F0F, 0x33333333, 0x55555555
   const unsigned int lo_mask[5] = {0x0000FFFFu, 0x00FF00FFu, 0x0F0F0F0Fu, 0x33333333u, 0x55555555u};
+  const int k = k0 + lane;
 #pragma unroll
-  for (int i = 0, j = 16; i < 5; ++i, j >>= 1) {
-    const unsigned int m = lo_mask[i], o = __shfl_xor_sync(0xffffffffu, t, j);
-    t = (lane & j) ? ((t & ~m) | ((o & ~m) >> j)) : ((t & m) | ((o & m) << j));
+  for (int i = 0; i < T_BLOCKS; ++i) {
+    if (!((live >> i) & 1u)) continue;   // warp-uniform
+    unsigned int v = t[i];
+#pragma unroll
+    for (int s = 0, j = 16; s < 5; ++s, j >>= 1) {
+      const unsigned int m = lo_mask[s], o = __shfl_xor_sync(0xffffffffu, v, j);
+      v = (lane & j) ? ((v & ~m) | ((o & ~m) >> j)) : ((v & m) | ((o & m) << j));
+    }
+    if (k < SK) bits_t[((long long)h * QW + qg * T_BLOCKS + i) * SK + k] = v;
   }
-  const int k = kw * 32 + lane;
-  if (k < SK) bits_t[((long long)h * QW + qw) * SK + k] = t;
 }
 
 }  // namespace
 
 namespace fa {
 
-int dropout_mask_transpose(const unsigned int* bits, unsigned int* bits_t, int NH, int SQ, int SK, cudaStream_t st) {
-  const long long warps = (long long)NH * ((SK + 31) / 32) * ((SQ + 31) / 32);
+int dropout_mask_transpose(const unsigned int* bits, unsigned int* bits_t, int NH, int SQ, int SK, int causal,
+                           int wl, int wr, cudaStream_t st) {
+  const long long qg = ((SQ + 31) / 32 + T_BLOCKS - 1) / T_BLOCKS;
+  const long long warps = (long long)NH * ((SK + 31) / 32) * qg;
   if (warps == 0) return FA_OK;
   const long long blocks = (warps + 7) / 8;
   if (blocks >= (1ll << 31)) {
@@ -136,9 +160,10 @@ int dropout_mask_transpose(const unsigned int* bits, unsigned int* bits_t, int N
     return FA_ERR_SIZE;
   }
   if (blocks * 256 < (1ll << 32))
-    dropout_mask_t_kernel<unsigned int><<<(unsigned)blocks, 256, 0, st>>>(bits, bits_t, NH, SQ, SK);
+    dropout_mask_t_kernel<unsigned int><<<(unsigned)blocks, 256, 0, st>>>(bits, bits_t, NH, SQ, SK, causal, wl, wr);
   else
-    dropout_mask_t_kernel<unsigned long long><<<(unsigned)blocks, 256, 0, st>>>(bits, bits_t, NH, SQ, SK);
+    dropout_mask_t_kernel<unsigned long long><<<(unsigned)blocks, 256, 0, st>>>(bits, bits_t, NH, SQ, SK, causal, wl,
+                                                                               wr);
   count_launch();
   return cuda_status(cudaGetLastError(), "dropout mask transpose launch");
 }

@@ -11,8 +11,10 @@ int bwd_simt(const FaBwdParams& p, int dtype, cudaStream_t st);
 int bwd_dsum(const FaBwdParams& p, int dtype, cudaStream_t st);
 int bwd_sm100(const FaBwdParams& p, int dtype, cudaStream_t st, bool* taken);
 int bwd_device_error(int clear);   // bits of the tensor-core backward's timed-out waits
-// key-major copy of a dropout keep mask ([NH][ceil(SQ/32)][SK], bit r of word (h, qw, k) = row 32 qw + r)
-int dropout_mask_transpose(const unsigned int* bits, unsigned int* bits_t, int NH, int SQ, int SK, cudaStream_t st);
+// key-major copy of a dropout keep mask ([NH][ceil(SQ/32)][SK], bit r of word (h, qw, k) = row 32 qw + r);
+// 32 x 32 blocks that no row can see under (causal, wl, wr) are not written
+int dropout_mask_transpose(const unsigned int* bits, unsigned int* bits_t, int NH, int SQ, int SK, int causal,
+                           int wl, int wr, cudaStream_t st);
 int dec_run(const FaDecParams& p, int dtype, cudaStream_t st, const void* new_k, const void* new_v);
 int combine_run(const FaCombineParams& p, cudaStream_t st);
 int dec_device_error(int clear);   // bit 0: a decode pipeline wait timed out

@@ -37,6 +37,7 @@ CASES = [
     ("d16", 1, 4, 4, 64, 64, 16, False, -1, -1, 0.0, False, 0.0),
     ("d128", 1, 4, 4, 64, 64, 128, False, -1, -1, 0.0, False, 0.0),
     ("d96_causal", 1, 4, 4, 80, 80, 96, True, -1, -1, 0.0, False, 0.0),
+    ("d128_window_dropout_gqa", 1, 4, 2, 160, 256, 128, False, 40, 24, 0.0, False, 0.1),
     ("d128_causal_dropout_gqa", 2, 8, 2, 192, 192, 128, True, -1, -1, 0.0, False, 0.1),
 ]
 
@@ -151,7 +152,7 @@ def test_backward_varlen_native(dt):
 
 
 @pytest.mark.parametrize("dt", ["fp16", "bf16", "fp32"])
-@pytest.mark.parametrize("name", ["dropout0.2", "d128_causal_dropout_gqa"])
+@pytest.mark.parametrize("name", ["dropout0.2", "d128_causal_dropout_gqa", "d128_window_dropout_gqa"])
 def test_backward_with_bitmask_equals_inkernel_philox(dt, name):
     """Backward reading the precomputed keep bits gives bitwise the same gradients as Philox in-kernel."""
     case = next(c for c in CASES if c[0] == name)
@@ -181,7 +182,8 @@ def test_backward_with_bitmask_equals_inkernel_philox(dt, name):
         QW = (p.SQ + 31) // 32
         row = bits.view(p.Hq, (p.SK + 31) // 32, p.SQ).cpu().numpy().view(np.uint32)
         col = bits_t.view(p.Hq, QW, p.SK).cpu().numpy().view(np.uint32)
-        for h, q, k in [(0, 0, 0), (1, 37, 5), (p.Hq - 1, p.SQ - 1, p.SK - 1), (2, 100, 64)]:
+        for h, q, k in [(0, 0, 0), (1, 37, 5), (p.Hq - 1, p.SQ - 1, p.SK - 1), (2, 100, 64),
+                        (0, min(100, p.SQ - 1), min(200, p.SK - 1))]:
             diag = q + p.SK - p.SQ
             hi = min(p.SK - 1, diag) if p.causal else p.SK - 1
             lo = max(0, diag - p.win_left) if p.win_left >= 0 else 0
