@@ -8,8 +8,8 @@
 // the row can see (causal / window) are skipped: no consumer reads them.
 //
 // The kernel is bound by the integer multiply pipe: a Philox4x32-10 draw is ~17 32 x 32 -> 64-bit
-// products and ~17 three-input XORs, and with every product on the integer multiplier that pipe
-// ran 91 % busy while issue ran at 64 %.  So the high halves of the M0 products of rounds 1-9 come
+// products (two integer-multiply instructions each) plus the XORs, and with every product on the
+// integer multiplier that pipe ran 91 % busy while issue ran at 64 %.  So the high halves of the M0 products of rounds 1-9 come
 // from the otherwise idle fp64 pipe instead (philox_r0_split); the draw is the same function, bit
 // for bit, as fa_philox_r0.
 #include "fa_common.cuh"
