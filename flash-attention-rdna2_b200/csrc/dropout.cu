@@ -2,16 +2,16 @@
 //
 // One thread per 32-bit word = 32 consecutive keys of one (head, query row); consecutive threads
 // take consecutive query rows, so stores are coalesced in the [NH][ceil(SK/32)][SQ] layout.  The
-// 32 Philox evaluations of a word are independent and are issued 8 at a time.  The keep decision
+// 32 Philox evaluations of a word are independent and are issued 4 at a time.  The keep decision
 // is the reference's (kernels/fa_common.hpp:71-88), u = (r0 >> 8) / 2^24, keep iff u >= p,
 // evaluated as the equivalent integer test r0 >= fa_drop_thresh(p) * 2^8.  Words that hold no key
 // the row can see (causal / window) are skipped: no consumer reads them.
 //
 // The kernel is bound by the integer multiply pipe: a Philox4x32-10 draw is ~17 32 x 32 -> 64-bit
 // products (two integer-multiply instructions each) plus the XORs, and with every product on the
-// integer multiplier that pipe ran 91 % busy while issue ran at 64 %.  So the high halves of the M0 products of rounds 1-9 come
-// from the otherwise idle fp64 pipe instead (philox_r0_split); the draw is the same function, bit
-// for bit, as fa_philox_r0.
+// integer multiplier that pipe ran 91 % busy while issue ran at 64 %.  So the high halves of the
+// M0 products of rounds 1-9 come from the otherwise idle fp64 pipe instead (philox_r0_split); the
+// draw is the same function, bit for bit, as fa_philox_r0.
 #include "fa_common.cuh"
 #include "fa_launch.h"
 
@@ -48,6 +48,10 @@ __device__ __forceinline__ uint32_t philox_r0_split(uint64_t seed, uint32_t c0, 
   return c0;
 }
 
+// Draws in flight per thread: 4 measured 0.675 ms on config 3's mask against 0.700 for 8 (the
+// integer form was flat from 2 to 32); 16 and 32 were slower (0.82, 0.87 ms).
+constexpr int MASK_DRAWS = 4;
+
 // Keep bits of counters base .. base + 31 (bit b set iff draw base + b is kept), bits b >= nvalid
 // cleared.  WIDE: counters may exceed 2^32 (64-bit counter per draw); otherwise the high counter
 // word is 0 for every draw of the launch.
@@ -55,15 +59,15 @@ template <bool WIDE>
 __device__ __forceinline__ uint32_t keep_word_split(uint64_t seed, uint64_t base, uint32_t thr8, int nvalid) {
   uint32_t word = 0;
 #pragma unroll 1
-  for (int b0 = 0; b0 < 32; b0 += 8) {
-    uint32_t r[8];
+  for (int b0 = 0; b0 < 32; b0 += MASK_DRAWS) {
+    uint32_t r[MASK_DRAWS];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
+    for (int u = 0; u < MASK_DRAWS; ++u) {
       const uint64_t idx = base + (uint64_t)(b0 + u);
       r[u] = philox_r0_split(seed, (uint32_t)idx, WIDE ? (uint32_t)(idx >> 32) : 0u);
     }
 #pragma unroll
-    for (int u = 0; u < 8; ++u)
+    for (int u = 0; u < MASK_DRAWS; ++u)
       if (r[u] >= thr8) word |= 1u << (b0 + u);
   }
   return nvalid >= 32 ? word : word & ((1u << nvalid) - 1u);
